@@ -1,0 +1,449 @@
+#!/usr/bin/env python
+"""Benchmark of the Q4_K decode GEMV path on B200 (one JSON line on rank 0).
+
+Workload (the reference's Q8_0/Q4_K matvec sweep, Q4_K half): batch-1 GEMVs
+over the four Llama-7B projection shapes (4096x4096, 11008x4096, 4096x11008,
+32000x4096), weights ~N(0, 0.02) quantized to Q4_K by this project's
+quantizer (the reference has none), activations ~N(0, 1).  One step = one
+GEMV per shape, activation packing included.  Weights rotate over R copies
+(4 x 133.9 MB) so every step streams them from HBM, not from the 126 MB L2.
+
+  value   device throughput, algorithmic bytes (weights + 4k + 4n per GEMV)
+          per second; inputs resident in HBM; K steps replayed from one CUDA
+          graph; timed with CUDA events; max over ranks.
+  e2e     the same metric through the C ABI's host-pointer entry point
+          (eosi_cuda_matmul_q: host activations in, host outputs back,
+          weights cached on the device as the backend does for a model).
+  roofline  per-launch CUDA-event times of the GEMV (+ its packing kernel)
+          inside the timed graph vs the measured HBM copy bandwidth.
+  cpu_baseline  the reference's own x86 kernel (compiled from its sources
+          into oracle/_ref) on the host cores, same workload.
+
+Multi-GPU (torchrun): weak scaling -- every rank streams its own row shard
+of N-times-taller matrices (rows are independent; no collective on the data
+path), value = all ranks' bytes / max-over-ranks time.
+
+`--impl reference` runs the reference's CPU implementation (eosi_avx2_matmul_q,
+the x86_avx2 backend's matmul_q slot) with all host threads on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import ctypes as C
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]  # (n, k)
+METRIC = "Q4_K GEMV HBM GB/s (batch-1 sweep 4096x4096, 11008x4096, 4096x11008, 32000x4096)"
+DT_Q4_K = 33
+
+
+def q4k_bytes(n: int, k: int) -> int:
+    return n * (k // 256) * 144
+
+
+def algo_bytes(n: int, k: int) -> int:
+    """Algorithmic bytes of one GEMV: weights + f32 activations + f32 outputs."""
+    return q4k_bytes(n, k) + 4 * k + 4 * n
+
+
+STEP_BYTES = sum(algo_bytes(n, k) for n, k in SHAPES)
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--copies", type=int, default=4, help="rotating weight copies (L2 defeat)")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample length")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# clocks: NVML sampled during the timed region (read-only)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._th = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001
+            self.nv = None
+            self.err = str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            self._sample()
+            time.sleep(self.period)
+
+    def _sample(self):
+        try:
+            mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+            rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            self.samples.append((mhz, rs))
+        except Exception:  # noqa: BLE001
+            pass
+
+    def start(self):
+        if self.nv is not None:
+            self._sample()
+            self._th = threading.Thread(target=self._run, daemon=True)
+            self._th.start()
+
+    def stop(self):
+        if self._th is not None:
+            self._stop.set()
+            self._th.join()
+            self._sample()
+
+    def summary(self):
+        if self.nv is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [s[0] for s in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        reasons = [name for b, name in self.REASONS.items() if bits & b and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(backend: str):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int, device=None) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def dist_done(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def measured_hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """Per-launch DRAM bytes of the GEMV from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "q4k_gemv_sweep.ncu.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch_avg:"):
+                    return int(float(line.split(":", 1)[1]))
+    except OSError:
+        pass
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU: the reference's own kernel (oracle/_ref), row-sharded over threads
+# ---------------------------------------------------------------------------
+class CpuSweep:
+    """eosi_avx2_matmul_q of the reference (or the oracle port when the
+    reference build is absent) over the sweep, rows split across threads;
+    ctypes releases the GIL so the threads run in parallel."""
+
+    def __init__(self, threads: int | None = None, row_fraction: float = 1.0):
+        from oracle.oracle import REF_KERNELS, Oracle, RefKernels
+        if RefKernels.available():
+            self.kind = "reference"
+            lib = RefKernels().lib
+            self.fn = lib.eosi_avx2_matmul_q
+        else:
+            self.kind = "port"
+            lib = Oracle().lib
+            self.fn = lib.orc_matmul_q
+        self.oracle = Oracle()
+        self.threads = threads or os.cpu_count() or 1
+        self.pool = cf.ThreadPoolExecutor(self.threads)
+        self.data = []
+        for s, (n, k) in enumerate(SHAPES):
+            rows = max(self.threads, int(n * row_fraction))
+            w = self.oracle.q4_k_quantize(self.oracle.gauss(rows * k, s, 0.02))
+            x = self.oracle.gauss(k, 10 + s, 1.0)
+            c = np.empty(rows, np.float32)
+            self.data.append((rows, k, w, x, c))
+        self.step_bytes = sum(algo_bytes(rows, k) for rows, k, *_ in self.data)
+        self.row_fraction = row_fraction
+
+    def _part(self, rows, k, w, x, c, lo, hi):
+        rb = (k // 256) * 144
+        rc = self.fn(x.ctypes.data, w.ctypes.data + lo * rb, DT_Q4_K, c.ctypes.data + 4 * lo, 1, hi - lo, k)
+        if rc != 0:
+            raise RuntimeError(f"reference matmul_q failed: {rc}")
+
+    def step(self):
+        futs = []
+        for rows, k, w, x, c in self.data:
+            for t in range(self.threads):
+                lo, hi = rows * t // self.threads, rows * (t + 1) // self.threads
+                if hi > lo:
+                    futs.append(self.pool.submit(self._part, rows, k, w, x, c, lo, hi))
+        for f in futs:
+            f.result()
+
+    def describe(self):
+        sample = "full sweep" if self.row_fraction >= 1.0 else f"{self.row_fraction:.3f} of each matrix's rows"
+        return f"{sample}, batch 1, {self.threads} threads over output rows"
+
+
+def cpu_baseline(seconds: float) -> dict:
+    cpu = CpuSweep()
+    cpu.step()
+    steps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds:
+        cpu.step()
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(cpu.step_bytes * steps / dt / 1e9, 3), "unit": "GB/s", "cores": cpu.threads,
+            "kind": cpu.kind, "sample": f"{steps} sweeps ({cpu.describe()}) in {dt:.1f} s, "
+                                        f"eosi_avx2_matmul_q (Q4_K -> int8 AVX2 path)"}
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup("gloo")
+    if rank != 0:
+        dist_done(world)
+        return
+    # size the sample so K + W steps stay within about two minutes
+    probe = CpuSweep(row_fraction=1.0)
+    t0 = time.perf_counter()
+    probe.step()
+    per_step = time.perf_counter() - t0
+    frac = min(1.0, 120.0 / max(per_step * (args.steps + args.warmup), 1e-9))
+    cpu = probe if frac >= 1.0 else CpuSweep(row_fraction=frac)
+    for _ in range(args.warmup):
+        cpu.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu.step()
+    dt = time.perf_counter() - t0
+    gbs = cpu.step_bytes * args.steps / dt / 1e9
+    line = {
+        "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "q4k_gemv_sweep", "shapes": SHAPES, "batch": 1, "host_threads": cpu.threads,
+                   "sample": cpu.describe()},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu.threads, "kind": cpu.kind,
+                         "sample": cpu.describe()},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    dist_done(world)
+
+
+# ---------------------------------------------------------------------------
+# GPU
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+
+    from eosllm_b200 import backend as B
+
+    world, rank, local = dist_setup("nccl")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B.load()
+    if B.load().eosi_cuda_probe() != 0:
+        raise SystemExit(f"CUDA backend unavailable: {B.last_error()}")
+    B.set_devices([local])
+    R = max(1, args.copies)
+
+    # ---- inputs resident in HBM: rank r owns rows [r*n, (r+1)*n) of N-times-taller matrices
+    weights, acts, outs, scratch = [], [], [], []
+    for s, (n, k) in enumerate(SHAPES):
+        copies = []
+        for r in range(R):
+            w = torch.empty(q4k_bytes(n, k), dtype=torch.uint8, device=dev)
+            B.q4_k_from_gauss_dev(w, n * k, seed=1000 * rank + 100 * r + s, sigma=0.02)
+            copies.append(w)
+        weights.append(copies)
+        x = torch.empty(k, dtype=torch.float32, device=dev)
+        B.fill_gauss_dev(x, k, 10 + s, 0, 1.0)
+        acts.append(x)
+        outs.append(torch.empty(n, dtype=torch.float32, device=dev))
+        scratch.append(torch.empty(B.q4_k_scratch_bytes(1, k), dtype=torch.uint8, device=dev))
+    torch.cuda.synchronize()
+
+    def capture(steps: int, with_events: bool):
+        g = torch.cuda.CUDAGraph()
+        evs = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(steps * len(SHAPES) + 1)] \
+            if with_events else []
+        side = torch.cuda.Stream(device=dev)
+        with torch.cuda.graph(g, stream=side, capture_error_mode="relaxed"):
+            st = torch.cuda.current_stream().cuda_stream
+            e = 0
+            if with_events:
+                evs[e].record()
+                e += 1
+            for i in range(steps):
+                r = i % R
+                for s, (n, k) in enumerate(SHAPES):
+                    B.matmul_q4_k_dev(acts[s], weights[s][r], outs[s], 1, n, k, scratch[s], st)
+                    if with_events:
+                        evs[e].record()
+                        e += 1
+        return g, evs
+
+    g_warm, _ = capture(max(args.warmup, 3), False)
+    g_timed, evs = capture(args.steps, True)
+    g_warm.replay()
+    torch.cuda.synchronize()
+    assert B.take_device_errors() == 0
+
+    clocks = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    g_timed.replay()
+    torch.cuda.synchronize()
+    clocks.stop()
+    barrier(world)
+    if B.take_device_errors() != 0:
+        raise SystemExit("device-side bounded wait reported an error")
+
+    total_ms = evs[0].elapsed_time(evs[-1])
+    per_launch = [evs[i].elapsed_time(evs[i + 1]) for i in range(len(evs) - 1)]
+    per_shape_ms = [statistics.mean(per_launch[s::len(SHAPES)]) for s in range(len(SHAPES))]
+    t_max = max_over_ranks(total_ms, world, dev)
+    value = world * STEP_BYTES * args.steps / (t_max * 1e-3) / 1e9
+    achieved = STEP_BYTES * args.steps / (sum(per_launch) * 1e-3) / 1e9
+    peak, peak_kind = measured_hbm_peak()
+    traffic = profiled_traffic()
+
+    # ---- e2e through the host-pointer C ABI (the backend vtable slot)
+    e2e = None
+    if not args.no_e2e:
+        host_w = [[weights[s][r].cpu().numpy() for r in range(R)] for s in range(len(SHAPES))]
+        host_x = [acts[s].cpu().numpy() for s in range(len(SHAPES))]
+        host_c = [np.empty((1, n), np.float32) for n, _ in SHAPES]
+        for s, (n, k) in enumerate(SHAPES):
+            for r in range(R):
+                B.cache_preload(host_w[s][r], DT_Q4_K, n, k)
+        lib = B.load()
+
+        def e2e_step(i):
+            r = i % R
+            for s, (n, k) in enumerate(SHAPES):
+                rc = lib.eosi_cuda_matmul_q(host_x[s].ctypes.data, host_w[s][r].ctypes.data, DT_Q4_K,
+                                            host_c[s].ctypes.data, 1, n, k)
+                if rc != 0:
+                    raise RuntimeError(B.last_error())
+
+        for i in range(max(args.warmup, 3)):
+            e2e_step(i)
+        e2e_steps = max(args.steps, 10)
+        barrier(world)
+        t0 = time.perf_counter()
+        for i in range(e2e_steps):
+            e2e_step(i)
+        dt = max_over_ranks(time.perf_counter() - t0, world, dev)
+        # check the e2e outputs against the device path (same kernels, same bits)
+        for s, (n, k) in enumerate(SHAPES):
+            B.matmul_q4_k_dev(acts[s], weights[s][(e2e_steps - 1) % R], outs[s], 1, n, k, scratch[s],
+                              torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            assert np.array_equal(outs[s].cpu().numpy().view(np.uint32), host_c[s][0].view(np.uint32))
+        e2e = {"value": round(world * STEP_BYTES * e2e_steps / dt / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": sum(4 * k for _, k in SHAPES),
+               "d2h_bytes_per_step": sum(4 * n for n, _ in SHAPES)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_max / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": "q4k_gemv_sweep", "shapes": SHAPES, "batch": 1,
+                       "weights": "Q4_K, ~N(0,0.02) (Irwin-Hall), own quantizer", "activations": "~N(0,1)",
+                       "l2": f"{R} rotating weight copies ({R * sum(q4k_bytes(n, k) for n, k in SHAPES) / 1e6:.1f}"
+                             " MB) > 126 MB L2",
+                       "timing": "CUDA graph of K steps, CUDA events per launch, max over ranks",
+                       "parallelism": f"row shards x{world}, no collective"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": traffic, "kernel": "q4k_gemv_kernel (+ act_pack_kernel, PDL-overlapped)",
+                         "per_shape_us": {f"{n}x{k}": round(ms * 1e3, 3) for (n, k), ms in zip(SHAPES, per_shape_ms)},
+                         "per_shape_frac": {f"{n}x{k}": round(algo_bytes(n, k) / (ms * 1e-3) / 1e9 / peak, 4)
+                                            for (n, k), ms in zip(SHAPES, per_shape_ms)}},
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "gpu_launches": args.steps * len(SHAPES) * 2,
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del g_timed, g_warm
+    dist_done(world)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

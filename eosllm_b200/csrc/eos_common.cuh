@@ -1,0 +1,199 @@
+// eos_common.cuh -- shared device helpers for the sm_100a quantized matmul
+// kernels: status codes, Q4_K/Q8_0 block constants, mbarrier + bulk-async
+// (TMA 1-D) copies, programmatic dependent launch, bounded waits.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+// eos_status_t values of the reference ABI (include/eosllm/eosllm.h:66-77).
+enum {
+  EOS_OK = 0,
+  EOS_E_INVALID_ARG = 1,
+  EOS_E_OUT_OF_MEMORY = 2,
+  EOS_E_UNSUPPORTED = 3,
+  EOS_E_FORMAT = 4,
+  EOS_E_NOT_FOUND = 6,
+  EOS_E_DEADLINE = 7,
+  EOS_E_IO = 8,
+  EOS_E_INTERNAL = 9
+};
+
+// eos_dtype_t values of the reference ABI (include/eosllm/tensor.h:22-37).
+enum { EOS_DT_F32 = 0, EOS_DT_F16 = 1, EOS_DT_Q8_0 = 32, EOS_DT_Q4_K = 33 };
+
+// GGUF block layouts (src/kernels/scalar/scalar.h:239-243).
+constexpr uint32_t Q4K_ELEMS = 256, Q4K_BYTES = 144;
+constexpr uint32_t Q80_ELEMS = 32, Q80_BYTES = 34;
+
+// Device-side error bits, OR-ed into a host-visible word by kernels whose
+// bounded waits ran out.  The host turns a non-zero word into EOS_E_INTERNAL.
+enum : uint32_t {
+  EOS_DEVERR_WAIT_FULL = 1u << 0,   // consumer gave up waiting for a stage
+  EOS_DEVERR_WAIT_EMPTY = 1u << 1,  // producer gave up waiting for a free slot
+  EOS_DEVERR_WAIT_ACT = 1u << 2,    // activation tile never arrived
+  EOS_DEVERR_DRAIN = 1u << 3,       // in-flight copies did not drain on exit
+  EOS_DEVERR_PEER = 1u << 4,        // a peer flag wait ran out
+};
+
+// One second: the bound on every spin-wait in this library's kernels.
+constexpr uint64_t EOS_WAIT_LIMIT_NS = 1000000000ull;
+
+namespace eos {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier ----------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Makes initialised barriers visible to the async (bulk-copy) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on phase `parity`: true when the phase completed, false when
+// EOS_WAIT_LIMIT_NS elapsed first (the caller records an error and leaves).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > EOS_WAIT_LIMIT_NS) return false;
+  }
+  return true;
+}
+
+// ---- bulk async copy (TMA, 1-D): global -> this CTA's shared memory ----
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ---- programmatic dependent launch --------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ void report(uint32_t* err, uint32_t bits) {
+  if (err) atomicOr(err, bits);
+}
+
+// ---- exact activation packing: x86 semantics of quantize_sub32 -----------
+// MAXPS/MAXSS: first operand if greater, else second (NaN -> second).
+__device__ __forceinline__ float x86_max(float a, float b) { return a > b ? a : b; }
+
+// CVTPS2DQ under the default MXCSR: round to nearest even; NaN and values
+// outside the int32 range give 0x80000000.
+__device__ __forceinline__ int32_t x86_cvtps(float x) {
+  if (!(x == x) || x >= 2147483648.0f || x < -2147483648.0f) return INT32_MIN;
+  return __float2int_rn(x);
+}
+
+// One warp packs one group of 32 activations, lane i holding element i:
+// returns this lane's int8 value; scale and (wrapping) sum are warp-uniform.
+// Restates src/kernels/avx2/matmul_q4_k_int8.c:98-154 bit for bit: the max
+// tree below is the exact lane pairing of the AVX2 code (two vector maxes,
+// then hmax_ps_8's halves / movehl / lane-1 shuffle).
+__device__ __forceinline__ int8_t quant_group32(float v, float& scale, int32_t& sum) {
+  const unsigned FULL = 0xffffffffu;
+  float t = __int_as_float(__float_as_int(v) & 0x7fffffff);
+  t = x86_max(t, __shfl_down_sync(FULL, t, 8));   // max(ma0, ma1) | max(ma2, ma3)
+  t = x86_max(t, __shfl_down_sync(FULL, t, 16));  // mx = max(.., ..)
+  t = x86_max(t, __shfl_down_sync(FULL, t, 4));   // max_ps(lo, hi)
+  t = x86_max(t, __shfl_down_sync(FULL, t, 2));   // max_ps(m, movehl(m))
+  t = x86_max(t, __shfl_down_sync(FULL, t, 1));   // max_ss(m, lane 1)
+  const float max_abs = __shfl_sync(FULL, t, 0);
+  float inv;
+  if (max_abs > 0.0f) {
+    scale = __fdiv_rn(max_abs, 127.0f);
+    inv = __fdiv_rn(127.0f, max_abs);
+  } else {
+    scale = 0.0f;
+    inv = 0.0f;
+  }
+  const int32_t q = x86_cvtps(__fmul_rn(v, inv));
+  sum = static_cast<int32_t>(__reduce_add_sync(FULL, static_cast<uint32_t>(q)));
+  return static_cast<int8_t>(q < -128 ? -128 : (q > 127 ? 127 : q));
+}
+
+// 6-bit sub-block scale/min unpack (src/kernels/avx2/matmul_q4_k_int8.c:58-67).
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t* q, uint32_t& sc, uint32_t& m) {
+  if (j < 4) {
+    sc = q[j] & 63u;
+    m = q[j + 4] & 63u;
+  } else {
+    sc = (q[j + 4] & 15u) | ((q[j - 4] >> 6) << 4);
+    m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+// Same unpack on the 12 scale bytes held as three little-endian words.
+__device__ __forceinline__ void q4k_scale_min_w(int j, uint32_t w0, uint32_t w1, uint32_t w2, uint32_t& sc,
+                                                uint32_t& m) {
+  // byte(i) of the 12-byte field
+  auto byte = [&](int i) -> uint32_t {
+    const uint32_t w = i < 4 ? w0 : (i < 8 ? w1 : w2);
+    return (w >> (8 * (i & 3))) & 0xffu;
+  };
+  if (j < 4) {
+    sc = byte(j) & 63u;
+    m = byte(j + 4) & 63u;
+  } else {
+    sc = (byte(j + 4) & 15u) | ((byte(j - 4) >> 6) << 4);
+    m = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
+  }
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xffffu)));
+}
+
+}  // namespace eos

@@ -1,0 +1,41 @@
+// eos_kernels.h -- internal launch interface between the C-ABI layer
+// (eos_backend.cu) and the kernel files.  Not installed; the public
+// boundary is include/eosllm_cuda.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+// Layouts the activation packer can write.
+enum { EOS_ACT_LAYOUT_GEMV = 0, EOS_ACT_LAYOUT_SOURCE = 1 };
+
+namespace eos {
+
+size_t act_layout_bytes(uint32_t m, uint32_t k, int layout);
+cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out, int layout, cudaStream_t st);
+
+// out_status: EOS_OK, or EOS_E_UNSUPPORTED when the shape cannot be staged.
+cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, float* c, uint32_t n, uint32_t k, uint32_t* err,
+                            int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status);
+void set_q4k_gemv_variant(int v);
+// n < 4 Q4_K: the reference's f32-dequant path, bit for bit.
+cudaError_t launch_q4k_f32_small_n(const float* a, const uint8_t* w, float* c, uint32_t m, uint32_t n, uint32_t k,
+                                   cudaStream_t st);
+
+cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t n, uint32_t k, uint32_t* err,
+                            int num_sms, int max_smem, cudaStream_t st, int* out_status);
+void set_q80_gemv_variant(int v);
+
+// Test/utility kernels (eos_util.cu).
+cudaError_t launch_unpack_scale_min(const uint8_t* scales12, uint32_t count, uint8_t* sc, uint8_t* m,
+                                    cudaStream_t st);
+cudaError_t launch_fill_gauss(float* dst, size_t n, uint64_t seed, uint64_t offset, float sigma, cudaStream_t st);
+cudaError_t launch_q4k_quantize(const float* src, uint8_t* dst, size_t n_el, cudaStream_t st);
+cudaError_t launch_q80_quantize(const float* src, uint8_t* dst, size_t n_el, cudaStream_t st);
+// Generator fused into the Q4_K quantizer: super-block b quantizes the
+// generated elements offset + 256b .. offset + 256b + 255.
+cudaError_t launch_q4k_from_gauss(uint8_t* dst, size_t nblocks, uint64_t seed, uint64_t offset, float sigma,
+                                  cudaStream_t st);
+
+}  // namespace eos

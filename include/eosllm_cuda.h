@@ -1,0 +1,168 @@
+/*
+ * eosllm_cuda.h -- C ABI of the B200 (sm_100a) backend for eosllm's
+ * quantized matmul path (libeosllm_cuda.so).
+ *
+ * Plain C: no CUDA or C++ types in any signature.  Every function returns an
+ * eos_status_t value as int (0 = EOS_OK, 1 = EOS_E_INVALID_ARG,
+ * 2 = EOS_E_OUT_OF_MEMORY, 3 = EOS_E_UNSUPPORTED, 9 = EOS_E_INTERNAL;
+ * include/eosllm/eosllm.h:66-77 of the reference), never aborts, and writes
+ * outputs only on EOS_OK.  The last failure is described by
+ * eosi_cuda_last_error().  Dtype codes are the reference's eos_dtype_t
+ * (include/eosllm/tensor.h:32-33): 32 = Q8_0, 33 = Q4_K.
+ *
+ * Two layers:
+ *   1. Host-pointer entry points with exactly the semantics of the
+ *      reference's backend slot eos_backend_ops_t.matmul_q
+ *      (include/eosllm/backend.h:43-46): synchronous, all pointers host
+ *      memory owned by the caller, C = A . deq(B)^T row-major.  Weights are
+ *      uploaded on first use and cached on the device(s), keyed by the host
+ *      pointer, dtype and shape (plus a fingerprint of the first and last
+ *      64 bytes, so a freed-and-reused address with new contents is
+ *      re-uploaded).  Output rows are sharded across the configured GPUs.
+ *   2. Device-pointer entry points (suffix _dev) that enqueue on a caller
+ *      stream (a cudaStream_t passed as void*, NULL = legacy default stream)
+ *      on the current device, for device-resident callers.
+ */
+#ifndef EOSLLM_CUDA_H
+#define EOSLLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EOSLLM_CUDA_API __attribute__((visibility("default")))
+#else
+#define EOSLLM_CUDA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- backend lifecycle ------------------------------------------------ */
+
+/* EOS_OK when at least one sm_100 GPU is usable.  Cached after the first
+ * call, so cheap enough for the registry to call at every session open.
+ * Replaces the backend probe slot eos_backend_vt_t.probe
+ * (include/eosllm/backend.h:71-76; cf. avx2_probe, src/kernels/avx2/avx2.c:79-81). */
+EOSLLM_CUDA_API int eosi_cuda_probe(void);
+
+/* Number of usable sm_100 devices (0 when none). */
+EOSLLM_CUDA_API int eosi_cuda_device_count(void);
+
+/* Select the GPUs the host-pointer entry points shard output rows across.
+ * ids == NULL or count <= 0 restores the default: the list in the
+ * EOSLLM_CUDA_DEVICES environment variable ("0,1,2"), else device 0.
+ * Drops the weight cache. */
+EOSLLM_CUDA_API int eosi_cuda_set_devices(const int *ids, int count);
+
+/* Release every device buffer, stream and cached weight.  The next call
+ * re-initialises lazily. */
+EOSLLM_CUDA_API void eosi_cuda_shutdown(void);
+
+/* Human-readable description of the last failure in this thread. */
+EOSLLM_CUDA_API const char *eosi_cuda_last_error(void);
+
+/* ---- host-pointer matmuls (the backend vtable slot) -------------------- */
+
+/* eos_backend_ops_t.matmul_q replacement (include/eosllm/backend.h:43-46);
+ * dispatch as in eosi_avx2_matmul_q (src/kernels/avx2/matmul_q4_k.c:155-171):
+ * Q4_K and Q8_0 run on the GPU, any other dtype is EOS_E_UNSUPPORTED. */
+EOSLLM_CUDA_API int eosi_cuda_matmul_q(const float *a, const void *b_quant, int b_dtype, float *c,
+                       uint32_t m, uint32_t n, uint32_t k);
+
+/* Q4_K: replaces eosi_avx2_matmul_q4_k_int8
+ * (src/kernels/avx2/matmul_q4_k_int8.c:164-269) and is bit-identical to it:
+ * activations packed to int8 exactly as quantize_sub32 (:98-154), exact
+ * integer sub-block dots, fp32 rescale in the reference's order.  k % 256
+ * must be 0 (EOS_E_INVALID_ARG otherwise, as at :173-174).  For n < 4 the
+ * reference routes to its f32-dequant path eosi_avx2_matmul_q4_k (:182-184,
+ * src/kernels/avx2/matmul_q4_k.c:70-153); so does this backend, with the
+ * same eight FMA accumulator lanes and horizontal sum, again bit-identical. */
+EOSLLM_CUDA_API int eosi_cuda_matmul_q4_k(const float *a, const void *b_q4, float *c,
+                          uint32_t m, uint32_t n, uint32_t k);
+
+/* Q8_0: replaces eosi_scalar_matmul_q8_0 (src/kernels/scalar/matmul_q8.c:21-58),
+ * f32 activations; agrees to fp32 rounding (different summation order).
+ * k % 32 must be 0. */
+EOSLLM_CUDA_API int eosi_cuda_matmul_q8_0(const float *a, const void *b_q8, float *c,
+                          uint32_t m, uint32_t n, uint32_t k);
+
+/* Forget the cached device copy of one host weight buffer (or of all). */
+EOSLLM_CUDA_API int eosi_cuda_cache_evict(const void *b_quant);
+EOSLLM_CUDA_API int eosi_cuda_cache_clear(void);
+
+/* Upload (or refresh) one weight buffer now instead of on first use. */
+EOSLLM_CUDA_API int eosi_cuda_cache_preload(const void *b_quant, int b_dtype, uint32_t n, uint32_t k);
+
+/* ---- device-pointer entry points (current device, caller stream) ------- */
+
+/* Scratch the Q4_K entry points need for m activation rows of length k:
+ * the packed int8 activations, scales and sums (5k/4 bytes per row). */
+EOSLLM_CUDA_API size_t eosi_cuda_q4_k_scratch_bytes(uint32_t m, uint32_t k);
+
+/* C[m,n] = A[m,k] . deq(W)^T with A, W, C and scratch in device memory.
+ * W is n rows of k/256 GGUF Q4_K super-blocks, 16-byte aligned; A and
+ * scratch 16-byte aligned; scratch >= eosi_cuda_q4_k_scratch_bytes(m, k).
+ * Asynchronous on `stream`; bit-identical to eosi_cuda_matmul_q4_k. */
+EOSLLM_CUDA_API int eosi_cuda_matmul_q4_k_dev(const float *a, const void *w, float *c, uint32_t m, uint32_t n,
+                              uint32_t k, void *scratch, void *stream);
+
+/* The two halves of eosi_cuda_matmul_q4_k_dev, for callers that pack one
+ * activation vector once and multiply it by several weights:
+ *   pack: a[m,k] -> act (eosi_cuda_q4_k_scratch_bytes(m, k) bytes);
+ *   gemv: c[n] = act(row 0) . deq(W)^T. */
+EOSLLM_CUDA_API int eosi_cuda_q4_k_pack_act_dev(const float *a, uint32_t m, uint32_t k, void *act, void *stream);
+EOSLLM_CUDA_API int eosi_cuda_q4_k_gemv_dev(const void *act, const void *w, float *c, uint32_t n, uint32_t k,
+                            void *stream);
+
+/* Q8_0 with device pointers (W 16-byte aligned, k % 256 == 0 on this path). */
+EOSLLM_CUDA_API int eosi_cuda_matmul_q8_0_dev(const float *a, const void *w, float *c, uint32_t m, uint32_t n,
+                              uint32_t k, void *stream);
+
+/* Activation packing in source order, for checking it against
+ * quantize_sub32 (src/kernels/avx2/matmul_q4_k_int8.c:98-154) bit for bit:
+ * aq[m*k] int8, scales[m*k/32] f32, sums[m*k/32] int32. */
+EOSLLM_CUDA_API int eosi_cuda_quantize_act_dev(const float *a, uint32_t m, uint32_t k, int8_t *aq, float *scales,
+                               int32_t *sums, void *stream);
+
+/* Scale/min unpack of `count` 12-byte Q4_K scale fields into 8 sc and 8 m
+ * bytes each -- the GEMV's own unpack, checked against get_scale_min
+ * (src/kernels/avx2/matmul_q4_k_int8.c:58-67). */
+EOSLLM_CUDA_API int eosi_cuda_unpack_scale_min_dev(const uint8_t *scales12, uint32_t count, uint8_t *sc, uint8_t *m,
+                                   void *stream);
+
+/* ---- weight formats and synthetic data on the device ------------------- */
+
+/* Q8_0 weight quantizer: src/quant/q8_0.c:58-93, bit for bit. */
+EOSLLM_CUDA_API int eosi_cuda_q8_0_quantize_dev(const float *src, void *dst, size_t n_elements, void *stream);
+
+/* Q4_K weight quantizer.  The reference has none (src/quant/q4_k.c:83-93
+ * returns EOS_E_UNSUPPORTED); this is the project's affine min/max fit,
+ * dequantized by the reference's q4_k_dequantize (src/quant/q4_k.c:42-81). */
+EOSLLM_CUDA_API int eosi_cuda_q4_k_quantize_dev(const float *src, void *dst, size_t n_elements, void *stream);
+
+/* Seeded synthetic values (Irwin-Hall(12) normal approximation on
+ * splitmix64; element i of stream `seed` is identical on host and device). */
+EOSLLM_CUDA_API int eosi_cuda_fill_gauss_dev(float *dst, size_t n, uint64_t seed, uint64_t offset, float sigma,
+                             void *stream);
+
+/* Generator fused into the Q4_K quantizer: n_elements synthetic values of
+ * stream `seed` (offset 0) quantized straight to Q4_K without an f32 copy. */
+EOSLLM_CUDA_API int eosi_cuda_q4_k_from_gauss_dev(void *dst, size_t n_elements, uint64_t seed, float sigma,
+                                  void *stream);
+
+/* ---- diagnostics --------------------------------------------------------- */
+
+/* Device-side error bits raised by bounded waits since the last call on the
+ * current device (0 = none); clears them. */
+EOSLLM_CUDA_API int eosi_cuda_take_device_errors(uint32_t *bits);
+
+/* Kernel variant override for tuning (-1 = automatic). */
+EOSLLM_CUDA_API int eosi_cuda_set_kernel_variant(int b_dtype, int variant);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* EOSLLM_CUDA_H */

@@ -1,0 +1,87 @@
+"""The C-ABI boundary on the CPU: the library loads, exports every entry
+point include/eosllm_cuda.h declares, and validates arguments with the
+reference's status codes before it ever touches a GPU."""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from eosllm_b200 import backend as B
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_exports_every_declared_symbol(cuda_lib):
+    declared = B.declared_symbols()
+    assert len(declared) >= 20
+    out = subprocess.run(["nm", "-D", "--defined-only", B.LIB_PATH], capture_output=True, text=True, check=True)
+    exported = {line.split()[-1] for line in out.stdout.splitlines() if " T " in line}
+    missing = [s for s in declared if s not in exported]
+    assert not missing, missing
+    # nothing else leaks out of the library
+    extra = [s for s in exported if not s.startswith("eosi_cuda_")]
+    assert not extra, extra
+    for s in declared:
+        assert hasattr(cuda_lib, s)
+
+
+def test_header_is_plain_c(tmp_path):
+    src = tmp_path / "t.c"
+    src.write_text('#include "eosllm_cuda.h"\nint main(void){return eosi_cuda_probe() < 0;}\n')
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-pedantic", "-I", os.path.join(ROOT, "include"),
+                    "-c", str(src), "-o", str(tmp_path / "t.o")], check=True)
+
+
+def test_argument_validation_matches_reference(cuda_lib):
+    a = np.ones(512, np.float32)
+    w = np.zeros(144 * 2, np.uint8)
+    c = np.full(2, 7.0, np.float32)
+    # NULL pointers -> EOS_E_INVALID_ARG (matmul_q4_k_int8.c:172)
+    assert B.matmul_q_status(None, w, B.DT_Q4_K, c, 1, 1, 512) == B.EOS_E_INVALID_ARG
+    assert B.matmul_q_status(a, None, B.DT_Q4_K, c, 1, 1, 512) == B.EOS_E_INVALID_ARG
+    assert B.matmul_q_status(a, w, B.DT_Q4_K, None, 1, 1, 512) == B.EOS_E_INVALID_ARG
+    # k % 256 != 0 -> EOS_E_INVALID_ARG (:173-174); k % 32 for Q8_0 (matmul_q8.c:33)
+    assert B.matmul_q_status(a, w, B.DT_Q4_K, c, 1, 1, 300) == B.EOS_E_INVALID_ARG
+    assert B.matmul_q_status(a, w, B.DT_Q8_0, c, 1, 1, 40) == B.EOS_E_INVALID_ARG
+    # any other dtype -> EOS_E_UNSUPPORTED (matmul_q4_k.c:168-169)
+    for dt in (0, 1, 34, 35, 99):
+        assert B.matmul_q_status(a, w, dt, c, 1, 1, 512) == B.EOS_E_UNSUPPORTED
+    assert "dtype" in B.last_error()
+    # outputs untouched on failure (eosllm.h:60-65)
+    assert np.all(c == 7.0)
+    # empty shapes succeed without work, like the reference's loops
+    assert B.matmul_q_status(a, w, B.DT_Q4_K, c, 0, 1, 512) == B.EOS_OK
+    assert B.matmul_q_status(a, w, B.DT_Q4_K, c, 1, 0, 512) == B.EOS_OK
+
+
+def test_probe_without_gpu_is_an_error_not_a_crash(cuda_lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert cuda_lib.eosi_cuda_probe() == B.EOS_E_UNSUPPORTED
+    assert cuda_lib.eosi_cuda_device_count() == 0
+    assert B.last_error()
+    # a real call fails loudly with the probe's status; nothing falls back to the CPU
+    a = np.ones(256, np.float32)
+    w = np.zeros(144 * 4, np.uint8)
+    c = np.zeros(4, np.float32)
+    assert B.matmul_q_status(a, w, B.DT_Q4_K, c, 1, 4, 256) == B.EOS_E_UNSUPPORTED
+    with pytest.raises(B.CudaBackendError):
+        B.matmul_q(a, w, B.DT_Q4_K, 1, 4, 256)
+
+
+def test_scratch_size_formula(cuda_lib):
+    for m, k in ((1, 256), (3, 4096), (2, 11008)):
+        assert B.q4_k_scratch_bytes(m, k) == m * (k + k // 4)
+
+
+def test_missing_library_fails_loudly(tmp_path, cuda_lib):
+    saved = B._lib
+    try:
+        B._lib = None
+        with pytest.raises(FileNotFoundError):
+            B.load(str(tmp_path / "nope.so"))
+    finally:
+        B._lib = saved
