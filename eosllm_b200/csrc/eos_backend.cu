@@ -289,12 +289,21 @@ int enqueue_matmul(DevInfo* info, int dtype, const float* d_a, const uint8_t* d_
       EOS_CK(eos::launch_q4k_f32_small_n(d_a, d_w, d_c, m, rows, k, st), "q4_k small-n kernel");
       return EOS_OK;
     }
+    if (m == 1) {  // one kernel: activation packing fused into the GEMV
+      int status = EOS_OK;
+      EOS_CK(eos::launch_q4k_gemv(d_w, nullptr, d_a, d_c, rows, k, info->err_d, info->num_sms, info->max_smem, true,
+                                  st, &status),
+             "q4_k gemv kernel");
+      if (status == EOS_OK) return EOS_OK;
+      if (d_act == nullptr) return fail(EOS_E_INVALID_ARG, "q4_k: k=%u needs the scratch buffer", k);
+    }
+    if (d_act == nullptr) return fail(EOS_E_INVALID_ARG, "NULL scratch");
     EOS_CK(eos::launch_act_pack(d_a, m, k, d_act, EOS_ACT_LAYOUT_GEMV, st), "activation pack kernel");
-    const size_t act_stride = (size_t)k + (k >> 2);
+    const size_t act_stride = eos::act_layout_bytes(1, k, EOS_ACT_LAYOUT_GEMV);
     for (uint32_t i = 0; i < m; ++i) {
       int status = EOS_OK;
-      EOS_CK(eos::launch_q4k_gemv(d_w, d_act + i * act_stride, d_c + (size_t)i * rows, rows, k, info->err_d,
-                                  info->num_sms, info->max_smem, true, st, &status),
+      EOS_CK(eos::launch_q4k_gemv(d_w, d_act + i * act_stride, nullptr, d_c + (size_t)i * rows, rows, k,
+                                  info->err_d, info->num_sms, info->max_smem, true, st, &status),
              "q4_k gemv kernel");
       if (status != EOS_OK) return fail(status, "q4_k gemv: shape %u x %u not supported", rows, k);
     }
@@ -527,7 +536,6 @@ int eosi_cuda_matmul_q4_k_dev(const float* a, const void* w, float* c, uint32_t 
                               void* scratch, void* stream) {
   int rc = check_args(a, w, c, EOS_DT_Q4_K, k);
   if (rc != EOS_OK) return rc;
-  if (n >= 4 && scratch == nullptr) return fail(EOS_E_INVALID_ARG, "NULL scratch");
   if (!al16(a) || !al16(w) || (scratch && !al16(scratch)))
     return fail(EOS_E_INVALID_ARG, "device pointers must be 16-byte aligned");
   if (m == 0 || n == 0) return EOS_OK;
@@ -558,7 +566,7 @@ int eosi_cuda_q4_k_gemv_dev(const void* act, const void* w, float* c, uint32_t n
   rc = dev_prologue(&info);
   if (rc != EOS_OK) return rc;
   int status = EOS_OK;
-  EOS_CK(eos::launch_q4k_gemv((const uint8_t*)w, (const uint8_t*)act, c, n, k, info->err_d, info->num_sms,
+  EOS_CK(eos::launch_q4k_gemv((const uint8_t*)w, (const uint8_t*)act, nullptr, c, n, k, info->err_d, info->num_sms,
                               info->max_smem, true, (cudaStream_t)stream, &status),
          "q4_k gemv kernel");
   if (status != EOS_OK) return fail(status, "q4_k gemv: shape %u x %u not supported", n, k);

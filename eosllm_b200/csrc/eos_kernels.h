@@ -15,9 +15,12 @@ namespace eos {
 size_t act_layout_bytes(uint32_t m, uint32_t k, int layout);
 cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out, int layout, cudaStream_t st);
 
-// out_status: EOS_OK, or EOS_E_UNSUPPORTED when the shape cannot be staged.
-cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, float* c, uint32_t n, uint32_t k, uint32_t* err,
-                            int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status);
+// Exactly one of `act` (packed activations, GEMV layout) and `a` (f32
+// activations, packed inside the kernel) is non-null.  out_status: EOS_OK, or
+// EOS_E_UNSUPPORTED when the shape cannot be staged on the fused path (the
+// caller then packs separately).
+cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
+                            uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status);
 void set_q4k_gemv_variant(int v);
 // n < 4 Q4_K: the reference's f32-dequant path, bit for bit.
 cudaError_t launch_q4k_f32_small_n(const float* a, const uint8_t* w, float* c, uint32_t m, uint32_t n, uint32_t k,

@@ -2,45 +2,65 @@
 // production x86 path eosi_avx2_matmul_q4_k_int8
 // (src/kernels/avx2/matmul_q4_k_int8.c:164-269).
 //
-// Two kernels per call:
-//   1. act_pack_kernel: one warp per 32 activations, the exact x86 packing of
-//      quantize_sub32 (:98-154).  It writes the "GEMV layout" below and lets
-//      the dependent GEMV launch early (programmatic dependent launch).
-//   2. q4k_gemv_kernel: persistent, one CTA per SM.  A producer warp streams
-//      the CTA's contiguous slab of weight rows HBM -> shared memory with 1-D
-//      bulk async copies (TMA) into an S-stage mbarrier ring; consumer warps
-//      compute integer dp4a dots per 32-element sub-block and the fp32
-//      rescale in the reference's evaluation order, so every output is
-//      bit-identical to the CPU kernel (the integer dots are exact, and the
-//      fp32 operations are issued with explicit round-to-nearest intrinsics
-//      in the same order with no FMA contraction).
+// Activation packing -- the exact x86 arithmetic of quantize_sub32
+// (:98-154) -- either runs inside the GEMV (each CTA packs the f32 vector
+// into shared memory while its first weight stages stream in) or in
+// act_pack_kernel, chained to the GEMV with programmatic dependent launch
+// (PDL), when one packed vector feeds several GEMVs or m > 1.
 //
-// GEMV activation layout (per activation row, 5k/4 bytes, k % 256 == 0):
-//   [0, k)        int8 a_q, super-block b occupies bytes [256b, 256b+256):
-//                 bytes 16c..16c+15        = sub-block 2(c/2),   half c%2
-//                 bytes 128+16c..128+16c+15 = sub-block 2(c/2)+1, half c%2
-//                 for chunk c = 0..7, i.e. exactly the a_q lanes that meet
-//                 the 16 qs bytes [16c, 16c+16) of the super-block, so each
-//                 quarter-warp reads 128 contiguous bytes (no bank conflict).
-//   [k, k + k/4)  per 32-group g: {float scale, int32 sum_aq} (8 bytes).
+// q4k_gemv_kernel: each CTA owns a contiguous slab of weight rows, cut into
+// stages of R rows.  Warp w of NW takes stages w, w+NW, ... and streams them
+// HBM -> shared memory with coalesced 16-byte cp.async copies through D
+// buffers of its own, computing one stage while the next D-1 land.  Weight
+// copies are issued before the PDL wait, so they overlap the previous
+// kernel's tail.  Two lanes share a super-block: lane h (0/1) takes qs pairs
+// 2h, 2h+1, i.e. sub-blocks 4h..4h+3: exact integer dp4a dots, then the
+// reference's fp32 rescale terms with round-to-nearest intrinsics (no FMA
+// contraction).  Lane 0 adds its four terms to 0, lane 1 continues that
+// partial with its four, so the super-block partial is the reference's
+// (((0 + t_0) + t_1) + ... + t_7).  Partials are then broadcast in
+// super-block order and one lane per row adds them: every output is
+// bit-identical to the CPU kernel.
+//
+// Shared-memory banking: a 16-byte load phase is 8 lanes = 4 super-blocks x
+// 2 halves.  With R = 1 the 4 super-blocks are consecutive b (b*144 == 16b
+// mod 128, halves at +64); with R >= 2 they are rows at a pitch == 32 (R=2)
+// or 16 (R>=4) mod 128.  Activation records are 480 bytes (== 96 mod 128)
+// with the second half at +272 (== 16 mod 128).  Every phase therefore hits
+// 8 distinct 16-byte bank groups.
+//
+// Activation record (per super-block b, 480 bytes at 480 b; k % 256 == 0):
+//   half h = 0, 1 at offset 272 h:
+//     [0, 128)    int8 a_q of sub-blocks 4h .. 4h+3, source order
+//     [128, 160)  per sub-block: {f32 scale, f32 (float)sum_aq} (the sum
+//                 stored converted, exactly the reference's (float) cast at
+//                 :256-261)
+//   bytes [160, 272) and [432, 480) are padding.
 #include "eos_common.cuh"
 #include "eos_kernels.h"
 
 namespace eos {
 
-// ---------------------------------------------------------------------------
-// Activation packing
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t gemv_layout_offset(uint32_t e) {
-  const uint32_t b = e >> 8, local = e & 255u, sub = local >> 5, pos = local & 31u;
-  const uint32_t c = ((sub >> 1) << 1) | (pos >> 4);
-  return (b << 8) | ((sub & 1u) << 7) | (c << 4) | (pos & 15u);
+constexpr uint32_t kActRec = 480;   // bytes per super-block of packed activations
+constexpr uint32_t kActHalf = 272;  // offset of the second half-record
+
+// Record position of 32-group g (sub-block g % 8 of super-block g / 8).
+__device__ __forceinline__ uint32_t rec_aq_offset(uint32_t g) {
+  const uint32_t s = g & 7u;
+  return (g >> 3) * kActRec + (s >> 2) * kActHalf + ((s & 3u) << 5);
+}
+__device__ __forceinline__ uint32_t rec_st_offset(uint32_t g) {
+  const uint32_t s = g & 7u;
+  return (g >> 3) * kActRec + (s >> 2) * kActHalf + 128u + ((s & 3u) << 3);
 }
 
-// grid: ceil(m*k/32 / 8) blocks of 256 threads; warp -> one 32-group.
+// ---------------------------------------------------------------------------
+// Activation packing kernel: one warp per 32-group.
+// ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) act_pack_kernel(const float* __restrict__ a, uint32_t m, uint32_t k,
                                                        uint8_t* __restrict__ out, int layout) {
-  pdl_trigger();
+  pdl_trigger();  // let the dependent GEMV start streaming its weights
+  pdl_wait();     // `a` may be the previous kernel's output
   const uint32_t groups_per_row = k >> 5;
   const uint32_t gid = blockIdx.x * 8u + (threadIdx.x >> 5);
   const uint32_t lane = threadIdx.x & 31u;
@@ -51,14 +71,9 @@ __global__ void __launch_bounds__(256) act_pack_kernel(const float* __restrict__
   int32_t sum;
   const int8_t q = quant_group32(v, scale, sum);
   if (layout == EOS_ACT_LAYOUT_GEMV) {
-    uint8_t* r = out + (size_t)row * (k + (k >> 2));
-    r[gemv_layout_offset((g << 5) + lane)] = static_cast<uint8_t>(q);
-    if (lane == 0) {
-      float2 st;
-      st.x = scale;
-      st.y = __int_as_float(sum);
-      *reinterpret_cast<float2*>(r + k + (g << 3)) = st;
-    }
+    uint8_t* r = out + (size_t)row * ((k >> 8) * kActRec);
+    r[rec_aq_offset(g) + lane] = static_cast<uint8_t>(q);
+    if (lane == 0) *reinterpret_cast<float2*>(r + rec_st_offset(g)) = make_float2(scale, (float)sum);
   } else {  // EOS_ACT_LAYOUT_SOURCE: int8[m*k], then float[m*k/32], then int32[m*k/32]
     out[(size_t)row * k + (g << 5) + lane] = static_cast<uint8_t>(q);
     if (lane == 0) {
@@ -71,206 +86,238 @@ __global__ void __launch_bounds__(256) act_pack_kernel(const float* __restrict__
 }
 
 // ---------------------------------------------------------------------------
-// Q4_K GEMV
+// Half a super-block, one lane
 // ---------------------------------------------------------------------------
-struct Q4kGemvParams {
-  const uint8_t* w;    // n rows x row_bytes (GGUF Q4_K super-blocks)
-  const uint8_t* act;  // GEMV activation layout, 5k/4 bytes
-  float* c;            // n outputs
-  uint32_t n, k, nb, row_bytes, stages, act_bytes;
-  uint32_t* err;
-};
+// dp4a with the first operand's bytes unsigned (the high nibbles kept in
+// place, i.e. 16 * q_hi <= 240) and the second's signed (activations).
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 
-// Dot products of RW weight rows with one packed activation row, computed by
-// one warp.  Lane = (g, l8): group g (0..3) takes super-block b0+g of each
-// 4-block step, lane l8 its qs bytes [16 l8, 16 l8 + 16).  Row pointers and
-// act may point to shared or global memory (16-byte aligned).  Every output
-// equals eosi_avx2_matmul_q4_k_int8's bit for bit: exact integer dots, then
-//   partial_b = (((0 + t_0) + t_1) + ... + t_7),
-//   t_s = ((d*sc_s)*as_s)*dot_s - ((dmin*m_s)*as_s)*sum_s   (no FMA),
-//   c = ((0 + partial_0) + partial_1) + ...
-// as at src/kernels/avx2/matmul_q4_k_int8.c:194, :254-261, :264.
-template <int RW>
-__device__ __forceinline__ void q4k_rows_dot(const uint8_t* const (&rowp)[RW], const uint8_t* act, uint32_t nb,
-                                             uint32_t k, uint32_t lane, float (&acc)[RW]) {
-  const unsigned FULL = 0xffffffffu;
-  const uint32_t g = lane >> 3, l8 = lane & 7u, pr = l8 >> 1;
-  const uint8_t* st_base = act + k;
+// Exact integer dots of one qs pair (32 bytes as two uint4) with the
+// activation lanes of its two sub-blocks: lo nibbles x sub 2p, hi nibbles x
+// sub 2p+1 (src/kernels/avx2/matmul_q4_k_int8.c:234-249).  The high-nibble
+// dot is taken on the nibble in place (x16, exact) and shifted back.
+__device__ __forceinline__ void pair_dots(uint4 q0, uint4 q1, int4 a0, int4 a1, int4 a2, int4 a3, int& dl, int& dh) {
+  constexpr uint32_t LO = 0x0F0F0F0Fu, HI = 0xF0F0F0F0u;
+  int l = __dp4a((int)(q0.x & LO), a0.x, 0);
+  int h = dp4a_us(q0.x & HI, a2.x, 0);
+  l = __dp4a((int)(q0.y & LO), a0.y, l);
+  h = dp4a_us(q0.y & HI, a2.y, h);
+  l = __dp4a((int)(q0.z & LO), a0.z, l);
+  h = dp4a_us(q0.z & HI, a2.z, h);
+  l = __dp4a((int)(q0.w & LO), a0.w, l);
+  h = dp4a_us(q0.w & HI, a2.w, h);
+  l = __dp4a((int)(q1.x & LO), a1.x, l);
+  h = dp4a_us(q1.x & HI, a3.x, h);
+  l = __dp4a((int)(q1.y & LO), a1.y, l);
+  h = dp4a_us(q1.y & HI, a3.y, h);
+  l = __dp4a((int)(q1.z & LO), a1.z, l);
+  h = dp4a_us(q1.z & HI, a3.z, h);
+  l = __dp4a((int)(q1.w & LO), a1.w, l);
+  h = dp4a_us(q1.w & HI, a3.w, h);
+  dl = l;
+  dh = h >> 4;  // exact: the sum is a multiple of 16
+}
+
+// t_s = ((d*sc_s)*as_s)*dot_s - ((dmin*m_s)*as_s)*sum_s, in the reference's
+// order (:254-261).
+__device__ __forceinline__ float sb_term(float d, float dmin, uint32_t sc, uint32_t m, float as, float sum, int dot) {
+  return __fsub_rn(__fmul_rn(__fmul_rn(__fmul_rn(d, (float)sc), as), (float)dot),
+                   __fmul_rn(__fmul_rn(__fmul_rn(dmin, (float)m), as), sum));
+}
+
+// The four terms of sub-blocks 4h..4h+3.  blk: the 144-byte GGUF super-block,
+// half: its 160-byte activation half-record (both 16-byte aligned, shared or
+// global memory).  The 6-bit scales/mins come out byte-parallel: get_scale_min
+// (:58-67) for all j at once.
+__device__ __forceinline__ void q4k_half_terms(const uint8_t* blk, const uint8_t* half, uint32_t h, float (&t)[4]) {
+  const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+  const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
+  // sc[4h .. 4h+3] and m[4h .. 4h+3] as bytes of one word each
+  const uint32_t scw = h == 0 ? (hdr.y & 0x3F3F3F3Fu) : ((hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u));
+  const uint32_t mw = h == 0 ? (hdr.z & 0x3F3F3F3Fu) : (((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u));
+  const uint8_t* qs = blk + 16 + 64 * h;
 #pragma unroll
-  for (int r = 0; r < RW; ++r) acc[r] = 0.0f;
-  for (uint32_t b0 = 0; b0 < nb; b0 += 4) {
-    const uint32_t b = (b0 + g) < nb ? (b0 + g) : (nb - 1);
-    // activation lanes + scales for this super-block, shared by the RW rows
-    const int4 alo = *reinterpret_cast<const int4*>(act + (b << 8) + (l8 << 4));
-    const int4 ahi = *reinterpret_cast<const int4*>(act + (b << 8) + 128 + (l8 << 4));
-    const float4 st = *reinterpret_cast<const float4*>(st_base + (((b << 3) + (pr << 1)) << 3));
+  for (int p = 0; p < 2; ++p) {
+    const uint4 q0 = *reinterpret_cast<const uint4*>(qs + 32 * p);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 32 * p + 16);
+    const int4 a0 = *reinterpret_cast<const int4*>(half + 64 * p);
+    const int4 a1 = *reinterpret_cast<const int4*>(half + 64 * p + 16);
+    const int4 a2 = *reinterpret_cast<const int4*>(half + 64 * p + 32);
+    const int4 a3 = *reinterpret_cast<const int4*>(half + 64 * p + 48);
+    const float4 st = *reinterpret_cast<const float4*>(half + 128 + 16 * p);
+    int dl, dh;
+    pair_dots(q0, q1, a0, a1, a2, a3, dl, dh);
+    t[2 * p] = sb_term(d, dmin, (scw >> (16 * p)) & 0xFFu, (mw >> (16 * p)) & 0xFFu, st.x, st.y, dl);
+    t[2 * p + 1] = sb_term(d, dmin, (scw >> (16 * p + 8)) & 0xFFu, (mw >> (16 * p + 8)) & 0xFFu, st.z, st.w, dh);
+  }
+}
+
+// Super-block partial from a lane pair (lane h = lane & 1 holds half h): the
+// result is valid on the odd lane.  All 32 lanes must call it.
+__device__ __forceinline__ float pair_partial(const float (&t)[4], uint32_t lane) {
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, t[0]), t[1]), t[2]), t[3]);
+  const float first = __shfl_up_sync(0xffffffffu, s, 1);
+  if (lane & 1u) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(first, t[0]), t[1]), t[2]), t[3]);
+  return s;
+}
+
+// ---------------------------------------------------------------------------
+// In-CTA activation packing into shared memory (fused path)
+// ---------------------------------------------------------------------------
+template <int NW>
+__device__ __forceinline__ void pack_into_smem(const float* __restrict__ a, uint32_t k, uint8_t* act_s,
+                                               uint32_t warp, uint32_t lane) {
+  const uint32_t groups = k >> 5;
+  for (uint32_t g0 = warp; g0 < groups; g0 += 4 * NW) {
+    float v[4];
 #pragma unroll
-    for (int r = 0; r < RW; ++r) {
-      const uint8_t* blk = rowp[r] + b * Q4K_BYTES;
-      const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-      const uint4 qs = *reinterpret_cast<const uint4*>(blk + 16 + (l8 << 4));
-      int dlo = __dp4a((int)(qs.x & 0x0F0F0F0Fu), alo.x, 0);
-      dlo = __dp4a((int)(qs.y & 0x0F0F0F0Fu), alo.y, dlo);
-      dlo = __dp4a((int)(qs.z & 0x0F0F0F0Fu), alo.z, dlo);
-      dlo = __dp4a((int)(qs.w & 0x0F0F0F0Fu), alo.w, dlo);
-      int dhi = __dp4a((int)((qs.x >> 4) & 0x0F0F0F0Fu), ahi.x, 0);
-      dhi = __dp4a((int)((qs.y >> 4) & 0x0F0F0F0Fu), ahi.y, dhi);
-      dhi = __dp4a((int)((qs.z >> 4) & 0x0F0F0F0Fu), ahi.z, dhi);
-      dhi = __dp4a((int)((qs.w >> 4) & 0x0F0F0F0Fu), ahi.w, dhi);
-      dlo += __shfl_xor_sync(FULL, dlo, 1);
-      dhi += __shfl_xor_sync(FULL, dhi, 1);
-      const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
-      uint32_t sc_lo, m_lo, sc_hi, m_hi;
-      q4k_scale_min_w((int)(pr << 1), hdr.y, hdr.z, hdr.w, sc_lo, m_lo);
-      q4k_scale_min_w((int)(pr << 1) + 1, hdr.y, hdr.z, hdr.w, sc_hi, m_hi);
-      const float t_lo =
-          __fsub_rn(__fmul_rn(__fmul_rn(__fmul_rn(d, (float)sc_lo), st.x), (float)dlo),
-                    __fmul_rn(__fmul_rn(__fmul_rn(dmin, (float)m_lo), st.x), (float)__float_as_int(st.y)));
-      const float t_hi =
-          __fsub_rn(__fmul_rn(__fmul_rn(__fmul_rn(d, (float)sc_hi), st.z), (float)dhi),
-                    __fmul_rn(__fmul_rn(__fmul_rn(dmin, (float)m_hi), st.z), (float)__float_as_int(st.w)));
-      float partial = 0.0f;
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t g = g0 + u * NW;
+      v[u] = g < groups ? a[(g << 5) + lane] : 0.0f;
+    }
 #pragma unroll
-      for (uint32_t q = 0; q < 4; ++q) {
-        const float xl = __shfl_sync(FULL, t_lo, (g << 3) + (q << 1));
-        const float xh = __shfl_sync(FULL, t_hi, (g << 3) + (q << 1));
-        partial = __fadd_rn(partial, xl);
-        partial = __fadd_rn(partial, xh);
-      }
-#pragma unroll
-      for (uint32_t q = 0; q < 4; ++q) {
-        const float pq = __shfl_sync(FULL, partial, q << 3);
-        if (b0 + q < nb) acc[r] = __fadd_rn(acc[r], pq);
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t g = g0 + u * NW;
+      if (g < groups) {  // warp-uniform
+        float scale;
+        int32_t sum;
+        const int8_t q = quant_group32(v[u], scale, sum);
+        act_s[rec_aq_offset(g) + lane] = static_cast<uint8_t>(q);
+        if (lane == 0) *reinterpret_cast<float2*>(act_s + rec_st_offset(g)) = make_float2(scale, (float)sum);
       }
     }
   }
 }
 
-// Fallback without staging (rows too long for the shared-memory ring):
-// one warp per weight row, straight from global memory.
-__global__ void __launch_bounds__(256) q4k_gemv_simple_kernel(const uint8_t* __restrict__ w,
-                                                              const uint8_t* __restrict__ act, float* __restrict__ c,
-                                                              uint32_t n, uint32_t k) {
-  pdl_wait();
-  const uint32_t row = blockIdx.x * 8u + (threadIdx.x >> 5);
-  if (row >= n) return;  // warp-uniform
-  const uint32_t nb = k / Q4K_ELEMS;
-  const uint8_t* rowp[1] = {w + (size_t)row * nb * Q4K_BYTES};
-  float acc[1];
-  q4k_rows_dot<1>(rowp, act, nb, k, threadIdx.x & 31u, acc);
-  if ((threadIdx.x & 31u) == 0) c[row] = acc[0];
-}
+// ---------------------------------------------------------------------------
+// Q4_K GEMV
+// ---------------------------------------------------------------------------
+struct Q4kGemvParams {
+  const uint8_t* w;    // n rows x row_bytes (GGUF Q4_K super-blocks)
+  const uint8_t* act;  // packed activation records, act_bytes (packed path)
+  const float* a;      // f32 activations, k (fused path)
+  float* c;            // n outputs
+  uint32_t n, k, nb, row_bytes, pitch, R, act_bytes;
+  uint32_t* err;
+};
 
-constexpr uint32_t kBarBytes = 256;  // 8 full + 8 empty + 1 act barrier, padded
-
-// CW consumer warps, each owning RW rows of every stage; one producer warp.
-template <int CW, int RW>
-__global__ void __launch_bounds__((CW + 1) * 32, 1) q4k_gemv_kernel(const Q4kGemvParams p) {
+template <int NW, int D>
+__global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* empty = full + 8;
-  uint64_t* actbar = full + 16;
-  uint8_t* act_s = smem + kBarBytes;
-  uint8_t* stage0 = act_s + ((p.act_bytes + 127u) & ~127u);
-  constexpr uint32_t R = CW * RW;
-  const uint32_t stage_bytes = R * p.row_bytes;
-  const uint32_t S = p.stages;
+  const uint32_t act_region = (p.act_bytes + 127u) & ~127u;
+  uint8_t* act_s = smem;
+  const uint32_t R = p.R, nb = p.nb, pitch = p.pitch, row_bytes = p.row_bytes;
+  const uint32_t buf_bytes = R * pitch;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  uint8_t* wbuf = smem + act_region + warp * D * buf_bytes;
 
   const uint32_t r0 = (uint32_t)(((uint64_t)p.n * blockIdx.x) / gridDim.x);
   const uint32_t r1 = (uint32_t)(((uint64_t)p.n * (blockIdx.x + 1)) / gridDim.x);
   const uint32_t nrows = r1 - r0;
   const uint32_t nst = (nrows + R - 1) / R;
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  if (nrows == 0) return;  // CTA-uniform
+  const uint32_t cpr = row_bytes >> 4;  // 16-byte chunks per row
+  const uint64_t pol_w = l2_policy_evict_first();
 
-  if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], CW);
+  auto issue = [&](uint32_t s, uint32_t slot) {
+    if (s < nst) {
+      const uint32_t rows = (nrows - s * R) < R ? (nrows - s * R) : R;
+      const uint8_t* src = p.w + (size_t)(r0 + s * R) * row_bytes;
+      uint8_t* dst = wbuf + slot * buf_bytes;
+      for (uint32_t r = 0; r < rows; ++r)
+        for (uint32_t t = lane; t < cpr; t += 32)
+          cp_async16(dst + r * pitch + (t << 4), src + (size_t)r * row_bytes + (t << 4), pol_w);
     }
-    mbar_init(actbar, 1);
-    fence_barrier_init();
+    cp_async_commit();  // one group per call, empty or not, keeps the counting uniform
+  };
+
+  // Weights do not depend on the previous kernel: start streaming them first.
+#pragma unroll
+  for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(warp + d * NW, d);
+
+  pdl_wait();  // the activations are the previous kernel's output
+  if (p.a != nullptr) {
+    pack_into_smem<NW>(p.a, p.k, act_s, warp, lane);
+  } else {
+    const uint4* src = reinterpret_cast<const uint4*>(p.act);
+    uint4* dst = reinterpret_cast<uint4*>(act_s);
+    for (uint32_t t = threadIdx.x; t < (p.act_bytes >> 4); t += NW * 32) dst[t] = src[t];
   }
   __syncthreads();
+  pdl_trigger();  // every CTA holds its activations: the next kernel may start
 
-  if (warp == CW) {  // ---------------- producer warp ----------------
-    if (lane == 0) {
-      const uint64_t pol_w = l2_policy_evict_first();
-      const uint64_t pol_a = l2_policy_evict_last();
-      const uint32_t prime = nst < S ? nst : S;
-      uint32_t issued = 0;
-      bool ok = true;
-      for (uint32_t s = 0; s < nst; ++s) {
-        const uint32_t slot = s % S;
-        if (s >= S && !mbar_wait(&empty[slot], ((s / S) - 1u) & 1u)) {
-          report(p.err, EOS_DEVERR_WAIT_EMPTY);
-          ok = false;
-          break;
-        }
-        const uint32_t rows = (nrows - s * R) < R ? (nrows - s * R) : R;
-        const uint32_t bytes = rows * p.row_bytes;
-        mbar_arrive_expect_tx(&full[slot], bytes);
-        bulk_g2s(stage0 + (size_t)slot * stage_bytes, p.w + (size_t)(r0 + s * R) * p.row_bytes, bytes, &full[slot],
-                 pol_w);
-        ++issued;
-        if (s + 1 == prime) {
-          // Weights do not depend on the packing kernel; the activations do.
-          pdl_wait();
-          mbar_arrive_expect_tx(actbar, p.act_bytes);
-          bulk_g2s(act_s, p.act, p.act_bytes, actbar, pol_a);
-        }
-      }
-      if (!ok) {
-        // Do not leave while our own copies may still land in shared memory.
-        for (uint32_t s = (issued > S ? issued - S : 0); s < issued; ++s)
-          if (!mbar_wait(&full[s % S], (s / S) & 1u)) report(p.err, EOS_DEVERR_DRAIN);
-        if (issued >= 1 && !mbar_wait(actbar, 0)) report(p.err, EOS_DEVERR_DRAIN);
-      }
-    }
-    return;
-  }
-
-  // -------------------- consumer warps --------------------
-  if (!mbar_wait(actbar, 0)) {
-    report(p.err, EOS_DEVERR_WAIT_ACT);
-    return;
-  }
-  const uint32_t nb = p.nb;
-
-  for (uint32_t s = 0; s < nst; ++s) {
-    const uint32_t slot = s % S;
-    if (!mbar_wait(&full[slot], (s / S) & 1u)) {
-      report(p.err, EOS_DEVERR_WAIT_FULL);
-      return;
-    }
-    const uint32_t rows = (nrows - s * R) < R ? (nrows - s * R) : R;
-    const uint8_t* stage = stage0 + (size_t)slot * stage_bytes;
-    const uint32_t rbase = warp * RW;
-    if (rbase < rows) {  // warp-uniform
-      const uint8_t* rowp[RW];
-#pragma unroll
-      for (int r = 0; r < RW; ++r) {
-        const uint32_t row = (rbase + r) < rows ? (rbase + r) : (rows - 1);
-        rowp[r] = stage + (size_t)row * p.row_bytes;
-      }
-      float acc[RW];
-      q4k_rows_dot<RW>(rowp, act_s, nb, p.k, lane, acc);
-      if (lane == 0) {
-#pragma unroll
-        for (int r = 0; r < RW; ++r)
-          if (rbase + r < rows) p.c[r0 + s * R + rbase + r] = acc[r];
-      }
-    }
+  const uint32_t h = lane & 1u;
+  uint32_t i = 0;
+  for (uint32_t s = warp; s < nst; s += NW, ++i) {
+    const uint32_t slot = i % D;
+    cp_async_wait<D - 1>();  // this warp's stage i has landed
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
+    const uint32_t rows = (nrows - s * R) < R ? (nrows - s * R) : R;
+    const uint8_t* stage = wbuf + slot * buf_bytes;
+    // item q = 2 * (b * rows + row) + h; odd lanes end up holding partials
+    const uint32_t units = rows * nb, items = 2u * units;
+    float acc = 0.0f;  // lane r < rows: c[row r] = 0; += partial_b in b order (:194, :264)
+    uint32_t rj = 0;   // row of the next unit to broadcast
+    for (uint32_t q0 = 0; q0 < items; q0 += 32) {
+      const uint32_t u = (q0 + lane) >> 1;  // (b, row) unit of this lane
+      float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      if (u < units) {
+        uint32_t row, b;
+        if (rows == R) {
+          row = u & (R - 1u);
+          b = u >> (31u - __clz(R));
+        } else {
+          b = u / rows;
+          row = u - b * rows;
+        }
+        q4k_half_terms(stage + row * pitch + b * Q4K_BYTES, act_s + b * kActRec + h * kActHalf, h, t);
+      }
+      const float part = pair_partial(t, lane);
+      // units q0/2 .. q0/2+15 of this chunk, in order: row = unit % rows
+      const uint32_t u0 = q0 >> 1, cnt = (units - u0) < 16u ? (units - u0) : 16u;
+      for (uint32_t j = 0; j < cnt; ++j) {
+        const float v = __shfl_sync(0xffffffffu, part, 2u * j + 1u);
+        if (rj == lane) acc = __fadd_rn(acc, v);
+        rj = (rj + 1u == rows) ? 0u : rj + 1u;
+      }
+    }
+    if (lane < rows) p.c[r0 + s * R + lane] = acc;
+    __syncwarp();  // all lanes done with this buffer before it is refilled
+    issue(s + D * NW, slot);
   }
+  cp_async_wait<0>();  // never exit with copies still landing in shared memory
+}
+
+// Fallback without staging (rows too long for shared memory): one warp per
+// weight row from global memory, packed activations in global memory.
+__global__ void __launch_bounds__(256) q4k_gemv_simple_kernel(const uint8_t* __restrict__ w,
+                                                              const uint8_t* __restrict__ act, float* __restrict__ c,
+                                                              uint32_t n, uint32_t k) {
+  pdl_wait();
+  const uint32_t row = blockIdx.x * 8u + (threadIdx.x >> 5), lane = threadIdx.x & 31u;
+  if (row >= n) return;  // warp-uniform
+  const uint32_t nb = k / Q4K_ELEMS, h = lane & 1u;
+  const uint8_t* rp = w + (size_t)row * nb * Q4K_BYTES;
+  float acc = 0.0f;
+  for (uint32_t b0 = 0; b0 < nb; b0 += 16) {
+    const uint32_t b = b0 + (lane >> 1);
+    float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (b < nb) q4k_half_terms(rp + b * Q4K_BYTES, act + (size_t)b * kActRec + h * kActHalf, h, t);
+    const float part = pair_partial(t, lane);
+    const uint32_t cnt = (nb - b0) < 16u ? (nb - b0) : 16u;
+    for (uint32_t j = 0; j < cnt; ++j) acc = __fadd_rn(acc, __shfl_sync(0xffffffffu, part, 2u * j + 1u));
+  }
+  if (lane == 0) c[row] = acc;
 }
 
 // ---------------------------------------------------------------------------
 // Host-side launchers
 // ---------------------------------------------------------------------------
 size_t act_layout_bytes(uint32_t m, uint32_t k, int layout) {
-  if (layout == EOS_ACT_LAYOUT_GEMV) return (size_t)m * (k + (k >> 2));
+  if (layout == EOS_ACT_LAYOUT_GEMV) return (size_t)m * (k / Q4K_ELEMS) * kActRec;
   return (size_t)m * k + (size_t)m * (k >> 5) * 8u;
 }
 
@@ -278,60 +325,95 @@ cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out
   const uint32_t groups = m * (k >> 5);
   const uint32_t blocks = (groups + 7u) / 8u;
   if (blocks == 0) return cudaSuccess;
-  act_pack_kernel<<<blocks, 256, 0, st>>>(a, m, k, out, layout);
-  return cudaGetLastError();
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(blocks);
+  lc.blockDim = dim3(256);
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, act_pack_kernel, a, m, k, out, layout);
 }
 
 namespace {
 struct GemvConfig {
   void (*fn)(const Q4kGemvParams);
-  int cw, rw;
+  int nw, d;
+  int smem_set;  // largest dynamic shared memory already allowed
 };
-
-template <int CW, int RW>
-GemvConfig make_cfg() {
-  return GemvConfig{q4k_gemv_kernel<CW, RW>, CW, RW};
-}
+GemvConfig g_cfgs[] = {{q4k_gemv_kernel<16, 4>, 16, 4, 0}, {q4k_gemv_kernel<16, 3>, 16, 3, 0},
+                       {q4k_gemv_kernel<16, 2>, 16, 2, 0}, {q4k_gemv_kernel<20, 3>, 20, 3, 0},
+                       {q4k_gemv_kernel<8, 4>, 8, 4, 0},   {q4k_gemv_kernel<12, 4>, 12, 4, 0},
+                       {q4k_gemv_kernel<24, 2>, 24, 2, 0}, {q4k_gemv_kernel<8, 6>, 8, 6, 0}};
+constexpr int kNumCfgs = sizeof(g_cfgs) / sizeof(g_cfgs[0]);
+int g_q4k_variant = -1;  // kernel config override (-1: automatic)
+int g_q4k_rows = 0;      // rows-per-stage override (0: automatic)
+int g_q4k_ctas = 0;      // CTAs-per-SM override (0: automatic)
 }  // namespace
 
-static int g_q4k_variant = -1;  // -1: automatic
+void set_q4k_gemv_variant(int v) {
+  // v < 0: automatic.  Else v = cfg + 16 * rows + 256 * ctas_per_sm, each
+  // field 0 = automatic.
+  g_q4k_variant = v < 0 ? -1 : (v % 16);
+  g_q4k_rows = v < 0 ? 0 : ((v / 16) % 16);
+  g_q4k_ctas = v < 0 ? 0 : (v / 256);
+}
 
-void set_q4k_gemv_variant(int v) { g_q4k_variant = v; }
-
-cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, float* c, uint32_t n, uint32_t k, uint32_t* err,
-                            int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status) {
+cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
+                            uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status) {
   *out_status = EOS_OK;
   if (n == 0) return cudaSuccess;
-  static const GemvConfig cfgs[] = {make_cfg<8, 1>(), make_cfg<8, 2>(), make_cfg<16, 1>(), make_cfg<4, 2>()};
   const uint32_t nb = k / Q4K_ELEMS;
   const uint32_t row_bytes = nb * Q4K_BYTES;
-  const uint32_t act_bytes = k + (k >> 2);
+  const uint32_t act_bytes = nb * kActRec;
   const uint32_t act_region = (act_bytes + 127u) & ~127u;
-  const uint32_t budget = (uint32_t)max_smem - kBarBytes - act_region;
-
-  int pick = g_q4k_variant;
-  if (pick < 0 || pick >= (int)(sizeof(cfgs) / sizeof(cfgs[0]))) {
-    // Prefer two rows per warp (activation lanes reused) while >= 3 stages fit.
-    pick = (budget / (16u * row_bytes) >= 3u) ? 1 : 0;
+  // rows per stage: at least 32 half-super-blocks (one per lane) per stage
+  uint32_t R = 1;
+  while (R < 16u && 2u * R * nb < 32u) R <<= 1;
+  if (g_q4k_rows == 1 || g_q4k_rows == 2 || g_q4k_rows == 4 || g_q4k_rows == 8) R = (uint32_t)g_q4k_rows;
+  const uint32_t target = R == 1 ? 0u : (R == 2 ? 32u : 16u);
+  const uint32_t pitch = row_bytes + ((target - (row_bytes & 127u)) & 127u);
+  // deepest per-warp pipeline that fits: 16 warps x D buffers, else fewer
+  int pick = -1;
+  if (g_q4k_variant >= 0 && g_q4k_variant < kNumCfgs) {
+    pick = g_q4k_variant;
+  } else {
+    const int order[] = {0, 1, 2, 4};
+    for (int o : order)
+      if (act_region + (uint32_t)(g_cfgs[o].nw * g_cfgs[o].d) * R * pitch <= (uint32_t)max_smem) {
+        pick = o;
+        break;
+      }
+    if (pick < 0) pick = 2;
   }
-  const GemvConfig cfg = cfgs[pick];
-  const uint32_t R = (uint32_t)(cfg.cw * cfg.rw);
-  uint32_t stages = budget / (R * row_bytes);
-  if (stages > 8u) stages = 8u;
-  if (stages < 2u) {  // row too long for the staged ring
+  GemvConfig& cfg = g_cfgs[pick];
+  const uint32_t smem = act_region + (uint32_t)(cfg.nw * cfg.d) * R * pitch;
+  if (smem > (uint32_t)max_smem) {  // rows too long to stage: unstaged kernel
+    if (act == nullptr) {           // it reads packed activations from global memory
+      *out_status = EOS_E_UNSUPPORTED;
+      return cudaSuccess;
+    }
     q4k_gemv_simple_kernel<<<(n + 7u) / 8u, 256, 0, st>>>(w, act, c, n, k);
     return cudaGetLastError();
   }
-  const uint32_t smem = kBarBytes + act_region + stages * R * row_bytes;
-  cudaError_t e = cudaFuncSetAttribute(cfg.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-
-  Q4kGemvParams prm{w, act, c, n, k, nb, row_bytes, stages, act_bytes, err};
-  uint32_t grid = (uint32_t)num_sms;
-  if (grid > n) grid = n;
+  if ((int)smem > cfg.smem_set) {
+    cudaError_t e = cudaFuncSetAttribute(cfg.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    cfg.smem_set = (int)smem;
+  }
+  uint32_t cps = (uint32_t)(max_smem + 1024) / (smem + 1024);
+  if (cps > 4u) cps = 4u;
+  if (cps < 1u) cps = 1u;
+  if (g_q4k_ctas > 0) cps = (uint32_t)g_q4k_ctas;
+  uint32_t grid = (uint32_t)num_sms * cps;
+  const uint32_t max_grid = (n + R - 1) / R;
+  if (grid > max_grid) grid = max_grid;
+  Q4kGemvParams prm{w, act, a, c, n, k, nb, row_bytes, pitch, R, act_bytes, err};
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
-  lc.blockDim = dim3((cfg.cw + 1) * 32);
+  lc.blockDim = dim3(cfg.nw * 32);
   lc.dynamicSmemBytes = smem;
   lc.stream = st;
   cudaLaunchAttribute attr[1];
@@ -339,8 +421,7 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, float* c, uint
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = pdl ? 1 : 0;
-  e = cudaLaunchKernelEx(&lc, cfg.fn, prm);
-  return e;
+  return cudaLaunchKernelEx(&lc, cfg.fn, prm);
 }
 
 }  // namespace eos

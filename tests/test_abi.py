@@ -74,7 +74,7 @@ def test_probe_without_gpu_is_an_error_not_a_crash(cuda_lib):
 
 def test_scratch_size_formula(cuda_lib):
     for m, k in ((1, 256), (3, 4096), (2, 11008)):
-        assert B.q4_k_scratch_bytes(m, k) == m * (k + k // 4)
+        assert B.q4_k_scratch_bytes(m, k) == m * (k // 256) * 480
 
 
 def test_missing_library_fails_loudly(tmp_path, cuda_lib):

@@ -117,15 +117,29 @@ def test_q4k_known_answer_and_int8_fixture(gpu):
     assert np.all(c == 0.0)
 
 
-def test_q4k_golden_cases_bitexact(gpu):
+def int8_vs_f32_bound(oracle, a, w, m, n, k):
+    """Worst-case gap between the int8-activation path and the f32 path:
+    each packed activation is within scale/2 of the f32 value, so
+    |c_int8 - c_f32| <= sum_k |w_jk| * scale_k / 2 (+ fp32 rounding)."""
+    deq = oracle.q4_k_dequantize(w, n * k).reshape(n, k).astype(np.float64)
+    bound = np.empty((m, n))
+    for i in range(m):
+        _, sc, _ = oracle.quantize_act(a[i * k:(i + 1) * k])
+        half = np.repeat(sc.astype(np.float64), 32) / 2.0
+        bound[i] = np.abs(deq) @ half + 1e-5 * (np.abs(deq) @ np.abs(a[i * k:(i + 1) * k].astype(np.float64)))
+    return bound
+
+
+def test_q4k_golden_cases_bitexact(gpu, oracle):
     g = golden("q4k_matmul.npz")
     idx = 0
     while f"c{idx}_shape" in g:
         m, n, k = (int(v) for v in g[f"c{idx}_shape"])
-        c = gpu.matmul_q(g[f"c{idx}_a"], g[f"c{idx}_w"], DT_Q4_K, m, n, k)
+        a, w = g[f"c{idx}_a"], g[f"c{idx}_w"]
+        c = gpu.matmul_q(a, w, DT_Q4_K, m, n, k)
         assert same_bits(c, g[f"c{idx}_matmul_q"]), (m, n, k)
-        s = g[f"c{idx}_scalar"]
-        assert np.all(np.abs(c - s) <= np.maximum(5e-3 * np.abs(s), 1e-3) * 4), (m, n, k)
+        # and within the activation-rounding bound of the scalar f32 oracle
+        assert np.all(np.abs(c - g[f"c{idx}_scalar"]) <= int8_vs_f32_bound(oracle, a, w, m, n, k)), (m, n, k)
         idx += 1
     assert idx == 10
 
@@ -145,9 +159,17 @@ def test_q4k_model_shapes_bitexact(gpu, oracle, n, k):
     scratch = torch.empty(gpu.q4_k_scratch_bytes(1, k), dtype=torch.uint8, device="cuda")
     gpu.matmul_q4_k_dev(da, dw, dc, 1, n, k, scratch)
     assert same_bits(host(dc), ref[0])
+    # fused packing (no scratch) and the two-kernel pack + gemv path agree too
+    dc.zero_()
+    gpu.matmul_q4_k_dev(da, dw, dc, 1, n, k, 0)
+    assert same_bits(host(dc), ref[0])
+    dc.zero_()
+    gpu.q4_k_pack_act_dev(da, 1, k, scratch)
+    gpu.q4_k_gemv_dev(scratch, dw, dc, n, k)
+    assert same_bits(host(dc), ref[0])
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5, 6, 7, 16, 32, 64, 128, 5 + 16 * 4, 2 * 256 + 2 + 16 * 2])
 def test_q4k_kernel_variants_bitexact(gpu, oracle, variant):
     try:
         gpu.set_kernel_variant(DT_Q4_K, variant)
