@@ -289,7 +289,7 @@ int enqueue_matmul(DevInfo* info, int dtype, const float* d_a, const uint8_t* d_
       EOS_CK(eos::launch_q4k_f32_small_n(d_a, d_w, d_c, m, rows, k, st), "q4_k small-n kernel");
       return EOS_OK;
     }
-    if (m == 1) {  // one kernel: activation packing fused into the GEMV
+    if (m == 1 && d_act == nullptr) {  // no scratch: activation packing fused into the GEMV
       int status = EOS_OK;
       EOS_CK(eos::launch_q4k_gemv(d_w, nullptr, d_a, d_c, rows, k, info->err_d, info->num_sms, info->max_smem, true,
                                   st, &status),

@@ -156,13 +156,20 @@ __device__ __forceinline__ int32_t x86_cvtps(float x) {
 // then hmax_ps_8's halves / movehl / lane-1 shuffle).
 __device__ __forceinline__ int8_t quant_group32(float v, float& scale, int32_t& sum) {
   const unsigned FULL = 0xffffffffu;
-  float t = __int_as_float(__float_as_int(v) & 0x7fffffff);
-  t = x86_max(t, __shfl_down_sync(FULL, t, 8));   // max(ma0, ma1) | max(ma2, ma3)
-  t = x86_max(t, __shfl_down_sync(FULL, t, 16));  // mx = max(.., ..)
-  t = x86_max(t, __shfl_down_sync(FULL, t, 4));   // max_ps(lo, hi)
-  t = x86_max(t, __shfl_down_sync(FULL, t, 2));   // max_ps(m, movehl(m))
-  t = x86_max(t, __shfl_down_sync(FULL, t, 1));   // max_ss(m, lane 1)
-  const float max_abs = __shfl_sync(FULL, t, 0);
+  const uint32_t abits = __float_as_uint(v) & 0x7fffffffu;
+  // Without NaNs every max order gives the same value, and |x| bit patterns
+  // order like the floats, so one integer max reduction is exact.
+  uint32_t mbits = __reduce_max_sync(FULL, abits);
+  if (mbits > 0x7f800000u) {  // a NaN: reproduce the AVX2 tree's exact pick
+    float t = __uint_as_float(abits);
+    t = x86_max(t, __shfl_down_sync(FULL, t, 8));   // max(ma0, ma1) | max(ma2, ma3)
+    t = x86_max(t, __shfl_down_sync(FULL, t, 16));  // mx = max(.., ..)
+    t = x86_max(t, __shfl_down_sync(FULL, t, 4));   // max_ps(lo, hi)
+    t = x86_max(t, __shfl_down_sync(FULL, t, 2));   // max_ps(m, movehl(m))
+    t = x86_max(t, __shfl_down_sync(FULL, t, 1));   // max_ss(m, lane 1)
+    mbits = __float_as_uint(__shfl_sync(FULL, t, 0));
+  }
+  const float max_abs = __uint_as_float(mbits);
   float inv;
   if (max_abs > 0.0f) {
     scale = __fdiv_rn(max_abs, 127.0f);

@@ -213,7 +213,11 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParam
   const uint32_t R = p.R, nb = p.nb, pitch = p.pitch, row_bytes = p.row_bytes;
   const uint32_t buf_bytes = R * pitch;
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  uint8_t* wbuf = smem + act_region + warp * D * buf_bytes;
+  // per-warp partial buffers [R][nb] floats, then per-warp weight buffers
+  const uint32_t pstride = (R * nb + 3u) & ~3u;
+  const uint32_t part_region = (NW * pstride * 4u + 127u) & ~127u;
+  float* part_w = reinterpret_cast<float*>(smem + act_region) + warp * pstride;
+  uint8_t* wbuf = smem + act_region + part_region + warp * D * buf_bytes;
 
   const uint32_t r0 = (uint32_t)(((uint64_t)p.n * blockIdx.x) / gridDim.x);
   const uint32_t r1 = (uint32_t)(((uint64_t)p.n * (blockIdx.x + 1)) / gridDim.x);
@@ -257,15 +261,14 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParam
     __syncwarp();
     const uint32_t rows = (nrows - s * R) < R ? (nrows - s * R) : R;
     const uint8_t* stage = wbuf + slot * buf_bytes;
-    // item q = 2 * (b * rows + row) + h; odd lanes end up holding partials
+    // item q = 2 * (b * rows + row) + h; the odd lane of each pair ends up
+    // holding the super-block partial and parks it at part_w[row][b]
     const uint32_t units = rows * nb, items = 2u * units;
-    float acc = 0.0f;  // lane r < rows: c[row r] = 0; += partial_b in b order (:194, :264)
-    uint32_t rj = 0;   // row of the next unit to broadcast
     for (uint32_t q0 = 0; q0 < items; q0 += 32) {
       const uint32_t u = (q0 + lane) >> 1;  // (b, row) unit of this lane
       float t[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      uint32_t row = 0, b = 0;
       if (u < units) {
-        uint32_t row, b;
         if (rows == R) {
           row = u & (R - 1u);
           b = u >> (31u - __clz(R));
@@ -276,17 +279,25 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParam
         q4k_half_terms(stage + row * pitch + b * Q4K_BYTES, act_s + b * kActRec + h * kActHalf, h, t);
       }
       const float part = pair_partial(t, lane);
-      // units q0/2 .. q0/2+15 of this chunk, in order: row = unit % rows
-      const uint32_t u0 = q0 >> 1, cnt = (units - u0) < 16u ? (units - u0) : 16u;
-      for (uint32_t j = 0; j < cnt; ++j) {
-        const float v = __shfl_sync(0xffffffffu, part, 2u * j + 1u);
-        if (rj == lane) acc = __fadd_rn(acc, v);
-        rj = (rj + 1u == rows) ? 0u : rj + 1u;
-      }
+      if (u < units && h) part_w[row * nb + b] = part;
     }
-    if (lane < rows) p.c[r0 + s * R + lane] = acc;
-    __syncwarp();  // all lanes done with this buffer before it is refilled
+    __syncwarp();  // partials parked, stage bytes no longer read
     issue(s + D * NW, slot);
+    if (lane < rows) {
+      // c[row] = 0; c[row] += partial_b for b in order (:194, :264)
+      const float* pr = part_w + lane * nb;
+      float acc = 0.0f;
+      uint32_t b = 0;
+      if ((nb & 3u) == 0) {
+        for (; b < nb; b += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(pr + b);
+          acc = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(acc, v.x), v.y), v.z), v.w);
+        }
+      }
+      for (; b < nb; ++b) acc = __fadd_rn(acc, pr[b]);
+      p.c[r0 + s * R + lane] = acc;
+    }
+    __syncwarp();  // partial buffer free for the next stage
   }
   cp_async_wait<0>();  // never exit with copies still landing in shared memory
 }
@@ -346,7 +357,9 @@ struct GemvConfig {
 GemvConfig g_cfgs[] = {{q4k_gemv_kernel<16, 4>, 16, 4, 0}, {q4k_gemv_kernel<16, 3>, 16, 3, 0},
                        {q4k_gemv_kernel<16, 2>, 16, 2, 0}, {q4k_gemv_kernel<20, 3>, 20, 3, 0},
                        {q4k_gemv_kernel<8, 4>, 8, 4, 0},   {q4k_gemv_kernel<12, 4>, 12, 4, 0},
-                       {q4k_gemv_kernel<24, 2>, 24, 2, 0}, {q4k_gemv_kernel<8, 6>, 8, 6, 0}};
+                       {q4k_gemv_kernel<24, 2>, 24, 2, 0}, {q4k_gemv_kernel<8, 6>, 8, 6, 0},
+                       {q4k_gemv_kernel<20, 2>, 20, 2, 0}, {q4k_gemv_kernel<12, 3>, 12, 3, 0},
+                       {q4k_gemv_kernel<16, 2>, 16, 2, 0}, {q4k_gemv_kernel<10, 4>, 10, 4, 0}};
 constexpr int kNumCfgs = sizeof(g_cfgs) / sizeof(g_cfgs[0]);
 int g_q4k_variant = -1;  // kernel config override (-1: automatic)
 int g_q4k_rows = 0;      // rows-per-stage override (0: automatic)
@@ -375,6 +388,7 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   if (g_q4k_rows == 1 || g_q4k_rows == 2 || g_q4k_rows == 4 || g_q4k_rows == 8) R = (uint32_t)g_q4k_rows;
   const uint32_t target = R == 1 ? 0u : (R == 2 ? 32u : 16u);
   const uint32_t pitch = row_bytes + ((target - (row_bytes & 127u)) & 127u);
+  auto part_bytes = [&](int nw) -> uint32_t { return ((uint32_t)nw * ((R * nb + 3u) & ~3u) * 4u + 127u) & ~127u; };
   // deepest per-warp pipeline that fits: 16 warps x D buffers, else fewer
   int pick = -1;
   if (g_q4k_variant >= 0 && g_q4k_variant < kNumCfgs) {
@@ -382,14 +396,15 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   } else {
     const int order[] = {0, 1, 2, 4};
     for (int o : order)
-      if (act_region + (uint32_t)(g_cfgs[o].nw * g_cfgs[o].d) * R * pitch <= (uint32_t)max_smem) {
+      if (act_region + part_bytes(g_cfgs[o].nw) + (uint32_t)(g_cfgs[o].nw * g_cfgs[o].d) * R * pitch <=
+          (uint32_t)max_smem) {
         pick = o;
         break;
       }
     if (pick < 0) pick = 2;
   }
   GemvConfig& cfg = g_cfgs[pick];
-  const uint32_t smem = act_region + (uint32_t)(cfg.nw * cfg.d) * R * pitch;
+  const uint32_t smem = act_region + part_bytes(cfg.nw) + (uint32_t)(cfg.nw * cfg.d) * R * pitch;
   if (smem > (uint32_t)max_smem) {  // rows too long to stage: unstaged kernel
     if (act == nullptr) {           // it reads packed activations from global memory
       *out_status = EOS_E_UNSUPPORTED;

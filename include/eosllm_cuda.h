@@ -104,8 +104,10 @@ EOSLLM_CUDA_API size_t eosi_cuda_q4_k_scratch_bytes(uint32_t m, uint32_t k);
 /* C[m,n] = A[m,k] . deq(W)^T with A, W, C and scratch in device memory.
  * W is n rows of k/256 GGUF Q4_K super-blocks, 16-byte aligned; A and
  * scratch 16-byte aligned; scratch >= eosi_cuda_q4_k_scratch_bytes(m, k).
- * For m == 1 the activation packing runs inside the GEMV kernel and scratch
- * may be NULL (rows too long to stage in shared memory still need it).
+ * With scratch, activations are packed by a separate kernel chained to the
+ * GEMV (programmatic dependent launch).  For m == 1 scratch may be NULL:
+ * every CTA of the GEMV then packs the vector itself into shared memory
+ * (rows too long to stage in shared memory still need scratch).
  * Asynchronous on `stream`; bit-identical to eosi_cuda_matmul_q4_k. */
 EOSLLM_CUDA_API int eosi_cuda_matmul_q4_k_dev(const float *a, const void *w, float *c, uint32_t m, uint32_t n,
                               uint32_t k, void *scratch, void *stream);
