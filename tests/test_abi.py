@@ -34,6 +34,20 @@ def test_header_is_plain_c(tmp_path):
                     "-c", str(src), "-o", str(tmp_path / "t.o")], check=True)
 
 
+def test_backend_glue_compiles_against_engine_headers(tmp_path):
+    """eosllm_b200/host/cuda_backend.c is C99 against the engine's own
+    include/eosllm/backend.h (present where the reference tree is)."""
+    ref_inc = os.path.join(os.environ.get("EOS_REFERENCE_DIR", "/root/reference"), "include")
+    if not os.path.isdir(ref_inc):
+        pytest.skip("engine headers not present on this machine")
+    src = os.path.join(ROOT, "eosllm_b200", "host", "cuda_backend.c")
+    for flag in ("-DEOSLLM_HAVE_KERNEL_CUDA=1", "-DEOSLLM_HAVE_KERNEL_CUDA=0"):
+        subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic", flag, "-I", ref_inc,
+                        "-I", os.path.join(ROOT, "include"), "-c", src, "-o", str(tmp_path / "glue.o")], check=True)
+    out = subprocess.run(["nm", str(tmp_path / "glue.o")], capture_output=True, text=True, check=True).stdout
+    assert "eosi_backend_cuda_register" in out
+
+
 def test_argument_validation_matches_reference(cuda_lib):
     a = np.ones(512, np.float32)
     w = np.zeros(144 * 2, np.uint8)
