@@ -74,6 +74,7 @@ _SIGNATURES = {
     "eosi_cuda_q4_k_from_gauss_dev": (C.c_int, [_vp, _sz, _u64, C.c_float, _vp]),
     "eosi_cuda_take_device_errors": (C.c_int, [C.POINTER(C.c_uint32)]),
     "eosi_cuda_set_kernel_variant": (C.c_int, [C.c_int, C.c_int]),
+    "eosi_cuda_matmul_q4_k_noalloc": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
 }
 
 _lib = None

@@ -405,6 +405,10 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
 
+namespace eos {
+void set_error_message(const char* msg) { fail(EOS_OK, "%s", msg); }
+}  // namespace eos
+
 // ===========================================================================
 // C ABI
 // ===========================================================================

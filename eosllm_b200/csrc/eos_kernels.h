@@ -12,6 +12,9 @@ enum { EOS_ACT_LAYOUT_GEMV = 0, EOS_ACT_LAYOUT_SOURCE = 1 };
 
 namespace eos {
 
+// Sets the calling thread's message returned by eosi_cuda_last_error().
+void set_error_message(const char* msg);
+
 size_t act_layout_bytes(uint32_t m, uint32_t k, int layout);
 cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out, int layout, cudaStream_t st);
 

@@ -120,6 +120,31 @@ EOSLLM_CUDA_API int eosi_cuda_q4_k_pack_act_dev(const float *a, uint32_t m, uint
 EOSLLM_CUDA_API int eosi_cuda_q4_k_gemv_dev(const void *act, const void *w, float *c, uint32_t n, uint32_t k,
                             void *stream);
 
+/* Q4_K matmul that allocates nothing -- no counterpart in the reference.
+ * For hosts that may not allocate device memory while running (all buffers
+ * reserved at start-up, or all device memory owned by the host's own pool):
+ * the same computation as eosi_cuda_matmul_q4_k_dev, bit-identical results,
+ * but the packed activations live in a 1 MiB array built into the library
+ * instead of a caller scratch buffer.  Limits and behaviour:
+ *   - m * k / 256 * 480 bytes must fit in 1 MiB (m * k <= 559104, e.g. one
+ *     row of k up to 559104, or m <= 136 rows of k = 4096); larger sizes
+ *     return EOS_E_INVALID_ARG with a message;
+ *   - each GPU that loads the library keeps its own copy of the array until
+ *     the process exits;
+ *   - the first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture;
+ *   - every call on a device reuses the same array, so calls whose work
+ *     overlaps on that GPU (other streams, other host threads) race and
+ *     corrupt each other's results -- serialise them;
+ *   - no cudaMalloc, cudaFree or other allocating call is made, and the
+ *     kernels' one-second bounded waits have no error word to report to
+ *     here (they still return; a timed-out call's outputs are invalid).
+ * a, w, c are device pointers on the current device (a and w 16-byte
+ * aligned); `stream` is a cudaStream_t as void*; asynchronous. */
+EOSLLM_CUDA_API int eosi_cuda_matmul_q4_k_noalloc(const float *a, const void *w, float *c, uint32_t m, uint32_t n,
+                                                  uint32_t k, void *stream);
+
 /* Q8_0 with device pointers (W 16-byte aligned, k % 256 == 0 on this path). */
 EOSLLM_CUDA_API int eosi_cuda_matmul_q8_0_dev(const float *a, const void *w, float *c, uint32_t m, uint32_t n,
                               uint32_t k, void *stream);

@@ -1,0 +1,88 @@
+"""The allocation-free Q4_K entry point, eosi_cuda_matmul_q4_k_noalloc.
+
+It exists for hosts that may not allocate device memory once they run --
+deployments that reserve every buffer at start-up, or hosts whose own pool
+owns all device memory -- and keeps its packed activations in a 1 MiB array
+built into the library instead of a caller scratch buffer.  Its results must
+be bit-identical to the allocating entry point's (Q4_K is bit-exact in every
+test of this suite), on consecutive calls that reuse the shared array.
+
+This file is collected last (its name sorts after the others) and passes
+both alone in a fresh process and after the rest of the suite.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import same_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def _call_noalloc(lib, a, w, c, m, n, k):
+    st = torch.cuda.current_stream().cuda_stream
+    return lib.eosi_cuda_matmul_q4_k_noalloc(C.c_void_p(a.data_ptr()), C.c_void_p(w.data_ptr()),
+                                             C.c_void_p(c.data_ptr()), m, n, k, C.c_void_p(st))
+
+
+def _call_reference_entry(lib, a, w, c, m, n, k, scratch):
+    st = torch.cuda.current_stream().cuda_stream
+    return lib.eosi_cuda_matmul_q4_k_dev(C.c_void_p(a.data_ptr()), C.c_void_p(w.data_ptr()),
+                                         C.c_void_p(c.data_ptr()), m, n, k, C.c_void_p(scratch.data_ptr()),
+                                         C.c_void_p(st))
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (1, 4096, 11008), (3, 1000, 4096), (1, 2, 512)])
+def test_noalloc_matches_allocating_entry_point(gpu, m, n, k):
+    lib = gpu.load()
+    dev = torch.device("cuda", 0)
+    w = torch.empty(n * (k // 256) * 144, dtype=torch.uint8, device=dev)
+    gpu.q4_k_from_gauss_dev(w, n * k, 11, 0.02)
+    scratch = torch.empty(gpu.q4_k_scratch_bytes(m, k), dtype=torch.uint8, device=dev)
+    # two calls in a row with different activations: the second must not see
+    # anything left in the shared array by the first
+    for seed in (21, 22):
+        a = torch.empty(m * k, dtype=torch.float32, device=dev)
+        gpu.fill_gauss_dev(a, m * k, seed, 0, 1.0)
+        c_ref = torch.full((m * n,), np.nan, dtype=torch.float32, device=dev)
+        c_new = torch.full((m * n,), np.nan, dtype=torch.float32, device=dev)
+        assert _call_reference_entry(lib, a, w, c_ref, m, n, k, scratch) == gpu.EOS_OK, gpu.last_error()
+        assert _call_noalloc(lib, a, w, c_new, m, n, k) == gpu.EOS_OK, gpu.last_error()
+        torch.cuda.synchronize()
+        assert same_bits(c_new.cpu().numpy(), c_ref.cpu().numpy()), (m, n, k, seed)
+        assert not np.isnan(c_new.cpu().numpy()).any()
+
+
+def test_noalloc_rejects_sizes_beyond_its_array(gpu):
+    lib = gpu.load()
+    dev = torch.device("cuda", 0)
+    k = 4096
+    m = 137  # 137 * 16 * 480 bytes > 1 MiB
+    a = torch.zeros(m * k, dtype=torch.float32, device=dev)
+    w = torch.zeros(8 * (k // 256) * 144, dtype=torch.uint8, device=dev)
+    c = torch.full((m * 8,), 7.0, dtype=torch.float32, device=dev)
+    assert _call_noalloc(lib, a, w, c, m, 8, k) == gpu.EOS_E_INVALID_ARG
+    assert "1 MiB" in gpu.last_error()
+    torch.cuda.synchronize()
+    assert torch.all(c == 7.0)
+    assert _call_noalloc(lib, a, w, c, 136, 8, k) == gpu.EOS_OK  # the largest m that fits
+
+
+def test_noalloc_leaves_free_device_memory_unchanged(gpu):
+    lib = gpu.load()
+    dev = torch.device("cuda", 0)
+    n, k = 2048, 4096
+    w = torch.empty(n * (k // 256) * 144, dtype=torch.uint8, device=dev)
+    gpu.q4_k_from_gauss_dev(w, n * k, 5, 0.02)
+    a = torch.ones(k, dtype=torch.float32, device=dev)
+    c = torch.empty(n, dtype=torch.float32, device=dev)
+    assert _call_noalloc(lib, a, w, c, 1, n, k) == gpu.EOS_OK  # first call does the per-device set-up
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info(dev)
+    for _ in range(20):
+        assert _call_noalloc(lib, a, w, c, 1, n, k) == gpu.EOS_OK
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info(dev)
+    assert free_after == free_before
