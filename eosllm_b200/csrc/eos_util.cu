@@ -59,7 +59,7 @@ __global__ void fill_gauss_kernel(float* dst, size_t n, uint64_t seed, uint64_t 
     dst[i] = gauss(key, offset + i, sigma);
 }
 
-// ---- Q4_K quantizer (one thread per 256-element super-block) -------------
+// ---- Q4_K quantizer ------------------------------------------------------
 __device__ __forceinline__ int rint_clamp(float v, int hi) {
   if (!(v > 0.0f)) return 0;
   if (v >= (float)hi) return hi;
@@ -67,65 +67,85 @@ __device__ __forceinline__ int rint_clamp(float v, int hi) {
   return q > hi ? hi : q;
 }
 
+// Eight lanes per super-block, lane j owning sub-block j: its 32 values stay
+// in registers; the super-block maxima are lane-group reductions (order does
+// not matter: scales and mins are >= 0 and a NaN is taken as 0, exactly as
+// the sequential `if (v > max) max = v` starting from 0 ignores it); lane
+// 2p+1 hands its nibbles to lane 2p, which writes the shared qs bytes.
 template <bool GEN>
-__global__ void q4k_quantize_kernel(const float* __restrict__ src, uint8_t* __restrict__ dst, size_t nblocks,
-                                    uint64_t seed, uint64_t offset, float sigma) {
-  const size_t b = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
-  if (b >= nblocks) return;
+__global__ void __launch_bounds__(256) q4k_quantize_kernel(const float* __restrict__ src, uint8_t* __restrict__ dst,
+                                                           size_t nblocks, uint64_t seed, uint64_t offset,
+                                                           float sigma) {
+  const unsigned FULL = 0xffffffffu;
+  const size_t gt = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  const size_t b = gt >> 3;
+  const uint32_t j = threadIdx.x & 7u;
+  const bool live = b < nblocks;
   const uint64_t key = GEN ? gauss_key(seed) : 0;
-  auto x = [&](uint32_t e) -> float {
-    return GEN ? gauss(key, offset + b * 256u + e, sigma) : src[b * 256u + e];
-  };
-  float scale[8], mins[8], max_scale = 0.0f, max_min = 0.0f;
-  for (int j = 0; j < 8; ++j) {
-    float lo = x(32u * j), hi = lo;
-    for (int l = 1; l < 32; ++l) {
-      const float v = x(32u * j + l);
-      if (v < lo) lo = v;
-      if (v > hi) hi = v;
-    }
-    if (lo > 0.0f) lo = 0.0f;
-    scale[j] = __fdiv_rn(__fsub_rn(hi, lo), 15.0f);
-    mins[j] = -lo;
-    if (scale[j] > max_scale) max_scale = scale[j];
-    if (mins[j] > max_min) max_min = mins[j];
+  float x[32];
+#pragma unroll
+  for (int l = 0; l < 32; ++l) {
+    const size_t e = b * 256u + 32u * j + (uint32_t)l;
+    x[l] = !live ? 0.0f : (GEN ? gauss(key, offset + e, sigma) : src[e]);
   }
-  const uint16_t dh = ref_f32_to_f16(__fdiv_rn(max_scale, 63.0f));
-  const uint16_t mh = ref_f32_to_f16(__fdiv_rn(max_min, 63.0f));
+  float lo = x[0], hi = x[0];
+#pragma unroll
+  for (int l = 1; l < 32; ++l) {
+    if (x[l] < lo) lo = x[l];
+    if (x[l] > hi) hi = x[l];
+  }
+  if (lo > 0.0f) lo = 0.0f;
+  const float scale = __fdiv_rn(__fsub_rn(hi, lo), 15.0f);
+  const float mins = -lo;
+  float ms = scale > 0.0f ? scale : 0.0f, mm = mins > 0.0f ? mins : 0.0f;
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) {
+    const float a = __shfl_xor_sync(FULL, ms, o), c = __shfl_xor_sync(FULL, mm, o);
+    ms = a > ms ? a : ms;
+    mm = c > mm ? c : mm;
+  }
+  const uint16_t dh = ref_f32_to_f16(__fdiv_rn(ms, 63.0f));
+  const uint16_t mh = ref_f32_to_f16(__fdiv_rn(mm, 63.0f));
   const float d = f16_bits_to_f32(dh), dmin = f16_bits_to_f32(mh);
-  uint32_t sc[8], mq[8];
-  for (int j = 0; j < 8; ++j) {
-    sc[j] = d > 0.0f ? (uint32_t)rint_clamp(__fdiv_rn(scale[j], d), 63) : 0u;
-    mq[j] = dmin > 0.0f ? (uint32_t)rint_clamp(__fdiv_rn(mins[j], dmin), 63) : 0u;
+  const uint32_t sc = d > 0.0f ? (uint32_t)rint_clamp(__fdiv_rn(scale, d), 63) : 0u;
+  const uint32_t mq = dmin > 0.0f ? (uint32_t)rint_clamp(__fdiv_rn(mins, dmin), 63) : 0u;
+  const float es = __fmul_rn(d, (float)sc), em = __fmul_rn(dmin, (float)mq);
+  // the 32 quants of this sub-block, one per byte: element l in byte l % 4 of word l / 4
+  uint32_t nib[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+#pragma unroll
+  for (int l = 0; l < 32; ++l) {
+    const uint32_t q = es > 0.0f ? (uint32_t)rint_clamp(__fdiv_rn(__fadd_rn(x[l], em), es), 15) : 0u;
+    nib[l >> 2] |= q << (8 * (l & 3));
   }
-  uint8_t* blk = dst + b * Q4K_BYTES;
-  uint32_t* w32 = reinterpret_cast<uint32_t*>(blk);  // super-blocks are 16-byte aligned
-  w32[0] = (uint32_t)dh | ((uint32_t)mh << 16);
-  // packing of tests/unit/test_runner.c:716-725
-  uint32_t s0 = 0, s1 = 0, s2 = 0;
-  for (int j = 0; j < 4; ++j) {
-    s0 |= ((sc[j] & 63u) | ((sc[j + 4] >> 4) << 6)) << (8 * j);
-    s1 |= ((mq[j] & 63u) | ((mq[j + 4] >> 4) << 6)) << (8 * j);
-    s2 |= ((sc[j + 4] & 15u) | ((mq[j + 4] & 15u) << 4)) << (8 * j);
+  // qs byte l of pair p = q[2p][l] | q[2p+1][l] << 4: lane 2p+1's quants
+  // become the high nibbles of lane 2p's bytes
+  uint32_t qs[8];
+#pragma unroll
+  for (int w = 0; w < 8; ++w) qs[w] = nib[w] | (__shfl_down_sync(FULL, nib[w], 1) << 4);
+  // all 8 scales and mins to lane 0 of the group
+  uint32_t scs[8], mqs[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    scs[i] = __shfl_sync(FULL, sc, (threadIdx.x & ~7u) | (uint32_t)i);
+    mqs[i] = __shfl_sync(FULL, mq, (threadIdx.x & ~7u) | (uint32_t)i);
   }
-  w32[1] = s0;
-  w32[2] = s1;
-  w32[3] = s2;
-  for (int pr = 0; pr < 4; ++pr) {
-    const float es_lo = __fmul_rn(d, (float)sc[2 * pr]), em_lo = __fmul_rn(dmin, (float)mq[2 * pr]);
-    const float es_hi = __fmul_rn(d, (float)sc[2 * pr + 1]), em_hi = __fmul_rn(dmin, (float)mq[2 * pr + 1]);
-    for (int l4 = 0; l4 < 32; l4 += 4) {
-      uint32_t word = 0;
-      for (int t = 0; t < 4; ++t) {
-        const int l = l4 + t;
-        const uint32_t qlo =
-            es_lo > 0.0f ? (uint32_t)rint_clamp(__fdiv_rn(__fadd_rn(x(64u * pr + l), em_lo), es_lo), 15) : 0u;
-        const uint32_t qhi =
-            es_hi > 0.0f ? (uint32_t)rint_clamp(__fdiv_rn(__fadd_rn(x(64u * pr + 32u + l), em_hi), es_hi), 15) : 0u;
-        word |= (qlo | (qhi << 4)) << (8 * t);
-      }
-      w32[4 + pr * 8 + l4 / 4] = word;
+  if (!live) return;
+  uint8_t* blk = dst + b * Q4K_BYTES;  // super-blocks are 16-byte aligned
+  if ((j & 1u) == 0) {  // pair p = j / 2 owns qs bytes [32p, 32p + 32) at offset 16 + 32p
+    uint4* q4 = reinterpret_cast<uint4*>(blk + 16 + 16 * j);
+    q4[0] = make_uint4(qs[0], qs[1], qs[2], qs[3]);
+    q4[1] = make_uint4(qs[4], qs[5], qs[6], qs[7]);
+  }
+  if (j == 0) {
+    // packing of tests/unit/test_runner.c:716-725
+    uint32_t s0 = 0, s1 = 0, s2 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      s0 |= ((scs[i] & 63u) | ((scs[i + 4] >> 4) << 6)) << (8 * i);
+      s1 |= ((mqs[i] & 63u) | ((mqs[i + 4] >> 4) << 6)) << (8 * i);
+      s2 |= ((scs[i + 4] & 15u) | ((mqs[i + 4] & 15u) << 4)) << (8 * i);
     }
+    *reinterpret_cast<uint4*>(blk) = make_uint4((uint32_t)dh | ((uint32_t)mh << 16), s0, s1, s2);
   }
 }
 
@@ -186,15 +206,15 @@ cudaError_t launch_fill_gauss(float* dst, size_t n, uint64_t seed, uint64_t offs
 cudaError_t launch_q4k_quantize(const float* src, uint8_t* dst, size_t n_el, cudaStream_t st) {
   const size_t nb = n_el / Q4K_ELEMS;
   if (nb == 0) return cudaSuccess;
-  q4k_quantize_kernel<false><<<(unsigned)((nb + 127) / 128), 128, 0, st>>>(src, dst, nb, 0, 0, 0.0f);
+  q4k_quantize_kernel<false><<<(unsigned)((nb + 31) / 32), 256, 0, st>>>(src, dst, nb, 0, 0, 0.0f);
   return cudaGetLastError();
 }
 
 cudaError_t launch_q4k_from_gauss(uint8_t* dst, size_t nblocks, uint64_t seed, uint64_t offset, float sigma,
                                   cudaStream_t st) {
   if (nblocks == 0) return cudaSuccess;
-  q4k_quantize_kernel<true><<<(unsigned)((nblocks + 127) / 128), 128, 0, st>>>(nullptr, dst, nblocks, seed, offset,
-                                                                                sigma);
+  q4k_quantize_kernel<true><<<(unsigned)((nblocks + 31) / 32), 256, 0, st>>>(nullptr, dst, nblocks, seed, offset,
+                                                                             sigma);
   return cudaGetLastError();
 }
 

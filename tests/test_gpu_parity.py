@@ -237,7 +237,7 @@ def test_q8_0_shapes(gpu, oracle, n, k):
     assert q80_close(gpu.matmul_q(a[:k], q8, DT_Q8_0, 1, n, k), ref[:1])
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3])
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5])
 def test_q8_0_kernel_variants(gpu, oracle, variant):
     try:
         gpu.set_kernel_variant(DT_Q8_0, variant)
