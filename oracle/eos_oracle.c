@@ -683,3 +683,141 @@ int orc_silu(const float *x, float *y, size_t n) {
     for (i = 0; i < n; ++i) y[i] = x[i] * (1.0f / (1.0f + expf(-x[i])));
     return ORC_OK;
 }
+
+/* ------------------------------------------------------------------ */
+/* Llama decoder step: restates src/modality/text/text.c:267-436       */
+/* ------------------------------------------------------------------ */
+
+struct orc_text {
+    orc_llama_t m;
+    uint32_t head_dim, pos;
+    float *k_cache, *v_cache;  /* [n_layer][max_ctx][n_kv_head * head_dim] (text.c:220-226) */
+    float *x, *xn, *q, *k, *v, *attn_out, *ff_gate, *ff_up, *ff_tmp;
+};
+
+int orc_text_open(const orc_llama_t *m, orc_text_t **out) {
+    orc_text_t *st;
+    size_t kvl;
+    if (!m || !out || m->n_head == 0 || m->n_kv_head == 0) return ORC_E_INVALID_ARG;
+    st = (orc_text_t *)calloc(1, sizeof(*st));
+    if (!st) return ORC_E_OUT_OF_MEMORY;
+    st->m = *m;
+    st->head_dim = m->n_embd / m->n_head; /* text.c:147 */
+    kvl = (size_t)m->max_ctx * m->n_kv_head * st->head_dim;
+    st->k_cache = (float *)calloc((size_t)m->n_layer * kvl, sizeof(float));
+    st->v_cache = (float *)calloc((size_t)m->n_layer * kvl, sizeof(float));
+    st->x = (float *)calloc(m->n_embd, 4);
+    st->xn = (float *)calloc(m->n_embd, 4);
+    st->q = (float *)calloc(m->n_embd, 4);
+    st->k = (float *)calloc((size_t)m->n_kv_head * st->head_dim, 4);
+    st->v = (float *)calloc((size_t)m->n_kv_head * st->head_dim, 4);
+    st->attn_out = (float *)calloc(m->n_embd, 4);
+    /* ff_gate doubles as the attention score scratch (text.c:370), so it
+     * must hold max_ctx entries too */
+    st->ff_gate = (float *)calloc(m->n_ff > m->max_ctx ? m->n_ff : m->max_ctx, 4);
+    st->ff_up = (float *)calloc(m->n_ff, 4);
+    st->ff_tmp = (float *)calloc(m->n_ff > m->n_embd ? m->n_ff : m->n_embd, 4);
+    if (!st->k_cache || !st->v_cache || !st->x || !st->xn || !st->q || !st->k || !st->v || !st->attn_out ||
+        !st->ff_gate || !st->ff_up || !st->ff_tmp) {
+        orc_text_close(st);
+        return ORC_E_OUT_OF_MEMORY;
+    }
+    *out = st;
+    return ORC_OK;
+}
+
+void orc_text_close(orc_text_t *st) {
+    if (!st) return;
+    free(st->k_cache); free(st->v_cache); free(st->x); free(st->xn); free(st->q); free(st->k);
+    free(st->v); free(st->attn_out); free(st->ff_gate); free(st->ff_up); free(st->ff_tmp);
+    free(st);
+}
+
+uint32_t orc_text_pos(const orc_text_t *st) { return st ? st->pos : 0; }
+
+static int orc_mw(const orc_text_t *st, const float *x, const void *w, int dt, float *y, uint32_t out_dim,
+                  uint32_t in_dim) {
+    /* matmul_w for Q8_0 / Q4_K (text.c:75-99): matmul_q with m = 1 */
+    (void)st;
+    return orc_matmul_q(x, w, dt, y, 1, out_dim, in_dim);
+}
+
+int orc_text_step(orc_text_t *st, uint32_t token, float *logits) {
+    const orc_llama_t *m;
+    uint32_t n_embd, n_head, n_kvh, hd, n_ff, pos, L, h, p, i;
+    size_t kv_stride;
+    int r;
+    if (!st || !logits) return ORC_E_INVALID_ARG;
+    m = &st->m;
+    if (token >= m->n_vocab) return ORC_E_INVALID_ARG;       /* text.c:277 */
+    if (st->pos >= m->max_ctx) return ORC_E_OUT_OF_MEMORY;   /* text.c:278 */
+    n_embd = m->n_embd; n_head = m->n_head; n_kvh = m->n_kv_head; hd = st->head_dim; n_ff = m->n_ff;
+    pos = st->pos;
+    kv_stride = (size_t)m->max_ctx * n_kvh * hd;
+
+    /* 1. embedding row, F16 (text.c:317-320) */
+    for (i = 0; i < n_embd; ++i) st->x[i] = orc_f16_to_f32(m->tok_embd[(size_t)token * n_embd + i]);
+
+    for (L = 0; L < m->n_layer; ++L) {
+        /* 2a-2b (text.c:344-352) */
+        if ((r = orc_rmsnorm(st->x, m->attn_norm[L], m->rms_eps, st->xn, 1, n_embd))) return r;
+        if ((r = orc_mw(st, st->xn, m->wq[L], m->wdtype, st->q, n_embd, n_embd))) return r;
+        if ((r = orc_mw(st, st->xn, m->wk[L], m->wdtype, st->k, n_kvh * hd, n_embd))) return r;
+        if ((r = orc_mw(st, st->xn, m->wv[L], m->wdtype, st->v, n_kvh * hd, n_embd))) return r;
+        /* 2c (text.c:355-356) */
+        if ((r = orc_rope(st->q, n_head, hd, pos, m->rope_base))) return r;
+        if ((r = orc_rope(st->k, n_kvh, hd, pos, m->rope_base))) return r;
+        /* 2d (text.c:359-362) */
+        memcpy(&st->k_cache[L * kv_stride + (size_t)pos * n_kvh * hd], st->k, (size_t)n_kvh * hd * 4);
+        memcpy(&st->v_cache[L * kv_stride + (size_t)pos * n_kvh * hd], st->v, (size_t)n_kvh * hd * 4);
+        /* 2e: attention with GQA grouping (text.c:366-401) */
+        {
+            const float scale = 1.0f / sqrtf((float)hd);
+            const float *Kc = &st->k_cache[L * kv_stride], *Vc = &st->v_cache[L * kv_stride];
+            float *att = st->ff_gate;
+            memset(st->attn_out, 0, (size_t)n_embd * 4);
+            for (h = 0; h < n_head; ++h) {
+                const uint32_t kvh = (h * n_kvh) / n_head;
+                const float *qh = st->q + (size_t)h * hd;
+                float maxv = -1e30f, sum = 0.0f;
+                for (p = 0; p <= pos; ++p) {
+                    const float *kp = Kc + (size_t)p * n_kvh * hd + (size_t)kvh * hd;
+                    float dot = 0.0f;
+                    for (i = 0; i < hd; ++i) dot += qh[i] * kp[i];
+                    att[p] = dot * scale;
+                    if (att[p] > maxv) maxv = att[p];
+                }
+                for (p = 0; p <= pos; ++p) {
+                    att[p] = expf(att[p] - maxv);
+                    sum += att[p];
+                }
+                if (sum > 0.0f) {
+                    float inv = 1.0f / sum;
+                    for (p = 0; p <= pos; ++p) att[p] *= inv;
+                }
+                for (p = 0; p <= pos; ++p) {
+                    const float *vp = Vc + (size_t)p * n_kvh * hd + (size_t)kvh * hd;
+                    float a = att[p];
+                    for (i = 0; i < hd; ++i) st->attn_out[h * hd + i] += a * vp[i];
+                }
+            }
+        }
+        /* 2f (text.c:404-406) */
+        if ((r = orc_mw(st, st->attn_out, m->wo[L], m->wdtype, st->ff_tmp, n_embd, n_embd))) return r;
+        for (i = 0; i < n_embd; ++i) st->x[i] += st->ff_tmp[i];
+        /* 2g-2h (text.c:409-417) */
+        if ((r = orc_rmsnorm(st->x, m->ffn_norm[L], m->rms_eps, st->xn, 1, n_embd))) return r;
+        if ((r = orc_mw(st, st->xn, m->wg[L], m->wdtype, st->ff_gate, n_ff, n_embd))) return r;
+        if ((r = orc_mw(st, st->xn, m->wu[L], m->wdtype, st->ff_up, n_ff, n_embd))) return r;
+        if ((r = orc_silu(st->ff_gate, st->ff_gate, n_ff))) return r;
+        for (i = 0; i < n_ff; ++i) st->ff_tmp[i] = st->ff_gate[i] * st->ff_up[i];
+        /* 2i (text.c:420-421) */
+        if ((r = orc_mw(st, st->ff_tmp, m->wd[L], m->wdtype, st->attn_out, n_embd, n_ff))) return r;
+        for (i = 0; i < n_embd; ++i) st->x[i] += st->attn_out[i];
+    }
+    /* 3. final norm + output projection (text.c:425-432) */
+    if ((r = orc_rmsnorm(st->x, m->output_norm, m->rms_eps, st->xn, 1, n_embd))) return r;
+    if ((r = orc_mw(st, st->xn, m->output_w, m->out_dtype, logits, m->n_vocab, n_embd))) return r;
+    st->pos++;
+    return ORC_OK;
+}

@@ -118,6 +118,32 @@ int orc_rmsnorm(const float *x, const float *w, float eps, float *y,
 int orc_rope(float *x, uint32_t n_heads, uint32_t head_dim, uint32_t pos, float base);
 int orc_silu(const float *x, float *y, size_t n);
 
+/* --- Llama decoder step: restates eosi_text_step ------------------------
+ * (src/modality/text/text.c:267-436) with the x86 dispatch the engine builds
+ * on an AVX2 host: matmul_q -> orc_matmul_q (int8 Q4_K, scalar Q8_0),
+ * rmsnorm / rope / silu -> the scalar ops.  Weights are caller-owned: per
+ * layer pointer tables (GGUF row-major, one row per output), F16 token
+ * embeddings [n_vocab][n_embd], F32 norms. */
+typedef struct {
+    uint32_t n_embd, n_layer, n_head, n_kv_head, n_ff, n_vocab, max_ctx;
+    float rms_eps, rope_base;
+    int wdtype;                     /* ORC_DT_Q4_K or ORC_DT_Q8_0 for all linears */
+    int out_dtype;                  /* dtype of output.weight */
+    const uint16_t *tok_embd;       /* F16 */
+    const float *output_norm;
+    const void *output_w;
+    const float *const *attn_norm;  /* [n_layer] */
+    const float *const *ffn_norm;
+    const void *const *wq, *const *wk, *const *wv, *const *wo;
+    const void *const *wg, *const *wu, *const *wd;
+} orc_llama_t;
+
+typedef struct orc_text orc_text_t;
+int  orc_text_open(const orc_llama_t *m, orc_text_t **out);
+int  orc_text_step(orc_text_t *st, uint32_t token, float *logits);
+uint32_t orc_text_pos(const orc_text_t *st);
+void orc_text_close(orc_text_t *st);
+
 #ifdef __cplusplus
 }
 #endif

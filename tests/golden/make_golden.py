@@ -20,6 +20,13 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
 from oracle.oracle import DT_Q4_K, DT_Q8_0, Oracle, RefKernels  # noqa: E402
+from oracle.llama import RefDecoder, make_llama  # noqa: E402
+from oracle.gguf_writer import write_llama  # noqa: E402
+
+# tiny Llama decoders whose logits the reference engine produces below
+DECODER_CASES = {"mha_q4k": dict(), "gqa_q4k": dict(n_kv_head=2),
+                 "mha_q80": dict(wdtype=DT_Q8_0, out_dtype=DT_Q8_0)}
+DECODER_TOKENS = [5, 17, 200, 3, 99, 42, 7, 250, 1, 319, 0, 128]
 
 OUT = os.path.dirname(os.path.abspath(__file__))
 
@@ -63,10 +70,29 @@ def act_edge_cases(rng: np.random.Generator) -> np.ndarray:
     return np.concatenate(groups)
 
 
+def decoder_fixture(o: Oracle) -> None:
+    """Logits of the reference engine's own eosi_text_step
+    (src/modality/text/text.c:267-436) for seeded synthetic models."""
+    import tempfile
+    out = {"tokens": np.array(DECODER_TOKENS, np.int64)}
+    for name, kw in DECODER_CASES.items():
+        m = make_llama(o, **kw)
+        with tempfile.TemporaryDirectory() as td:
+            path = os.path.join(td, "model.gguf")
+            write_llama(path, m)
+            rd = RefDecoder(path, m["config"]["max_ctx"], m["config"]["n_vocab"])
+            out[f"{name}_logits"] = np.stack([rd.step(t) for t in DECODER_TOKENS])
+            rd.close()
+    np.savez_compressed(os.path.join(OUT, "decoder_tiny.npz"), **out)
+
+
 def main() -> None:
     if not RefKernels.available():
         raise SystemExit("oracle/_ref is not built: run `make -C oracle ref` where the reference exists")
     o, r = Oracle(), RefKernels()
+    if "--decoder-only" in sys.argv:
+        decoder_fixture(o)
+        return
     rng = np.random.default_rng(20240601)
 
     # 1. the reference's own known-answer block (test_runner.c:727-803)
@@ -122,6 +148,9 @@ def main() -> None:
         cases[f"c{idx}_a"] = x
         cases[f"c{idx}_matmul_q"] = r.matmul_q(x, q8, DT_Q8_0, m, n, k)[1]
     np.savez_compressed(os.path.join(OUT, "q8_0_matmul.npz"), **cases)
+
+    # 5. tiny decoders run by the reference engine itself
+    decoder_fixture(o)
     print("golden fixtures written to", OUT)
 
 
