@@ -70,6 +70,10 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-decode", action="store_true", help="skip the 7B-shape decode measurement")
+    p.add_argument("--decode-prompt", type=int, default=512)
+    p.add_argument("--decode-gen", type=int, default=256)
+    p.add_argument("--decode-cpu-steps", type=int, default=2, help="oracle decoder steps timed on the host")
     return p.parse_args()
 
 
@@ -435,6 +439,15 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_seconds)
 
+    decode = None
+    if not args.no_decode and world > 1:
+        decode = {"unavailable": "the tensor-parallel decoder needs the peer exchange, not built yet"}
+    elif not args.no_decode:
+        del g_timed, g_warm, g_launch
+        weights.clear()
+        torch.cuda.empty_cache()
+        decode = run_decode(args, dev, world, rank)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -456,10 +469,100 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "gpu_launches": args.steps * len(SHAPES) * 2,
             "clocks": clocks.summary(),
+            "decode_7b": decode,
         }
         print(json.dumps(line), flush=True)
-    del g_timed, g_warm, g_launch
     dist_done(world)
+
+
+LLAMA_7B = dict(n_embd=4096, n_layer=32, n_head=32, n_kv_head=32, n_ff=11008, n_vocab=32000)
+
+
+def run_decode(args, dev, world, rank) -> dict:
+    """7B-shape Q4_K greedy decoding through the device-resident decoder:
+    random-init Llama-architecture model generated on the device (weights
+    ~N(0, 0.02) -> Q4_K, F16 embeddings, F32 norms, stream seed 4), prompt of
+    `decode_prompt` ids uniform in [0, 32000) from seed 4, then
+    `decode_gen` greedy tokens.  Device time with CUDA events on the
+    decoder's stream around each phase; the whole generation goes through
+    eosi_cuda_text_generate (host prompt in, host tokens out)."""
+    import torch
+
+    from eosllm_b200 import backend as B
+    from eosllm_b200.text import TextDecoder, synthetic_llama, weight_bytes_per_token
+    P, G = args.decode_prompt, args.decode_gen
+    cfg = dict(LLAMA_7B, max_ctx=P + G)
+    model = synthetic_llama(**cfg, seed=4, device=dev.index)
+    dec = TextDecoder(model, device=dev.index, rank=rank, world=world)
+    host_model = None
+    if rank == 0 and world == 1 and args.decode_cpu_steps > 0 and not args.no_cpu_baseline:
+        host_model = dict(config=model["config"], tok_embd=model["tok_embd"].cpu().numpy().view(np.uint16),
+                          output_norm=model["output_norm"].cpu().numpy(), output=model["output"].cpu().numpy(),
+                          layers=[{k: v.cpu().numpy() for k, v in lay.items()} for lay in model["layers"]])
+    del model
+    torch.cuda.empty_cache()
+    prompt = np.random.default_rng(4).integers(0, cfg["n_vocab"], P).astype(np.uint32)
+    st = torch.cuda.ExternalStream(dec.stream, device=dev)
+    dec.generate(prompt[:16], 8)  # warm-up: graph upload, first-touch
+    dec.reset()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    clocks = ClockSampler(dev.index)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    w0 = time.perf_counter()
+    ev[0].record(st)
+    first = dec.generate(prompt, 1)  # P steps; the last one picks token 0
+    ev[1].record(st)
+    w1 = time.perf_counter()
+    ev[2].record(st)
+    toks = dec.generate(first, G)  # G steps at positions P .. P+G-1
+    ev[3].record(st)
+    w2 = time.perf_counter()
+    torch.cuda.synchronize()
+    clocks.stop()
+    barrier(world)
+    prefill_ms = max_over_ranks(ev[0].elapsed_time(ev[1]), world, dev)
+    decode_ms = max_over_ranks(ev[2].elapsed_time(ev[3]), world, dev)
+    wall_decode = max_over_ranks(w2 - w1, world, dev)
+    wbytes = weight_bytes_per_token(dict(cfg, wdtype=B.DT_Q4_K, out_dtype=B.DT_Q4_K))
+    kv_avg = 2 * cfg["n_layer"] * cfg["n_embd"] * 4 * (P + (G + 1) / 2)  # fp32 K and V rows 0..p, mean p
+    peak, peak_kind = measured_hbm_peak()
+    ms_tok = decode_ms / G
+    out = {
+        "metric": "7B-shape Q4_K greedy decode tokens/s", "value": round(G / (decode_ms * 1e-3), 2),
+        "unit": "tok/s", "ms_per_token": round(ms_tok, 4), "n_gpus": world,
+        "prefill_tok_s": round(P / (prefill_ms * 1e-3), 2), "prompt": P, "generated": G,
+        "config": dict(cfg, wdtype="Q4_K", out_dtype="Q4_K", kv_cache="f32", parallelism=f"tp{world}"),
+        "e2e": {"value": round(G / wall_decode, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 4},
+        "roofline": {"bound": "hbm", "bytes_per_token": int(wbytes + kv_avg), "weight_bytes_per_token": wbytes,
+                     "kv_bytes_per_token_mean": int(kv_avg),
+                     "achieved": round((wbytes + kv_avg) / world / (ms_tok * 1e-3) / 1e9, 1), "peak": peak,
+                     "unit": "GB/s per GPU", "peak_kind": peak_kind,
+                     "frac": round((wbytes + kv_avg) / world / (ms_tok * 1e-3) / 1e9 / peak, 4),
+                     "tok_s_at_peak": round(world * peak * 1e9 / (wbytes + kv_avg), 1),
+                     "tok_s_weight_only_at_peak": round(world * peak * 1e9 / wbytes, 1)},
+        "first_tokens": [int(x) for x in toks[:8]],
+        "clocks": clocks.summary(),
+    }
+    if host_model is not None:
+        # the reference's algorithm on the host (the C restatement, bit-exact
+        # with the engine): a few steps at position 0.., single thread
+        from oracle.llama import OracleDecoder
+        from oracle.oracle import Oracle
+        od = OracleDecoder(Oracle(), host_model)
+        t0 = time.perf_counter()
+        for t in prompt[:args.decode_cpu_steps]:
+            od.step(int(t))
+        dt = time.perf_counter() - t0
+        od.close()
+        out["cpu_baseline"] = {"value": round(args.decode_cpu_steps / dt, 4), "unit": "tok/s", "cores": 1,
+                               "kind": "port",
+                               "sample": f"{args.decode_cpu_steps} steps of orc_text_step at positions 0.. "
+                                         "(C restatement of eosi_text_step, AVX2-path arithmetic)"}
+    dec.close()
+    return out
 
 
 def main():

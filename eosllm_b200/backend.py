@@ -75,6 +75,13 @@ _SIGNATURES = {
     "eosi_cuda_take_device_errors": (C.c_int, [C.POINTER(C.c_uint32)]),
     "eosi_cuda_set_kernel_variant": (C.c_int, [C.c_int, C.c_int]),
     "eosi_cuda_matmul_q4_k_noalloc": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "eosi_cuda_text_open": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
+    "eosi_cuda_text_step": (C.c_int, [_vp, _u32, _vp]),
+    "eosi_cuda_text_generate": (C.c_int, [_vp, _vp, _u32, _u32, _vp]),
+    "eosi_cuda_text_reset": (C.c_int, [_vp]),
+    "eosi_cuda_text_pos": (_u32, [_vp]),
+    "eosi_cuda_text_stream": (_vp, [_vp]),
+    "eosi_cuda_text_close": (None, [_vp]),
 }
 
 _lib = None

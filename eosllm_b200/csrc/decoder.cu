@@ -1,0 +1,863 @@
+// decoder.cu -- device-resident Llama decoder step for sm_100a: the work of
+// eosi_text_step (src/modality/text/text.c:267-436) with every tensor in HBM
+// and the greedy pick of the next token (src/sched/greedy.c:48-73) on the
+// device, so a whole generation runs without a host round trip per token.
+//
+// One token = one CUDA graph replay.  The position, the token fed in and the
+// greedy pick live in a DecState word block in device memory, so the same
+// graph serves every step.  Kernels of a step are chained with programmatic
+// dependent launch (PDL): each kernel triggers its dependent early and waits
+// (griddepcontrol.wait) before it touches any buffer an earlier kernel
+// writes or reads, so the GEMVs stream their weights while the small
+// kernels before them run.
+//
+// Per layer (tensor-parallel rank r of G; G == 1 is the whole model):
+//   norm_pack    x = x_prev + sum(partials)   (residual, text.c:404-406 and
+//                :420-421), rmsnorm (src/kernels/scalar/rmsnorm.c:14-37),
+//                then the Q8 activation packing of the next GEMV
+//   GEMV         [q; k; v] rows of this rank's heads          (text.c:349-352)
+//   attention    RoPE on q and k (src/kernels/scalar/rope.c:16-38), K/V append
+//                at `pos` (text.c:359-362), softmax attention with the GQA
+//                head map (text.c:364-401), split over positions; the last
+//                CTA of a head merges the pieces and packs the head's output
+//   GEMV         O projection on this rank's head columns -> partial x
+//   norm_pack    ffn_norm
+//   GEMV         [gate; up] rows of this rank's FFN slice     (text.c:413-415)
+//   silu_pack    silu(gate) * up (src/kernels/scalar/silu.c:12-23), packed
+//   GEMV         down projection on this rank's FFN columns -> partial x
+// then norm_pack(output_norm), the LM-head GEMV and argmax_kernel.
+//
+// Numerics: every GEMV is the bit-exact reference kernel (q4k_gemv.cu,
+// q80_gemv.cu).  The glue ops use IEEE round-to-nearest arithmetic in the
+// reference's operation order where that is cheap (rmsnorm scaling, RoPE
+// products, SiLU), but sums over a vector (rmsnorm's mean square, attention
+// dot products and softmax sums) are parallel reductions, and expf / powf /
+// sinf / cosf are CUDA's, so logits agree with the CPU engine to a
+// tolerance, not bit for bit.
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <utility>
+#include <vector>
+
+#include "eosllm_cuda.h"
+#include "eos_common.cuh"
+#include "eos_kernels.h"
+
+namespace eos {
+
+// Words the step kernels share in device memory.
+struct DecState {
+  uint32_t pos;         // position of the next step == tokens consumed
+  uint32_t n_prompt;    // steps at pos < n_prompt read their token from prompt[pos]
+  uint32_t next_token;  // greedy pick of the previous step
+  uint32_t arg_count;   // argmax CTA arrivals (reset by the last CTA)
+  uint32_t err;         // EOS_DEVERR_* bits
+  uint32_t pad[3];
+};
+
+constexpr uint32_t kMaxParts = 8;
+constexpr uint32_t kAttnChunk = 64;     // positions per attention CTA
+constexpr uint32_t kArgmaxBlocks = 64;  // CTAs of the argmax kernel (upper bound)
+
+// ---------------------------------------------------------------------------
+// Residual + rmsnorm + activation packing
+// ---------------------------------------------------------------------------
+struct NormPackParams {
+  const float* x_in;              // residual stream; nullptr: embedding lookup
+  const float* parts[kMaxParts];  // partial sums added to x_in, in rank order
+  uint32_t nparts;
+  const uint16_t* tok_embd;  // F16 [n_vocab][n]      (embedding mode)
+  const uint32_t* prompt;    // token of step pos when pos < n_prompt
+  const DecState* state;
+  float* x_out;     // updated residual stream (may be nullptr)
+  const float* w;   // norm weight
+  float eps;
+  uint32_t n;
+  uint8_t* act;     // Q4_K consumers: packed records for k = n
+  float* act_f32;   // Q8_0 consumers: the normalised vector
+};
+
+// Residual element i: x_in[i] + (((p_0 + p_1) + ...)); the reference adds
+// one full-length result (x[i] += t[i]), which is the nparts == 1 case.
+__device__ __forceinline__ float residual_at(const NormPackParams& p, const uint16_t* emb, uint32_t i) {
+  if (emb != nullptr) return f16_bits_to_f32(emb[i]);  // exact widening (src/util/f16.h)
+  const float v = p.x_in[i];
+  if (p.nparts == 0) return v;
+  float s = p.parts[0][i];
+  for (uint32_t j = 1; j < p.nparts; ++j) s = __fadd_rn(s, p.parts[j][i]);
+  return __fadd_rn(v, s);
+}
+
+// Grid: ceil(n / 256) CTAs of 256 threads.  Every CTA reduces the mean
+// square of the whole vector (the same fixed order in every CTA, so all agree
+// bit for bit) and then normalises and packs its own 256 elements.
+__global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) {
+  __shared__ float red[8];
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const uint16_t* emb = nullptr;
+  if (p.x_in == nullptr) {
+    const uint32_t pos = p.state->pos;
+    const uint32_t tok = pos < p.state->n_prompt ? p.prompt[pos] : p.state->next_token;
+    emb = p.tok_embd + (size_t)tok * p.n;
+  }
+  float ss = 0.0f;
+  for (uint32_t i = tid; i < p.n; i += 256u) {
+    const float v = residual_at(p, emb, i);
+    ss = __fadd_rn(ss, __fmul_rn(v, v));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) tot = __fadd_rn(tot, red[w]);
+  // ms /= cols; s = 1 / sqrtf(ms + eps); y = x * s * w  (rmsnorm.c:24-33)
+  const float ms = __fdiv_rn(tot, (float)p.n);
+  const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+  const uint32_t i = blockIdx.x * 256u + tid;
+  if (i >= p.n) return;  // warp-uniform: n % 32 == 0
+  const float v = residual_at(p, emb, i);
+  if (p.x_out != nullptr) p.x_out[i] = v;
+  const float y = __fmul_rn(__fmul_rn(v, s), p.w[i]);
+  if (p.act != nullptr)
+    pack_group_to_record(y, i >> 5, lane, p.act);
+  else
+    p.act_f32[i] = y;
+}
+
+// ---------------------------------------------------------------------------
+// Attention over the KV cache, split over positions
+// ---------------------------------------------------------------------------
+struct AttnParams {
+  const float* qkv;  // [hl*hd q | kvl*hd k | kvl*hd v] of this step
+  float* kc;         // this layer's caches: [max_ctx][kvl*hd] f32 (text.c:220-226)
+  float* vc;
+  float* part;       // [hl][max_chunks][hd + 4]: {max, sum, -, -, o[hd]}
+  uint32_t* count;   // [hl] chunk arrivals, reset by the merging CTA
+  const DecState* state;
+  uint8_t* act;      // Q4_K: packed records of the O-projection input (k = hl*hd)
+  float* act_f32;    // Q8_0: the attention output itself
+  uint32_t hl, h0, kvl, kv0, n_head, n_kv_head, max_chunks;
+  float base, scale;
+};
+
+// RoPE of the pair (x0, x1) at dims (i, i+1) of a head of size HD
+// (rope.c:25-33): th = pos * base^(-i/HD), then the rotation with separately
+// rounded products.
+template <int HD>
+__device__ __forceinline__ void rope_pair(float& x0, float& x1, uint32_t i, uint32_t pos, float base) {
+  const float th = __fmul_rn((float)pos, powf(base, __fdiv_rn(-(float)i, (float)HD)));
+  float sn, cs;
+  sincosf(th, &sn, &cs);
+  const float p0 = x0, p1 = x1;
+  x0 = __fsub_rn(__fmul_rn(p0, cs), __fmul_rn(p1, sn));
+  x1 = __fadd_rn(__fmul_rn(p0, sn), __fmul_rn(p1, cs));
+}
+
+// Grid (hl, max_chunks), 128 threads.  E = dims per lane (head_dim = 32 E).
+template <int E>
+__global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
+  constexpr uint32_t HD = 32u * E;
+  __shared__ float s_score[kAttnChunk];
+  __shared__ __align__(16) float s_o[4][HD];
+  __shared__ float s_l[4];
+  __shared__ float s_out[HD];
+  __shared__ uint32_t s_last;
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t hloc = blockIdx.x, c = blockIdx.y;
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const uint32_t pos = p.state->pos;
+  const uint32_t p0 = c * kAttnChunk;
+  if (p0 > pos) return;  // chunk beyond the context: no work, not counted
+  const uint32_t p1 = (p0 + kAttnChunk) < (pos + 1u) ? (p0 + kAttnChunk) : (pos + 1u);
+  const uint32_t np = p1 - p0;
+  const uint32_t gh = p.h0 + hloc;
+  const uint32_t gkv = (gh * p.n_kv_head) / p.n_head;  // GQA map (text.c:367)
+  const uint32_t kvi = gkv - p.kv0;
+  const uint32_t row = p.kvl * HD;  // floats per cache position
+  const uint32_t d0 = lane * E;
+
+  float q[E], kn[E], vn[E];
+  const float* qp = p.qkv + hloc * HD + d0;
+  const float* kp = p.qkv + p.hl * HD + kvi * HD + d0;
+  const float* vp = p.qkv + p.hl * HD + p.kvl * HD + kvi * HD + d0;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    q[e] = qp[e];
+    kn[e] = kp[e];
+    vn[e] = vp[e];
+  }
+#pragma unroll
+  for (int e = 0; e < E; e += 2) {
+    rope_pair<HD>(q[e], q[e + 1], d0 + e, pos, p.base);
+    rope_pair<HD>(kn[e], kn[e + 1], d0 + e, pos, p.base);
+  }
+  const bool has_pos = p1 == pos + 1u;
+  // the first local head of each KV group appends this step's K and V
+  if (has_pos && warp == 0 && (hloc == 0 || ((gh - 1u) * p.n_kv_head) / p.n_head != gkv)) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      p.kc[(size_t)pos * row + kvi * HD + d0 + e] = kn[e];
+      p.vc[(size_t)pos * row + kvi * HD + d0 + e] = vn[e];
+    }
+  }
+
+  // scores: one warp per position
+  for (uint32_t j = warp; j < np; j += 4u) {
+    const uint32_t t = p0 + j;
+    float acc = 0.0f;
+    if (t == pos) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc = __fmaf_rn(q[e], kn[e], acc);
+    } else {
+      const float* kr = p.kc + (size_t)t * row + kvi * HD + d0;
+#pragma unroll
+      for (int e = 0; e < E; ++e) acc = __fmaf_rn(q[e], kr[e], acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) s_score[j] = __fmul_rn(acc, p.scale);
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (uint32_t j = 0; j < np; ++j) mx = fmaxf(mx, s_score[j]);
+  // o = sum_t exp(s_t - mx) v_t over this chunk, one warp per position
+  float o[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) o[e] = 0.0f;
+  float l = 0.0f;
+  for (uint32_t j = warp; j < np; j += 4u) {
+    const uint32_t t = p0 + j;
+    const float a = expf(s_score[j] - mx);
+    l += a;
+    if (t == pos) {
+#pragma unroll
+      for (int e = 0; e < E; ++e) o[e] = __fmaf_rn(a, vn[e], o[e]);
+    } else {
+      const float* vr = p.vc + (size_t)t * row + kvi * HD + d0;
+#pragma unroll
+      for (int e = 0; e < E; ++e) o[e] = __fmaf_rn(a, vr[e], o[e]);
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) s_o[warp][d0 + e] = o[e];
+  if (lane == 0) s_l[warp] = l;
+  __syncthreads();
+  float* out = p.part + ((size_t)hloc * p.max_chunks + c) * (HD + 4u);
+  for (uint32_t d = tid; d < HD; d += 128u) out[4 + d] = ((s_o[0][d] + s_o[1][d]) + s_o[2][d]) + s_o[3][d];
+  if (tid == 0) {
+    out[0] = mx;
+    out[1] = ((s_l[0] + s_l[1]) + s_l[2]) + s_l[3];
+  }
+  __threadfence();
+  __syncthreads();
+  const uint32_t nvalid = pos / kAttnChunk + 1u;
+  if (tid == 0) s_last = atomicAdd(&p.count[hloc], 1u) == nvalid - 1u;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+
+  // last CTA of the head: merge the chunks (log-sum-exp), normalise
+  const float* base = p.part + (size_t)hloc * p.max_chunks * (HD + 4u);
+  float gmx = -INFINITY;
+  for (uint32_t cc = 0; cc < nvalid; ++cc) gmx = fmaxf(gmx, __ldcg(base + cc * (HD + 4u)));
+  float L = 0.0f;
+  for (uint32_t cc = 0; cc < nvalid; ++cc) {
+    const float* pc = base + cc * (HD + 4u);
+    L += __ldcg(pc + 1) * expf(__ldcg(pc) - gmx);
+  }
+  const float inv = 1.0f / L;
+  for (uint32_t d = tid; d < HD; d += 128u) {
+    float acc = 0.0f;
+    for (uint32_t cc = 0; cc < nvalid; ++cc) {
+      const float* pc = base + cc * (HD + 4u);
+      acc = __fmaf_rn(__ldcg(pc + 4 + d), expf(__ldcg(pc) - gmx), acc);
+    }
+    s_out[d] = acc * inv;
+  }
+  if (tid == 0) p.count[hloc] = 0u;
+  __syncthreads();
+  if (p.act != nullptr) {
+    for (uint32_t g = warp; g < E; g += 4u) pack_group_to_record(s_out[g * 32u + lane], hloc * E + g, lane, p.act);
+  } else {
+    for (uint32_t d = tid; d < HD; d += 128u) p.act_f32[hloc * HD + d] = s_out[d];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// silu(gate) * up, packed for the down projection
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) silu_pack_kernel(const float* __restrict__ gu, uint32_t ffl,
+                                                        uint8_t* __restrict__ act, float* __restrict__ act_f32) {
+  pdl_trigger();
+  pdl_wait();
+  const uint32_t i = blockIdx.x * 256u + threadIdx.x;
+  if (i >= ffl) return;  // warp-uniform: ffl % 32 == 0
+  const float g = gu[i], u = gu[ffl + i];
+  // x * (1 / (1 + expf(-x))) (silu.c:17), then gate * up (text.c:417)
+  const float h = __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), u);
+  if (act != nullptr)
+    pack_group_to_record(h, i >> 5, threadIdx.x & 31u, act);
+  else
+    act_f32[i] = h;
+}
+
+// ---------------------------------------------------------------------------
+// Greedy pick: the first index of the largest logit (greedy.c:66-69: strict >
+// from logits[0], so a NaN logits[0] keeps index 0 and other NaNs never win)
+// ---------------------------------------------------------------------------
+struct ArgmaxParams {
+  const float* logits;
+  uint32_t n;
+  float* part_v;     // [gridDim.x]
+  uint32_t* part_i;
+  DecState* state;
+  uint32_t* out_tokens;  // [max_ctx]: pick of step pos
+};
+
+__device__ __forceinline__ bool arg_better(float av, uint32_t ai, float bv, uint32_t bi) {
+  if (av != av) return false;
+  if (bv != bv) return true;
+  return av > bv || (av == bv && ai < bi);
+}
+
+__device__ __forceinline__ void arg_reduce_block(float& v, uint32_t& idx, float* sv, uint32_t* si) {
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (arg_better(ov, oi, v, idx)) {
+      v = ov;
+      idx = oi;
+    }
+  }
+  if (lane == 0) {
+    sv[warp] = v;
+    si[warp] = idx;
+  }
+  __syncthreads();
+  v = sv[0];
+  idx = si[0];
+  for (uint32_t w = 1; w < blockDim.x / 32u; ++w)
+    if (arg_better(sv[w], si[w], v, idx)) {
+      v = sv[w];
+      idx = si[w];
+    }
+}
+
+__global__ void __launch_bounds__(256) argmax_kernel(const ArgmaxParams p) {
+  __shared__ float sv[8];
+  __shared__ uint32_t si[8];
+  __shared__ uint32_t s_last;
+  pdl_trigger();
+  pdl_wait();
+  float v = __int_as_float(0x7fc00000);  // "nothing yet"
+  uint32_t idx = 0xffffffffu;
+  for (uint32_t i = blockIdx.x * 256u + threadIdx.x; i < p.n; i += gridDim.x * 256u) {
+    const float x = p.logits[i];
+    if (arg_better(x, i, v, idx)) {
+      v = x;
+      idx = i;
+    }
+  }
+  arg_reduce_block(v, idx, sv, si);
+  if (threadIdx.x == 0) {
+    p.part_v[blockIdx.x] = v;
+    p.part_i[blockIdx.x] = idx;
+    __threadfence();
+    s_last = atomicAdd(&p.state->arg_count, 1u) == gridDim.x - 1u;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  __syncthreads();
+  v = __int_as_float(0x7fc00000);
+  idx = 0xffffffffu;
+  for (uint32_t b = threadIdx.x; b < gridDim.x; b += 256u) {
+    const float bv = __ldcg(p.part_v + b);
+    const uint32_t bi = __ldcg(p.part_i + b);
+    if (arg_better(bv, bi, v, idx)) {
+      v = bv;
+      idx = bi;
+    }
+  }
+  __syncthreads();
+  arg_reduce_block(v, idx, sv, si);
+  if (threadIdx.x == 0) {
+    const float first = __ldcg(p.logits);
+    const uint32_t tok = (first != first || idx == 0xffffffffu) ? 0u : idx;
+    const uint32_t pos = p.state->pos;
+    p.out_tokens[pos] = tok;
+    p.state->next_token = tok;
+    p.state->arg_count = 0u;
+    p.state->pos = pos + 1u;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace {
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, kernel, std::forward<Args>(args)...);
+}
+
+size_t wbytes(int dt, uint64_t n, uint64_t k) {
+  return dt == EOS_DT_Q4_K ? (size_t)(n * (k / Q4K_ELEMS) * Q4K_BYTES) : (size_t)(n * (k / Q80_ELEMS) * Q80_BYTES);
+}
+uint32_t blk_elems(int dt) { return dt == EOS_DT_Q4_K ? Q4K_ELEMS : Q80_ELEMS; }
+
+}  // namespace
+
+struct DecLayer {
+  uint8_t* wqkv;
+  uint8_t* wo;
+  uint8_t* wgu;
+  uint8_t* wd;
+  float* attn_norm;
+  float* ffn_norm;
+};
+
+struct TextDecoder {
+  eosi_cuda_llama_t m{};
+  int device = 0, rank = 0, world = 1;
+  uint32_t hd = 0, hl = 0, h0 = 0, kvl = 0, kv0 = 0, ffl = 0, ff0 = 0, vl = 0, v0 = 0, max_chunks = 0;
+  int num_sms = 0, max_smem = 0;
+  cudaStream_t st = nullptr;
+  std::vector<void*> allocs;
+  std::vector<DecLayer> layers;
+  uint16_t* tok_embd = nullptr;
+  float* out_norm = nullptr;
+  uint8_t* wout = nullptr;
+  // activations
+  float *x0 = nullptr, *x1 = nullptr, *qkv = nullptr, *part_o = nullptr, *part_d = nullptr, *gu = nullptr;
+  float* logits = nullptr;
+  uint8_t *act_e = nullptr, *act_o = nullptr, *act_d = nullptr;  // Q4_K records
+  float *actf_e = nullptr, *actf_o = nullptr, *actf_d = nullptr;  // Q8_0 inputs
+  float *kc = nullptr, *vc = nullptr;
+  float* attn_part = nullptr;
+  uint32_t* attn_count = nullptr;
+  float* arg_v = nullptr;
+  uint32_t* arg_i = nullptr;
+  DecState* state = nullptr;
+  uint32_t* prompt = nullptr;
+  uint32_t* out_tokens = nullptr;
+  uint32_t* gemv_err = nullptr;
+  uint32_t arg_blocks = 0;
+  cudaGraphExec_t graph = nullptr;
+  uint32_t host_pos = 0;
+  bool step_mode = false;  // prompt[] holds every fed token (n_prompt = max_ctx)
+
+  template <typename T>
+  cudaError_t alloc(T** p, size_t bytes) {
+    void* v = nullptr;
+    cudaError_t e = cudaMalloc(&v, bytes < 16 ? 16 : bytes);
+    if (e != cudaSuccess) return e;
+    allocs.push_back(v);
+    *p = static_cast<T*>(v);
+    return cudaMemsetAsync(v, 0, bytes < 16 ? 16 : bytes, st);
+  }
+
+  ~TextDecoder() {
+    if (graph) cudaGraphExecDestroy(graph);
+    if (st) cudaStreamSynchronize(st);
+    for (void* p : allocs) cudaFree(p);
+    if (st) cudaStreamDestroy(st);
+  }
+
+  cudaMemcpyKind kind() const {
+    return m.weights_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  }
+
+  // rows [r0, r0 + rows) of an [n][k] quantized matrix into dst
+  cudaError_t copy_rows(uint8_t* dst, const void* src, int dt, uint64_t k, uint64_t r0, uint64_t rows) {
+    const size_t rb = wbytes(dt, 1, k);
+    return cudaMemcpyAsync(dst, static_cast<const uint8_t*>(src) + r0 * rb, rows * rb, kind(), st);
+  }
+  // all n rows, columns [c0, c0 + cols) (block-aligned) into a dense [n][cols] matrix
+  cudaError_t copy_cols(uint8_t* dst, const void* src, int dt, uint64_t n, uint64_t k, uint64_t c0, uint64_t cols) {
+    const size_t rb = wbytes(dt, 1, k), sb = wbytes(dt, 1, cols), off = wbytes(dt, 1, c0);
+    return cudaMemcpy2DAsync(dst, sb, static_cast<const uint8_t*>(src) + off, rb, sb, n, kind(), st);
+  }
+
+  int open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws);
+  cudaError_t record_step(cudaStream_t s);
+  int capture();
+};
+
+int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
+  m = *desc;
+  device = dev;
+  rank = rk;
+  world = ws;
+  const int wdt = m.wdtype, odt = m.out_dtype;
+  if (m.n_head == 0 || m.n_kv_head == 0 || m.n_embd % m.n_head) return EOS_E_INVALID_ARG;
+  hd = m.n_embd / m.n_head;
+  if (hd != 64 && hd != 128 && hd != 256) {
+    set_error_message("cuda text: head_dim must be 64, 128 or 256");
+    return EOS_E_UNSUPPORTED;
+  }
+  if ((wdt != EOS_DT_Q4_K && wdt != EOS_DT_Q8_0) || (odt != EOS_DT_Q4_K && odt != EOS_DT_Q8_0)) {
+    set_error_message("cuda text: linears must be Q4_K or Q8_0");
+    return EOS_E_UNSUPPORTED;
+  }
+  if (m.n_embd % 256 || m.n_ff % blk_elems(wdt) || m.n_embd % blk_elems(odt)) {
+    set_error_message("cuda text: n_embd must be a multiple of 256 and n_ff of the block size");
+    return EOS_E_UNSUPPORTED;
+  }
+  if (ws < 1 || ws > (int)kMaxParts || rk < 0 || rk >= ws || m.n_head % ws || m.n_kv_head % ws) {
+    set_error_message("cuda text: world size must divide the head counts (at most 8 ranks)");
+    return EOS_E_INVALID_ARG;
+  }
+  hl = m.n_head / ws;
+  h0 = hl * rk;
+  kvl = m.n_kv_head / ws;
+  kv0 = kvl * rk;
+  if (wdt == EOS_DT_Q4_K && (hl * hd) % 256) {
+    set_error_message("cuda text: a rank's head columns must be whole Q4_K super-blocks");
+    return EOS_E_UNSUPPORTED;
+  }
+  {
+    // FFN slice in whole blocks of the down projection's k
+    const uint32_t be = blk_elems(wdt), units = m.n_ff / be;
+    ff0 = (uint32_t)(((uint64_t)units * rk) / ws) * be;
+    ffl = (uint32_t)(((uint64_t)units * (rk + 1)) / ws) * be - ff0;
+  }
+  v0 = (uint32_t)(((uint64_t)m.n_vocab * rk) / ws);
+  vl = (uint32_t)(((uint64_t)m.n_vocab * (rk + 1)) / ws) - v0;
+  max_chunks = (m.max_ctx + kAttnChunk - 1) / kAttnChunk;
+
+  if (cudaSetDevice(dev) != cudaSuccess) return EOS_E_INTERNAL;
+  cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return EOS_E_INTERNAL;
+
+  const uint32_t E = m.n_embd;
+  cudaError_t e = cudaSuccess;
+  auto chk = [&](cudaError_t r) {
+    if (e == cudaSuccess) e = r;
+  };
+  // ---- resident weights (this rank's slices) ----
+  layers.resize(m.n_layer);
+  for (uint32_t L = 0; L < m.n_layer; ++L) {
+    DecLayer& d = layers[L];
+    const size_t rb = wbytes(wdt, 1, E);
+    chk(alloc(&d.wqkv, rb * (hl * hd + 2 * kvl * hd)));
+    chk(copy_rows(d.wqkv, m.wq[L], wdt, E, h0 * hd, hl * hd));
+    chk(copy_rows(d.wqkv + rb * hl * hd, m.wk[L], wdt, E, kv0 * hd, kvl * hd));
+    chk(copy_rows(d.wqkv + rb * (hl * hd + kvl * hd), m.wv[L], wdt, E, kv0 * hd, kvl * hd));
+    chk(alloc(&d.wo, wbytes(wdt, E, hl * hd)));
+    chk(copy_cols(d.wo, m.wo[L], wdt, E, E, h0 * hd, hl * hd));
+    chk(alloc(&d.wgu, 2 * rb * ffl));
+    chk(copy_rows(d.wgu, m.wg[L], wdt, E, ff0, ffl));
+    chk(copy_rows(d.wgu + rb * ffl, m.wu[L], wdt, E, ff0, ffl));
+    chk(alloc(&d.wd, wbytes(wdt, E, ffl)));
+    chk(copy_cols(d.wd, m.wd[L], wdt, E, m.n_ff, ff0, ffl));
+    chk(alloc(&d.attn_norm, 4ull * E));
+    chk(cudaMemcpyAsync(d.attn_norm, m.attn_norm[L], 4ull * E, kind(), st));
+    chk(alloc(&d.ffn_norm, 4ull * E));
+    chk(cudaMemcpyAsync(d.ffn_norm, m.ffn_norm[L], 4ull * E, kind(), st));
+  }
+  chk(alloc(&tok_embd, 2ull * m.n_vocab * E));
+  chk(cudaMemcpyAsync(tok_embd, m.tok_embd, 2ull * m.n_vocab * E, kind(), st));
+  chk(alloc(&out_norm, 4ull * E));
+  chk(cudaMemcpyAsync(out_norm, m.output_norm, 4ull * E, kind(), st));
+  chk(alloc(&wout, wbytes(odt, vl, E)));
+  chk(copy_rows(wout, m.output_w, odt, E, v0, vl));
+  // ---- activations and caches ----
+  chk(alloc(&x0, 4ull * E));
+  chk(alloc(&x1, 4ull * E));
+  chk(alloc(&qkv, 4ull * (hl * hd + 2 * kvl * hd)));
+  chk(alloc(&part_o, 4ull * E));
+  chk(alloc(&part_d, 4ull * E));
+  chk(alloc(&gu, 8ull * ffl));
+  chk(alloc(&logits, 4ull * (vl > 0 ? vl : 1)));
+  if (wdt == EOS_DT_Q4_K) {
+    chk(alloc(&act_o, (size_t)(hl * hd / 256) * kActRec));
+    chk(alloc(&act_d, (size_t)(ffl / 256) * kActRec));
+  } else {
+    chk(alloc(&actf_o, 4ull * hl * hd));
+    chk(alloc(&actf_d, 4ull * ffl));
+  }
+  // the normalised residual feeds the block linears (wdtype) and the head (out_dtype)
+  if (wdt == EOS_DT_Q4_K || odt == EOS_DT_Q4_K) chk(alloc(&act_e, (size_t)(E / 256) * kActRec));
+  if (wdt == EOS_DT_Q8_0 || odt == EOS_DT_Q8_0) chk(alloc(&actf_e, 4ull * E));
+  const size_t kv_bytes = 4ull * m.n_layer * m.max_ctx * kvl * hd;
+  chk(alloc(&kc, kv_bytes));
+  chk(alloc(&vc, kv_bytes));
+  chk(alloc(&attn_part, 4ull * hl * max_chunks * (hd + 4)));
+  chk(alloc(&attn_count, 4ull * hl));
+  arg_blocks = (vl + 2047u) / 2048u;
+  if (arg_blocks > kArgmaxBlocks) arg_blocks = kArgmaxBlocks;
+  if (arg_blocks < 1) arg_blocks = 1;
+  chk(alloc(&arg_v, 4ull * kArgmaxBlocks));
+  chk(alloc(&arg_i, 4ull * kArgmaxBlocks));
+  chk(alloc(&state, sizeof(DecState)));
+  chk(alloc(&prompt, 4ull * m.max_ctx));
+  chk(alloc(&out_tokens, 4ull * m.max_ctx));
+  chk(alloc(&gemv_err, 16));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    set_error_message(cudaGetErrorString(e));
+    return e == cudaErrorMemoryAllocation ? EOS_E_OUT_OF_MEMORY : EOS_E_INTERNAL;
+  }
+  return capture();
+}
+
+cudaError_t TextDecoder::record_step(cudaStream_t s) {
+  const uint32_t E = m.n_embd;
+  const int wdt = m.wdtype, odt = m.out_dtype;
+  const uint32_t nqkv = hl * hd + 2 * kvl * hd;
+  cudaError_t e = cudaSuccess;
+  int status = EOS_OK;
+  auto gemv = [&](int dt, const uint8_t* w, const uint8_t* act, const float* actf, float* c, uint32_t n,
+                  uint32_t k) -> cudaError_t {
+    if (n == 0) return cudaSuccess;
+    if (dt == EOS_DT_Q4_K) return launch_q4k_gemv(w, act, nullptr, c, n, k, gemv_err, num_sms, max_smem, true, s,
+                                                  &status);
+    return launch_q80_gemv(w, actf, c, n, k, gemv_err, num_sms, max_smem, s, &status);
+  };
+  auto norm_pack = [&](const float* x_in, const float* part, float* x_out, const float* w, int dt_a, int dt_b)
+      -> cudaError_t {
+    NormPackParams p{};
+    p.x_in = x_in;
+    p.nparts = part ? 1u : 0u;
+    p.parts[0] = part;
+    p.tok_embd = tok_embd;
+    p.prompt = prompt;
+    p.state = state;
+    p.x_out = x_out;
+    p.w = w;
+    p.eps = m.rms_eps;
+    p.n = E;
+    // one consumer dtype per launch; the head may differ from the block linears
+    (void)dt_b;
+    p.act = dt_a == EOS_DT_Q4_K ? act_e : nullptr;
+    p.act_f32 = dt_a == EOS_DT_Q8_0 ? actf_e : nullptr;
+    return launch_pdl(norm_pack_kernel, dim3(E / 256u), dim3(256), s, p);
+  };
+  for (uint32_t L = 0; L < m.n_layer && e == cudaSuccess; ++L) {
+    const DecLayer& d = layers[L];
+    // x1 = (L == 0 ? embedding : x0 + down partial); act_e = pack(rmsnorm(x1))
+    e = norm_pack(L == 0 ? nullptr : x0, L == 0 ? nullptr : part_d, x1, d.attn_norm, wdt, wdt);
+    if (e == cudaSuccess) e = gemv(wdt, d.wqkv, act_e, actf_e, qkv, nqkv, E);
+    if (e == cudaSuccess) {
+      AttnParams a{};
+      a.qkv = qkv;
+      a.kc = kc + (size_t)L * m.max_ctx * kvl * hd;
+      a.vc = vc + (size_t)L * m.max_ctx * kvl * hd;
+      a.part = attn_part;
+      a.count = attn_count;
+      a.state = state;
+      a.act = act_o;
+      a.act_f32 = actf_o;
+      a.hl = hl;
+      a.h0 = h0;
+      a.kvl = kvl;
+      a.kv0 = kv0;
+      a.n_head = m.n_head;
+      a.n_kv_head = m.n_kv_head;
+      a.max_chunks = max_chunks;
+      a.base = m.rope_base;
+      a.scale = 1.0f / sqrtf((float)hd);  // text.c:365
+      const dim3 grid(hl, max_chunks);
+      if (hd == 64) e = launch_pdl(attn_kernel<2>, grid, dim3(128), s, a);
+      else if (hd == 128) e = launch_pdl(attn_kernel<4>, grid, dim3(128), s, a);
+      else e = launch_pdl(attn_kernel<8>, grid, dim3(128), s, a);
+    }
+    if (e == cudaSuccess) e = gemv(wdt, d.wo, act_o, actf_o, part_o, E, hl * hd);
+    // x0 = x1 + O partial; act_e = pack(rmsnorm(x0))
+    if (e == cudaSuccess) e = norm_pack(x1, part_o, x0, d.ffn_norm, wdt, wdt);
+    if (e == cudaSuccess) e = gemv(wdt, d.wgu, act_e, actf_e, gu, 2 * ffl, E);
+    if (e == cudaSuccess)
+      e = launch_pdl(silu_pack_kernel, dim3((ffl + 255u) / 256u), dim3(256), s, (const float*)gu, ffl, act_d,
+                     actf_d);
+    if (e == cudaSuccess) e = gemv(wdt, d.wd, act_d, actf_d, part_d, E, ffl);
+  }
+  // final norm + LM head + greedy pick (text.c:425-432, greedy.c:66-69)
+  if (e == cudaSuccess)
+    e = norm_pack(m.n_layer ? x0 : nullptr, m.n_layer ? part_d : nullptr, x1, out_norm, odt, odt);
+  if (e == cudaSuccess) e = gemv(odt, wout, act_e, actf_e, logits, vl, E);
+  if (e == cudaSuccess) {
+    ArgmaxParams a{logits, vl, arg_v, arg_i, state, out_tokens};
+    e = launch_pdl(argmax_kernel, dim3(arg_blocks), dim3(256), s, a);
+  }
+  if (e == cudaSuccess && status != EOS_OK) e = cudaErrorNotSupported;
+  return e;
+}
+
+int TextDecoder::capture() {
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);
+  if (e == cudaSuccess) {
+    const cudaError_t r = record_step(st);
+    e = cudaStreamEndCapture(st, &g);
+    if (r != cudaSuccess) e = r;
+  }
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&graph, g, 0);
+  if (g) cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    set_error_message(cudaGetErrorString(e));
+    return EOS_E_INTERNAL;
+  }
+  return EOS_OK;
+}
+
+}  // namespace eos
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+using eos::TextDecoder;
+
+struct eosi_cuda_text {
+  TextDecoder d;
+};
+
+namespace {
+int dec_fail(cudaError_t e) {
+  eos::set_error_message(cudaGetErrorString(e));
+  return EOS_E_INTERNAL;
+}
+int dec_check_device_errors(eosi_cuda_text_t* t) {
+  uint32_t words[2] = {0, 0};
+  cudaError_t e = cudaMemcpyAsync(&words[0], &t->d.state->err, 4, cudaMemcpyDeviceToHost, t->d.st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&words[1], t->d.gemv_err, 4, cudaMemcpyDeviceToHost, t->d.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(t->d.st);
+  if (e != cudaSuccess) return dec_fail(e);
+  if (words[0] | words[1]) {
+    eos::set_error_message("cuda text: a device-side bounded wait ran out");
+    return EOS_E_INTERNAL;
+  }
+  return EOS_OK;
+}
+}  // namespace
+
+extern "C" {
+
+EOSLLM_CUDA_API int eosi_cuda_text_open(const eosi_cuda_llama_t* m, int device, int rank, int world,
+                                        eosi_cuda_text_t** out) {
+  if (m == nullptr || out == nullptr || m->tok_embd == nullptr || m->output_norm == nullptr ||
+      m->output_w == nullptr || (m->n_layer > 0 && (m->attn_norm == nullptr || m->ffn_norm == nullptr ||
+                                                    m->wq == nullptr || m->wk == nullptr || m->wv == nullptr ||
+                                                    m->wo == nullptr || m->wg == nullptr || m->wu == nullptr ||
+                                                    m->wd == nullptr)) ||
+      m->max_ctx == 0 || m->n_vocab == 0) {
+    eos::set_error_message("cuda text: NULL or empty model description");
+    return EOS_E_INVALID_ARG;
+  }
+  *out = nullptr;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    eos::set_error_message("cuda text: no such CUDA device");
+    return EOS_E_UNSUPPORTED;
+  }
+  eosi_cuda_text_t* t = new (std::nothrow) eosi_cuda_text_t();
+  if (t == nullptr) return EOS_E_OUT_OF_MEMORY;
+  const int s = t->d.open(m, device, rank, world);
+  if (s != EOS_OK) {
+    delete t;
+    return s;
+  }
+  *out = t;
+  return EOS_OK;
+}
+
+EOSLLM_CUDA_API int eosi_cuda_text_step(eosi_cuda_text_t* t, uint32_t token, float* logits) {
+  if (t == nullptr || logits == nullptr) return EOS_E_INVALID_ARG;
+  TextDecoder& d = t->d;
+  if (token >= d.m.n_vocab) {  // text.c:277
+    eos::set_error_message("cuda text: token id out of range");
+    return EOS_E_INVALID_ARG;
+  }
+  if (d.host_pos >= d.m.max_ctx) {  // text.c:278
+    eos::set_error_message("cuda text: context is full");
+    return EOS_E_OUT_OF_MEMORY;
+  }
+  if (cudaSetDevice(d.device) != cudaSuccess) return EOS_E_INTERNAL;
+  cudaError_t e = cudaSuccess;
+  if (!d.step_mode) {  // every later step reads its token from prompt[pos]
+    const uint32_t np = d.m.max_ctx;
+    e = cudaMemcpyAsync(&d.state->n_prompt, &np, 4, cudaMemcpyHostToDevice, d.st);
+    d.step_mode = true;
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(d.prompt + d.host_pos, &token, 4, cudaMemcpyHostToDevice, d.st);
+  if (e == cudaSuccess) e = cudaGraphLaunch(d.graph, d.st);
+  if (e == cudaSuccess && d.world == 1)
+    e = cudaMemcpyAsync(logits, d.logits, 4ull * d.m.n_vocab, cudaMemcpyDeviceToHost, d.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d.st);
+  if (e != cudaSuccess) return dec_fail(e);
+  d.host_pos++;
+  return dec_check_device_errors(t);
+}
+
+EOSLLM_CUDA_API int eosi_cuda_text_generate(eosi_cuda_text_t* t, const uint32_t* prompt, uint32_t n_prompt,
+                                            uint32_t n_gen, uint32_t* out_tokens) {
+  if (t == nullptr || prompt == nullptr || n_prompt == 0 || (n_gen > 0 && out_tokens == nullptr))
+    return EOS_E_INVALID_ARG;
+  TextDecoder& d = t->d;
+  for (uint32_t i = 0; i < n_prompt; ++i)
+    if (prompt[i] >= d.m.n_vocab) {
+      eos::set_error_message("cuda text: token id out of range");
+      return EOS_E_INVALID_ARG;
+    }
+  const uint64_t steps = (uint64_t)n_prompt + (n_gen > 0 ? n_gen - 1u : 0u);
+  if (d.host_pos + steps > d.m.max_ctx) {
+    eos::set_error_message("cuda text: prompt plus generation exceed the context");
+    return EOS_E_OUT_OF_MEMORY;
+  }
+  if (cudaSetDevice(d.device) != cudaSuccess) return EOS_E_INTERNAL;
+  const uint32_t np = d.host_pos + n_prompt;
+  cudaError_t e = cudaMemcpyAsync(d.prompt + d.host_pos, prompt, 4ull * n_prompt, cudaMemcpyHostToDevice, d.st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&d.state->n_prompt, &np, 4, cudaMemcpyHostToDevice, d.st);
+  d.step_mode = false;
+  for (uint64_t i = 0; i < steps && e == cudaSuccess; ++i) e = cudaGraphLaunch(d.graph, d.st);
+  // the pick of step (n_prompt - 1 + j) is generated token j
+  if (e == cudaSuccess && n_gen > 0)
+    e = cudaMemcpyAsync(out_tokens, d.out_tokens + np - 1u, 4ull * n_gen, cudaMemcpyDeviceToHost, d.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d.st);
+  if (e != cudaSuccess) return dec_fail(e);
+  d.host_pos += (uint32_t)steps;
+  return dec_check_device_errors(t);
+}
+
+EOSLLM_CUDA_API int eosi_cuda_text_reset(eosi_cuda_text_t* t) {
+  if (t == nullptr) return EOS_E_INVALID_ARG;
+  TextDecoder& d = t->d;
+  if (cudaSetDevice(d.device) != cudaSuccess) return EOS_E_INTERNAL;
+  cudaError_t e = cudaMemsetAsync(d.state, 0, sizeof(eos::DecState), d.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d.st);
+  if (e != cudaSuccess) return dec_fail(e);
+  d.host_pos = 0;
+  d.step_mode = false;
+  return EOS_OK;
+}
+
+EOSLLM_CUDA_API uint32_t eosi_cuda_text_pos(const eosi_cuda_text_t* t) { return t ? t->d.host_pos : 0u; }
+
+EOSLLM_CUDA_API void* eosi_cuda_text_stream(eosi_cuda_text_t* t) { return t ? (void*)t->d.st : nullptr; }
+
+EOSLLM_CUDA_API void eosi_cuda_text_close(eosi_cuda_text_t* t) {
+  if (t == nullptr) return;
+  cudaSetDevice(t->d.device);
+  delete t;
+}
+
+}  // extern "C"

@@ -21,7 +21,7 @@
 #include <unordered_map>
 #include <vector>
 
-#include "../../include/eosllm_cuda.h"
+#include "eosllm_cuda.h"
 #include "eos_common.cuh"
 #include "eos_kernels.h"
 

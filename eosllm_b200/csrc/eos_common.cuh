@@ -211,6 +211,29 @@ __device__ __forceinline__ void q4k_scale_min_w(int j, uint32_t w0, uint32_t w1,
   }
 }
 
+// Packed Q4_K activation record (layout documented in q4k_gemv.cu).
+constexpr uint32_t kActRec = 480;   // bytes per super-block of packed activations
+constexpr uint32_t kActHalf = 272;  // offset of the second half-record
+
+// Record position of 32-group g (sub-block g % 8 of super-block g / 8).
+__device__ __forceinline__ uint32_t rec_aq_offset(uint32_t g) {
+  const uint32_t s = g & 7u;
+  return (g >> 3) * kActRec + (s >> 2) * kActHalf + ((s & 3u) << 5);
+}
+__device__ __forceinline__ uint32_t rec_st_offset(uint32_t g) {
+  const uint32_t s = g & 7u;
+  return (g >> 3) * kActRec + (s >> 2) * kActHalf + 128u + ((s & 3u) << 3);
+}
+
+// Packs the warp's 32-group g (lane i holds element i) into a record.
+__device__ __forceinline__ void pack_group_to_record(float v, uint32_t g, uint32_t lane, uint8_t* rec) {
+  float scale;
+  int32_t sum;
+  const int8_t q = quant_group32(v, scale, sum);
+  rec[rec_aq_offset(g) + lane] = static_cast<uint8_t>(q);
+  if (lane == 0) *reinterpret_cast<float2*>(rec + rec_st_offset(g)) = make_float2(scale, (float)sum);
+}
+
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xffffu)));
 }

@@ -18,7 +18,7 @@
 // device current, and passes it to the kernels.
 #include <mutex>
 
-#include "../../include/eosllm_cuda.h"
+#include "eosllm_cuda.h"
 #include "eos_common.cuh"
 #include "eos_kernels.h"
 

@@ -41,19 +41,6 @@
 
 namespace eos {
 
-constexpr uint32_t kActRec = 480;   // bytes per super-block of packed activations
-constexpr uint32_t kActHalf = 272;  // offset of the second half-record
-
-// Record position of 32-group g (sub-block g % 8 of super-block g / 8).
-__device__ __forceinline__ uint32_t rec_aq_offset(uint32_t g) {
-  const uint32_t s = g & 7u;
-  return (g >> 3) * kActRec + (s >> 2) * kActHalf + ((s & 3u) << 5);
-}
-__device__ __forceinline__ uint32_t rec_st_offset(uint32_t g) {
-  const uint32_t s = g & 7u;
-  return (g >> 3) * kActRec + (s >> 2) * kActHalf + 128u + ((s & 3u) << 3);
-}
-
 // ---------------------------------------------------------------------------
 // Activation packing kernel: one warp per 32-group.
 // ---------------------------------------------------------------------------

@@ -181,6 +181,64 @@ EOSLLM_CUDA_API int eosi_cuda_fill_gauss_dev(float *dst, size_t n, uint64_t seed
 EOSLLM_CUDA_API int eosi_cuda_q4_k_from_gauss_dev(void *dst, size_t n_elements, uint64_t seed, float sigma,
                                   void *stream);
 
+/* ---- device-resident Llama decoder ------------------------------------------
+ * The work of eosi_text_open / eosi_text_step / eosi_text_close
+ * (src/modality/text/text.h:62-78, text.c:131-436 of the reference) with
+ * every weight, the KV cache and the greedy pick (src/sched/greedy.c:48-73)
+ * on one GPU, or row/column-sharded across `world` GPUs (one process per
+ * GPU, rank r on its own device).  Linears are Q4_K or Q8_0, token
+ * embeddings F16, norms F32, the KV cache f32 like the reference's. */
+typedef struct {
+    uint32_t n_embd, n_layer, n_head, n_kv_head, n_ff, n_vocab, max_ctx;
+    float rms_eps, rope_base;
+    int32_t wdtype;            /* 33 (Q4_K) or 32 (Q8_0): every block linear */
+    int32_t out_dtype;         /* dtype of output.weight */
+    int32_t weights_on_device; /* 0: host pointers (e.g. into the GGUF buffer);
+                                  1: device pointers on `device` */
+    const uint16_t *tok_embd;  /* F16 [n_vocab][n_embd] */
+    const float *output_norm;  /* F32 [n_embd] */
+    const void *output_w;      /* [n_vocab] rows of n_embd */
+    /* per-layer tables of n_layer pointers, GGUF row-major (one row per
+     * output): attn_q [n_embd], attn_k / attn_v [n_kv_head*head_dim],
+     * attn_output [n_embd], ffn_gate / ffn_up [n_ff] rows of n_embd,
+     * ffn_down [n_embd] rows of n_ff */
+    const float *const *attn_norm;
+    const float *const *ffn_norm;
+    const void *const *wq;
+    const void *const *wk;
+    const void *const *wv;
+    const void *const *wo;
+    const void *const *wg;
+    const void *const *wu;
+    const void *const *wd;
+} eosi_cuda_llama_t;
+
+typedef struct eosi_cuda_text eosi_cuda_text_t;
+
+/* Upload this rank's slices of the model to `device` and build the per-token
+ * step.  head_dim must be 64, 128 or 256; n_embd a multiple of 256; `world`
+ * must divide n_head and n_kv_head.  Replaces eosi_text_open (text.c:131-260). */
+EOSLLM_CUDA_API int eosi_cuda_text_open(const eosi_cuda_llama_t *m, int device, int rank, int world,
+                                        eosi_cuda_text_t **out);
+/* One decoder step at the current position: token -> logits[n_vocab]
+ * (host memory), position + 1.  Same contract as eosi_text_step
+ * (text.c:267-436): EOS_E_INVALID_ARG for token >= n_vocab,
+ * EOS_E_OUT_OF_MEMORY when the context is full. */
+EOSLLM_CUDA_API int eosi_cuda_text_step(eosi_cuda_text_t *t, uint32_t token, float *logits);
+/* Greedy generation without a host round trip per token: feeds prompt
+ * [0, n_prompt) from the current position, then n_gen - 1 of its own picks,
+ * and returns the n_gen picks (the first is the pick after the last prompt
+ * token), as eos_session_feed + eos_session_step with the greedy scheduler
+ * do (src/core/session.c:211-262, src/sched/greedy.c:48-73). */
+EOSLLM_CUDA_API int eosi_cuda_text_generate(eosi_cuda_text_t *t, const uint32_t *prompt, uint32_t n_prompt,
+                                            uint32_t n_gen, uint32_t *out_tokens);
+/* Position back to 0 (the KV cache is overwritten as steps proceed). */
+EOSLLM_CUDA_API int eosi_cuda_text_reset(eosi_cuda_text_t *t);
+EOSLLM_CUDA_API uint32_t eosi_cuda_text_pos(const eosi_cuda_text_t *t);
+/* The decoder's cudaStream_t (as void*), for timing with events. */
+EOSLLM_CUDA_API void *eosi_cuda_text_stream(eosi_cuda_text_t *t);
+EOSLLM_CUDA_API void eosi_cuda_text_close(eosi_cuda_text_t *t);
+
 /* ---- diagnostics --------------------------------------------------------- */
 
 /* Device-side error bits raised by bounded waits since the last call on the

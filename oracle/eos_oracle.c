@@ -643,6 +643,29 @@ float orc_xs_rand_unit(uint32_t *st) {
 /* Decoder ops                                                         */
 /* ------------------------------------------------------------------ */
 
+static int g_orc_sum_order = 0;
+
+void orc_set_sum_order(int order) { g_orc_sum_order = order; }
+
+/* Sum of squares in the order of a 256-thread reduction: thread t sums
+ * elements t, t + 256, ...; then a xor butterfly (16, 8, 4, 2, 1) inside
+ * each 32-thread warp; then the 8 warp totals in warp order. */
+static float orc_sumsq_strided256(const float *x, uint32_t n) {
+    float t[256], u[256], s;
+    uint32_t i, j;
+    int off;
+    for (i = 0; i < 256; ++i) t[i] = 0.0f;
+    for (j = 0; j < n; j += 256)
+        for (i = 0; i < 256 && j + i < n; ++i) t[i] += x[j + i] * x[j + i];
+    for (off = 16; off > 0; off >>= 1) {
+        for (i = 0; i < 256; ++i) u[i] = t[i] + t[(i & ~31u) | ((i & 31u) ^ (uint32_t)off)];
+        for (i = 0; i < 256; ++i) t[i] = u[i];
+    }
+    s = t[0];
+    for (i = 1; i < 8; ++i) s += t[32 * i];
+    return s;
+}
+
 int orc_rmsnorm(const float *x, const float *w, float eps, float *y,
                 uint32_t rows, uint32_t cols) {
     /* src/kernels/scalar/rmsnorm.c:14-37 */
@@ -652,7 +675,10 @@ int orc_rmsnorm(const float *x, const float *w, float eps, float *y,
         const float *xr = x + (size_t)i * cols;
         float *yr = y + (size_t)i * cols;
         float ms = 0.0f, s;
-        for (j = 0; j < cols; ++j) ms += xr[j] * xr[j];
+        if (g_orc_sum_order == 1)
+            ms = orc_sumsq_strided256(xr, cols);
+        else
+            for (j = 0; j < cols; ++j) ms += xr[j] * xr[j];
         ms /= (float)cols;
         s = 1.0f / sqrtf(ms + eps);
         for (j = 0; j < cols; ++j) yr[j] = xr[j] * s * (w ? w[j] : 1.0f);

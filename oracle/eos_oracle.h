@@ -113,6 +113,13 @@ uint32_t orc_xorshift32(uint32_t *state);
 float    orc_xs_rand_unit(uint32_t *state);
 
 /* --- decoder ops (src/kernels/scalar/{rmsnorm,rope,silu}.c) -------------- */
+/* Summation order of rmsnorm's mean square: 0 (default) = the reference's
+ * sequential loop; 1 = a 256-wide strided reduction (per-thread partials,
+ * warp butterfly, warps in order).  Order 1 exists only to MEASURE how much
+ * the reference algorithm itself moves under a rounding-level change of one
+ * sum: decoder tests bound the GPU's deviation by that envelope.  Parity
+ * results always use order 0. */
+void orc_set_sum_order(int order);
 int orc_rmsnorm(const float *x, const float *w, float eps, float *y,
                 uint32_t rows, uint32_t cols);
 int orc_rope(float *x, uint32_t n_heads, uint32_t head_dim, uint32_t pos, float base);

@@ -61,8 +61,13 @@ class _OrcLlama(C.Structure):
 
 
 class OracleDecoder:
-    def __init__(self, o: Oracle, model: dict):
-        self.o, self.model = o, model
+    """orc_text_step on `model`.  sum_order 1 runs rmsnorm's mean square in
+    a 256-wide strided order (orc_set_sum_order) to measure the reference
+    algorithm's own sensitivity; 0 is the reference's order."""
+
+    def __init__(self, o: Oracle, model: dict, sum_order: int = 0):
+        self.o, self.model, self.sum_order = o, model, sum_order
+        o.lib.orc_set_sum_order.argtypes = [C.c_int]
         c = model["config"]
         L = o.lib
         L.orc_text_open.argtypes = [C.POINTER(_OrcLlama), C.POINTER(C.c_void_p)]
@@ -87,7 +92,11 @@ class OracleDecoder:
 
     def step(self, token: int) -> np.ndarray:
         out = np.empty(self.model["config"]["n_vocab"], np.float32)
-        rc = self.o.lib.orc_text_step(self.st, token, out.ctypes.data)
+        self.o.lib.orc_set_sum_order(self.sum_order)
+        try:
+            rc = self.o.lib.orc_text_step(self.st, token, out.ctypes.data)
+        finally:
+            self.o.lib.orc_set_sum_order(0)
         assert rc == 0, rc
         return out
 

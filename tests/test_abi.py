@@ -99,3 +99,38 @@ def test_missing_library_fails_loudly(tmp_path, cuda_lib):
             B.load(str(tmp_path / "nope.so"))
     finally:
         B._lib = saved
+
+
+def test_llama_desc_layout_matches_header(tmp_path):
+    """eosllm_b200.text.LlamaDesc (ctypes) has the C layout of
+    eosi_cuda_llama_t: same size and field offsets as gcc computes."""
+    from eosllm_b200.text import LlamaDesc
+    names = [f[0] for f in LlamaDesc._fields_]
+    src = tmp_path / "layout.c"
+    body = "".join(f'    printf("%s %zu\\n", "{n}", offsetof(eosi_cuda_llama_t, {n}));\n'
+                   for n in names if n != "output_w") + \
+        '    printf("output_w %zu\\n", offsetof(eosi_cuda_llama_t, output_w));\n'
+    src.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "eosllm_cuda.h"\nint main(void) {\n'
+                   '    printf("sizeof %zu\\n", sizeof(eosi_cuda_llama_t));\n' + body + "    return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src), "-o",
+                    str(exe)], check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                       check=True).stdout.splitlines())
+    assert int(got["sizeof"]) == C.sizeof(LlamaDesc)
+    for n in names:
+        assert int(got[n]) == getattr(LlamaDesc, n).offset, n
+
+
+def test_text_decoder_rejects_bad_descriptions(cuda_lib):
+    """NULL or empty descriptions fail with EOS_E_INVALID_ARG before any
+    device work (works without a GPU)."""
+    from eosllm_b200.text import LlamaDesc
+    h = C.c_void_p()
+    assert cuda_lib.eosi_cuda_text_open(None, 0, 0, 1, C.byref(h)) == B.EOS_E_INVALID_ARG
+    d = LlamaDesc()
+    assert cuda_lib.eosi_cuda_text_open(C.byref(d), 0, 0, 1, C.byref(h)) == B.EOS_E_INVALID_ARG
+    assert not h.value
+    assert cuda_lib.eosi_cuda_text_step(None, 0, None) == B.EOS_E_INVALID_ARG
+    assert cuda_lib.eosi_cuda_text_generate(None, None, 0, 0, None) == B.EOS_E_INVALID_ARG
+    cuda_lib.eosi_cuda_text_close(None)
