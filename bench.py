@@ -70,6 +70,8 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--workload", choices=["all", "sweep", "decode"], default="all",
+                   help="sweep: the GEMV sweep line only; decode: the 7B decode line only")
     p.add_argument("--no-decode", action="store_true", help="skip the 7B-shape decode measurement")
     p.add_argument("--decode-prompt", type=int, default=512)
     p.add_argument("--decode-gen", type=int, default=256)
@@ -309,6 +311,17 @@ def run_ours(args):
     if B.load().eosi_cuda_probe() != 0:
         raise SystemExit(f"CUDA backend unavailable: {B.last_error()}")
     B.set_devices([local])
+    if args.workload == "decode":
+        d = run_decode(args, dev, world, rank)
+        if rank == 0:
+            line = dict(d, steps=args.decode_gen, warmup=16, ms_per_step=d["ms_per_token"], higher_is_better=True,
+                        scaling="strong",
+                        vs_baseline=None, dtype="int8", data="synthetic",
+                        gpu_launches=args.decode_gen * d.pop("launches_per_token"))
+            line["config"] = dict(line["config"], workload="llama_7b_shape_q4k_decode")
+            print(json.dumps(line), flush=True)
+        dist_done(world)
+        return
     R = max(1, args.copies)
 
     # ---- inputs resident in HBM: rank r owns rows [r*n, (r+1)*n) of N-times-taller matrices
@@ -440,7 +453,9 @@ def run_ours(args):
         cpu = cpu_baseline(args.cpu_seconds)
 
     decode = None
-    if not args.no_decode and world > 1:
+    if args.workload == "sweep":
+        pass
+    elif not args.no_decode and world > 1:
         decode = {"unavailable": "the tensor-parallel decoder needs the peer exchange, not built yet"}
     elif not args.no_decode:
         del g_timed, g_warm, g_launch
@@ -543,6 +558,7 @@ def run_decode(args, dev, world, rank) -> dict:
                      "frac": round((wbytes + kv_avg) / world / (ms_tok * 1e-3) / 1e9 / peak, 4),
                      "tok_s_at_peak": round(world * peak * 1e9 / (wbytes + kv_avg), 1),
                      "tok_s_weight_only_at_peak": round(world * peak * 1e9 / wbytes, 1)},
+        "launches_per_token": 8 * cfg["n_layer"] + 3,
         "first_tokens": [int(x) for x in toks[:8]],
         "clocks": clocks.summary(),
     }

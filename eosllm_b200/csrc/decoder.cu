@@ -78,35 +78,79 @@ struct NormPackParams {
   float* act_f32;   // Q8_0 consumers: the normalised vector
 };
 
-// Residual element i: x_in[i] + (((p_0 + p_1) + ...)); the reference adds
-// one full-length result (x[i] += t[i]), which is the nparts == 1 case.
-__device__ __forceinline__ float residual_at(const NormPackParams& p, const uint16_t* emb, uint32_t i) {
-  if (emb != nullptr) return f16_bits_to_f32(emb[i]);  // exact widening (src/util/f16.h)
-  const float v = p.x_in[i];
-  if (p.nparts == 0) return v;
-  float s = p.parts[0][i];
-  for (uint32_t j = 1; j < p.nparts; ++j) s = __fadd_rn(s, p.parts[j][i]);
-  return __fadd_rn(v, s);
+constexpr uint32_t kNormMaxChunks = 16;  // float4 chunks per thread: n <= 16384
+
+__device__ __forceinline__ float4 ld4(const float* p, uint32_t c) { return reinterpret_cast<const float4*>(p)[c]; }
+__device__ __forceinline__ float4 add4(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
 }
 
-// Grid: ceil(n / 256) CTAs of 256 threads.  Every CTA reduces the mean
-// square of the whole vector (the same fixed order in every CTA, so all agree
-// bit for bit) and then normalises and packs its own 256 elements.
+// Grid: n / 256 CTAs of 256 threads; thread t holds the float4 chunks
+// t, t + 256, ... of the vector, all loaded in one batch.  Every CTA reduces
+// the mean square of the whole vector (the same fixed order in every CTA, so
+// all agree bit for bit) and then normalises and packs its own 256 elements
+// (CTA b: chunks [64 b, 64 b + 64), held by threads 64 (b % 4) + q at
+// iteration b / 4).  Residual element i is x_in[i] + (((p_0 + p_1) + ...)):
+// the reference adds one full-length result (x[i] += t[i], text.c:406),
+// which is the nparts == 1 case.
 __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) {
   __shared__ float red[8];
+  __shared__ __align__(16) float ys[256];
   pdl_trigger();
   pdl_wait();
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-  const uint16_t* emb = nullptr;
+  const uint32_t nch = p.n >> 2, b = blockIdx.x;
+  const uint32_t jown = b >> 2;
+  const bool owner = (tid >> 6) == (b & 3u);
+  float4 v[kNormMaxChunks];
   if (p.x_in == nullptr) {
     const uint32_t pos = p.state->pos;
     const uint32_t tok = pos < p.state->n_prompt ? p.prompt[pos] : p.state->next_token;
-    emb = p.tok_embd + (size_t)tok * p.n;
+    const uint2* emb = reinterpret_cast<const uint2*>(p.tok_embd + (size_t)tok * p.n);
+#pragma unroll
+    for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
+      const uint32_t c = tid + 256u * j;
+      if (c < nch) {
+        const uint2 h = emb[c];  // F16 -> F32 is exact (src/util/f16.h)
+        v[j] = make_float4(f16_bits_to_f32(h.x), f16_bits_to_f32(h.x >> 16), f16_bits_to_f32(h.y),
+                           f16_bits_to_f32(h.y >> 16));
+      }
+    }
+  } else {
+#pragma unroll
+    for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
+      const uint32_t c = tid + 256u * j;
+      if (c < nch) v[j] = ld4(p.x_in, c);
+    }
+    if (p.nparts > 0) {
+      float4 t[kNormMaxChunks];
+#pragma unroll
+      for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
+        const uint32_t c = tid + 256u * j;
+        if (c < nch) t[j] = ld4(p.parts[0], c);
+      }
+      for (uint32_t q = 1; q < p.nparts; ++q) {
+#pragma unroll
+        for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
+          const uint32_t c = tid + 256u * j;
+          if (c < nch) t[j] = add4(t[j], ld4(p.parts[q], c));
+        }
+      }
+#pragma unroll
+      for (uint32_t j = 0; j < kNormMaxChunks; ++j)
+        if (tid + 256u * j < nch) v[j] = add4(v[j], t[j]);
+    }
   }
+  const float4 w4 = owner ? ld4(p.w, (b << 6) + (tid & 63u)) : make_float4(0.f, 0.f, 0.f, 0.f);
   float ss = 0.0f;
-  for (uint32_t i = tid; i < p.n; i += 256u) {
-    const float v = residual_at(p, emb, i);
-    ss = __fadd_rn(ss, __fmul_rn(v, v));
+#pragma unroll
+  for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
+    if (tid + 256u * j < nch) {
+      ss = __fadd_rn(ss, __fmul_rn(v[j].x, v[j].x));
+      ss = __fadd_rn(ss, __fmul_rn(v[j].y, v[j].y));
+      ss = __fadd_rn(ss, __fmul_rn(v[j].z, v[j].z));
+      ss = __fadd_rn(ss, __fmul_rn(v[j].w, v[j].w));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
@@ -117,16 +161,26 @@ __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) 
   for (int w = 1; w < 8; ++w) tot = __fadd_rn(tot, red[w]);
   // ms /= cols; s = 1 / sqrtf(ms + eps); y = x * s * w  (rmsnorm.c:24-33)
   const float ms = __fdiv_rn(tot, (float)p.n);
-  const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
-  const uint32_t i = blockIdx.x * 256u + tid;
-  if (i >= p.n) return;  // warp-uniform: n % 32 == 0
-  const float v = residual_at(p, emb, i);
-  if (p.x_out != nullptr) p.x_out[i] = v;
-  const float y = __fmul_rn(__fmul_rn(v, s), p.w[i]);
+  const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+  if (owner) {
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (uint32_t j = 0; j < kNormMaxChunks; ++j)
+      if (j == jown) x = v[j];
+    const uint32_t c = (b << 6) + (tid & 63u);
+    if (p.x_out != nullptr) reinterpret_cast<float4*>(p.x_out)[c] = x;
+    const uint32_t o = (tid & 63u) << 2;
+    ys[o] = __fmul_rn(__fmul_rn(x.x, sc), w4.x);
+    ys[o + 1] = __fmul_rn(__fmul_rn(x.y, sc), w4.y);
+    ys[o + 2] = __fmul_rn(__fmul_rn(x.z, sc), w4.z);
+    ys[o + 3] = __fmul_rn(__fmul_rn(x.w, sc), w4.w);
+  }
+  __syncthreads();
+  const float y = ys[tid];
   if (p.act != nullptr)
-    pack_group_to_record(y, i >> 5, lane, p.act);
+    pack_group_to_record(y, (b << 3) + warp, lane, p.act);
   else
-    p.act_f32[i] = y;
+    p.act_f32[(b << 8) + tid] = y;
 }
 
 // ---------------------------------------------------------------------------
@@ -158,19 +212,30 @@ __device__ __forceinline__ void rope_pair(float& x0, float& x1, uint32_t i, uint
   x1 = __fadd_rn(__fmul_rn(p0, sn), __fmul_rn(p1, cs));
 }
 
+// Dynamic shared memory of attn_kernel<E>: the K and V rows of one chunk.
+__host__ __device__ constexpr uint32_t attn_smem_bytes(uint32_t hd) { return 2u * kAttnChunk * hd * 4u; }
+
 // Grid (hl, max_chunks), 128 threads.  E = dims per lane (head_dim = 32 E).
+// CTA (h, c) covers positions [64 c, 64 c + 64) up to `pos`: it stages the
+// cached K and V rows of the chunk into shared memory with one batch of
+// 16-byte cp.async copies -- issued before the PDL wait, since rows < pos
+// were written by earlier steps -- then computes the scores (one warp per
+// position, lane = E dims), the chunk's softmax pieces (max, sum, sum of
+// weighted V) and parks them; the last CTA of the head merges the chunks.
 template <int E>
 __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
   constexpr uint32_t HD = 32u * E;
+  extern __shared__ __align__(16) float kv_s[];  // [kAttnChunk][HD] K, then V
   __shared__ float s_score[kAttnChunk];
   __shared__ __align__(16) float s_o[4][HD];
   __shared__ float s_l[4];
   __shared__ float s_out[HD];
   __shared__ uint32_t s_last;
   pdl_trigger();
-  pdl_wait();
   const uint32_t hloc = blockIdx.x, c = blockIdx.y;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  // pos was written by the previous step's argmax_kernel, which completed
+  // before this step's first kernel started
   const uint32_t pos = p.state->pos;
   const uint32_t p0 = c * kAttnChunk;
   if (p0 > pos) return;  // chunk beyond the context: no work, not counted
@@ -181,6 +246,26 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
   const uint32_t kvi = gkv - p.kv0;
   const uint32_t row = p.kvl * HD;  // floats per cache position
   const uint32_t d0 = lane * E;
+  float* ks = kv_s;
+  float* vs = kv_s + kAttnChunk * HD;
+  {
+    const uint32_t ncached = (p1 < pos ? p1 : pos) - p0;  // rows < pos in this chunk
+    const uint32_t per_row = HD / 4u;
+    const uint64_t pol = l2_policy_evict_first();
+    const float* kg = p.kc + (size_t)p0 * row + kvi * HD;
+    const float* vg = p.vc + (size_t)p0 * row + kvi * HD;
+    for (uint32_t t = tid; t < ncached * per_row; t += 128u) {
+      const uint32_t r = t / per_row, q4 = (t - r * per_row) * 4u;
+      cp_async16(ks + r * HD + q4, kg + (size_t)r * row + q4, pol);
+    }
+    cp_async_commit();
+    for (uint32_t t = tid; t < ncached * per_row; t += 128u) {
+      const uint32_t r = t / per_row, q4 = (t - r * per_row) * 4u;
+      cp_async16(vs + r * HD + q4, vg + (size_t)r * row + q4, pol);
+    }
+    cp_async_commit();
+  }
+  pdl_wait();  // q, k, v of this step come from the QKV GEMV
 
   float q[E], kn[E], vn[E];
   const float* qp = p.qkv + hloc * HD + d0;
@@ -207,15 +292,15 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
     }
   }
 
-  // scores: one warp per position
+  cp_async_wait<1>();  // this thread's K copies
+  __syncthreads();     // everyone's
   for (uint32_t j = warp; j < np; j += 4u) {
-    const uint32_t t = p0 + j;
+    const float* kr = ks + j * HD + d0;
     float acc = 0.0f;
-    if (t == pos) {
+    if (p0 + j == pos) {
 #pragma unroll
       for (int e = 0; e < E; ++e) acc = __fmaf_rn(q[e], kn[e], acc);
     } else {
-      const float* kr = p.kc + (size_t)t * row + kvi * HD + d0;
 #pragma unroll
       for (int e = 0; e < E; ++e) acc = __fmaf_rn(q[e], kr[e], acc);
     }
@@ -223,6 +308,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (lane == 0) s_score[j] = __fmul_rn(acc, p.scale);
   }
+  cp_async_wait<0>();
   __syncthreads();
   float mx = -INFINITY;
   for (uint32_t j = 0; j < np; ++j) mx = fmaxf(mx, s_score[j]);
@@ -232,14 +318,13 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
   for (int e = 0; e < E; ++e) o[e] = 0.0f;
   float l = 0.0f;
   for (uint32_t j = warp; j < np; j += 4u) {
-    const uint32_t t = p0 + j;
     const float a = expf(s_score[j] - mx);
+    const float* vr = vs + j * HD + d0;
     l += a;
-    if (t == pos) {
+    if (p0 + j == pos) {
 #pragma unroll
       for (int e = 0; e < E; ++e) o[e] = __fmaf_rn(a, vn[e], o[e]);
     } else {
-      const float* vr = p.vc + (size_t)t * row + kvi * HD + d0;
 #pragma unroll
       for (int e = 0; e < E; ++e) o[e] = __fmaf_rn(a, vr[e], o[e]);
     }
@@ -419,6 +504,22 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStre
   return cudaLaunchKernelEx(&lc, kernel, std::forward<Args>(args)...);
 }
 
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_smem(void (*kernel)(KArgs...), dim3 grid, dim3 block, uint32_t smem, cudaStream_t st,
+                            Args&&... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, kernel, std::forward<Args>(args)...);
+}
+
 size_t wbytes(int dt, uint64_t n, uint64_t k) {
   return dt == EOS_DT_Q4_K ? (size_t)(n * (k / Q4K_ELEMS) * Q4K_BYTES) : (size_t)(n * (k / Q80_ELEMS) * Q80_BYTES);
 }
@@ -518,8 +619,9 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
     set_error_message("cuda text: linears must be Q4_K or Q8_0");
     return EOS_E_UNSUPPORTED;
   }
-  if (m.n_embd % 256 || m.n_ff % blk_elems(wdt) || m.n_embd % blk_elems(odt)) {
-    set_error_message("cuda text: n_embd must be a multiple of 256 and n_ff of the block size");
+  if (m.n_embd % 256 || m.n_embd > 256u * 4u * kNormMaxChunks || m.n_ff % blk_elems(wdt) ||
+      m.n_embd % blk_elems(odt)) {
+    set_error_message("cuda text: n_embd must be a multiple of 256 (at most 16384), n_ff of the block size");
     return EOS_E_UNSUPPORTED;
   }
   if (ws < 1 || ws > (int)kMaxParts || rk < 0 || rk >= ws || m.n_head % ws || m.n_kv_head % ws) {
@@ -678,9 +780,10 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
       a.base = m.rope_base;
       a.scale = 1.0f / sqrtf((float)hd);  // text.c:365
       const dim3 grid(hl, max_chunks);
-      if (hd == 64) e = launch_pdl(attn_kernel<2>, grid, dim3(128), s, a);
-      else if (hd == 128) e = launch_pdl(attn_kernel<4>, grid, dim3(128), s, a);
-      else e = launch_pdl(attn_kernel<8>, grid, dim3(128), s, a);
+      const uint32_t sm = attn_smem_bytes(hd);
+      if (hd == 64) e = launch_pdl_smem(attn_kernel<2>, grid, dim3(128), sm, s, a);
+      else if (hd == 128) e = launch_pdl_smem(attn_kernel<4>, grid, dim3(128), sm, s, a);
+      else e = launch_pdl_smem(attn_kernel<8>, grid, dim3(128), sm, s, a);
     }
     if (e == cudaSuccess) e = gemv(wdt, d.wo, act_o, actf_o, part_o, E, hl * hd);
     // x0 = x1 + O partial; act_e = pack(rmsnorm(x0))
@@ -705,7 +808,11 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
 
 int TextDecoder::capture() {
   cudaGraph_t g = nullptr;
-  cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);
+  const int sm = (int)attn_smem_bytes(hd);
+  cudaError_t e = hd == 64    ? cudaFuncSetAttribute(attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm)
+                  : hd == 128 ? cudaFuncSetAttribute(attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm)
+                              : cudaFuncSetAttribute(attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  if (e == cudaSuccess) e = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);
   if (e == cudaSuccess) {
     const cudaError_t r = record_step(st);
     e = cudaStreamEndCapture(st, &g);
