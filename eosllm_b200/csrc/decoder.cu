@@ -35,26 +35,18 @@
 // sinf / cosf are CUDA's, so logits agree with the CPU engine to a
 // tolerance, not bit for bit.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <utility>
 #include <vector>
 
-#include "eosllm_cuda.h"
+#include "decoder_internal.h"
 #include "eos_common.cuh"
 #include "eos_kernels.h"
+#include "eosllm_cuda.h"
 
 namespace eos {
-
-// Words the step kernels share in device memory.
-struct DecState {
-  uint32_t pos;         // position of the next step == tokens consumed
-  uint32_t n_prompt;    // steps at pos < n_prompt read their token from prompt[pos]
-  uint32_t next_token;  // greedy pick of the previous step
-  uint32_t arg_count;   // argmax CTA arrivals (reset by the last CTA)
-  uint32_t err;         // EOS_DEVERR_* bits
-  uint32_t pad[3];
-};
 
 constexpr uint32_t kMaxParts = 8;
 constexpr uint32_t kAttnChunk = 64;     // positions per attention CTA
@@ -527,15 +519,6 @@ uint32_t blk_elems(int dt) { return dt == EOS_DT_Q4_K ? Q4K_ELEMS : Q80_ELEMS; }
 
 }  // namespace
 
-struct DecLayer {
-  uint8_t* wqkv;
-  uint8_t* wo;
-  uint8_t* wgu;
-  uint8_t* wd;
-  float* attn_norm;
-  float* ffn_norm;
-};
-
 struct TextDecoder {
   eosi_cuda_llama_t m{};
   int device = 0, rank = 0, world = 1;
@@ -704,7 +687,8 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
   const size_t kv_bytes = 4ull * m.n_layer * m.max_ctx * kvl * hd;
   chk(alloc(&kc, kv_bytes));
   chk(alloc(&vc, kv_bytes));
-  chk(alloc(&attn_part, 4ull * hl * max_chunks * (hd + 4)));
+  const uint32_t chunks32 = (m.max_ctx + 31u) / 32u;
+  chk(alloc(&attn_part, 4ull * hl * (chunks32 > max_chunks ? chunks32 : max_chunks) * (hd + 4)));
   chk(alloc(&attn_count, 4ull * hl));
   arg_blocks = (vl + 2047u) / 2048u;
   if (arg_blocks > kArgmaxBlocks) arg_blocks = kArgmaxBlocks;

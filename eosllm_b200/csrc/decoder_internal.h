@@ -1,0 +1,30 @@
+// decoder_internal.h -- structures of the device-resident decoder
+// (decoder.cu).  Internal: the public boundary is include/eosllm_cuda.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace eos {
+
+// Words the step kernels share in device memory.
+struct DecState {
+  uint32_t pos;         // position of the next step == tokens consumed
+  uint32_t n_prompt;    // steps at pos < n_prompt read their token from prompt[pos]
+  uint32_t next_token;  // greedy pick of the previous step
+  uint32_t arg_count;   // argmax CTA arrivals (reset by the last CTA)
+  uint32_t err;         // EOS_DEVERR_* bits
+  uint32_t pad[3];
+};
+
+// One layer's resident weights (this rank's slices).
+struct DecLayer {
+  uint8_t* wqkv;  // [q rows; k rows; v rows] x n_embd
+  uint8_t* wo;    // n_embd rows x (this rank's head columns)
+  uint8_t* wgu;   // [gate rows; up rows] of this rank's FFN slice x n_embd
+  uint8_t* wd;    // n_embd rows x (this rank's FFN columns)
+  float* attn_norm;
+  float* ffn_norm;
+};
+
+}  // namespace eos

@@ -38,6 +38,7 @@
 //   bytes [160, 272) and [432, 480) are padding.
 #include "eos_common.cuh"
 #include "eos_kernels.h"
+#include "q4k_dot.cuh"
 
 namespace eos {
 
@@ -70,86 +71,6 @@ __global__ void __launch_bounds__(256) act_pack_kernel(const float* __restrict__
       sm[gid] = sum;
     }
   }
-}
-
-// ---------------------------------------------------------------------------
-// Half a super-block, one lane
-// ---------------------------------------------------------------------------
-// dp4a with the first operand's bytes unsigned (the high nibbles kept in
-// place, i.e. 16 * q_hi <= 240) and the second's signed (activations).
-__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
-  int d;
-  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
-// Exact integer dots of one qs pair (32 bytes as two uint4) with the
-// activation lanes of its two sub-blocks: lo nibbles x sub 2p, hi nibbles x
-// sub 2p+1 (src/kernels/avx2/matmul_q4_k_int8.c:234-249).  The high-nibble
-// dot is taken on the nibble in place (x16, exact) and shifted back.
-__device__ __forceinline__ void pair_dots(uint4 q0, uint4 q1, int4 a0, int4 a1, int4 a2, int4 a3, int& dl, int& dh) {
-  constexpr uint32_t LO = 0x0F0F0F0Fu, HI = 0xF0F0F0F0u;
-  int l = __dp4a((int)(q0.x & LO), a0.x, 0);
-  int h = dp4a_us(q0.x & HI, a2.x, 0);
-  l = __dp4a((int)(q0.y & LO), a0.y, l);
-  h = dp4a_us(q0.y & HI, a2.y, h);
-  l = __dp4a((int)(q0.z & LO), a0.z, l);
-  h = dp4a_us(q0.z & HI, a2.z, h);
-  l = __dp4a((int)(q0.w & LO), a0.w, l);
-  h = dp4a_us(q0.w & HI, a2.w, h);
-  l = __dp4a((int)(q1.x & LO), a1.x, l);
-  h = dp4a_us(q1.x & HI, a3.x, h);
-  l = __dp4a((int)(q1.y & LO), a1.y, l);
-  h = dp4a_us(q1.y & HI, a3.y, h);
-  l = __dp4a((int)(q1.z & LO), a1.z, l);
-  h = dp4a_us(q1.z & HI, a3.z, h);
-  l = __dp4a((int)(q1.w & LO), a1.w, l);
-  h = dp4a_us(q1.w & HI, a3.w, h);
-  dl = l;
-  dh = h >> 4;  // exact: the sum is a multiple of 16
-}
-
-// t_s = ((d*sc_s)*as_s)*dot_s - ((dmin*m_s)*as_s)*sum_s, in the reference's
-// order (:254-261).
-__device__ __forceinline__ float sb_term(float d, float dmin, uint32_t sc, uint32_t m, float as, float sum, int dot) {
-  return __fsub_rn(__fmul_rn(__fmul_rn(__fmul_rn(d, (float)sc), as), (float)dot),
-                   __fmul_rn(__fmul_rn(__fmul_rn(dmin, (float)m), as), sum));
-}
-
-// The four terms of sub-blocks 4h..4h+3.  blk: the 144-byte GGUF super-block,
-// half: its 160-byte activation half-record (both 16-byte aligned, shared or
-// global memory).  The 6-bit scales/mins come out byte-parallel: get_scale_min
-// (:58-67) for all j at once.
-__device__ __forceinline__ void q4k_half_terms(const uint8_t* blk, const uint8_t* half, uint32_t h, float (&t)[4]) {
-  const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-  const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
-  // sc[4h .. 4h+3] and m[4h .. 4h+3] as bytes of one word each
-  const uint32_t scw = h == 0 ? (hdr.y & 0x3F3F3F3Fu) : ((hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u));
-  const uint32_t mw = h == 0 ? (hdr.z & 0x3F3F3F3Fu) : (((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u));
-  const uint8_t* qs = blk + 16 + 64 * h;
-#pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    const uint4 q0 = *reinterpret_cast<const uint4*>(qs + 32 * p);
-    const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 32 * p + 16);
-    const int4 a0 = *reinterpret_cast<const int4*>(half + 64 * p);
-    const int4 a1 = *reinterpret_cast<const int4*>(half + 64 * p + 16);
-    const int4 a2 = *reinterpret_cast<const int4*>(half + 64 * p + 32);
-    const int4 a3 = *reinterpret_cast<const int4*>(half + 64 * p + 48);
-    const float4 st = *reinterpret_cast<const float4*>(half + 128 + 16 * p);
-    int dl, dh;
-    pair_dots(q0, q1, a0, a1, a2, a3, dl, dh);
-    t[2 * p] = sb_term(d, dmin, (scw >> (16 * p)) & 0xFFu, (mw >> (16 * p)) & 0xFFu, st.x, st.y, dl);
-    t[2 * p + 1] = sb_term(d, dmin, (scw >> (16 * p + 8)) & 0xFFu, (mw >> (16 * p + 8)) & 0xFFu, st.z, st.w, dh);
-  }
-}
-
-// Super-block partial from a lane pair (lane h = lane & 1 holds half h): the
-// result is valid on the odd lane.  All 32 lanes must call it.
-__device__ __forceinline__ float pair_partial(const float (&t)[4], uint32_t lane) {
-  float s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(0.0f, t[0]), t[1]), t[2]), t[3]);
-  const float first = __shfl_up_sync(0xffffffffu, s, 1);
-  if (lane & 1u) s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(first, t[0]), t[1]), t[2]), t[3]);
-  return s;
 }
 
 // ---------------------------------------------------------------------------
@@ -289,6 +210,97 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParam
   cp_async_wait<0>();  // never exit with copies still landing in shared memory
 }
 
+// Column-major variant: a warp stage is R rows; a lane PAIR owns one
+// super-block column b (16 columns per pass) and computes all R rows of it,
+// so each activation half-record is read from shared memory once per stage
+// instead of once per row.  Same terms, partials and ordered row sums as
+// q4k_gemv_kernel, so outputs are bit-identical.
+template <int NW, int D, int R>
+__global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_cols_kernel(const Q4kGemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t act_region = (p.act_bytes + 127u) & ~127u;
+  uint8_t* act_s = smem;
+  const uint32_t nb = p.nb, pitch = p.pitch, row_bytes = p.row_bytes;
+  const uint32_t buf_bytes = R * pitch;
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const uint32_t pstride = (R * nb + 3u) & ~3u;
+  const uint32_t part_region = (NW * pstride * 4u + 127u) & ~127u;
+  float* part_w = reinterpret_cast<float*>(smem + act_region) + warp * pstride;
+  uint8_t* wbuf = smem + act_region + part_region + warp * D * buf_bytes;
+
+  const uint32_t r0 = (uint32_t)(((uint64_t)p.n * blockIdx.x) / gridDim.x);
+  const uint32_t r1 = (uint32_t)(((uint64_t)p.n * (blockIdx.x + 1)) / gridDim.x);
+  const uint32_t nrows = r1 - r0;
+  const uint32_t nst = (nrows + R - 1) / R;
+  const uint32_t cpr = row_bytes >> 4;
+  const uint64_t pol_w = l2_policy_evict_first();
+
+  auto issue = [&](uint32_t s, uint32_t slot) {
+    if (s < nst) {
+      const uint32_t rows = (nrows - s * R) < R ? (nrows - s * R) : R;
+      const uint8_t* src = p.w + (size_t)(r0 + s * R) * row_bytes;
+      uint8_t* dst = wbuf + slot * buf_bytes;
+      for (uint32_t r = 0; r < rows; ++r)
+        for (uint32_t t = lane; t < cpr; t += 32)
+          cp_async16(dst + r * pitch + (t << 4), src + (size_t)r * row_bytes + (t << 4), pol_w);
+    }
+    cp_async_commit();
+  };
+
+#pragma unroll
+  for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(warp + d * NW, d);
+
+  pdl_wait();
+  if (p.a != nullptr) {
+    pack_into_smem<NW>(p.a, p.k, act_s, warp, lane);
+  } else {
+    const uint4* src = reinterpret_cast<const uint4*>(p.act);
+    uint4* dst = reinterpret_cast<uint4*>(act_s);
+    for (uint32_t t = threadIdx.x; t < (p.act_bytes >> 4); t += NW * 32) dst[t] = src[t];
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  const uint32_t h = lane & 1u;
+  uint32_t i = 0;
+  for (uint32_t s = warp; s < nst; s += NW, ++i) {
+    const uint32_t slot = i % D;
+    cp_async_wait<D - 1>();
+    __syncwarp();
+    const uint32_t rows = (nrows - s * R) < R ? (nrows - s * R) : R;
+    const uint8_t* stage = wbuf + slot * buf_bytes;
+    for (uint32_t b0 = 0; b0 < nb; b0 += 16u) {
+      const uint32_t b = b0 + (lane >> 1);
+      const uint32_t bc = b < nb ? b : nb - 1u;
+      float t[R][4];
+      q4k_half_terms_rows<R>(stage + bc * Q4K_BYTES, pitch, act_s + bc * kActRec + h * kActHalf, h, t, rows);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const float part = pair_partial(t[r], lane);
+        if (h && b < nb && (uint32_t)r < rows) part_w[r * nb + b] = part;
+      }
+    }
+    __syncwarp();
+    issue(s + D * NW, slot);
+    if (lane < rows) {
+      const float* pr = part_w + lane * nb;
+      float acc = 0.0f;  // c = 0; c += partial_b in order (:194, :264)
+      uint32_t b = 0;
+      for (; b + 8u <= nb; b += 8u) {
+        float v8[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v8[j] = pr[b + j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v8[j]);
+      }
+      for (; b < nb; ++b) acc = __fadd_rn(acc, pr[b]);
+      p.c[r0 + s * R + lane] = acc;
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+}
+
 // Fallback without staging (rows too long for shared memory): one warp per
 // weight row from global memory, packed activations in global memory.
 __global__ void __launch_bounds__(256) q4k_gemv_simple_kernel(const uint8_t* __restrict__ w,
@@ -339,14 +351,20 @@ namespace {
 struct GemvConfig {
   void (*fn)(const Q4kGemvParams);
   int nw, d;
+  int cols;      // 0: q4k_gemv_kernel (rows per stage chosen at launch); R: q4k_gemv_cols_kernel<., ., R>
   int smem_set;  // largest dynamic shared memory already allowed
 };
-GemvConfig g_cfgs[] = {{q4k_gemv_kernel<16, 4>, 16, 4, 0}, {q4k_gemv_kernel<16, 3>, 16, 3, 0},
-                       {q4k_gemv_kernel<16, 2>, 16, 2, 0}, {q4k_gemv_kernel<20, 3>, 20, 3, 0},
-                       {q4k_gemv_kernel<8, 4>, 8, 4, 0},   {q4k_gemv_kernel<12, 4>, 12, 4, 0},
-                       {q4k_gemv_kernel<24, 2>, 24, 2, 0}, {q4k_gemv_kernel<8, 6>, 8, 6, 0},
-                       {q4k_gemv_kernel<20, 2>, 20, 2, 0}, {q4k_gemv_kernel<12, 3>, 12, 3, 0},
-                       {q4k_gemv_kernel<16, 2>, 16, 2, 0}, {q4k_gemv_kernel<10, 4>, 10, 4, 0}};
+GemvConfig g_cfgs[] = {
+    {q4k_gemv_kernel<16, 4>, 16, 4, 0, 0},      {q4k_gemv_kernel<16, 3>, 16, 3, 0, 0},
+    {q4k_gemv_kernel<16, 2>, 16, 2, 0, 0},      {q4k_gemv_kernel<20, 3>, 20, 3, 0, 0},
+    {q4k_gemv_kernel<8, 4>, 8, 4, 0, 0},        {q4k_gemv_kernel<12, 4>, 12, 4, 0, 0},
+    {q4k_gemv_kernel<24, 2>, 24, 2, 0, 0},      {q4k_gemv_kernel<8, 6>, 8, 6, 0, 0},
+    {q4k_gemv_kernel<20, 2>, 20, 2, 0, 0},      {q4k_gemv_kernel<12, 3>, 12, 3, 0, 0},
+    {q4k_gemv_kernel<16, 2>, 16, 2, 0, 0},      {q4k_gemv_kernel<10, 4>, 10, 4, 0, 0},
+    {q4k_gemv_cols_kernel<12, 2, 4>, 12, 2, 4, 0}, {q4k_gemv_cols_kernel<16, 3, 2>, 16, 3, 2, 0},
+    {q4k_gemv_cols_kernel<8, 3, 4>, 8, 3, 4, 0},   {q4k_gemv_cols_kernel<16, 2, 2>, 16, 2, 2, 0},
+    {q4k_gemv_cols_kernel<8, 2, 2>, 8, 2, 2, 0},   {q4k_gemv_cols_kernel<12, 3, 2>, 12, 3, 2, 0},
+    {q4k_gemv_cols_kernel<16, 2, 1>, 16, 2, 1, 0}, {q4k_gemv_cols_kernel<8, 4, 2>, 8, 4, 2, 0}};
 constexpr int kNumCfgs = sizeof(g_cfgs) / sizeof(g_cfgs[0]);
 int g_q4k_variant = -1;  // kernel config override (-1: automatic)
 int g_q4k_rows = 0;      // rows-per-stage override (0: automatic)
@@ -354,11 +372,11 @@ int g_q4k_ctas = 0;      // CTAs-per-SM override (0: automatic)
 }  // namespace
 
 void set_q4k_gemv_variant(int v) {
-  // v < 0: automatic.  Else v = cfg + 16 * rows + 256 * ctas_per_sm, each
-  // field 0 = automatic.
-  g_q4k_variant = v < 0 ? -1 : (v % 16);
-  g_q4k_rows = v < 0 ? 0 : ((v / 16) % 16);
-  g_q4k_ctas = v < 0 ? 0 : (v / 256);
+  // v < 0: automatic.  Else v = cfg + 32 * rows + 512 * ctas_per_sm, each
+  // field 0 = automatic (rows applies to the row-major kernels only).
+  g_q4k_variant = v < 0 ? -1 : (v % 32);
+  g_q4k_rows = v < 0 ? 0 : ((v / 32) % 16);
+  g_q4k_ctas = v < 0 ? 0 : (v / 512);
 }
 
 cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
@@ -369,29 +387,43 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   const uint32_t row_bytes = nb * Q4K_BYTES;
   const uint32_t act_bytes = nb * kActRec;
   const uint32_t act_region = (act_bytes + 127u) & ~127u;
-  // rows per stage: at least 32 half-super-blocks (one per lane) per stage
-  uint32_t R = 1;
-  while (R < 16u && 2u * R * nb < 32u) R <<= 1;
-  if (g_q4k_rows == 1 || g_q4k_rows == 2 || g_q4k_rows == 4 || g_q4k_rows == 8) R = (uint32_t)g_q4k_rows;
-  const uint32_t target = R == 1 ? 0u : (R == 2 ? 32u : 16u);
-  const uint32_t pitch = row_bytes + ((target - (row_bytes & 127u)) & 127u);
-  auto part_bytes = [&](int nw) -> uint32_t { return ((uint32_t)nw * ((R * nb + 3u) & ~3u) * 4u + 127u) & ~127u; };
-  // deepest per-warp pipeline that fits: 16 warps x D buffers, else fewer
+  // row-major kernel: rows per stage give at least 32 half-super-blocks
+  // (one per lane) per stage; rows padded to a bank-spreading pitch
+  uint32_t R_rm = 1;
+  while (R_rm < 16u && 2u * R_rm * nb < 32u) R_rm <<= 1;
+  if (g_q4k_rows == 1 || g_q4k_rows == 2 || g_q4k_rows == 4 || g_q4k_rows == 8) R_rm = (uint32_t)g_q4k_rows;
+  const uint32_t target = R_rm == 1 ? 0u : (R_rm == 2 ? 32u : 16u);
+  const uint32_t pitch_rm = row_bytes + ((target - (row_bytes & 127u)) & 127u);
+  // column-major kernels: R rows per stage, unpadded (a load phase spans
+  // four columns of one row, always distinct banks)
+  auto geom = [&](const GemvConfig& g, uint32_t& R, uint32_t& pitch) {
+    R = g.cols ? (uint32_t)g.cols : R_rm;
+    pitch = g.cols ? row_bytes : pitch_rm;
+  };
+  auto smem_of = [&](const GemvConfig& g) -> uint32_t {
+    uint32_t R, pitch;
+    geom(g, R, pitch);
+    const uint32_t part = ((uint32_t)g.nw * ((R * nb + 3u) & ~3u) * 4u + 127u) & ~127u;
+    return act_region + part + (uint32_t)(g.nw * g.d) * R * pitch;
+  };
+  // first configuration that fits: column-major with activation reuse over
+  // several rows, then the row-major pipelines
   int pick = -1;
   if (g_q4k_variant >= 0 && g_q4k_variant < kNumCfgs) {
     pick = g_q4k_variant;
   } else {
-    const int order[] = {0, 1, 2, 4};
+    const int order[] = {16, 15, 12, 13, 18, 0, 1, 2, 4};
     for (int o : order)
-      if (act_region + part_bytes(g_cfgs[o].nw) + (uint32_t)(g_cfgs[o].nw * g_cfgs[o].d) * R * pitch <=
-          (uint32_t)max_smem) {
+      if (smem_of(g_cfgs[o]) <= (uint32_t)max_smem) {
         pick = o;
         break;
       }
     if (pick < 0) pick = 2;
   }
   GemvConfig& cfg = g_cfgs[pick];
-  const uint32_t smem = act_region + part_bytes(cfg.nw) + (uint32_t)(cfg.nw * cfg.d) * R * pitch;
+  uint32_t R, pitch;
+  geom(cfg, R, pitch);
+  const uint32_t smem = smem_of(cfg);
   if (smem > (uint32_t)max_smem) {  // rows too long to stage: unstaged kernel
     if (act == nullptr) {           // it reads packed activations from global memory
       *out_status = EOS_E_UNSUPPORTED;

@@ -169,7 +169,10 @@ def test_q4k_model_shapes_bitexact(gpu, oracle, n, k):
     assert same_bits(host(dc), ref[0])
 
 
-@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5, 6, 7, 16, 32, 64, 128, 5 + 16 * 4, 2 * 256 + 2 + 16 * 2])
+# variant = config + 32 * rows_per_stage + 512 * ctas_per_sm; configs 0-11 are
+# the row-major kernel, 12-19 the column-major one (rows reuse activations)
+@pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5, 6, 7, 32, 64, 128, 256, 5 + 32 * 4, 2 * 512 + 2 + 32 * 2,
+                                     12, 13, 14, 15, 16, 17, 18, 19, 2 * 512 + 15])
 def test_q4k_kernel_variants_bitexact(gpu, oracle, variant):
     try:
         gpu.set_kernel_variant(DT_Q4_K, variant)
