@@ -50,6 +50,8 @@ namespace eos {
 
 constexpr uint32_t kMaxParts = 8;
 constexpr uint32_t kAttnChunk = 64;     // positions per attention CTA
+constexpr uint32_t kMaxAttnChunks = 256;  // max_ctx <= 16384
+constexpr uint32_t kMergeBatch = 16;      // chunks whose o[d] the merge loads in one batch
 constexpr uint32_t kArgmaxBlocks = 64;  // CTAs of the argmax kernel (upper bound)
 
 // ---------------------------------------------------------------------------
@@ -222,6 +224,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
   __shared__ __align__(16) float s_o[4][HD];
   __shared__ float s_l[4];
   __shared__ float s_out[HD];
+  __shared__ float s_wc[kMaxAttnChunks];  // merge: chunk maxima, then weights
+  __shared__ float s_lc[kMaxAttnChunks];  // merge: chunk sums
   __shared__ uint32_t s_last;
   pdl_trigger();
   const uint32_t hloc = blockIdx.x, c = blockIdx.y;
@@ -302,8 +306,10 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
   }
   cp_async_wait<0>();
   __syncthreads();
-  float mx = -INFINITY;
-  for (uint32_t j = 0; j < np; ++j) mx = fmaxf(mx, s_score[j]);
+  // chunk max: every warp reduces the <= 64 scores itself (no serial loop)
+  float mx = fmaxf(lane < np ? s_score[lane] : -INFINITY, lane + 32u < np ? s_score[lane + 32u] : -INFINITY);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   // o = sum_t exp(s_t - mx) v_t over this chunk, one warp per position
   float o[E];
 #pragma unroll
@@ -339,23 +345,44 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
   if (!s_last) return;
   __threadfence();
 
-  // last CTA of the head: merge the chunks (log-sum-exp), normalise
+  // last CTA of the head: merge the chunks (log-sum-exp), normalise.  The
+  // chunk maxima and sums load in parallel, the weights are computed once,
+  // and each thread's o[d] of up to kMergeBatch chunks load in one batch.
   const float* base = p.part + (size_t)hloc * p.max_chunks * (HD + 4u);
-  float gmx = -INFINITY;
-  for (uint32_t cc = 0; cc < nvalid; ++cc) gmx = fmaxf(gmx, __ldcg(base + cc * (HD + 4u)));
-  float L = 0.0f;
-  for (uint32_t cc = 0; cc < nvalid; ++cc) {
-    const float* pc = base + cc * (HD + 4u);
-    L += __ldcg(pc + 1) * expf(__ldcg(pc) - gmx);
+  for (uint32_t cc = tid; cc < nvalid; cc += 128u) {
+    s_wc[cc] = __ldcg(base + cc * (HD + 4u));
+    s_lc[cc] = __ldcg(base + cc * (HD + 4u) + 1);
   }
+  constexpr int NDT = (HD + 127) / 128;  // dims per thread
+  float od[NDT][kMergeBatch];
+#pragma unroll
+  for (int e = 0; e < NDT; ++e) {
+    const uint32_t d = tid + 128u * e;
+#pragma unroll
+    for (uint32_t cc = 0; cc < kMergeBatch; ++cc)
+      od[e][cc] = (d < HD && cc < nvalid) ? __ldcg(base + cc * (HD + 4u) + 4u + d) : 0.0f;
+  }
+  __syncthreads();
+  float gmx = -INFINITY;
+  for (uint32_t cc = 0; cc < nvalid; ++cc) gmx = fmaxf(gmx, s_wc[cc]);
+  __syncthreads();
+  for (uint32_t cc = tid; cc < nvalid; cc += 128u) s_wc[cc] = expf(s_wc[cc] - gmx);
+  __syncthreads();
+  float L = 0.0f;
+  for (uint32_t cc = 0; cc < nvalid; ++cc) L += s_lc[cc] * s_wc[cc];
   const float inv = 1.0f / L;
-  for (uint32_t d = tid; d < HD; d += 128u) {
-    float acc = 0.0f;
-    for (uint32_t cc = 0; cc < nvalid; ++cc) {
-      const float* pc = base + cc * (HD + 4u);
-      acc = __fmaf_rn(__ldcg(pc + 4 + d), expf(__ldcg(pc) - gmx), acc);
+#pragma unroll
+  for (int e = 0; e < NDT; ++e) {
+    const uint32_t d = tid + 128u * e;
+    if (d < HD) {
+      float acc = 0.0f;
+#pragma unroll
+      for (uint32_t cc = 0; cc < kMergeBatch; ++cc)
+        if (cc < nvalid) acc = __fmaf_rn(od[e][cc], s_wc[cc], acc);
+      for (uint32_t cc = kMergeBatch; cc < nvalid; ++cc)
+        acc = __fmaf_rn(__ldcg(base + cc * (HD + 4u) + 4u + d), s_wc[cc], acc);
+      s_out[d] = acc * inv;
     }
-    s_out[d] = acc * inv;
   }
   if (tid == 0) p.count[hloc] = 0u;
   __syncthreads();
@@ -605,6 +632,10 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
   if (m.n_embd % 256 || m.n_embd > 256u * 4u * kNormMaxChunks || m.n_ff % blk_elems(wdt) ||
       m.n_embd % blk_elems(odt)) {
     set_error_message("cuda text: n_embd must be a multiple of 256 (at most 16384), n_ff of the block size");
+    return EOS_E_UNSUPPORTED;
+  }
+  if (m.max_ctx > kAttnChunk * kMaxAttnChunks) {
+    set_error_message("cuda text: max_ctx above 16384");
     return EOS_E_UNSUPPORTED;
   }
   if (ws < 1 || ws > (int)kMaxParts || rk < 0 || rk >= ws || m.n_head % ws || m.n_kv_head % ws) {

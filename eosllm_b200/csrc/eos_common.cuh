@@ -35,7 +35,6 @@ enum : uint32_t {
   EOS_DEVERR_WAIT_ACT = 1u << 2,    // activation tile never arrived
   EOS_DEVERR_DRAIN = 1u << 3,       // in-flight copies did not drain on exit
   EOS_DEVERR_PEER = 1u << 4,        // a peer flag wait ran out
-  EOS_DEVERR_CHECK = 1u << 5,       // a self-check found an index out of range (access skipped)
 };
 
 // One second: the bound on every spin-wait in this library's kernels.
@@ -224,101 +223,6 @@ __device__ __forceinline__ uint32_t rec_aq_offset(uint32_t g) {
 __device__ __forceinline__ uint32_t rec_st_offset(uint32_t g) {
   const uint32_t s = g & 7u;
   return (g >> 3) * kActRec + (s >> 2) * kActHalf + 128u + ((s & 3u) << 3);
-}
-
-// One THREAD packs a whole 32-group v[0..31] into record group g: the same
-// arithmetic as quant_group32 (quantize_sub32, matmul_q4_k_int8.c:98-154),
-// with the AVX2 max tree written out element-wise -- lane-wise maxes of the
-// four 8-float vectors (:112-113), then hmax_ps_8's halves, movehl and lane-1
-// steps (:84-94) -- so NaN picks match too.  For many groups at once (each
-// thread its own group) this has no cross-lane dependency chain.
-__device__ __forceinline__ void pack_group_thread(const float (&v)[32], uint32_t g, uint8_t* rec) {
-  float mx[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float a0 = fabsf(v[i]), a1 = fabsf(v[8 + i]), a2 = fabsf(v[16 + i]), a3 = fabsf(v[24 + i]);
-    mx[i] = x86_max(x86_max(a0, a1), x86_max(a2, a3));
-  }
-  float m4[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) m4[i] = x86_max(mx[i], mx[i + 4]);
-  const float max_abs = x86_max(x86_max(m4[0], m4[2]), x86_max(m4[1], m4[3]));
-  float scale, inv;
-  if (max_abs > 0.0f) {
-    scale = __fdiv_rn(max_abs, 127.0f);
-    inv = __fdiv_rn(127.0f, max_abs);
-  } else {
-    scale = 0.0f;
-    inv = 0.0f;
-  }
-  uint32_t w[8];
-  uint32_t sum = 0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    uint32_t word = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int32_t q = x86_cvtps(__fmul_rn(v[4 * j + k], inv));
-      sum += static_cast<uint32_t>(q);
-      const int32_t c = q < -128 ? -128 : (q > 127 ? 127 : q);
-      word |= (static_cast<uint32_t>(c) & 0xffu) << (8 * k);
-    }
-    w[j] = word;
-  }
-  uint4* dst = reinterpret_cast<uint4*>(rec + rec_aq_offset(g));
-  dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-  dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-  *reinterpret_cast<float2*>(rec + rec_st_offset(g)) = make_float2(scale, (float)static_cast<int32_t>(sum));
-}
-
-// A lane PAIR packs 32-group g: the even lane holds elements 0..15, the odd
-// lane 16..31 (v[0..15] each).  Same arithmetic as pack_group_thread: the
-// even lane forms max(a[i], a[8 + i]), the odd lane max(a[16 + i], a[24 + i])
-// for i < 8, one exchange, then both finish the identical tree; the wrapping
-// int32 sums of the halves are added exactly.  All 32 lanes must call it.
-__device__ __forceinline__ void pack_group_pair(const float (&v)[16], uint32_t g, uint32_t lane, uint8_t* rec,
-                                                bool active) {
-  const unsigned FULL = 0xffffffffu;
-  const uint32_t odd = lane & 1u;
-  float mine[8], other[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) mine[i] = x86_max(fabsf(v[i]), fabsf(v[8 + i]));
-#pragma unroll
-  for (int i = 0; i < 8; ++i) other[i] = __shfl_xor_sync(FULL, mine[i], 1);
-  float mx[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) mx[i] = odd ? x86_max(other[i], mine[i]) : x86_max(mine[i], other[i]);
-  float m4[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) m4[i] = x86_max(mx[i], mx[i + 4]);
-  const float max_abs = x86_max(x86_max(m4[0], m4[2]), x86_max(m4[1], m4[3]));
-  float scale, inv;
-  if (max_abs > 0.0f) {
-    scale = __fdiv_rn(max_abs, 127.0f);
-    inv = __fdiv_rn(127.0f, max_abs);
-  } else {
-    scale = 0.0f;
-    inv = 0.0f;
-  }
-  uint32_t w[4];
-  uint32_t sum = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t word = 0;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int32_t q = x86_cvtps(__fmul_rn(v[4 * j + k], inv));
-      sum += static_cast<uint32_t>(q);
-      const int32_t c = q < -128 ? -128 : (q > 127 ? 127 : q);
-      word |= (static_cast<uint32_t>(c) & 0xffu) << (8 * k);
-    }
-    w[j] = word;
-  }
-  sum += __shfl_xor_sync(FULL, sum, 1);
-  if (active) {
-    *reinterpret_cast<uint4*>(rec + rec_aq_offset(g) + 16u * odd) = make_uint4(w[0], w[1], w[2], w[3]);
-    if (!odd) *reinterpret_cast<float2*>(rec + rec_st_offset(g)) = make_float2(scale, (float)static_cast<int32_t>(sum));
-  }
 }
 
 // Packs the warp's 32-group g (lane i holds element i) into a record.
