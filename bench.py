@@ -464,8 +464,6 @@ def run_ours(args):
     decode = None
     if args.workload == "sweep":
         pass
-    elif not args.no_decode and world > 1:
-        decode = {"unavailable": "the tensor-parallel decoder needs the peer exchange, not built yet"}
     elif not args.no_decode:
         del g_timed, g_warm, g_trains
         weights.clear()
@@ -520,6 +518,8 @@ def run_decode(args, dev, world, rank) -> dict:
     cfg = dict(LLAMA_7B, max_ctx=P + G)
     model = synthetic_llama(**cfg, seed=4, device=dev.index)
     dec = TextDecoder(model, device=dev.index, rank=rank, world=world)
+    if world > 1:
+        dec.connect()  # IPC handles all-gathered over the process group; data path: peer reads over NVLink
     host_model = None
     if rank == 0 and world == 1 and args.decode_cpu_steps > 0 and not args.no_cpu_baseline:
         host_model = dict(config=model["config"], tok_embd=model["tok_embd"].cpu().numpy().view(np.uint16),

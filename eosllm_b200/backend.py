@@ -81,6 +81,9 @@ _SIGNATURES = {
     "eosi_cuda_text_reset": (C.c_int, [_vp]),
     "eosi_cuda_text_pos": (_u32, [_vp]),
     "eosi_cuda_text_stream": (_vp, [_vp]),
+    "eosi_cuda_text_ipc_handle": (C.c_int, [_vp, _vp, _sz]),
+    "eosi_cuda_text_attach_peers": (C.c_int, [_vp, _vp, _sz]),
+    "eosi_cuda_text_partition": (C.c_int, [_vp, C.c_int, C.c_int, _vp]),
     "eosi_cuda_text_close": (None, [_vp]),
 }
 

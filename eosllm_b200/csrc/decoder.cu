@@ -35,6 +35,7 @@
 // sinf / cosf are CUDA's, so logits agree with the CPU engine to a
 // tolerance, not bit for bit.
 #include <cmath>
+#include <cstddef>
 #include <cstdlib>
 #include <cstring>
 #include <new>
@@ -70,7 +71,54 @@ struct NormPackParams {
   uint32_t n;
   uint8_t* act;     // Q4_K consumers: packed records for k = n
   float* act_f32;   // Q8_0 consumers: the normalised vector
+  // tensor parallel: before reading parts[], announce this rank's partial
+  // (own_flag = epoch) and wait for every rank's flag (bounded)
+  uint32_t world;
+  uint32_t* own_flag;
+  const uint32_t* rank_flag[kMaxParts];
+  uint32_t xchg;          // exchange index within the step
+  uint32_t xchg_per_step;
 };
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Tensor-parallel handshake of exchange `epoch`: thread 0 of CTA 0 publishes
+// this rank's flag after a system-scope fence (the partial it announces was
+// written by the previous kernel, complete at the PDL wait); threads t < world
+// wait for rank t's flag (bounded: EOS_DEVERR_PEER after EOS_WAIT_LIMIT_NS).
+// Returns false when a wait ran out.
+__device__ __forceinline__ bool xchg_sync(uint32_t world, uint32_t* own_flag, const uint32_t* const* rank_flag,
+                                          uint32_t epoch, uint32_t* err, bool publish) {
+  __shared__ uint32_t s_ok;
+  if (threadIdx.x == 0) s_ok = 1u;
+  if (publish && threadIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(own_flag, epoch);
+  }
+  __syncthreads();
+  if (threadIdx.x < world) {
+    const uint32_t* f = rank_flag[threadIdx.x];
+    if (ld_acquire_sys(f) < epoch) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(f) < epoch) {
+        if (global_timer_ns() - t0 > EOS_WAIT_LIMIT_NS) {
+          report(err, EOS_DEVERR_PEER);
+          s_ok = 0u;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return s_ok != 0u;
+}
 
 constexpr uint32_t kNormMaxChunks = 16;  // float4 chunks per thread: n <= 16384
 
@@ -92,6 +140,11 @@ __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) 
   __shared__ __align__(16) float ys[256];
   pdl_trigger();
   pdl_wait();
+  if (p.world > 1 && p.nparts > 0) {
+    const uint32_t epoch = p.state->epoch * p.xchg_per_step + p.xchg + 1u;
+    if (!xchg_sync(p.world, p.own_flag, p.rank_flag, epoch, const_cast<uint32_t*>(&p.state->err), blockIdx.x == 0))
+      return;  // a peer never arrived: the error bit is set, outputs are invalid
+  }
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   const uint32_t nch = p.n >> 2, b = blockIdx.x;
   const uint32_t jown = b >> 2;
@@ -121,13 +174,13 @@ __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) 
 #pragma unroll
       for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
         const uint32_t c = tid + 256u * j;
-        if (c < nch) t[j] = ld4(p.parts[0], c);
+        if (c < nch) t[j] = __ldcv(reinterpret_cast<const float4*>(p.parts[0]) + c);
       }
       for (uint32_t q = 1; q < p.nparts; ++q) {
 #pragma unroll
         for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
           const uint32_t c = tid + 256u * j;
-          if (c < nch) t[j] = add4(t[j], ld4(p.parts[q], c));
+          if (c < nch) t[j] = add4(t[j], __ldcv(reinterpret_cast<const float4*>(p.parts[q]) + c));
         }
       }
 #pragma unroll
@@ -416,12 +469,17 @@ __global__ void __launch_bounds__(256) silu_pack_kernel(const float* __restrict_
 // from logits[0], so a NaN logits[0] keeps index 0 and other NaNs never win)
 // ---------------------------------------------------------------------------
 struct ArgmaxParams {
-  const float* logits;
+  const float* logits;   // this rank's vocabulary slice
   uint32_t n;
   float* part_v;     // [gridDim.x]
   uint32_t* part_i;
   DecState* state;
   uint32_t* out_tokens;  // [max_ctx]: pick of step pos
+  // tensor parallel: every rank's slice result, merged in rank order
+  uint32_t world, rank, v0;  // v0: global index of logits[0]
+  XFlags* own_x;
+  const XFlags* rank_x[kMaxParts];
+  uint32_t xchg, xchg_per_step;
 };
 
 __device__ __forceinline__ bool arg_better(float av, uint32_t ai, float bv, uint32_t bi) {
@@ -493,14 +551,44 @@ __global__ void __launch_bounds__(256) argmax_kernel(const ArgmaxParams p) {
   }
   __syncthreads();
   arg_reduce_block(v, idx, sv, si);
+  const float first = __ldcg(p.logits);
+  uint32_t first_nan = (p.rank == 0 && first != first) ? 1u : 0u;
+  uint32_t gidx = idx == 0xffffffffu ? idx : p.v0 + idx;
+  if (p.world > 1) {
+    if (threadIdx.x == 0) {
+      p.own_x->arg_v = v;
+      p.own_x->arg_i = gidx;
+      p.own_x->first_nan = first_nan;
+    }
+    const uint32_t* rf[kMaxParts];
+#pragma unroll
+    for (uint32_t q = 0; q < kMaxParts; ++q) rf[q] = q < p.world ? &p.rank_x[q]->flag[2] : nullptr;
+    const uint32_t epoch = p.state->epoch * p.xchg_per_step + p.xchg + 1u;
+    if (!xchg_sync(p.world, &p.own_x->flag[2], rf, epoch, &p.state->err, true)) return;
+    if (threadIdx.x == 0) {
+      v = __int_as_float(0x7fc00000);
+      gidx = 0xffffffffu;
+      for (uint32_t q = 0; q < p.world; ++q) {  // rank order = vocabulary order
+        (void)ld_acquire_sys(rf[q]);
+        const volatile XFlags* x = p.rank_x[q];
+        const float qv = x->arg_v;
+        const uint32_t qi = x->arg_i;
+        if (q == 0) first_nan = x->first_nan;
+        if (arg_better(qv, qi, v, gidx)) {
+          v = qv;
+          gidx = qi;
+        }
+      }
+    }
+  }
   if (threadIdx.x == 0) {
-    const float first = __ldcg(p.logits);
-    const uint32_t tok = (first != first || idx == 0xffffffffu) ? 0u : idx;
+    const uint32_t tok = (first_nan || gidx == 0xffffffffu) ? 0u : gidx;
     const uint32_t pos = p.state->pos;
     p.out_tokens[pos] = tok;
     p.state->next_token = tok;
     p.state->arg_count = 0u;
     p.state->pos = pos + 1u;
+    p.state->epoch = p.state->epoch + 1u;
   }
 }
 
@@ -572,6 +660,12 @@ struct TextDecoder {
   uint32_t* out_tokens = nullptr;
   uint32_t* gemv_err = nullptr;
   uint32_t arg_blocks = 0;
+  // exchange buffer: this rank's O and down partials, logits slice and
+  // handshake words; the other ranks read it through CUDA IPC mappings
+  uint8_t* xbuf = nullptr;
+  size_t xoff_po = 0, xoff_pd = 0, xoff_lg = 0, xoff_fl = 0, xbytes = 0;
+  uint8_t* xpeer[kMaxParts] = {};  // every rank's exchange buffer (own included)
+  bool peer_opened[kMaxParts] = {};
   cudaGraphExec_t graph = nullptr;
   uint32_t host_pos = 0;
   bool step_mode = false;  // prompt[] holds every fed token (n_prompt = max_ctx)
@@ -589,6 +683,8 @@ struct TextDecoder {
   ~TextDecoder() {
     if (graph) cudaGraphExecDestroy(graph);
     if (st) cudaStreamSynchronize(st);
+    for (int q = 0; q < world && q < (int)kMaxParts; ++q)
+      if (peer_opened[q]) cudaIpcCloseMemHandle(xpeer[q]);
     for (void* p : allocs) cudaFree(p);
     if (st) cudaStreamDestroy(st);
   }
@@ -609,19 +705,28 @@ struct TextDecoder {
   }
 
   int open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws);
+  int attach(const uint8_t* handles);
+  const XFlags* xflags(int q) const { return reinterpret_cast<const XFlags*>(xpeer[q] + xoff_fl); }
+  XFlags* own_flags() const { return reinterpret_cast<XFlags*>(xbuf + xoff_fl); }
   cudaError_t record_step(cudaStream_t s);
   int capture();
 };
 
-int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
-  m = *desc;
-  device = dev;
-  rank = rk;
-  world = ws;
+// The slice of the model rank rk of ws owns: heads [h0, h0 + hl) (and their
+// KV heads) for q/k/v and the O projection's columns, FFN units [ff0, ff0 +
+// ffl) for gate/up rows and the down projection's columns, vocabulary rows
+// [v0, v0 + vl) of the LM head.  Host only; returns an eos_status_t.
+struct Geometry {
+  uint32_t hd, hl, h0, kvl, kv0, ffl, ff0, vl, v0;
+};
+int model_geometry(const eosi_cuda_llama_t& m, int rk, int ws, Geometry& g) {
   const int wdt = m.wdtype, odt = m.out_dtype;
-  if (m.n_head == 0 || m.n_kv_head == 0 || m.n_embd % m.n_head) return EOS_E_INVALID_ARG;
-  hd = m.n_embd / m.n_head;
-  if (hd != 64 && hd != 128 && hd != 256) {
+  if (m.n_head == 0 || m.n_kv_head == 0 || m.n_embd % m.n_head) {
+    set_error_message("cuda text: n_embd must be a multiple of n_head");
+    return EOS_E_INVALID_ARG;
+  }
+  g.hd = m.n_embd / m.n_head;
+  if (g.hd != 64 && g.hd != 128 && g.hd != 256) {
     set_error_message("cuda text: head_dim must be 64, 128 or 256");
     return EOS_E_UNSUPPORTED;
   }
@@ -642,22 +747,45 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
     set_error_message("cuda text: world size must divide the head counts (at most 8 ranks)");
     return EOS_E_INVALID_ARG;
   }
-  hl = m.n_head / ws;
-  h0 = hl * rk;
-  kvl = m.n_kv_head / ws;
-  kv0 = kvl * rk;
-  if (wdt == EOS_DT_Q4_K && (hl * hd) % 256) {
+  g.hl = m.n_head / ws;
+  g.h0 = g.hl * rk;
+  g.kvl = m.n_kv_head / ws;
+  g.kv0 = g.kvl * rk;
+  if (wdt == EOS_DT_Q4_K && (g.hl * g.hd) % 256) {
     set_error_message("cuda text: a rank's head columns must be whole Q4_K super-blocks");
     return EOS_E_UNSUPPORTED;
   }
-  {
-    // FFN slice in whole blocks of the down projection's k
-    const uint32_t be = blk_elems(wdt), units = m.n_ff / be;
-    ff0 = (uint32_t)(((uint64_t)units * rk) / ws) * be;
-    ffl = (uint32_t)(((uint64_t)units * (rk + 1)) / ws) * be - ff0;
+  // FFN slice in whole blocks of the down projection's k
+  const uint32_t be = blk_elems(wdt), units = m.n_ff / be;
+  g.ff0 = (uint32_t)(((uint64_t)units * rk) / ws) * be;
+  g.ffl = (uint32_t)(((uint64_t)units * (rk + 1)) / ws) * be - g.ff0;
+  g.v0 = (uint32_t)(((uint64_t)m.n_vocab * rk) / ws);
+  g.vl = (uint32_t)(((uint64_t)m.n_vocab * (rk + 1)) / ws) - g.v0;
+  if (g.ffl == 0 || g.vl == 0) {
+    set_error_message("cuda text: too many ranks for the FFN or the vocabulary");
+    return EOS_E_INVALID_ARG;
   }
-  v0 = (uint32_t)(((uint64_t)m.n_vocab * rk) / ws);
-  vl = (uint32_t)(((uint64_t)m.n_vocab * (rk + 1)) / ws) - v0;
+  return EOS_OK;
+}
+
+int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
+  m = *desc;
+  device = dev;
+  rank = rk;
+  world = ws;
+  const int wdt = m.wdtype, odt = m.out_dtype;
+  Geometry g{};
+  const int gs = model_geometry(m, rk, ws, g);
+  if (gs != EOS_OK) return gs;
+  hd = g.hd;
+  hl = g.hl;
+  h0 = g.h0;
+  kvl = g.kvl;
+  kv0 = g.kv0;
+  ffl = g.ffl;
+  ff0 = g.ff0;
+  vl = g.vl;
+  v0 = g.v0;
   max_chunks = (m.max_ctx + kAttnChunk - 1) / kAttnChunk;
 
   if (cudaSetDevice(dev) != cudaSuccess) return EOS_E_INTERNAL;
@@ -701,10 +829,22 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
   chk(alloc(&x0, 4ull * E));
   chk(alloc(&x1, 4ull * E));
   chk(alloc(&qkv, 4ull * (hl * hd + 2 * kvl * hd)));
-  chk(alloc(&part_o, 4ull * E));
-  chk(alloc(&part_d, 4ull * E));
+  {
+    const uint32_t vmax = (m.n_vocab + ws - 1) / ws + 1;
+    auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
+    xoff_po = 0;
+    xoff_pd = up(4ull * E);
+    xoff_lg = xoff_pd + up(4ull * E);
+    xoff_fl = xoff_lg + up(4ull * vmax);
+    xbytes = xoff_fl + up(sizeof(XFlags));
+    chk(alloc(&xbuf, xbytes));
+    part_o = reinterpret_cast<float*>(xbuf + xoff_po);
+    part_d = reinterpret_cast<float*>(xbuf + xoff_pd);
+    logits = reinterpret_cast<float*>(xbuf + xoff_lg);
+    xpeer[rk] = xbuf;
+  }
   chk(alloc(&gu, 8ull * ffl));
-  chk(alloc(&logits, 4ull * (vl > 0 ? vl : 1)));
+
   if (wdt == EOS_DT_Q4_K) {
     chk(alloc(&act_o, (size_t)(hl * hd / 256) * kActRec));
     chk(alloc(&act_d, (size_t)(ffl / 256) * kActRec));
@@ -735,6 +875,27 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
     set_error_message(cudaGetErrorString(e));
     return e == cudaErrorMemoryAllocation ? EOS_E_OUT_OF_MEMORY : EOS_E_INTERNAL;
   }
+  // tensor parallel: the step graph reads the other ranks' exchange buffers,
+  // so it is built by attach() once their IPC handles are known
+  return ws == 1 ? capture() : EOS_OK;
+}
+
+int TextDecoder::attach(const uint8_t* handles) {
+  if (world == 1 || graph != nullptr) return graph != nullptr ? EOS_OK : capture();
+  if (cudaSetDevice(device) != cudaSuccess) return EOS_E_INTERNAL;
+  for (int q = 0; q < world; ++q) {
+    if (q == rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handles + (size_t)q * sizeof(cudaIpcMemHandle_t), sizeof(h));
+    void* ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      set_error_message(cudaGetErrorString(e));
+      return EOS_E_INTERNAL;
+    }
+    xpeer[q] = static_cast<uint8_t*>(ptr);
+    peer_opened[q] = true;
+  }
   return capture();
 }
 
@@ -751,12 +912,25 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
                                                   &status);
     return launch_q80_gemv(w, actf, c, n, k, gemv_err, num_sms, max_smem, s, &status);
   };
-  auto norm_pack = [&](const float* x_in, const float* part, float* x_out, const float* w, int dt_a, int dt_b)
-      -> cudaError_t {
+  const uint32_t xps = 2u * m.n_layer + 1u;  // exchanges per step
+  // `part`: nullptr (no partial), part_o or part_d; xk: exchange index
+  auto norm_pack = [&](const float* x_in, const float* part, float* x_out, const float* w, int dt_a, int dt_b,
+                       uint32_t xk = 0) -> cudaError_t {
     NormPackParams p{};
     p.x_in = x_in;
-    p.nparts = part ? 1u : 0u;
-    p.parts[0] = part;
+    p.nparts = 0;
+    if (part != nullptr) {
+      const size_t off = part == part_o ? xoff_po : xoff_pd;
+      p.nparts = (uint32_t)world;
+      for (int q = 0; q < world; ++q) {
+        p.parts[q] = reinterpret_cast<const float*>(xpeer[q] + off);
+        p.rank_flag[q] = &reinterpret_cast<const XFlags*>(xpeer[q] + xoff_fl)->flag[part == part_o ? 0 : 1];
+      }
+      p.own_flag = &own_flags()->flag[part == part_o ? 0 : 1];
+    }
+    p.world = (uint32_t)world;
+    p.xchg = xk;
+    p.xchg_per_step = xps;
     p.tok_embd = tok_embd;
     p.prompt = prompt;
     p.state = state;
@@ -773,7 +947,7 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
   for (uint32_t L = 0; L < m.n_layer && e == cudaSuccess; ++L) {
     const DecLayer& d = layers[L];
     // x1 = (L == 0 ? embedding : x0 + down partial); act_e = pack(rmsnorm(x1))
-    e = norm_pack(L == 0 ? nullptr : x0, L == 0 ? nullptr : part_d, x1, d.attn_norm, wdt, wdt);
+    e = norm_pack(L == 0 ? nullptr : x0, L == 0 ? nullptr : part_d, x1, d.attn_norm, wdt, wdt, 2u * L - 1u);
     if (e == cudaSuccess) e = gemv(wdt, d.wqkv, act_e, actf_e, qkv, nqkv, E);
     if (e == cudaSuccess) {
       AttnParams a{};
@@ -802,7 +976,7 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
     }
     if (e == cudaSuccess) e = gemv(wdt, d.wo, act_o, actf_o, part_o, E, hl * hd);
     // x0 = x1 + O partial; act_e = pack(rmsnorm(x0))
-    if (e == cudaSuccess) e = norm_pack(x1, part_o, x0, d.ffn_norm, wdt, wdt);
+    if (e == cudaSuccess) e = norm_pack(x1, part_o, x0, d.ffn_norm, wdt, wdt, 2u * L);
     if (e == cudaSuccess) e = gemv(wdt, d.wgu, act_e, actf_e, gu, 2 * ffl, E);
     if (e == cudaSuccess)
       e = launch_pdl(silu_pack_kernel, dim3((ffl + 255u) / 256u), dim3(256), s, (const float*)gu, ffl, act_d,
@@ -811,10 +985,24 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
   }
   // final norm + LM head + greedy pick (text.c:425-432, greedy.c:66-69)
   if (e == cudaSuccess)
-    e = norm_pack(m.n_layer ? x0 : nullptr, m.n_layer ? part_d : nullptr, x1, out_norm, odt, odt);
+    e = norm_pack(m.n_layer ? x0 : nullptr, m.n_layer ? part_d : nullptr, x1, out_norm, odt, odt,
+                  m.n_layer ? 2u * m.n_layer - 1u : 0u);
   if (e == cudaSuccess) e = gemv(odt, wout, act_e, actf_e, logits, vl, E);
   if (e == cudaSuccess) {
-    ArgmaxParams a{logits, vl, arg_v, arg_i, state, out_tokens};
+    ArgmaxParams a{};
+    a.logits = logits;
+    a.n = vl;
+    a.part_v = arg_v;
+    a.part_i = arg_i;
+    a.state = state;
+    a.out_tokens = out_tokens;
+    a.world = (uint32_t)world;
+    a.rank = (uint32_t)rank;
+    a.v0 = v0;
+    a.own_x = own_flags();
+    for (int q = 0; q < world; ++q) a.rank_x[q] = xflags(q);
+    a.xchg = 2u * m.n_layer;
+    a.xchg_per_step = xps;
     e = launch_pdl(argmax_kernel, dim3(arg_blocks), dim3(256), s, a);
   }
   if (e == cudaSuccess && status != EOS_OK) e = cudaErrorNotSupported;
@@ -913,6 +1101,10 @@ EOSLLM_CUDA_API int eosi_cuda_text_step(eosi_cuda_text_t* t, uint32_t token, flo
     eos::set_error_message("cuda text: context is full");
     return EOS_E_OUT_OF_MEMORY;
   }
+  if (d.graph == nullptr) {
+    eos::set_error_message("cuda text: tensor-parallel decoder not attached to its peers");
+    return EOS_E_INVALID_ARG;
+  }
   if (cudaSetDevice(d.device) != cudaSuccess) return EOS_E_INTERNAL;
   cudaError_t e = cudaSuccess;
   if (!d.step_mode) {  // every later step reads its token from prompt[pos]
@@ -922,8 +1114,13 @@ EOSLLM_CUDA_API int eosi_cuda_text_step(eosi_cuda_text_t* t, uint32_t token, flo
   }
   if (e == cudaSuccess) e = cudaMemcpyAsync(d.prompt + d.host_pos, &token, 4, cudaMemcpyHostToDevice, d.st);
   if (e == cudaSuccess) e = cudaGraphLaunch(d.graph, d.st);
-  if (e == cudaSuccess && d.world == 1)
-    e = cudaMemcpyAsync(logits, d.logits, 4ull * d.m.n_vocab, cudaMemcpyDeviceToHost, d.st);
+  // every rank's vocabulary slice (complete: this rank's pick waited for all
+  // of them, and no rank writes logits again before this rank's next step)
+  for (int q = 0; q < d.world && e == cudaSuccess; ++q) {
+    eos::Geometry g{};
+    eos::model_geometry(d.m, q, d.world, g);
+    e = cudaMemcpyAsync(logits + g.v0, d.xpeer[q] + d.xoff_lg, 4ull * g.vl, cudaMemcpyDeviceToHost, d.st);
+  }
   if (e == cudaSuccess) e = cudaStreamSynchronize(d.st);
   if (e != cudaSuccess) return dec_fail(e);
   d.host_pos++;
@@ -935,6 +1132,10 @@ EOSLLM_CUDA_API int eosi_cuda_text_generate(eosi_cuda_text_t* t, const uint32_t*
   if (t == nullptr || prompt == nullptr || n_prompt == 0 || (n_gen > 0 && out_tokens == nullptr))
     return EOS_E_INVALID_ARG;
   TextDecoder& d = t->d;
+  if (d.graph == nullptr) {
+    eos::set_error_message("cuda text: tensor-parallel decoder not attached to its peers");
+    return EOS_E_INVALID_ARG;
+  }
   for (uint32_t i = 0; i < n_prompt; ++i)
     if (prompt[i] >= d.m.n_vocab) {
       eos::set_error_message("cuda text: token id out of range");
@@ -964,7 +1165,9 @@ EOSLLM_CUDA_API int eosi_cuda_text_reset(eosi_cuda_text_t* t) {
   if (t == nullptr) return EOS_E_INVALID_ARG;
   TextDecoder& d = t->d;
   if (cudaSetDevice(d.device) != cudaSuccess) return EOS_E_INTERNAL;
-  cudaError_t e = cudaMemsetAsync(d.state, 0, sizeof(eos::DecState), d.st);
+  // position, prompt length, pick, argmax count and error word; the exchange
+  // epoch keeps counting (the peers' flags hold earlier epochs)
+  cudaError_t e = cudaMemsetAsync(d.state, 0, offsetof(eos::DecState, epoch), d.st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(d.st);
   if (e != cudaSuccess) return dec_fail(e);
   d.host_pos = 0;
@@ -973,6 +1176,32 @@ EOSLLM_CUDA_API int eosi_cuda_text_reset(eosi_cuda_text_t* t) {
 }
 
 EOSLLM_CUDA_API uint32_t eosi_cuda_text_pos(const eosi_cuda_text_t* t) { return t ? t->d.host_pos : 0u; }
+
+EOSLLM_CUDA_API int eosi_cuda_text_ipc_handle(eosi_cuda_text_t* t, void* out, size_t cap) {
+  if (t == nullptr || out == nullptr || cap < sizeof(cudaIpcMemHandle_t)) return EOS_E_INVALID_ARG;
+  if (cudaSetDevice(t->d.device) != cudaSuccess) return EOS_E_INTERNAL;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, t->d.xbuf);
+  if (e != cudaSuccess) return dec_fail(e);
+  memcpy(out, &h, sizeof(h));
+  return EOS_OK;
+}
+
+EOSLLM_CUDA_API int eosi_cuda_text_attach_peers(eosi_cuda_text_t* t, const void* handles, size_t bytes) {
+  if (t == nullptr || handles == nullptr || bytes < (size_t)t->d.world * sizeof(cudaIpcMemHandle_t))
+    return EOS_E_INVALID_ARG;
+  return t->d.attach(static_cast<const uint8_t*>(handles));
+}
+
+EOSLLM_CUDA_API int eosi_cuda_text_partition(const eosi_cuda_llama_t* m, int rank, int world, uint32_t* out) {
+  if (m == nullptr || out == nullptr) return EOS_E_INVALID_ARG;
+  eos::Geometry g{};
+  const int s = eos::model_geometry(*m, rank, world, g);
+  if (s != EOS_OK) return s;
+  const uint32_t v[9] = {g.hd, g.h0, g.hl, g.kv0, g.kvl, g.ff0, g.ffl, g.v0, g.vl};
+  memcpy(out, v, sizeof(v));
+  return EOS_OK;
+}
 
 EOSLLM_CUDA_API void* eosi_cuda_text_stream(eosi_cuda_text_t* t) { return t ? (void*)t->d.st : nullptr; }
 

@@ -14,7 +14,20 @@ struct DecState {
   uint32_t next_token;  // greedy pick of the previous step
   uint32_t arg_count;   // argmax CTA arrivals (reset by the last CTA)
   uint32_t err;         // EOS_DEVERR_* bits
-  uint32_t pad[3];
+  uint32_t epoch;       // completed steps (never reset): tensor-parallel exchange epochs
+  uint32_t pad[2];
+};
+
+// Tensor-parallel exchange words of one rank, in its exchange buffer (read by
+// the other ranks through CUDA IPC mappings).  Flag values are epochs:
+// step_epoch * (2 n_layer + 1) + exchange + 1.
+struct XFlags {
+  uint32_t flag[3];  // [0] O-projection partial ready, [1] down partial ready, [2] argmax result ready
+  uint32_t pad0;
+  float arg_v;       // this rank's best logit
+  uint32_t arg_i;    // its global vocabulary index
+  uint32_t first_nan;  // rank 0: logits[0] is NaN
+  uint32_t pad1;
 };
 
 // One layer's resident weights (this rank's slices).

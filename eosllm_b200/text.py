@@ -76,6 +76,27 @@ class TextDecoder:
                 "eosi_cuda_text_open")
         self._keep = None  # weights are resident on the device now
 
+    def ipc_handle(self) -> bytes:
+        """This rank's exchange-buffer IPC handle (tensor parallel)."""
+        buf = (C.c_ubyte * 64)()
+        B.check(self.lib.eosi_cuda_text_ipc_handle(self.handle, buf, 64), "eosi_cuda_text_ipc_handle")
+        return bytes(buf)
+
+    def attach_peers(self, handles: list) -> None:
+        """Map every rank's exchange buffer (handles in rank order) and build
+        the step (tensor parallel)."""
+        blob = b"".join(handles)
+        buf = (C.c_ubyte * len(blob)).from_buffer_copy(blob)
+        B.check(self.lib.eosi_cuda_text_attach_peers(self.handle, buf, len(blob)), "eosi_cuda_text_attach_peers")
+
+    def connect(self, group=None) -> None:
+        """attach_peers with the handles all-gathered over a torch.distributed
+        process group (any backend)."""
+        import torch.distributed as dist
+        handles = [None] * dist.get_world_size(group)
+        dist.all_gather_object(handles, self.ipc_handle(), group=group)
+        self.attach_peers(handles)
+
     def step(self, token: int) -> np.ndarray:
         """eosi_text_step: logits of the next position for `token`."""
         out = np.empty(self.n_vocab, np.float32)
@@ -116,6 +137,18 @@ class TextDecoder:
             self.close()
         except Exception:
             pass
+
+
+def partition(config: dict, rank: int, world: int) -> dict:
+    """The slice of the model rank `rank` of `world` owns (host only)."""
+    d = LlamaDesc()
+    for k in ("n_embd", "n_layer", "n_head", "n_kv_head", "n_ff", "n_vocab", "max_ctx"):
+        setattr(d, k, int(config[k]))
+    d.wdtype, d.out_dtype = int(config["wdtype"]), int(config["out_dtype"])
+    out = (C.c_uint32 * 9)()
+    B.check(B.load().eosi_cuda_text_partition(C.byref(d), rank, world, out), "eosi_cuda_text_partition")
+    keys = ("head_dim", "head0", "heads", "kv_head0", "kv_heads", "ff0", "ff_len", "vocab0", "vocab_len")
+    return dict(zip(keys, list(out)))
 
 
 def synthetic_llama(n_embd=256, n_layer=2, n_head=4, n_kv_head=4, n_ff=512, n_vocab=320, max_ctx=64, seed=3,

@@ -235,6 +235,24 @@ EOSLLM_CUDA_API int eosi_cuda_text_generate(eosi_cuda_text_t *t, const uint32_t 
 /* Position back to 0 (the KV cache is overwritten as steps proceed). */
 EOSLLM_CUDA_API int eosi_cuda_text_reset(eosi_cuda_text_t *t);
 EOSLLM_CUDA_API uint32_t eosi_cuda_text_pos(const eosi_cuda_text_t *t);
+/* Tensor parallel (world > 1): after eosi_cuda_text_open on every rank, each
+ * rank exports the IPC handle of its exchange buffer (EOSI_CUDA_IPC_HANDLE_BYTES
+ * bytes), the host gathers all ranks' handles in rank order (e.g. an
+ * all-gather over the process group) and passes them to
+ * eosi_cuda_text_attach_peers, which maps the peers' buffers and builds the
+ * step.  Per layer the ranks exchange the O-projection and down-projection
+ * partial sums (each rank reads every rank's partial over NVLink and sums
+ * them in rank order, so all ranks hold the same residual stream) and at the
+ * end their slice's greedy pick; every exchange is a flag handshake with a
+ * one-second bound (EOS_E_INTERNAL when a rank never arrives).  Every rank
+ * must make the same calls in the same order (step / generate / reset). */
+#define EOSI_CUDA_IPC_HANDLE_BYTES 64
+EOSLLM_CUDA_API int eosi_cuda_text_ipc_handle(eosi_cuda_text_t *t, void *out, size_t cap);
+EOSLLM_CUDA_API int eosi_cuda_text_attach_peers(eosi_cuda_text_t *t, const void *handles, size_t bytes);
+/* This rank's slice of the model (host only, no GPU needed): out[9] =
+ * {head_dim, head0, heads, kv_head0, kv_heads, ff0, ff_len, vocab0,
+ * vocab_len}. */
+EOSLLM_CUDA_API int eosi_cuda_text_partition(const eosi_cuda_llama_t *m, int rank, int world, uint32_t *out);
 /* The decoder's cudaStream_t (as void*), for timing with events. */
 EOSLLM_CUDA_API void *eosi_cuda_text_stream(eosi_cuda_text_t *t);
 EOSLLM_CUDA_API void eosi_cuda_text_close(eosi_cuda_text_t *t);

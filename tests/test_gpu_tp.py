@@ -1,0 +1,92 @@
+"""Tensor-parallel decoder on two GPUs (one child process per GPU, gloo for
+the host-side handle exchange; the data path is the decoder's own peer
+reads over NVLink).  Logits of rank-synchronous steps and a greedy
+generation are checked against the decoder oracle; both ranks must pick the
+same tokens.  Skipped on machines with fewer than two GPUs."""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+CASES = [dict(n_embd=512, n_head=4, n_kv_head=2, n_ff=768, n_vocab=1000, n_layer=2),
+         dict(n_embd=512, n_head=8, n_kv_head=2, n_ff=512, n_vocab=77, n_layer=2, wdtype=32, out_dtype=32),
+         dict(n_embd=4096, n_head=32, n_kv_head=32, n_ff=11008, n_vocab=512, n_layer=1, seed=9)]
+
+
+def _tp_worker(rank: int, world: int, port: int, kw: dict, tokens, prompt, n_gen: int, q) -> None:
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.cuda.set_device(rank)
+        from oracle.llama import make_llama
+        from oracle.oracle import Oracle
+        from eosllm_b200.text import TextDecoder
+        model = make_llama(Oracle(), max_ctx=96, **kw)
+        dec = TextDecoder(model, device=rank, rank=rank, world=world)
+        dec.connect()
+        logits = []
+        for t in tokens:
+            dist.barrier()
+            logits.append(dec.step(int(t)))
+        dist.barrier()
+        dec.reset()
+        dist.barrier()
+        picks = dec.generate(prompt, n_gen)
+        all_picks = [None] * world
+        dist.all_gather_object(all_picks, picks.tolist())
+        dist.barrier()
+        dec.close()
+        q.put((rank, np.stack(logits), all_picks))
+    except Exception as e:  # report, never hang the parent
+        q.put((rank, None, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kw", CASES)
+def test_two_gpu_decoder_matches_oracle(gpu, oracle, kw):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from oracle.llama import OracleDecoder, make_llama
+    from test_gpu_decoder import ENVELOPE_FACTOR, LOGIT_TOL, envelope_check, pick_agrees
+    world = 2
+    rng = np.random.default_rng(21)
+    tokens = rng.integers(0, kw["n_vocab"], 40)
+    prompt = rng.integers(0, kw["n_vocab"], 30)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + os.getpid() % 300
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, kw, tokens, prompt, 20, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, lg, picks = q.get(timeout=600)
+        res[r] = (lg, picks)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(world):
+        assert res[r][0] is not None, res[r][1]
+    np.testing.assert_array_equal(res[0][0].view(np.uint32), res[1][0].view(np.uint32))  # same logits on both ranks
+    picks = res[0][1]
+    assert picks[0] == picks[1]  # both ranks generated the same tokens
+    model = make_llama(oracle, max_ctx=96, **kw)
+    it = iter(res[0][0])
+    _, e_env = envelope_check(oracle, model, tokens, lambda t: next(it))
+    band = max(LOGIT_TOL, ENVELOPE_FACTOR * max(e_env))
+    od = OracleDecoder(oracle, model)
+    logits = None
+    for t in prompt:
+        logits = od.step(int(t))
+    for j, p in enumerate(picks[0]):
+        assert pick_agrees(logits, int(p), band), (j, p)
+        if j + 1 < len(picks[0]):
+            logits = od.step(int(p))
+    od.close()
