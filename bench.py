@@ -70,8 +70,9 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    p.add_argument("--workload", choices=["all", "sweep", "decode"], default="all",
-                   help="sweep: the GEMV sweep line only; decode: the 7B decode line only")
+    p.add_argument("--workload", choices=["all", "sweep", "decode", "prefill"], default="all",
+                   help="sweep: the GEMV sweep line only; decode: the 7B decode line; prefill: the GEMM line")
+    p.add_argument("--no-prefill", action="store_true", help="skip the tensor-core prefill measurement")
     p.add_argument("--no-decode", action="store_true", help="skip the 7B-shape decode measurement")
     p.add_argument("--decode-prompt", type=int, default=512)
     p.add_argument("--decode-gen", type=int, default=256)
@@ -311,6 +312,17 @@ def run_ours(args):
     if B.load().eosi_cuda_probe() != 0:
         raise SystemExit(f"CUDA backend unavailable: {B.last_error()}")
     B.set_devices([local])
+    if args.workload == "prefill":
+        d = run_prefill(args, dev)
+        if rank == 0:
+            line = dict(d, n_gpus=world, steps=20, warmup=3, ms_per_step=d["per_m"][str(PREFILL_M[-1])]["ms"],
+                        higher_is_better=True, scaling="weak", vs_baseline=None, dtype="bf16x3 (int8-exact operands)",
+                        data="synthetic", gpu_launches=2 * 20 * len(PREFILL_M),
+                        config={"workload": "q4k_prefill_gemm", "m": list(PREFILL_M), "n": PREFILL_NK[0],
+                                "k": PREFILL_NK[1]})
+            print(json.dumps(line), flush=True)
+        dist_done(world)
+        return
     if args.workload == "decode":
         d = run_decode(args, dev, world, rank)
         if rank == 0:
@@ -461,6 +473,10 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_seconds)
 
+    prefill = None
+    if args.workload == "all" and not args.no_prefill:
+        prefill = run_prefill(args, dev)
+
     decode = None
     if args.workload == "sweep":
         pass
@@ -494,12 +510,73 @@ def run_ours(args):
             "gpu_launches": args.steps * (len(ks) + len(SHAPES)),
             "clocks": clocks.summary(),
             "decode_7b": decode,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     dist_done(world)
 
 
 LLAMA_7B = dict(n_embd=4096, n_layer=32, n_head=32, n_kv_head=32, n_ff=11008, n_vocab=32000)
+PREFILL_M = (128, 512, 2048)
+PREFILL_NK = (11008, 4096)
+
+
+def measured_bf16_peak():
+    """Dense bf16 TFLOP/s measured on this pool (burst), else the fallback."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        for key in ("bf16_tflops", "bf16_dense_tflops"):
+            if key in d:
+                return float(d[key]), "measured"
+    except (OSError, ValueError):
+        pass
+    return 1590.0, "fallback"
+
+
+def run_prefill(args, dev, reps: int = 20) -> dict:
+    """Q4_K W [11008 x 4096] (~N(0,0.02), seed 2) times A [M x 4096]
+    (~N(0,1)) for M in 128/512/2048 on the tensor cores.  Weights are split
+    into the bf16 hi/lo prefill copy once (as for a loaded model); each timed
+    call packs and splits the activations and runs the GEMM.  FLOPs = 2 M N K
+    (the product once; the kernel issues three bf16 MMAs per product, so
+    the tensor pipe does 3x that)."""
+    import torch
+
+    from eosllm_b200 import backend as B
+    n, k = PREFILL_NK
+    w = torch.empty(q4k_bytes(n, k), dtype=torch.uint8, device=dev)
+    B.q4_k_from_gauss_dev(w, n * k, seed=2, sigma=0.02)
+    whi = torch.empty(n * k, dtype=torch.bfloat16, device=dev)
+    wlo = torch.empty_like(whi)
+    B.prefill_split_weights_dev(w, n, k, whi, wlo)
+    peak, peak_kind = measured_bf16_peak()
+    out = {"metric": "Q4_K prefill GEMM TFLOP/s (tcgen05, N=11008 K=4096)", "unit": "TFLOP/s",
+           "peak_bf16_tflops": peak, "peak_kind": peak_kind, "per_m": {}}
+    st = torch.cuda.current_stream().cuda_stream
+    for m in PREFILL_M:
+        a = torch.empty((m, k), dtype=torch.float32, device=dev)
+        B.fill_gauss_dev(a, m * k, 1000 + m, 0, 1.0)
+        scratch = torch.empty(B.prefill_scratch_bytes(m, k), dtype=torch.uint8, device=dev)
+        c = torch.empty((m, n), dtype=torch.float32, device=dev)
+        for _ in range(3):
+            B.prefill_dev(a, whi, wlo, c, m, n, k, scratch, st)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            B.prefill_dev(a, whi, wlo, c, m, n, k, scratch, st)
+        e1.record()
+        torch.cuda.synchronize()
+        if B.take_device_errors() != 0:
+            raise SystemExit("prefill: device-side bounded wait reported an error")
+        ms = e0.elapsed_time(e1) / reps
+        tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
+        out["per_m"][str(m)] = {"ms": round(ms, 4), "tflops": round(tf, 1),
+                                "tensor_pipe_tflops": round(3 * tf, 1),
+                                "tensor_frac": round(3 * tf / peak, 4)}
+    out["value"] = out["per_m"][str(PREFILL_M[-1])]["tflops"]
+    return out
 
 
 def run_decode(args, dev, world, rank) -> dict:

@@ -75,6 +75,10 @@ _SIGNATURES = {
     "eosi_cuda_take_device_errors": (C.c_int, [C.POINTER(C.c_uint32)]),
     "eosi_cuda_set_kernel_variant": (C.c_int, [C.c_int, C.c_int]),
     "eosi_cuda_matmul_q4_k_noalloc": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "eosi_cuda_q4_k_prefill_weight_bytes": (_sz, [_u32, _u32]),
+    "eosi_cuda_q4_k_prefill_scratch_bytes": (_sz, [_u32, _u32]),
+    "eosi_cuda_q4_k_prefill_split_weights_dev": (C.c_int, [_vp, _u32, _u32, _vp, _vp, _vp]),
+    "eosi_cuda_q4_k_prefill_dev": (C.c_int, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp]),
     "eosi_cuda_text_open": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
     "eosi_cuda_text_step": (C.c_int, [_vp, _u32, _vp]),
     "eosi_cuda_text_generate": (C.c_int, [_vp, _vp, _u32, _u32, _vp]),
@@ -255,3 +259,24 @@ def weight_bytes(dtype: int, n: int, k: int) -> int:
     if dtype == DT_Q8_0:
         return n * (k // 32) * 34
     raise ValueError(dtype)
+
+
+# ---------------------------------------------------------------------------
+# Tensor-core prefill
+# ---------------------------------------------------------------------------
+def prefill_weight_bytes(n: int, k: int) -> int:
+    return int(load().eosi_cuda_q4_k_prefill_weight_bytes(n, k))
+
+
+def prefill_scratch_bytes(m: int, k: int) -> int:
+    return int(load().eosi_cuda_q4_k_prefill_scratch_bytes(m, k))
+
+
+def prefill_split_weights_dev(w, n, k, w_hi, w_lo, stream=0) -> None:
+    check(load().eosi_cuda_q4_k_prefill_split_weights_dev(_ptr(w), n, k, _ptr(w_hi), _ptr(w_lo), stream or None),
+          "eosi_cuda_q4_k_prefill_split_weights_dev")
+
+
+def prefill_dev(a, w_hi, w_lo, c, m, n, k, scratch, stream=0) -> None:
+    check(load().eosi_cuda_q4_k_prefill_dev(_ptr(a), _ptr(w_hi), _ptr(w_lo), _ptr(c), m, n, k, _ptr(scratch),
+                                            stream or None), "eosi_cuda_q4_k_prefill_dev")

@@ -181,6 +181,25 @@ EOSLLM_CUDA_API int eosi_cuda_fill_gauss_dev(float *dst, size_t n, uint64_t seed
 EOSLLM_CUDA_API int eosi_cuda_q4_k_from_gauss_dev(void *dst, size_t n_elements, uint64_t seed, float sigma,
                                   void *stream);
 
+/* ---- tensor-core prefill (m > 1) ----------------------------------------------
+ * C[m,n] = A[m,k] . deq(W)[n,k]^T on the sm_100a tensor cores (tcgen05): no
+ * counterpart in the reference, which processes a prompt one token at a time
+ * through the same int8 kernel (src/core/session.c:231-236).  Activations
+ * are packed exactly as quantize_sub32 (matmul_q4_k_int8.c:98-154) does,
+ * weights dequantized as (d*sc)*q - dmin*m; both are split into bf16 hi+lo
+ * parts and multiplied as hi*hi + lo*hi + hi*lo with f32 accumulation, so C
+ * agrees with eosi_cuda_matmul_q4_k (the int8 reference) to ~1e-5 relative
+ * (not bit for bit).  Weights are split once (a resident prefill copy of
+ * 2 * eosi_cuda_q4_k_prefill_weight_bytes bytes); each call needs
+ * eosi_cuda_q4_k_prefill_scratch_bytes of scratch.  All pointers device,
+ * 16-byte aligned; k % 256 == 0. */
+EOSLLM_CUDA_API size_t eosi_cuda_q4_k_prefill_weight_bytes(uint32_t n, uint32_t k);
+EOSLLM_CUDA_API size_t eosi_cuda_q4_k_prefill_scratch_bytes(uint32_t m, uint32_t k);
+EOSLLM_CUDA_API int eosi_cuda_q4_k_prefill_split_weights_dev(const void *w, uint32_t n, uint32_t k, void *w_hi,
+                                                             void *w_lo, void *stream);
+EOSLLM_CUDA_API int eosi_cuda_q4_k_prefill_dev(const float *a, const void *w_hi, const void *w_lo, float *c,
+                                               uint32_t m, uint32_t n, uint32_t k, void *scratch, void *stream);
+
 /* ---- device-resident Llama decoder ------------------------------------------
  * The work of eosi_text_open / eosi_text_step / eosi_text_close
  * (src/modality/text/text.h:62-78, text.c:131-436 of the reference) with
