@@ -71,12 +71,13 @@ struct NormPackParams {
   uint32_t n;
   uint8_t* act;     // Q4_K consumers: packed records for k = n
   float* act_f32;   // Q8_0 consumers: the normalised vector
-  // tensor parallel: before reading parts[], announce this rank's partial
-  // (own_flag = epoch) and wait for every rank's flag (bounded)
+  // tensor parallel: before reading parts[] (this rank's receive slots, one
+  // per source rank, filled by the sources' GEMVs), announce this rank's
+  // partial in every rank's flag slot and wait for every source's flag
   uint32_t world;
-  uint32_t* own_flag;
-  const uint32_t* rank_flag[kMaxParts];
-  uint32_t xchg;          // exchange index within the step
+  uint32_t* pub_flag[kMaxParts];  // flag slot of this rank at rank q (IPC-mapped; own local)
+  const uint32_t* wait_flag;      // this rank's slots [q], q < world
+  uint32_t xchg;                  // exchange index within the step
   uint32_t xchg_per_step;
 };
 
@@ -89,22 +90,26 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-// Tensor-parallel handshake of exchange `epoch`: thread 0 of CTA 0 publishes
-// this rank's flag after a system-scope fence (the partial it announces was
-// written by the previous kernel, complete at the PDL wait); threads t < world
-// wait for rank t's flag (bounded: EOS_DEVERR_PEER after EOS_WAIT_LIMIT_NS).
+// Tensor-parallel handshake of exchange `epoch`: thread 0 of the publishing
+// CTA raises this rank's flag in every rank's receive words with release
+// stores after a system-scope fence.  What it announces -- partial sums the
+// previous GEMV pushed into the peers' receive slots (that grid completed
+// before this kernel's griddepcontrol.wait returned), or values this CTA
+// wrote -- is then visible to a peer that acquires the flag;
+// threads t < world wait for source t's flag in this rank's own words
+// (local polling; bounded: EOS_DEVERR_PEER after EOS_WAIT_LIMIT_NS).
 // Returns false when a wait ran out.
-__device__ __forceinline__ bool xchg_sync(uint32_t world, uint32_t* own_flag, const uint32_t* const* rank_flag,
+__device__ __forceinline__ bool xchg_sync(uint32_t world, uint32_t* const* pub_flag, const uint32_t* wait_flag,
                                           uint32_t epoch, uint32_t* err, bool publish) {
   __shared__ uint32_t s_ok;
   if (threadIdx.x == 0) s_ok = 1u;
   if (publish && threadIdx.x == 0) {
     __threadfence_system();
-    st_release_sys(own_flag, epoch);
+    for (uint32_t q = 0; q < world; ++q) st_release_sys(pub_flag[q], epoch);
   }
   __syncthreads();
   if (threadIdx.x < world) {
-    const uint32_t* f = rank_flag[threadIdx.x];
+    const uint32_t* f = wait_flag + threadIdx.x;
     if (ld_acquire_sys(f) < epoch) {
       const uint64_t t0 = global_timer_ns();
       while (ld_acquire_sys(f) < epoch) {
@@ -142,7 +147,7 @@ __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) 
   pdl_wait();
   if (p.world > 1 && p.nparts > 0) {
     const uint32_t epoch = p.state->epoch * p.xchg_per_step + p.xchg + 1u;
-    if (!xchg_sync(p.world, p.own_flag, p.rank_flag, epoch, const_cast<uint32_t*>(&p.state->err), blockIdx.x == 0))
+    if (!xchg_sync(p.world, p.pub_flag, p.wait_flag, epoch, const_cast<uint32_t*>(&p.state->err), blockIdx.x == 0))
       return;  // a peer never arrived: the error bit is set, outputs are invalid
   }
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
@@ -174,13 +179,13 @@ __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) 
 #pragma unroll
       for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
         const uint32_t c = tid + 256u * j;
-        if (c < nch) t[j] = __ldcv(reinterpret_cast<const float4*>(p.parts[0]) + c);
+        if (c < nch) t[j] = __ldcg(reinterpret_cast<const float4*>(p.parts[0]) + c);
       }
       for (uint32_t q = 1; q < p.nparts; ++q) {
 #pragma unroll
         for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
           const uint32_t c = tid + 256u * j;
-          if (c < nch) t[j] = add4(t[j], __ldcv(reinterpret_cast<const float4*>(p.parts[q]) + c));
+          if (c < nch) t[j] = add4(t[j], __ldcg(reinterpret_cast<const float4*>(p.parts[q]) + c));
         }
       }
 #pragma unroll
@@ -475,10 +480,11 @@ struct ArgmaxParams {
   uint32_t* part_i;
   DecState* state;
   uint32_t* out_tokens;  // [max_ctx]: pick of step pos
-  // tensor parallel: every rank's slice result, merged in rank order
+  // tensor parallel: every rank's slice result, pushed into every rank's
+  // receive words and merged in rank order
   uint32_t world, rank, v0;  // v0: global index of logits[0]
-  XFlags* own_x;
-  const XFlags* rank_x[kMaxParts];
+  XRecv* recv[kMaxParts];    // rank q's receive words (IPC-mapped; own local)
+  XRecv* own;
   uint32_t xchg, xchg_per_step;
 };
 
@@ -555,30 +561,32 @@ __global__ void __launch_bounds__(256) argmax_kernel(const ArgmaxParams p) {
   uint32_t first_nan = (p.rank == 0 && first != first) ? 1u : 0u;
   uint32_t gidx = idx == 0xffffffffu ? idx : p.v0 + idx;
   if (p.world > 1) {
-    if (threadIdx.x == 0) {
-      p.own_x->arg_v = v;
-      p.own_x->arg_i = gidx;
-      p.own_x->first_nan = first_nan;
-    }
-    const uint32_t* rf[kMaxParts];
+    uint32_t* pub[kMaxParts];
 #pragma unroll
-    for (uint32_t q = 0; q < kMaxParts; ++q) rf[q] = q < p.world ? &p.rank_x[q]->flag[2] : nullptr;
+    for (uint32_t q = 0; q < kMaxParts; ++q) pub[q] = q < p.world ? &p.recv[q]->flag[2][p.rank] : nullptr;
+    if (threadIdx.x == 0) {  // push this slice's result into every rank's words
+      for (uint32_t q = 0; q < p.world; ++q) {
+        p.recv[q]->arg_v[p.rank] = v;
+        p.recv[q]->arg_i[p.rank] = gidx;
+        if (p.rank == 0) p.recv[q]->first_nan = first_nan;
+      }
+    }
     const uint32_t epoch = p.state->epoch * p.xchg_per_step + p.xchg + 1u;
-    if (!xchg_sync(p.world, &p.own_x->flag[2], rf, epoch, &p.state->err, true)) return;
+    if (!xchg_sync(p.world, pub, &p.own->flag[2][0], epoch, &p.state->err, true)) return;
     if (threadIdx.x == 0) {
       v = __int_as_float(0x7fc00000);
       gidx = 0xffffffffu;
+      const volatile XRecv* x = p.own;
       for (uint32_t q = 0; q < p.world; ++q) {  // rank order = vocabulary order
-        (void)ld_acquire_sys(rf[q]);
-        const volatile XFlags* x = p.rank_x[q];
-        const float qv = x->arg_v;
-        const uint32_t qi = x->arg_i;
-        if (q == 0) first_nan = x->first_nan;
+        (void)ld_acquire_sys(&p.own->flag[2][q]);
+        const float qv = x->arg_v[q];
+        const uint32_t qi = x->arg_i[q];
         if (arg_better(qv, qi, v, gidx)) {
           v = qv;
           gidx = qi;
         }
       }
+      first_nan = x->first_nan;
     }
   }
   if (threadIdx.x == 0) {
@@ -660,12 +668,16 @@ struct TextDecoder {
   uint32_t* out_tokens = nullptr;
   uint32_t* gemv_err = nullptr;
   uint32_t arg_blocks = 0;
-  // exchange buffer: this rank's O and down partials, logits slice and
-  // handshake words; the other ranks read it through CUDA IPC mappings
+  // exchange buffer: receive slots [source rank][n_embd] for the O and down
+  // partials, this rank's logits slice and its receive words; the other
+  // ranks write (push) into it through CUDA IPC mappings
   uint8_t* xbuf = nullptr;
   size_t xoff_po = 0, xoff_pd = 0, xoff_lg = 0, xoff_fl = 0, xbytes = 0;
   uint8_t* xpeer[kMaxParts] = {};  // every rank's exchange buffer (own included)
   bool peer_opened[kMaxParts] = {};
+  float* push_o[kMaxParts] = {};   // where this rank's O partial goes on the other ranks
+  float* push_d[kMaxParts] = {};
+  uint32_t n_push = 0;
   cudaGraphExec_t graph = nullptr;
   uint32_t host_pos = 0;
   bool step_mode = false;  // prompt[] holds every fed token (n_prompt = max_ctx)
@@ -706,8 +718,7 @@ struct TextDecoder {
 
   int open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws);
   int attach(const uint8_t* handles);
-  const XFlags* xflags(int q) const { return reinterpret_cast<const XFlags*>(xpeer[q] + xoff_fl); }
-  XFlags* own_flags() const { return reinterpret_cast<XFlags*>(xbuf + xoff_fl); }
+  XRecv* xrecv(int q) const { return reinterpret_cast<XRecv*>(xpeer[q] + xoff_fl); }
   cudaError_t record_step(cudaStream_t s);
   int capture();
 };
@@ -833,13 +844,13 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
     const uint32_t vmax = (m.n_vocab + ws - 1) / ws + 1;
     auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
     xoff_po = 0;
-    xoff_pd = up(4ull * E);
-    xoff_lg = xoff_pd + up(4ull * E);
+    xoff_pd = up(4ull * E * ws);
+    xoff_lg = xoff_pd + up(4ull * E * ws);
     xoff_fl = xoff_lg + up(4ull * vmax);
-    xbytes = xoff_fl + up(sizeof(XFlags));
+    xbytes = xoff_fl + up(sizeof(XRecv));
     chk(alloc(&xbuf, xbytes));
-    part_o = reinterpret_cast<float*>(xbuf + xoff_po);
-    part_d = reinterpret_cast<float*>(xbuf + xoff_pd);
+    part_o = reinterpret_cast<float*>(xbuf + xoff_po) + (size_t)E * rk;  // own slot
+    part_d = reinterpret_cast<float*>(xbuf + xoff_pd) + (size_t)E * rk;
     logits = reinterpret_cast<float*>(xbuf + xoff_lg);
     xpeer[rk] = xbuf;
   }
@@ -896,6 +907,13 @@ int TextDecoder::attach(const uint8_t* handles) {
     xpeer[q] = static_cast<uint8_t*>(ptr);
     peer_opened[q] = true;
   }
+  n_push = 0;
+  for (int q = 0; q < world; ++q) {
+    if (q == rank) continue;
+    push_o[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_po) + (size_t)m.n_embd * rank;
+    push_d[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_pd) + (size_t)m.n_embd * rank;
+    ++n_push;
+  }
   return capture();
 }
 
@@ -905,12 +923,15 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
   const uint32_t nqkv = hl * hd + 2 * kvl * hd;
   cudaError_t e = cudaSuccess;
   int status = EOS_OK;
+  // push: the O and down partials also go straight into the other ranks'
+  // receive slots (tensor parallel)
   auto gemv = [&](int dt, const uint8_t* w, const uint8_t* act, const float* actf, float* c, uint32_t n,
-                  uint32_t k) -> cudaError_t {
+                  uint32_t k, float* const* extra = nullptr, uint32_t n_extra = 0) -> cudaError_t {
     if (n == 0) return cudaSuccess;
-    if (dt == EOS_DT_Q4_K) return launch_q4k_gemv(w, act, nullptr, c, n, k, gemv_err, num_sms, max_smem, true, s,
-                                                  &status);
-    return launch_q80_gemv(w, actf, c, n, k, gemv_err, num_sms, max_smem, s, &status);
+    if (dt == EOS_DT_Q4_K)
+      return launch_q4k_gemv(w, act, nullptr, c, n, k, gemv_err, num_sms, max_smem, true, s, &status, extra,
+                             n_extra);
+    return launch_q80_gemv(w, actf, c, n, k, gemv_err, num_sms, max_smem, s, &status, extra, n_extra);
   };
   const uint32_t xps = 2u * m.n_layer + 1u;  // exchanges per step
   // `part`: nullptr (no partial), part_o or part_d; xk: exchange index
@@ -921,12 +942,13 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
     p.nparts = 0;
     if (part != nullptr) {
       const size_t off = part == part_o ? xoff_po : xoff_pd;
+      const uint32_t type = part == part_o ? 0u : 1u;
       p.nparts = (uint32_t)world;
       for (int q = 0; q < world; ++q) {
-        p.parts[q] = reinterpret_cast<const float*>(xpeer[q] + off);
-        p.rank_flag[q] = &reinterpret_cast<const XFlags*>(xpeer[q] + xoff_fl)->flag[part == part_o ? 0 : 1];
+        p.parts[q] = reinterpret_cast<const float*>(xbuf + off) + (size_t)E * q;  // local slot of source q
+        p.pub_flag[q] = &xrecv(q)->flag[type][rank];
       }
-      p.own_flag = &own_flags()->flag[part == part_o ? 0 : 1];
+      p.wait_flag = &xrecv(rank)->flag[type][0];
     }
     p.world = (uint32_t)world;
     p.xchg = xk;
@@ -974,14 +996,14 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
       else if (hd == 128) e = launch_pdl_smem(attn_kernel<4>, grid, dim3(128), sm, s, a);
       else e = launch_pdl_smem(attn_kernel<8>, grid, dim3(128), sm, s, a);
     }
-    if (e == cudaSuccess) e = gemv(wdt, d.wo, act_o, actf_o, part_o, E, hl * hd);
+    if (e == cudaSuccess) e = gemv(wdt, d.wo, act_o, actf_o, part_o, E, hl * hd, push_o, n_push);
     // x0 = x1 + O partial; act_e = pack(rmsnorm(x0))
     if (e == cudaSuccess) e = norm_pack(x1, part_o, x0, d.ffn_norm, wdt, wdt, 2u * L);
     if (e == cudaSuccess) e = gemv(wdt, d.wgu, act_e, actf_e, gu, 2 * ffl, E);
     if (e == cudaSuccess)
       e = launch_pdl(silu_pack_kernel, dim3((ffl + 255u) / 256u), dim3(256), s, (const float*)gu, ffl, act_d,
                      actf_d);
-    if (e == cudaSuccess) e = gemv(wdt, d.wd, act_d, actf_d, part_d, E, ffl);
+    if (e == cudaSuccess) e = gemv(wdt, d.wd, act_d, actf_d, part_d, E, ffl, push_d, n_push);
   }
   // final norm + LM head + greedy pick (text.c:425-432, greedy.c:66-69)
   if (e == cudaSuccess)
@@ -999,8 +1021,8 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
     a.world = (uint32_t)world;
     a.rank = (uint32_t)rank;
     a.v0 = v0;
-    a.own_x = own_flags();
-    for (int q = 0; q < world; ++q) a.rank_x[q] = xflags(q);
+    a.own = xrecv(rank);
+    for (int q = 0; q < world; ++q) a.recv[q] = xrecv(q);
     a.xchg = 2u * m.n_layer;
     a.xchg_per_step = xps;
     e = launch_pdl(argmax_kernel, dim3(arg_blocks), dim3(256), s, a);

@@ -18,16 +18,15 @@ struct DecState {
   uint32_t pad[2];
 };
 
-// Tensor-parallel exchange words of one rank, in its exchange buffer (read by
-// the other ranks through CUDA IPC mappings).  Flag values are epochs:
-// step_epoch * (2 n_layer + 1) + exchange + 1.
-struct XFlags {
-  uint32_t flag[3];  // [0] O-projection partial ready, [1] down partial ready, [2] argmax result ready
-  uint32_t pad0;
-  float arg_v;       // this rank's best logit
-  uint32_t arg_i;    // its global vocabulary index
-  uint32_t first_nan;  // rank 0: logits[0] is NaN
-  uint32_t pad1;
+// Tensor-parallel receive words of one rank, in its exchange buffer; the
+// other ranks write them through CUDA IPC mappings (push).  Flag values are
+// epochs: step_epoch * (2 n_layer + 1) + exchange + 1.
+struct XRecv {
+  uint32_t flag[3][8];  // [0] O partial, [1] down partial, [2] argmax result; [.][q]: written by rank q
+  float arg_v[8];       // rank q's best logit
+  uint32_t arg_i[8];    // its global vocabulary index
+  uint32_t first_nan;   // from rank 0: logits[0] is NaN
+  uint32_t pad[7];
 };
 
 // One layer's resident weights (this rank's slices).

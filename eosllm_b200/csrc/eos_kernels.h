@@ -22,8 +22,13 @@ cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out
 // activations, packed inside the kernel) is non-null.  out_status: EOS_OK, or
 // EOS_E_UNSUPPORTED when the shape cannot be staged on the fused path (the
 // caller then packs separately).
+// c_extra / n_extra (<= 7): further destinations of every output, written
+// after c (tensor-parallel push into other GPUs' IPC-mapped buffers; visible
+// to them once the grid has completed); not supported by the unstaged
+// fallback.
 cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
-                            uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status);
+                            uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status,
+                            float* const* c_extra = nullptr, uint32_t n_extra = 0);
 void set_q4k_gemv_variant(int v);
 // n < 4 Q4_K: the reference's f32-dequant path, bit for bit.
 cudaError_t launch_q4k_f32_small_n(const float* a, const uint8_t* w, float* c, uint32_t m, uint32_t n, uint32_t k,
@@ -36,7 +41,8 @@ cudaError_t launch_prefill_gemm(const void* a_hi, const void* a_lo, const void* 
                                 uint32_t m, uint32_t n, uint32_t k, uint32_t* err, cudaStream_t st, int* out_status);
 
 cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t n, uint32_t k, uint32_t* err,
-                            int num_sms, int max_smem, cudaStream_t st, int* out_status);
+                            int num_sms, int max_smem, cudaStream_t st, int* out_status,
+                            float* const* c_extra = nullptr, uint32_t n_extra = 0);
 void set_q80_gemv_variant(int v);
 
 // Test/utility kernels (eos_util.cu).

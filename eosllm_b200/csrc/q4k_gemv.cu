@@ -111,7 +111,22 @@ struct Q4kGemvParams {
   float* c;            // n outputs
   uint32_t n, k, nb, row_bytes, pitch, R, act_bytes;
   uint32_t* err;
+  // further copies of every output (tensor-parallel push: other GPUs'
+  // receive buffers, mapped through CUDA IPC), written after c
+  float* c_extra[7];
+  uint32_t n_extra;
 };
+
+// c[r] = v and the same value into every extra destination (other GPUs'
+// receive slots, plain stores over NVLink).  No fence here: the consumer
+// learns of the rows through a flag that a later kernel raises after this
+// grid has completed (griddepcontrol.wait) and after its own system-scope
+// fence, and a grid's stores -- remote ones included -- are performed when
+// it completes.  (A fence per writing thread measured ~9 us per exchange.)
+__device__ __forceinline__ void gemv_store(const Q4kGemvParams& p, uint32_t r, float v) {
+  p.c[r] = v;
+  for (uint32_t j = 0; j < p.n_extra; ++j) p.c_extra[j][r] = v;
+}
 
 template <int NW, int D>
 __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParams p) {
@@ -203,7 +218,7 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParam
         }
       }
       for (; b < nb; ++b) acc = __fadd_rn(acc, pr[b]);
-      p.c[r0 + s * R + lane] = acc;
+      gemv_store(p, r0 + s * R + lane, acc);
     }
     __syncwarp();  // partial buffer free for the next stage
   }
@@ -294,7 +309,7 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_cols_kernel(const Q4kGemv
         for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v8[j]);
       }
       for (; b < nb; ++b) acc = __fadd_rn(acc, pr[b]);
-      p.c[r0 + s * R + lane] = acc;
+      gemv_store(p, r0 + s * R + lane, acc);
     }
     __syncwarp();
   }
@@ -380,7 +395,12 @@ void set_q4k_gemv_variant(int v) {
 }
 
 cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
-                            uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status) {
+                            uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status,
+                            float* const* c_extra, uint32_t n_extra) {
+  if (n_extra > 7) {
+    *out_status = EOS_E_INVALID_ARG;
+    return cudaSuccess;
+  }
   *out_status = EOS_OK;
   if (n == 0) return cudaSuccess;
   const uint32_t nb = k / Q4K_ELEMS;
@@ -425,7 +445,7 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   geom(cfg, R, pitch);
   const uint32_t smem = smem_of(cfg);
   if (smem > (uint32_t)max_smem) {  // rows too long to stage: unstaged kernel
-    if (act == nullptr) {           // it reads packed activations from global memory
+    if (act == nullptr || n_extra != 0) {  // it reads packed activations, writes one destination
       *out_status = EOS_E_UNSUPPORTED;
       return cudaSuccess;
     }
@@ -444,7 +464,8 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   uint32_t grid = (uint32_t)num_sms * cps;
   const uint32_t max_grid = (n + R - 1) / R;
   if (grid > max_grid) grid = max_grid;
-  Q4kGemvParams prm{w, act, a, c, n, k, nb, row_bytes, pitch, R, act_bytes, err};
+  Q4kGemvParams prm{w, act, a, c, n, k, nb, row_bytes, pitch, R, act_bytes, err, {}, n_extra};
+  for (uint32_t j = 0; j < n_extra; ++j) prm.c_extra[j] = c_extra[j];
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
   lc.blockDim = dim3(cfg.nw * 32);

@@ -78,6 +78,8 @@ struct Q80GemvParams {
   uint32_t n, k, nblk, row_bytes, pitch;
   uint32_t cb, chunks;  // blocks per chunk (multiple of 8), chunks per row
   uint32_t* err;
+  float* c_extra[7];  // further copies of every output (tensor-parallel push)
+  uint32_t n_extra;
 };
 
 // Four signed bytes -> two float2 of exact values: 2^23 + (b + 128) built by
@@ -186,7 +188,12 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
       acc += __shfl_xor_sync(0xffffffffu, acc, 4);
       acc += __shfl_xor_sync(0xffffffffu, acc, 2);
       acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-      if (lane == 0) p.c[r0 + row] = acc;
+      if (lane == 0) {
+        p.c[r0 + row] = acc;
+        // extra destinations: plain remote stores, ordered before the
+        // consumer's flag by grid completion (see gemv_store, q4k_gemv.cu)
+        for (uint32_t j = 0; j < p.n_extra; ++j) p.c_extra[j][r0 + row] = acc;
+      }
       acc = 0.0f;
       ch = 0;
       row += NW;
@@ -211,7 +218,12 @@ int g_q80_variant = -1;
 void set_q80_gemv_variant(int v) { g_q80_variant = v; }
 
 cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t n, uint32_t k, uint32_t* err,
-                            int num_sms, int max_smem, cudaStream_t st, int* out_status) {
+                            int num_sms, int max_smem, cudaStream_t st, int* out_status, float* const* c_extra,
+                            uint32_t n_extra) {
+  if (n_extra > 7) {
+    *out_status = EOS_E_INVALID_ARG;
+    return cudaSuccess;
+  }
   *out_status = EOS_OK;
   if (n == 0) return cudaSuccess;
   const uint32_t nblk = k / Q80_ELEMS;
@@ -237,6 +249,10 @@ cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t
   }
   if (!aligned || pick < 0 ||
       act_region + (uint32_t)(g_q80_cfgs[pick].nw * g_q80_cfgs[pick].d) * pitch > (uint32_t)max_smem) {
+    if (n_extra != 0) {  // the unstaged kernel writes one destination
+      *out_status = EOS_E_UNSUPPORTED;
+      return cudaSuccess;
+    }
     q80_gemv_simple_kernel<<<(n + 7u) / 8u, 256, 0, st>>>(w, a, c, n, k);
     return cudaGetLastError();
   }
@@ -252,7 +268,8 @@ cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t
   if (cps < 1u) cps = 1u;
   uint32_t grid = (uint32_t)num_sms * cps;
   if (grid > n) grid = n;
-  Q80GemvParams prm{w, a, c, n, k, nblk, row_bytes, pitch, cb, chunks, err};
+  Q80GemvParams prm{w, a, c, n, k, nblk, row_bytes, pitch, cb, chunks, err, {}, n_extra};
+  for (uint32_t j = 0; j < n_extra; ++j) prm.c_extra[j] = c_extra[j];
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
   lc.blockDim = dim3(cfg.nw * 32);
