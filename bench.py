@@ -535,37 +535,42 @@ def measured_bf16_peak():
 
 
 def run_prefill(args, dev, reps: int = 20) -> dict:
-    """Q4_K W [11008 x 4096] (~N(0,0.02), seed 2) times A [M x 4096]
-    (~N(0,1)) for M in 128/512/2048 on the tensor cores.  Weights are split
-    into the bf16 hi/lo prefill copy once (as for a loaded model); each timed
-    call packs and splits the activations and runs the GEMM.  FLOPs = 2 M N K
-    (the product once; the kernel issues three bf16 MMAs per product, so
-    the tensor pipe does 3x that)."""
+    """Q4_K W [11008 x 4096] (~N(0,0.02), seed 2) times A [M x 4096] (~N(0,1))
+    for M in 128/512/2048 on the tensor cores, bit-exact with the int8
+    reference.  Weights are prepared once (as for a loaded model); each timed
+    call packs the activations and runs the GEMM.  FLOPs = 2 M N K.  The
+    kernel's bound is its epilogue: per output and 32-element sub-block it
+    applies the reference's rescale (7 f32 operations: convert, 4 multiplies,
+    subtract, add) on the CUDA cores, against one int8 MMA on the tensor
+    pipe; `epilogue_frac` compares those operations per second with the
+    f32 issue rate (148 SMs x 128 lanes x the sampled SM clock)."""
     import torch
 
     from eosllm_b200 import backend as B
     n, k = PREFILL_NK
     w = torch.empty(q4k_bytes(n, k), dtype=torch.uint8, device=dev)
     B.q4_k_from_gauss_dev(w, n * k, seed=2, sigma=0.02)
-    whi = torch.empty(n * k, dtype=torch.bfloat16, device=dev)
-    wlo = torch.empty_like(whi)
-    B.prefill_split_weights_dev(w, n, k, whi, wlo)
+    wprep = torch.empty(B.prefill_weight_bytes(n, k), dtype=torch.uint8, device=dev)
+    B.prefill_prepare_weights_dev(w, n, k, wprep)
     peak, peak_kind = measured_bf16_peak()
-    out = {"metric": "Q4_K prefill GEMM TFLOP/s (tcgen05, N=11008 K=4096)", "unit": "TFLOP/s",
+    props = torch.cuda.get_device_properties(dev)
+    out = {"metric": "Q4_K prefill GEMM TFLOP/s (tcgen05 kind::i8, bit-exact, N=11008 K=4096)", "unit": "TFLOP/s",
            "peak_bf16_tflops": peak, "peak_kind": peak_kind, "per_m": {}}
     st = torch.cuda.current_stream().cuda_stream
+    clocks = ClockSampler(dev.index)
+    clocks.start()
     for m in PREFILL_M:
         a = torch.empty((m, k), dtype=torch.float32, device=dev)
         B.fill_gauss_dev(a, m * k, 1000 + m, 0, 1.0)
         scratch = torch.empty(B.prefill_scratch_bytes(m, k), dtype=torch.uint8, device=dev)
         c = torch.empty((m, n), dtype=torch.float32, device=dev)
         for _ in range(3):
-            B.prefill_dev(a, whi, wlo, c, m, n, k, scratch, st)
+            B.prefill_dev(a, wprep, c, m, n, k, scratch, st)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         e0.record()
         for _ in range(reps):
-            B.prefill_dev(a, whi, wlo, c, m, n, k, scratch, st)
+            B.prefill_dev(a, wprep, c, m, n, k, scratch, st)
         e1.record()
         torch.cuda.synchronize()
         if B.take_device_errors() != 0:
@@ -573,8 +578,15 @@ def run_prefill(args, dev, reps: int = 20) -> dict:
         ms = e0.elapsed_time(e1) / reps
         tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
         out["per_m"][str(m)] = {"ms": round(ms, 4), "tflops": round(tf, 1),
-                                "tensor_pipe_tflops": round(3 * tf, 1),
-                                "tensor_frac": round(3 * tf / peak, 4)}
+                                "epilogue_gops": round(7.0 * m * n * (k // 32) / (ms * 1e-3) / 1e9, 1)}
+    clocks.stop()
+    cs = clocks.summary()
+    mhz = cs["sm_mhz"] or cs["sm_max_mhz"] or 1965
+    f32_rate = props.multi_processor_count * 128 * mhz * 1e6 / 1e9  # G operations / s
+    for v in out["per_m"].values():
+        v["epilogue_frac"] = round(v["epilogue_gops"] / f32_rate, 4)
+    out["f32_issue_gops"] = round(f32_rate, 1)
+    out["clocks"] = cs
     out["value"] = out["per_m"][str(PREFILL_M[-1])]["tflops"]
     return out
 
@@ -596,7 +608,7 @@ def run_decode(args, dev, world, rank) -> dict:
     model = synthetic_llama(**cfg, seed=4, device=dev.index)
     dec = TextDecoder(model, device=dev.index, rank=rank, world=world)
     if world > 1:
-        dec.connect()  # IPC handles all-gathered over the process group; data path: peer reads over NVLink
+        dec.connect()  # IPC handles all-gathered over the process group; data path: GEMV pushes over NVLink
     host_model = None
     if rank == 0 and world == 1 and args.decode_cpu_steps > 0 and not args.no_cpu_baseline:
         host_model = dict(config=model["config"], tok_embd=model["tok_embd"].cpu().numpy().view(np.uint16),
@@ -606,7 +618,7 @@ def run_decode(args, dev, world, rank) -> dict:
     torch.cuda.empty_cache()
     prompt = np.random.default_rng(4).integers(0, cfg["n_vocab"], P).astype(np.uint32)
     st = torch.cuda.ExternalStream(dec.stream, device=dev)
-    dec.generate(prompt[:16], 8)  # warm-up: graph upload, first-touch
+    dec.generate(prompt[:64], 8)  # warm-up: graph upload, batched-prefill scratch, first-touch
     dec.reset()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     clocks = ClockSampler(dev.index)
@@ -636,6 +648,10 @@ def run_decode(args, dev, world, rank) -> dict:
         "metric": "7B-shape Q4_K greedy decode tokens/s", "value": round(G / (decode_ms * 1e-3), 2),
         "unit": "tok/s", "ms_per_token": round(ms_tok, 4), "n_gpus": world,
         "prefill_tok_s": round(P / (prefill_ms * 1e-3), 2), "prompt": P, "generated": G,
+        # one GPU: prompt tokens 0..P-2 in one batched pass on the tensor cores
+        # (eosi_cuda_text_prefill), the last through the step graph; tensor
+        # parallel: every prompt token through the step graph
+        "prefill_mode": "batched_tcgen05" if world == 1 else "steps",
         "config": dict(cfg, wdtype="Q4_K", out_dtype="Q4_K", kv_cache="f32", parallelism=f"tp{world}"),
         "e2e": {"value": round(G / wall_decode, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},

@@ -77,12 +77,14 @@ _SIGNATURES = {
     "eosi_cuda_matmul_q4_k_noalloc": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "eosi_cuda_q4_k_prefill_weight_bytes": (_sz, [_u32, _u32]),
     "eosi_cuda_q4_k_prefill_scratch_bytes": (_sz, [_u32, _u32]),
-    "eosi_cuda_q4_k_prefill_split_weights_dev": (C.c_int, [_vp, _u32, _u32, _vp, _vp, _vp]),
-    "eosi_cuda_q4_k_prefill_dev": (C.c_int, [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp]),
+    "eosi_cuda_q4_k_prefill_prepare_weights_dev": (C.c_int, [_vp, _u32, _u32, _vp, _vp]),
+    "eosi_cuda_q4_k_prefill_dev": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp]),
     "eosi_cuda_text_open": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
     "eosi_cuda_text_step": (C.c_int, [_vp, _u32, _vp]),
     "eosi_cuda_text_generate": (C.c_int, [_vp, _vp, _u32, _u32, _vp]),
     "eosi_cuda_text_reset": (C.c_int, [_vp]),
+    "eosi_cuda_text_prefill": (C.c_int, [_vp, _vp, _u32]),
+    "eosi_cuda_text_set_prefill_min": (C.c_int, [_vp, _u32]),
     "eosi_cuda_text_pos": (_u32, [_vp]),
     "eosi_cuda_text_stream": (_vp, [_vp]),
     "eosi_cuda_text_ipc_handle": (C.c_int, [_vp, _vp, _sz]),
@@ -272,11 +274,12 @@ def prefill_scratch_bytes(m: int, k: int) -> int:
     return int(load().eosi_cuda_q4_k_prefill_scratch_bytes(m, k))
 
 
-def prefill_split_weights_dev(w, n, k, w_hi, w_lo, stream=0) -> None:
-    check(load().eosi_cuda_q4_k_prefill_split_weights_dev(_ptr(w), n, k, _ptr(w_hi), _ptr(w_lo), stream or None),
-          "eosi_cuda_q4_k_prefill_split_weights_dev")
+def prefill_prepare_weights_dev(w, n, k, w_prep, stream=0) -> None:
+    """Q4_K [n][k] -> the prefill GEMM's weight layout (prefill_weight_bytes)."""
+    check(load().eosi_cuda_q4_k_prefill_prepare_weights_dev(_ptr(w), n, k, _ptr(w_prep), stream or None),
+          "eosi_cuda_q4_k_prefill_prepare_weights_dev")
 
 
-def prefill_dev(a, w_hi, w_lo, c, m, n, k, scratch, stream=0) -> None:
-    check(load().eosi_cuda_q4_k_prefill_dev(_ptr(a), _ptr(w_hi), _ptr(w_lo), _ptr(c), m, n, k, _ptr(scratch),
+def prefill_dev(a, w_prep, c, m, n, k, scratch, stream=0) -> None:
+    check(load().eosi_cuda_q4_k_prefill_dev(_ptr(a), _ptr(w_prep), _ptr(c), m, n, k, _ptr(scratch),
                                             stream or None), "eosi_cuda_q4_k_prefill_dev")

@@ -251,19 +251,6 @@ struct AttnParams {
   float base, scale;
 };
 
-// RoPE of the pair (x0, x1) at dims (i, i+1) of a head of size HD
-// (rope.c:25-33): th = pos * base^(-i/HD), then the rotation with separately
-// rounded products.
-template <int HD>
-__device__ __forceinline__ void rope_pair(float& x0, float& x1, uint32_t i, uint32_t pos, float base) {
-  const float th = __fmul_rn((float)pos, powf(base, __fdiv_rn(-(float)i, (float)HD)));
-  float sn, cs;
-  sincosf(th, &sn, &cs);
-  const float p0 = x0, p1 = x1;
-  x0 = __fsub_rn(__fmul_rn(p0, cs), __fmul_rn(p1, sn));
-  x1 = __fadd_rn(__fmul_rn(p0, sn), __fmul_rn(p1, cs));
-}
-
 // Dynamic shared memory of attn_kernel<E>: the K and V rows of one chunk.
 __host__ __device__ constexpr uint32_t attn_smem_bytes(uint32_t hd) { return 2u * kAttnChunk * hd * 4u; }
 
@@ -681,6 +668,13 @@ struct TextDecoder {
   cudaGraphExec_t graph = nullptr;
   uint32_t host_pos = 0;
   bool step_mode = false;  // prompt[] holds every fed token (n_prompt = max_ctx)
+  // batched prefill (prefill_text.cu): scratch for pf_rows tokens, allocated
+  // at first use; generate() prefills in batch when at least prefill_min
+  // prompt tokens precede the last one (0: never)
+  uint32_t pf_rows = 0;
+  float *pf_x = nullptr, *pf_qkv = nullptr, *pf_gu = nullptr;
+  void *pf_act = nullptr, *pf_w = nullptr;  // GEMM operand buffers (activations, prepared weights)
+  uint32_t prefill_min = 16;
 
   template <typename T>
   cudaError_t alloc(T** p, size_t bytes) {
@@ -718,6 +712,9 @@ struct TextDecoder {
 
   int open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws);
   int attach(const uint8_t* handles);
+  // the batched path serves one GPU with Q4_K linears
+  bool prefill_ok() const { return world == 1 && m.wdtype == EOS_DT_Q4_K && m.n_layer > 0; }
+  cudaError_t prefill(uint32_t n);  // tokens at prompt[host_pos, host_pos + n)
   XRecv* xrecv(int q) const { return reinterpret_cast<XRecv*>(xpeer[q] + xoff_fl); }
   cudaError_t record_step(cudaStream_t s);
   int capture();
@@ -1031,6 +1028,70 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
   return e;
 }
 
+constexpr uint32_t kPrefillRows = 1024;  // tokens per batched-prefill block
+
+// Batched prefill of the n tokens at prompt[host_pos ...]: per block of up to
+// pf_rows tokens and per layer, the block's rows go through the GEMMs and
+// the prefill kernels, which write their K/V rows into the cache; the next
+// block attends to them.  Only the cache matters afterwards (the next step
+// reads it), so the last layer stops after its K/V rows and no block computes
+// logits.  Leaves state->pos = host_pos + n (not host_pos itself: the caller
+// commits it after its synchronisation).
+cudaError_t TextDecoder::prefill(uint32_t n) {
+  const uint32_t E = m.n_embd, nqkv = hl * hd + 2u * kvl * hd, kq = hl * hd;
+  cudaError_t e = cudaSuccess;
+  if (pf_rows == 0) {
+    const uint32_t rows = m.max_ctx < kPrefillRows ? m.max_ctx : kPrefillRows;
+    // the operand size grows with the row count: `rows` bounds every block
+    size_t amax = 0;
+    for (const uint32_t kk : {E, kq, ffl})
+      if (prefill_operand_bytes(rows, kk) > amax) amax = prefill_operand_bytes(rows, kk);
+    size_t wmax = prefill_operand_bytes(nqkv, E);
+    for (const size_t b : {prefill_operand_bytes(E, kq), prefill_operand_bytes(2u * ffl, E),
+                           prefill_operand_bytes(E, ffl)})
+      if (b > wmax) wmax = b;
+    if (e == cudaSuccess) e = alloc(&pf_x, 4ull * rows * E);
+    if (e == cudaSuccess) e = alloc(&pf_qkv, 4ull * rows * nqkv);
+    if (e == cudaSuccess) e = alloc(&pf_gu, 8ull * rows * ffl);
+    if (e == cudaSuccess) e = alloc(&pf_act, amax);
+    if (e == cudaSuccess) e = alloc(&pf_w, wmax);
+    if (e != cudaSuccess) return e;
+    pf_rows = rows;
+  }
+  int status = EOS_OK;
+  // C (+)= A . deq(W)^T, W prepared on the fly into the weight buffer
+  auto gemm = [&](const uint8_t* w, uint32_t nn, uint32_t kk, float* c, uint32_t mm, bool acc) {
+    if (e == cudaSuccess) e = launch_prefill_w_prep(w, nn, kk, pf_w, st);
+    if (e == cudaSuccess) e = launch_prefill_gemm(pf_act, pf_w, c, mm, nn, kk, gemv_err, st, &status, acc);
+    if (e == cudaSuccess && status != EOS_OK) e = cudaErrorNotSupported;
+  };
+  const float scale = 1.0f / sqrtf((float)hd);  // text.c:365
+  for (uint32_t b0 = 0; b0 < n && e == cudaSuccess; b0 += pf_rows) {
+    const uint32_t mm = (n - b0) < pf_rows ? (n - b0) : pf_rows;
+    const uint32_t pos0 = host_pos + b0;
+    for (uint32_t L = 0; L < m.n_layer && e == cudaSuccess; ++L) {
+      const DecLayer& d = layers[L];
+      float* kcl = kc + (size_t)L * m.max_ctx * kvl * hd;
+      float* vcl = vc + (size_t)L * m.max_ctx * kvl * hd;
+      e = launch_pf_norm_pack(pf_x, L == 0 ? prompt + pos0 : nullptr, tok_embd, d.attn_norm, m.rms_eps, mm, E,
+                              pf_act, st);
+      gemm(d.wqkv, nqkv, E, pf_qkv, mm, false);
+      if (e == cudaSuccess) e = launch_pf_rope_kv(pf_qkv, kcl, vcl, mm, hl, kvl, hd, pos0, m.rope_base, st);
+      if (L + 1u == m.n_layer) break;  // the cache needs nothing more of the last layer
+      if (e == cudaSuccess)
+        e = launch_pf_attn(pf_qkv, kcl, vcl, pf_act, mm, hl, kvl, h0, kv0, m.n_head, m.n_kv_head, hd, pos0,
+                           scale, st);
+      gemm(d.wo, E, kq, pf_x, mm, true);
+      if (e == cudaSuccess)
+        e = launch_pf_norm_pack(pf_x, nullptr, tok_embd, d.ffn_norm, m.rms_eps, mm, E, pf_act, st);
+      gemm(d.wgu, 2u * ffl, E, pf_gu, mm, false);
+      if (e == cudaSuccess) e = launch_pf_silu_pack(pf_gu, mm, ffl, pf_act, st);
+      gemm(d.wd, E, ffl, pf_x, mm, true);
+    }
+  }
+  return e;
+}
+
 int TextDecoder::capture() {
   cudaGraph_t g = nullptr;
   const int sm = (int)attn_smem_bytes(hd);
@@ -1173,7 +1234,16 @@ EOSLLM_CUDA_API int eosi_cuda_text_generate(eosi_cuda_text_t* t, const uint32_t*
   cudaError_t e = cudaMemcpyAsync(d.prompt + d.host_pos, prompt, 4ull * n_prompt, cudaMemcpyHostToDevice, d.st);
   if (e == cudaSuccess) e = cudaMemcpyAsync(&d.state->n_prompt, &np, 4, cudaMemcpyHostToDevice, d.st);
   d.step_mode = false;
-  for (uint64_t i = 0; i < steps && e == cudaSuccess; ++i) e = cudaGraphLaunch(d.graph, d.st);
+  // all prompt tokens but the last in one batched pass; the last one and the
+  // generated ones go through the step graph (logits, pick)
+  uint32_t batched = 0;
+  if (d.prefill_ok() && d.prefill_min > 0 && n_prompt - 1u >= d.prefill_min) {
+    batched = n_prompt - 1u;
+    if (e == cudaSuccess) e = d.prefill(batched);
+    const uint32_t pos = d.host_pos + batched;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&d.state->pos, &pos, 4, cudaMemcpyHostToDevice, d.st);
+  }
+  for (uint64_t i = batched; i < steps && e == cudaSuccess; ++i) e = cudaGraphLaunch(d.graph, d.st);
   // the pick of step (n_prompt - 1 + j) is generated token j
   if (e == cudaSuccess && n_gen > 0)
     e = cudaMemcpyAsync(out_tokens, d.out_tokens + np - 1u, 4ull * n_gen, cudaMemcpyDeviceToHost, d.st);
@@ -1181,6 +1251,40 @@ EOSLLM_CUDA_API int eosi_cuda_text_generate(eosi_cuda_text_t* t, const uint32_t*
   if (e != cudaSuccess) return dec_fail(e);
   d.host_pos += (uint32_t)steps;
   return dec_check_device_errors(t);
+}
+
+EOSLLM_CUDA_API int eosi_cuda_text_prefill(eosi_cuda_text_t* t, const uint32_t* tokens, uint32_t n) {
+  if (t == nullptr || (tokens == nullptr && n > 0)) return EOS_E_INVALID_ARG;
+  TextDecoder& d = t->d;
+  if (!d.prefill_ok()) {
+    eos::set_error_message("cuda text: batched prefill needs one GPU and Q4_K linears");
+    return EOS_E_UNSUPPORTED;
+  }
+  for (uint32_t i = 0; i < n; ++i)
+    if (tokens[i] >= d.m.n_vocab) {
+      eos::set_error_message("cuda text: token id out of range");
+      return EOS_E_INVALID_ARG;
+    }
+  if ((uint64_t)d.host_pos + n > d.m.max_ctx) {
+    eos::set_error_message("cuda text: prompt exceeds the context");
+    return EOS_E_OUT_OF_MEMORY;
+  }
+  if (n == 0) return EOS_OK;
+  if (cudaSetDevice(d.device) != cudaSuccess) return EOS_E_INTERNAL;
+  cudaError_t e = cudaMemcpyAsync(d.prompt + d.host_pos, tokens, 4ull * n, cudaMemcpyHostToDevice, d.st);
+  if (e == cudaSuccess) e = d.prefill(n);
+  const uint32_t pos = d.host_pos + n;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&d.state->pos, &pos, 4, cudaMemcpyHostToDevice, d.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d.st);
+  if (e != cudaSuccess) return dec_fail(e);
+  d.host_pos = pos;
+  return dec_check_device_errors(t);
+}
+
+EOSLLM_CUDA_API int eosi_cuda_text_set_prefill_min(eosi_cuda_text_t* t, uint32_t min_tokens) {
+  if (t == nullptr) return EOS_E_INVALID_ARG;
+  t->d.prefill_min = min_tokens;
+  return EOS_OK;
 }
 
 EOSLLM_CUDA_API int eosi_cuda_text_reset(eosi_cuda_text_t* t) {

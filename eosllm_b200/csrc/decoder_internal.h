@@ -39,4 +39,37 @@ struct DecLayer {
   float* ffn_norm;
 };
 
+// RoPE of the pair (x0, x1) at dims (i, i+1) of a head of size HD
+// (rope.c:25-33): th = pos * base^(-i/HD), then the rotation with separately
+// rounded products.  Shared by the step attention and the batched prefill so
+// both rotate identically.
+template <int HD>
+__device__ __forceinline__ void rope_pair(float& x0, float& x1, uint32_t i, uint32_t pos, float base) {
+  const float th = __fmul_rn((float)pos, powf(base, __fdiv_rn(-(float)i, (float)HD)));
+  float sn, cs;
+  sincosf(th, &sn, &cs);
+  const float p0 = x0, p1 = x1;
+  x0 = __fsub_rn(__fmul_rn(p0, cs), __fmul_rn(p1, sn));
+  x1 = __fadd_rn(__fmul_rn(p0, sn), __fmul_rn(p1, cs));
+}
+
+// Batched prefill kernels (prefill_text.cu).  `act`: the prefill GEMM's
+// activation buffer for m rows of k (int8 values, then the per-32 scale
+// pairs; prefill_operand_bytes(m, k) bytes).
+// x[m][n] = embedding(tokens) when tokens != nullptr; then rmsnorm * w and the
+// Q8 packing per 32.
+cudaError_t launch_pf_norm_pack(float* x, const uint32_t* tokens, const uint16_t* tok_embd, const float* w, float eps,
+                                uint32_t m, uint32_t n, void* act, cudaStream_t st);
+// RoPE on q (in place) and k at positions pos0 + row; k and v rows into the
+// layer's caches.
+cudaError_t launch_pf_rope_kv(float* qkv, float* kc, float* vc, uint32_t m, uint32_t hl, uint32_t kvl, uint32_t hd,
+                              uint32_t pos0, float base, cudaStream_t st);
+// Causal attention of query rows [0, m) (positions pos0 + row) over cache
+// positions [0, pos0 + row], packed for the O GEMM (k = hl*hd).
+cudaError_t launch_pf_attn(const float* qkv, const float* kc, const float* vc, void* act, uint32_t m, uint32_t hl,
+                           uint32_t kvl, uint32_t h0, uint32_t kv0, uint32_t n_head, uint32_t n_kv_head,
+                           uint32_t hd, uint32_t pos0, float scale, cudaStream_t st);
+// silu(gate) * up of gu[m][2 ffl] (gate | up), packed (k = ffl).
+cudaError_t launch_pf_silu_pack(const float* gu, uint32_t m, uint32_t ffl, void* act, cudaStream_t st);
+
 }  // namespace eos

@@ -577,38 +577,35 @@ int eosi_cuda_q4_k_gemv_dev(const void* act, const void* w, float* c, uint32_t n
   return EOS_OK;
 }
 
-size_t eosi_cuda_q4_k_prefill_weight_bytes(uint32_t n, uint32_t k) { return (size_t)n * k * 2u; }
+size_t eosi_cuda_q4_k_prefill_weight_bytes(uint32_t n, uint32_t k) { return eos::prefill_operand_bytes(n, k); }
 
-size_t eosi_cuda_q4_k_prefill_scratch_bytes(uint32_t m, uint32_t k) { return (size_t)m * k * 4u; }
+size_t eosi_cuda_q4_k_prefill_scratch_bytes(uint32_t m, uint32_t k) { return eos::prefill_operand_bytes(m, k); }
 
-int eosi_cuda_q4_k_prefill_split_weights_dev(const void* w, uint32_t n, uint32_t k, void* w_hi, void* w_lo,
-                                             void* stream) {
-  int rc = check_args(w, w_hi, w_lo, EOS_DT_Q4_K, k);
+int eosi_cuda_q4_k_prefill_prepare_weights_dev(const void* w, uint32_t n, uint32_t k, void* w_prep, void* stream) {
+  int rc = check_args(w, w_prep, w_prep, EOS_DT_Q4_K, k);
   if (rc != EOS_OK) return rc;
-  if (!al16(w_hi) || !al16(w_lo)) return fail(EOS_E_INVALID_ARG, "split weights must be 16-byte aligned");
+  if (!al16(w) || !al16(w_prep)) return fail(EOS_E_INVALID_ARG, "prefill weights must be 16-byte aligned");
   DevInfo* info = nullptr;
   rc = dev_prologue(&info);
   if (rc != EOS_OK) return rc;
-  EOS_CK(eos::launch_prefill_w_split((const uint8_t*)w, n, k, w_hi, w_lo, (cudaStream_t)stream), "prefill weight split");
+  EOS_CK(eos::launch_prefill_w_prep((const uint8_t*)w, n, k, w_prep, (cudaStream_t)stream), "prefill weight prep");
   return EOS_OK;
 }
 
-int eosi_cuda_q4_k_prefill_dev(const float* a, const void* w_hi, const void* w_lo, float* c, uint32_t m, uint32_t n,
-                               uint32_t k, void* scratch, void* stream) {
-  int rc = check_args(a, w_hi, c, EOS_DT_Q4_K, k);
+int eosi_cuda_q4_k_prefill_dev(const float* a, const void* w_prep, float* c, uint32_t m, uint32_t n, uint32_t k,
+                               void* scratch, void* stream) {
+  int rc = check_args(a, w_prep, c, EOS_DT_Q4_K, k);
   if (rc != EOS_OK) return rc;
-  if (w_lo == nullptr || scratch == nullptr) return fail(EOS_E_INVALID_ARG, "NULL weight or scratch pointer");
-  if (!al16(a) || !al16(w_hi) || !al16(w_lo) || !al16(scratch) || !al16(c))
+  if (scratch == nullptr) return fail(EOS_E_INVALID_ARG, "NULL scratch pointer");
+  if (!al16(a) || !al16(w_prep) || !al16(scratch) || !al16(c))
     return fail(EOS_E_INVALID_ARG, "prefill pointers must be 16-byte aligned");
   if (m == 0 || n == 0) return EOS_OK;
   DevInfo* info = nullptr;
   rc = dev_prologue(&info);
   if (rc != EOS_OK) return rc;
-  uint8_t* a_hi = static_cast<uint8_t*>(scratch);
-  uint8_t* a_lo = a_hi + (size_t)m * k * 2u;
-  EOS_CK(eos::launch_prefill_act_split(a, m, k, a_hi, a_lo, (cudaStream_t)stream), "prefill activation split");
+  EOS_CK(eos::launch_prefill_act_pack(a, m, k, scratch, (cudaStream_t)stream), "prefill activation packing");
   int status = EOS_OK;
-  EOS_CK(eos::launch_prefill_gemm(a_hi, a_lo, w_hi, w_lo, c, m, n, k, info->err_d, (cudaStream_t)stream, &status),
+  EOS_CK(eos::launch_prefill_gemm(scratch, w_prep, c, m, n, k, info->err_d, (cudaStream_t)stream, &status),
          "prefill gemm");
   if (status != EOS_OK) return fail(status, "prefill gemm: tensor maps unavailable for %u x %u x %u", m, n, k);
   return EOS_OK;

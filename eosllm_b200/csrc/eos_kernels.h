@@ -34,11 +34,15 @@ void set_q4k_gemv_variant(int v);
 cudaError_t launch_q4k_f32_small_n(const float* a, const uint8_t* w, float* c, uint32_t m, uint32_t n, uint32_t k,
                                    cudaStream_t st);
 
-// Tensor-core prefill (prefill_gemm.cu): operands split into bf16 hi/lo.
-cudaError_t launch_prefill_act_split(const float* a, uint32_t m, uint32_t k, void* hi, void* lo, cudaStream_t st);
-cudaError_t launch_prefill_w_split(const uint8_t* w, uint32_t n, uint32_t k, void* hi, void* lo, cudaStream_t st);
-cudaError_t launch_prefill_gemm(const void* a_hi, const void* a_lo, const void* w_hi, const void* w_lo, float* c,
-                                uint32_t m, uint32_t n, uint32_t k, uint32_t* err, cudaStream_t st, int* out_status);
+// Tensor-core prefill (prefill_gemm.cu), bit-exact with the int8 reference.
+// Operand buffers: int8 values [rows][k], then at align1024(rows*k) the
+// per-32 scale pairs [k/32][pad4(rows)]; prefill_operand_bytes gives the size.
+size_t prefill_operand_bytes(uint32_t rows, uint32_t k);
+cudaError_t launch_prefill_act_pack(const float* a, uint32_t m, uint32_t k, void* act, cudaStream_t st);
+cudaError_t launch_prefill_w_prep(const uint8_t* w, uint32_t n, uint32_t k, void* wprep, cudaStream_t st);
+// accumulate: C = C_old + A.W^T (the decoder's residual adds).
+cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, uint32_t m, uint32_t n, uint32_t k,
+                                uint32_t* err, cudaStream_t st, int* out_status, bool accumulate = false);
 
 cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t n, uint32_t k, uint32_t* err,
                             int num_sms, int max_smem, cudaStream_t st, int* out_status,

@@ -1,38 +1,56 @@
 // prefill_gemm.cu -- batched (m > 1) Q4_K matmul on the sm_100a tensor cores
-// (tcgen05 / TMEM / TMA): C[m,n] = A[m,k] . deq(W)[n,k]^T for prompt
-// processing, where the decode GEMV's one-row-at-a-time form would leave the
-// tensor cores idle.
+// (tcgen05 / TMEM / TMA), bit-exact with the reference's int8 kernel:
+// C[m,n] = A[m,k] . deq(W)[n,k]^T for prompt processing, where the decode
+// GEMV's one-row-at-a-time form would leave the tensor cores idle.
 //
-// Numerics.  The reference computes every output with its int8 path
-// (src/kernels/avx2/matmul_q4_k_int8.c:164-269): activations quantized per 32
-// by quantize_sub32 (a_q, scale as), weights as (d*sc)*q - dmin*m.  In exact
-// arithmetic that is sum_p A'_p W'_p with A' = as * a_q and W' = d*sc*q - dmin*m
-// (the scalar dequant order, src/kernels/scalar/matmul_q4_k.c:79-98).  Here A'
-// and W' are formed exactly as the reference's arithmetic does (same packing
-// kernel, same fp32 operations), split into bf16 hi + lo parts, and the
-// product is taken as hi*hi + lo*hi + hi*lo: three kind::f16 MMAs per K step,
-// f32 accumulation in TMEM.  The dropped lo*lo term and the bf16 rounding of
-// lo leave ~2^-16 relative error per product, so outputs agree with the int8
-// reference to fp32-summation level (~1e-5 relative); the bound the tests
-// state is 1e-3.  Non-finite activations give non-finite outputs (not
-// bit-matched).
+// The reference's arithmetic (src/kernels/avx2/matmul_q4_k_int8.c:164-269):
+// activations are packed per 32 by quantize_sub32 (int8 a_q, scale as, sum of
+// the a_q), and for row i, output j
+//     c = 0;  c += partial_b  for super-blocks b in order            (:194, :264)
+//     partial_b = 0;  partial_b += t_s  for sub-blocks s = 0..7      (:254-261)
+//     t_s = ((d*sc_s)*as_s)*dot_s - ((dmin*m_s)*as_s)*sum_s
+// where dot_s = sum_l q_l a_q,l over the sub-block's 32 elements is an exact
+// integer (4-bit weights times int8 activations).  Here every dot_s of a
+// 128 x 128 output tile is one tcgen05.mma kind::i8 (M128 N128 K32, both
+// operands signed 8-bit -- the 4-bit weights are stored as int8 0..15 -- with
+// exact s32 accumulation into TMEM), and the epilogue warps apply t_s, the
+// partial and the row sum in exactly that f32 order (IEEE round-to-nearest,
+// no FMA contraction).  So C equals the reference bit for bit, like the GEMV.
 //
-// Kernel: one CTA per 128 x 256 output tile, 128 threads.  Thread 0 is the
-// TMA producer, thread 32 the MMA issuer, all four warps the epilogue (warp w
-// reads TMEM lanes 32w..32w+31).  Per 64-wide K block a stage holds four
-// 128B-swizzled bf16 tiles (A hi/lo 128x64, W hi/lo 256x64) = 96 KB; two
-// stages.  Each 16-wide K step issues three tcgen05.mma (M128 N256 K16) into
-// a 256-column f32 accumulator; tcgen05.commit frees a stage when its MMAs
-// complete.  TMA boxes start at K offsets that are multiples of 64 elements
-// (128 bytes), so every x coordinate is 16-byte aligned; no multicast.
+// Operand layouts (prepared by prefill_w_prep_kernel / the packers):
+//   weights  wq  int8 [n][k] (the 4-bit values), then at byte offset
+//                align1024(n*k) per sub-block s two f32 rows of pad4(n):
+//                d*sc_s at [2s][col], -(dmin*m_s) at [2s + 1][col]
+//   activ.   aq  int8 [m][k], then at align1024(m*k) per sub-block s two f32
+//                rows of pad4(m): as_s at [2s][row], sum_s at [2s + 1][row]
+// (the min term is stored negated: t = t1 + (-t2) is exactly t1 - t2).
 //
-// Waits are bounded (EOS_WAIT_LIMIT_NS): on a timeout the thread records an
-// error bit and stops issuing; the MMA issuer always commits the "done"
-// barrier after its last MMA (MMAs complete on their own), the producer waits
-// (bounded) for its last copies, and TMEM is freed only after the done
-// barrier.
+// Kernel: one CTA per 128 x 128 output tile, 576 threads.  Warp 0 lane 0 is
+// the TMA producer, warp 1 lane 0 the MMA issuer, warps 2..17 the epilogue
+// (warp w reads TMEM lanes 32(w % 4) .. +31 = tile rows, columns
+// 32((w - 2) / 4) .. +31; four epilogue warps per SM sub-partition hide the
+// TMEM-load and shared-memory latencies).  A stage holds a 128-byte K slice
+// (four sub-blocks): the A and B tiles (128B-swizzled, K-major) and the four
+// sub-blocks' scale rows of the tile's rows and columns = 40 KB; four
+// stages.  TMEM holds four s32 accumulators of 128 columns (512 columns), one
+// per sub-block of a stage: the MMA of sub-block s of stage kb waits until the
+// epilogue has read accumulator s of stage kb-1, so tensor core and epilogue
+// overlap.  A stage is released when its MMAs have completed (tcgen05.commit)
+// and all sixteen epilogue warps have read its scales.  The row sums c live
+// in shared memory (updated once per super-block), the partials in
+// registers; every operation is a scalar IEEE round-to-nearest multiply or
+// add (__fmul_rn / __fadd_rn are never contracted into FMAs).  Packed f32x2
+// multiplies and adds were tried here: their results did not match the
+// scalar operations bit for bit, so they are not used.
+//
+// Waits are bounded (EOS_WAIT_LIMIT_NS): on a timeout the waiting role
+// records an error bit and stops; the MMA issuer always commits the "done"
+// barrier after its last MMA (MMAs complete on their own), the producer
+// drains its copies (bounded), and TMEM is freed only after "done".  TMA
+// boxes start at K offsets that are multiples of 128 bytes and at row / column
+// offsets that are multiples of 128, so every x coordinate is 16-byte
+// aligned; no multicast.
 #include <cuda.h>
-#include <cuda_bf16.h>
 
 #include "eos_common.cuh"
 #include "eos_kernels.h"
@@ -40,67 +58,84 @@
 
 namespace eos {
 
-constexpr uint32_t PG_BM = 128, PG_BN = 256, PG_BK = 64, PG_STAGES = 2;
-constexpr uint32_t PG_A_BYTES = PG_BM * PG_BK * 2;                    // 16 KB
-constexpr uint32_t PG_B_BYTES = PG_BN * PG_BK * 2;                    // 32 KB
-constexpr uint32_t PG_STAGE_BYTES = 2 * PG_A_BYTES + 2 * PG_B_BYTES;  // 96 KB
-constexpr uint32_t PG_SMEM = PG_STAGES * PG_STAGE_BYTES + 1024 + 256;
-constexpr uint32_t PG_TMEM_COLS = 256;
+constexpr uint32_t QG_BM = 128, QG_BN = 128, QG_BK = 128;  // BK in bytes = int8 elements
+constexpr uint32_t QG_SUBS = QG_BK / 32u;                  // sub-blocks per stage
+constexpr uint32_t QG_STAGES = 4;
+constexpr uint32_t QG_A_BYTES = QG_BM * QG_BK;                                   // 16 KB
+constexpr uint32_t QG_B_BYTES = QG_BN * QG_BK;                                   // 16 KB
+constexpr uint32_t QG_AS_BYTES = QG_SUBS * QG_BM * 8u;                           // 4 KB
+constexpr uint32_t QG_BS_BYTES = QG_SUBS * QG_BN * 8u;                           // 4 KB
+constexpr uint32_t QG_STAGE_BYTES = QG_A_BYTES + QG_B_BYTES + QG_AS_BYTES + QG_BS_BYTES;  // 40 KB
+constexpr uint32_t QG_EPI_WARPS = 16;
+constexpr uint32_t QG_COLS = QG_BN * 4u / QG_EPI_WARPS;  // columns per epilogue thread (32)
+constexpr uint32_t QG_THREADS = 32u * (2u + QG_EPI_WARPS);
+constexpr uint32_t QG_ACC_BYTES = QG_EPI_WARPS * 32u * QG_COLS * 4u;  // row sums in shared memory
+constexpr uint32_t QG_SMEM = QG_STAGES * QG_STAGE_BYTES + QG_ACC_BYTES + 1024u + 256u;
+constexpr uint32_t QG_TMEM_COLS = 512;
+
+__host__ __device__ constexpr size_t qg_align1024(size_t x) { return (x + 1023u) & ~(size_t)1023u; }
 
 // ---------------------------------------------------------------------------
 // Operand preparation
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
-  hi = __float2bfloat16_rn(x);
-  lo = __float2bfloat16_rn(__fsub_rn(x, __bfloat162float(hi)));
+// One thread per (row n, super-block b); consecutive threads take consecutive
+// rows of the same super-block, so the scale stores are coalesced.  Values:
+// q (0..15) as int8 at [n][256 b + 32 s + l]; d*sc_s and -(dmin*m_s) with the
+// reference's rounding of d*sc and dmin*m (both __fmul_rn).
+__global__ void __launch_bounds__(256) prefill_w_prep_kernel(const uint8_t* __restrict__ w, uint32_t n, uint32_t k,
+                                                             int8_t* __restrict__ wq, float* __restrict__ wsc) {
+  const uint32_t nb = k / Q4K_ELEMS;
+  const uint64_t t = (uint64_t)blockIdx.x * 256u + threadIdx.x;
+  if (t >= (uint64_t)n * nb) return;
+  const uint32_t b = (uint32_t)(t / n), row = (uint32_t)(t % n);
+  const uint8_t* blk = w + ((size_t)row * nb + b) * Q4K_BYTES;
+  const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+  const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
+  const uint32_t npad = pf_pad4(n);
+  const uint32_t sc8[3] = {hdr.y, hdr.z, hdr.w};
+  const uint8_t* scb = reinterpret_cast<const uint8_t*>(sc8);
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    uint32_t sc, m;
+    q4k_scale_min(s, scb, sc, m);
+    wsc[(size_t)(2u * (b * 8u + s)) * npad + row] = __fmul_rn(d, (float)sc);
+    wsc[(size_t)(2u * (b * 8u + s) + 1u) * npad + row] = -__fmul_rn(dmin, (float)m);
+  }
+  // sub-block pair p: bytes 32p .. 32p+31 of qs; low nibbles = sub-block 2p,
+  // high nibbles = sub-block 2p+1
+  uint4* out = reinterpret_cast<uint4*>(wq + (size_t)row * k + (size_t)b * Q4K_ELEMS);
+  const uint4* qs = reinterpret_cast<const uint4*>(blk + 16);
+  constexpr uint32_t LO = 0x0F0F0F0Fu;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 x = qs[2 * p + h];
+      out[4 * p + h] = make_uint4(x.x & LO, x.y & LO, x.z & LO, x.w & LO);
+      out[4 * p + 2 + h] = make_uint4((x.x >> 4) & LO, (x.y >> 4) & LO, (x.z >> 4) & LO, (x.w >> 4) & LO);
+    }
+  }
 }
 
-// A'[i] = scale * a_q[i] with the exact quantize_sub32 packing
-// (matmul_q4_k_int8.c:98-154), one warp per 32-group.
-__global__ void __launch_bounds__(256) prefill_act_split_kernel(const float* __restrict__ a, uint32_t groups,
-                                                                __nv_bfloat16* __restrict__ hi,
-                                                                __nv_bfloat16* __restrict__ lo) {
+// quantize_sub32 per 32 activations (matmul_q4_k_int8.c:98-154), one warp
+// per group: int8 values, the scale and the sum.
+__global__ void __launch_bounds__(256) prefill_act_pack_kernel(const float* __restrict__ a, uint32_t m, uint32_t k,
+                                                               int8_t* __restrict__ aq, float* __restrict__ asc) {
+  const uint32_t groups = m * (k / 32u);
   const uint32_t g = blockIdx.x * 8u + (threadIdx.x >> 5), lane = threadIdx.x & 31u;
   if (g >= groups) return;  // warp-uniform
-  const size_t i = (size_t)g * 32u + lane;
-  float scale;
-  int32_t sum;
-  const int8_t q = quant_group32(a[i], scale, sum);
-  split_bf16(__fmul_rn(scale, (float)q), hi[i], lo[i]);
-}
-
-// W'[i] = (d*sc)*q - dmin*m (src/kernels/scalar/matmul_q4_k.c:79-98), one
-// thread per 32-weight sub-block.
-__global__ void __launch_bounds__(256) prefill_w_split_kernel(const uint8_t* __restrict__ w, uint32_t subblocks,
-                                                              __nv_bfloat16* __restrict__ hi,
-                                                              __nv_bfloat16* __restrict__ lo) {
-  const uint32_t t = blockIdx.x * 256u + threadIdx.x;
-  if (t >= subblocks) return;
-  const uint32_t b = t >> 3, s = t & 7u;  // super-block, sub-block
-  const uint8_t* blk = w + (size_t)b * Q4K_BYTES;
-  const float d = f16_bits_to_f32(blk[0] | (blk[1] << 8)), dmin = f16_bits_to_f32(blk[2] | (blk[3] << 8));
-  uint32_t sc, m;
-  q4k_scale_min((int)s, blk + 4, sc, m);
-  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
-  // sub-block s: qs bytes 32*(s/2) .. +31, low nibbles for even s, high for odd
-  const uint8_t* qs = blk + 16 + 32u * (s >> 1);
-  const uint32_t shift = (s & 1u) * 4u;
-  const size_t o = (size_t)b * Q4K_ELEMS + s * 32u;
-#pragma unroll 4
-  for (uint32_t l = 0; l < 32; ++l) {
-    const float v = __fsub_rn(__fmul_rn(d1, (float)((qs[l] >> shift) & 15u)), m1);
-    split_bf16(v, hi[o + l], lo[o + l]);
-  }
+  const uint32_t row = g / (k / 32u), s = g % (k / 32u);
+  pf_pack_group(a[(size_t)g * 32u + lane], row, s, lane, k, pf_pad4(m), aq, asc);
 }
 
 // ---------------------------------------------------------------------------
 // tcgen05 / TMA helpers
 // ---------------------------------------------------------------------------
 // Shared-memory matrix descriptor of a K-major, 128B-swizzled tile whose rows
-// are 128 bytes (64 bf16) and whose 8-row groups are 1024 bytes apart: start
-// address >> 4, LBO 16 B (unused for swizzled K-major), SBO 1024 B,
-// version 1, layout type 2 (SWIZZLE_128B).
-__device__ __forceinline__ uint64_t pg_sw128_desc(uint32_t smem_addr) {
+// are 128 bytes and whose 8-row groups are 1024 bytes apart: start address
+// >> 4, LBO 16 B (unused for swizzled K-major), SBO 1024 B, version 1, layout
+// type 2 (SWIZZLE_128B).  Advancing K by 32 bytes adds 2 to the start field.
+__device__ __forceinline__ uint64_t qg_sw128_desc(uint32_t smem_addr) {
   uint64_t dsc = (uint64_t)((smem_addr >> 4) & 0x3FFFu);
   dsc |= (uint64_t)1u << 16;
   dsc |= (uint64_t)(1024u >> 4) << 32;
@@ -109,24 +144,26 @@ __device__ __forceinline__ uint64_t pg_sw128_desc(uint32_t smem_addr) {
   return dsc;
 }
 
-// Instruction descriptor: D f32, A and B bf16, both K-major, M = 128, N = 256.
-constexpr uint32_t PG_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((PG_BN >> 3) << 17) | ((PG_BM >> 4) << 24);
+// Instruction descriptor, kind::i8: D s32 (2 << 4), A and B signed 8-bit
+// (1 << 7, 1 << 10), both K-major, N = 128, M = 128.
+constexpr uint32_t QG_IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((QG_BN >> 3) << 17) | ((QG_BM >> 4) << 24);
 
-__device__ __forceinline__ void pg_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+// D = A . B^T into a fresh accumulator (enable-input-d false)
+__device__ __forceinline__ void qg_mma(uint32_t tmem_d, uint64_t da, uint64_t db) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(PG_IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(QG_IDESC), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
 
-__device__ __forceinline__ void pg_commit(uint64_t* bar) {
+__device__ __forceinline__ void qg_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
 
-__device__ __forceinline__ void pg_tma_2d(void* dst, const CUtensorMap* map, uint32_t x, uint32_t y, uint64_t* bar) {
+__device__ __forceinline__ void qg_tma_2d(void* dst, const CUtensorMap* map, uint32_t x, uint32_t y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           smem_u32(dst)),
@@ -137,6 +174,21 @@ __device__ __forceinline__ void pg_tma_2d(void* dst, const CUtensorMap* map, uin
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// 32 consecutive s32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void qg_ld32(uint32_t taddr, int32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // GEMM
 // ---------------------------------------------------------------------------
@@ -144,35 +196,43 @@ struct PrefillParams {
   float* c;
   uint32_t m, n, k;
   uint32_t* err;
+  uint32_t accumulate;  // C = C_old + A.W^T (residual add, old value first)
 };
 
-__global__ void __launch_bounds__(128, 1)
-    prefill_gemm_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
-                        const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
+__global__ void __launch_bounds__(QG_THREADS, 1)
+    prefill_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        const __grid_constant__ CUtensorMap map_as, const __grid_constant__ CUtensorMap map_bs,
                         const PrefillParams p) {
-  extern __shared__ uint8_t pg_smem_raw[];
+  extern __shared__ uint8_t qg_smem_raw[];
   // 1024-byte aligned stage buffers (128B swizzle atoms)
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(pg_smem_raw) + 1023u) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PG_STAGES * PG_STAGE_BYTES);
-  uint64_t* empty = full + PG_STAGES;
-  uint64_t* done = empty + PG_STAGES;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(qg_smem_raw) + 1023u) & ~uintptr_t(1023));
+  float* acc_s = reinterpret_cast<float*>(smem + QG_STAGES * QG_STAGE_BYTES);  // [warp][column][lane]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + QG_STAGES * QG_STAGE_BYTES + QG_ACC_BYTES);
+  uint64_t* empty = full + QG_STAGES;
+  uint64_t* tfull = empty + QG_STAGES;
+  uint64_t* tempty = tfull + QG_SUBS;
+  uint64_t* done = tempty + QG_SUBS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
-  const uint32_t m0 = blockIdx.y * PG_BM, n0 = blockIdx.x * PG_BN;
-  const uint32_t nkb = p.k / PG_BK;
+  const uint32_t m0 = blockIdx.y * QG_BM, n0 = blockIdx.x * QG_BN;
+  const uint32_t nkb = p.k / QG_BK;
 
   if (tid == 0) {
-    for (uint32_t s = 0; s < PG_STAGES; ++s) {
+    for (uint32_t s = 0; s < QG_STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], 1 + QG_EPI_WARPS);
+    }
+    for (uint32_t j = 0; j < QG_SUBS; ++j) {
+      mbar_init(&tfull[j], 1);
+      mbar_init(&tempty[j], QG_EPI_WARPS);
     }
     mbar_init(done, 1);
     fence_barrier_init();
   }
-  if (warp == 0) {  // TMEM accumulator: 128 lanes x 256 f32 columns
+  if (warp == 0) {  // TMEM: 128 lanes x 512 s32 columns = four 128-column accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(PG_TMEM_COLS)
+                 "r"(QG_TMEM_COLS)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -181,88 +241,139 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  auto sa_hi = [&](uint32_t s) { return smem + s * PG_STAGE_BYTES; };
-  auto sa_lo = [&](uint32_t s) { return smem + s * PG_STAGE_BYTES + PG_A_BYTES; };
-  auto sb_hi = [&](uint32_t s) { return smem + s * PG_STAGE_BYTES + 2 * PG_A_BYTES; };
-  auto sb_lo = [&](uint32_t s) { return smem + s * PG_STAGE_BYTES + 2 * PG_A_BYTES + PG_B_BYTES; };
-
-  if (tid == 0) {
-    // ---- TMA producer ----
-    uint32_t issued = 0;
-    for (uint32_t kb = 0; kb < nkb; ++kb) {
-      const uint32_t s = kb % PG_STAGES;
-      if (kb >= PG_STAGES && !mbar_wait(&empty[s], ((kb / PG_STAGES) - 1u) & 1u)) {
-        report(p.err, EOS_DEVERR_WAIT_EMPTY);
-        break;
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      uint32_t issued = 0;
+      for (uint32_t kb = 0; kb < nkb; ++kb) {
+        const uint32_t s = kb % QG_STAGES;
+        if (kb >= QG_STAGES && !mbar_wait(&empty[s], ((kb / QG_STAGES) - 1u) & 1u)) {
+          report(p.err, EOS_DEVERR_WAIT_EMPTY);
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], QG_STAGE_BYTES);
+        uint8_t* base = smem + s * QG_STAGE_BYTES;
+        qg_tma_2d(base, &map_a, kb * QG_BK, m0, &full[s]);
+        qg_tma_2d(base + QG_A_BYTES, &map_b, kb * QG_BK, n0, &full[s]);
+        qg_tma_2d(base + QG_A_BYTES + QG_B_BYTES, &map_as, m0, 2u * kb * QG_SUBS, &full[s]);
+        qg_tma_2d(base + QG_A_BYTES + QG_B_BYTES + QG_AS_BYTES, &map_bs, n0, 2u * kb * QG_SUBS, &full[s]);
+        issued = kb + 1;
       }
-      mbar_arrive_expect_tx(&full[s], PG_STAGE_BYTES);
-      const uint32_t x = kb * PG_BK;
-      pg_tma_2d(sa_hi(s), &map_ahi, x, m0, &full[s]);
-      pg_tma_2d(sa_lo(s), &map_alo, x, m0, &full[s]);
-      pg_tma_2d(sb_hi(s), &map_bhi, x, n0, &full[s]);
-      pg_tma_2d(sb_lo(s), &map_blo, x, n0, &full[s]);
-      issued = kb + 1;
+      // never leave copies in flight: the last use of every stage has landed
+      for (uint32_t kb = issued > QG_STAGES ? issued - QG_STAGES : 0u; kb < issued; ++kb)
+        if (!mbar_wait(&full[kb % QG_STAGES], (kb / QG_STAGES) & 1u)) report(p.err, EOS_DEVERR_DRAIN);
     }
-    // never leave copies in flight: the last use of every stage has landed
-    for (uint32_t kb = issued > PG_STAGES ? issued - PG_STAGES : 0u; kb < issued; ++kb)
-      if (!mbar_wait(&full[kb % PG_STAGES], (kb / PG_STAGES) & 1u)) report(p.err, EOS_DEVERR_DRAIN);
-  } else if (tid == 32) {
-    // ---- MMA issuer ----
-    for (uint32_t kb = 0; kb < nkb; ++kb) {
-      const uint32_t s = kb % PG_STAGES;
-      if (!mbar_wait(&full[s], (kb / PG_STAGES) & 1u)) {
-        report(p.err, EOS_DEVERR_WAIT_FULL);
-        break;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      bool ok = true;
+      for (uint32_t kb = 0; kb < nkb && ok; ++kb) {
+        const uint32_t s = kb % QG_STAGES;
+        if (!mbar_wait(&full[s], (kb / QG_STAGES) & 1u)) {
+          report(p.err, EOS_DEVERR_WAIT_FULL);
+          break;
+        }
+        tc_fence_after();
+        uint8_t* base = smem + s * QG_STAGE_BYTES;
+        const uint64_t da = qg_sw128_desc(smem_u32(base)), db = qg_sw128_desc(smem_u32(base + QG_A_BYTES));
+        for (uint32_t j = 0; j < QG_SUBS; ++j) {
+          // accumulator j is free once the epilogue has read it for stage kb-1
+          if (kb > 0 && !mbar_wait(&tempty[j], (kb - 1u) & 1u)) {
+            report(p.err, EOS_DEVERR_WAIT_EMPTY);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          qg_mma(tmem + j * QG_BN, da + 2u * j, db + 2u * j);  // K offset 32 j bytes
+          qg_commit(&tfull[j]);
+        }
+        qg_commit(&empty[s]);  // the stage's A/B tiles are consumed once these MMAs complete
       }
-      tc_fence_after();
-      const uint64_t ahi = pg_sw128_desc(smem_u32(sa_hi(s))), alo = pg_sw128_desc(smem_u32(sa_lo(s)));
-      const uint64_t bhi = pg_sw128_desc(smem_u32(sb_hi(s))), blo = pg_sw128_desc(smem_u32(sb_lo(s)));
+      qg_commit(done);  // every MMA issued above has completed
+    }
+  } else {
+    // ---- epilogue: s32 dots -> reference-order f32 terms, partials, row sums ----
+    const uint32_t e = warp - 2u, quad = warp & 3u, cg = e >> 2;
+    const uint32_t lrow = quad * 32u + lane;  // tile row of this thread
+    const uint32_t col0 = cg * QG_COLS;       // first tile column of this thread
+    // row sums c (updated once per super-block) in shared memory, column pair
+    // c2 at acc[32 c2]; super-block partials (updated every sub-block) in
+    // registers
+    float2* acc = reinterpret_cast<float2*>(acc_s) + e * (QG_COLS / 2u) * 32u + lane;
+    float2 part[QG_COLS / 2];
 #pragma unroll
-      for (uint32_t kk = 0; kk < PG_BK / 16u; ++kk) {
-        const uint64_t adv = (uint64_t)(kk * 2u);  // 16 bf16 = 32 bytes along K, in 16-byte units
-        pg_mma(tmem, ahi + adv, bhi + adv, (kb | kk) != 0u ? 1u : 0u);
-        pg_mma(tmem, alo + adv, bhi + adv, 1u);
-        pg_mma(tmem, ahi + adv, blo + adv, 1u);
-      }
-      pg_commit(&empty[s]);  // stage s free once these MMAs have read it
+    for (uint32_t c2 = 0; c2 < QG_COLS / 2; ++c2) {
+      acc[32 * c2] = make_float2(0.0f, 0.0f);  // c = 0 (:194)
+      part[c2] = make_float2(0.0f, 0.0f);
     }
-    pg_commit(done);  // every MMA issued above has completed
-  }
-  __syncwarp();
-
-  // ---- epilogue: TMEM -> registers -> global ----
-  // (warp-uniform: tcgen05.ld is .sync.aligned)
-  const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0u)) != 0;
-  if (!ok && lane == 0) report(p.err, EOS_DEVERR_WAIT_FULL);
-  tc_fence_after();
-  const uint32_t row = m0 + warp * 32u + lane;
-  if (ok) {
-#pragma unroll 1
-    for (uint32_t c0 = 0; c0 < PG_BN; c0 += 32u) {
-      uint32_t r[32];
-      const uint32_t taddr = tmem + ((warp * 32u) << 16) + c0;
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-          "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-          "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-          : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-            "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-            "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-            "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-          : "r"(taddr)
-          : "memory");
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    bool ok = true;
+    for (uint32_t kb = 0; kb < nkb && ok; ++kb) {
+      const uint32_t s = kb % QG_STAGES;
+      ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (kb / QG_STAGES) & 1u)) != 0;  // scales landed
+      if (!ok) break;
+      const uint8_t* base = smem + s * QG_STAGE_BYTES;
+      const float* as_s = reinterpret_cast<const float*>(base + QG_A_BYTES + QG_B_BYTES);  // [2 j + {0,1}][128]
+      const float* bs_s = reinterpret_cast<const float*>(base + QG_A_BYTES + QG_B_BYTES + QG_AS_BYTES);
+      for (uint32_t j = 0; j < QG_SUBS && ok; ++j) {
+        const uint32_t sb = (kb * QG_SUBS + j) & 7u;  // sub-block index within its super-block
+        ok = __all_sync(0xffffffffu, mbar_wait(&tfull[j], kb & 1u)) != 0;
+        if (!ok) break;
+        tc_fence_after();
+        int32_t r[32];
+        qg_ld32(tmem + ((quad * 32u) << 16) + j * QG_BN + col0, r);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[j]);  // accumulator j may be overwritten
+        const float as = as_s[(2u * j) * QG_BM + lrow], sum = as_s[(2u * j + 1u) * QG_BM + lrow];
+        const float2* dsc = reinterpret_cast<const float2*>(bs_s + (2u * j) * QG_BN + col0);       // d*sc
+        const float2* nmn = reinterpret_cast<const float2*>(bs_s + (2u * j + 1u) * QG_BN + col0);  // -(dmin*m)
+#pragma unroll
+        for (uint32_t c2 = 0; c2 < QG_COLS / 2; ++c2) {
+          const float2 dot = make_float2((float)r[2 * c2], (float)r[2 * c2 + 1]);
+          // t = ((d*sc)*as)*dot - ((dmin*m)*as)*sum   (:254-261)
+          const float2 dd = dsc[c2], nn = nmn[c2];
+          // t1 + (-t2): t2 carries the stored sign of -(dmin*m), exactly -t2
+          const float tx = __fadd_rn(__fmul_rn(__fmul_rn(dd.x, as), dot.x), __fmul_rn(__fmul_rn(nn.x, as), sum));
+          const float ty = __fadd_rn(__fmul_rn(__fmul_rn(dd.y, as), dot.y), __fmul_rn(__fmul_rn(nn.y, as), sum));
+          float2 pp = part[c2];
+          pp.x = __fadd_rn(sb == 0 ? 0.0f : pp.x, tx);  // partial = 0; partial += t
+          pp.y = __fadd_rn(sb == 0 ? 0.0f : pp.y, ty);
+          part[c2] = pp;
+          if (sb == 7) {  // c += partial (:264)
+            float2 a2 = acc[32 * c2];
+            a2.x = __fadd_rn(a2.x, pp.x);
+            a2.y = __fadd_rn(a2.y, pp.y);
+            acc[32 * c2] = a2;
+          }
+        }
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&empty[s]);  // this warp has read the stage's scales
+    }
+    if (!ok) {
+      if (lane == 0) report(p.err, EOS_DEVERR_WAIT_FULL);
+    } else {
+      const uint32_t row = m0 + lrow, gcol = n0 + col0;
       if (row < p.m) {
-        float* crow = p.c + (size_t)row * p.n + n0 + c0;
-        if (n0 + c0 + 32u <= p.n && (p.n & 3u) == 0) {
+        float* crow = p.c + (size_t)row * p.n + gcol;
+        if (gcol + QG_COLS <= p.n && (p.n & 3u) == 0) {
 #pragma unroll
-          for (uint32_t j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(crow + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                               __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          for (uint32_t c2 = 0; c2 < QG_COLS / 2; c2 += 2) {
+            const float2 v0 = acc[32 * c2], v1 = acc[32 * (c2 + 1)];
+            float4 v = make_float4(v0.x, v0.y, v1.x, v1.y);
+            if (p.accumulate) {
+              const float4 o = *reinterpret_cast<const float4*>(crow + 2 * c2);
+              v = make_float4(__fadd_rn(o.x, v.x), __fadd_rn(o.y, v.y), __fadd_rn(o.z, v.z), __fadd_rn(o.w, v.w));
+            }
+            *reinterpret_cast<float4*>(crow + 2 * c2) = v;
+          }
         } else {
 #pragma unroll
-          for (uint32_t j = 0; j < 32; ++j)
-            if (n0 + c0 + j < p.n) crow[j] = __uint_as_float(r[j]);
+          for (uint32_t c = 0; c < QG_COLS; ++c) {
+            const float2 v2 = acc[32 * (c / 2)];
+            const float v = (c & 1u) ? v2.y : v2.x;
+            if (gcol + c < p.n) crow[c] = p.accumulate ? __fadd_rn(crow[c], v) : v;
+          }
         }
       }
     }
@@ -270,10 +381,11 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_before();
   __syncthreads();
   // the done barrier follows the last MMA (MMAs wait on nothing, so it always
-  // completes); free the accumulator
+  // completes); free the accumulators only then
   if (warp == 0) {
+    if (!__all_sync(0xffffffffu, mbar_wait(done, 0u)) && lane == 0) report(p.err, EOS_DEVERR_DRAIN);
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PG_TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(QG_TMEM_COLS) : "memory");
   }
 }
 
@@ -288,68 +400,90 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
   if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
+    void* q = nullptr;
+    cudaDriverEntryPointQueryResult r;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) == cudaSuccess &&
+        r == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(q);
   }
   return fn;
 }
 
-// rows x k bf16 row-major, boxes of box_rows x 64 with the 128-byte swizzle
-bool make_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t k, uint32_t box_rows) {
+// rows x k int8 row-major, boxes of 128 rows x 128 bytes with the 128-byte swizzle
+bool make_i8_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t k) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[2] = {k, rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)k * 2u};
-  const cuuint32_t box[2] = {PG_BK, box_rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)k};
+  const cuuint32_t box[2] = {QG_BK, 128u};
   const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// [2 k/32][pad4(cols)] f32 scale rows, boxes of 128 columns x 8 rows (four sub-blocks)
+bool make_scale_map(CUtensorMap* map, const void* base, uint32_t cols, uint32_t k) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {cols, 2u * (k / 32u)};
+  const cuuint64_t strides[1] = {(cuuint64_t)pf_pad4(cols) * 4u};
+  const cuuint32_t box[2] = {128u, 2u * QG_SUBS};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 }  // namespace
 
-cudaError_t launch_prefill_act_split(const float* a, uint32_t m, uint32_t k, void* hi, void* lo, cudaStream_t st) {
+size_t prefill_operand_bytes(uint32_t rows, uint32_t k) {
+  return qg_align1024((size_t)rows * k) + (size_t)(k / 32u) * 2u * pf_pad4(rows) * 4u;
+}
+
+cudaError_t launch_prefill_act_pack(const float* a, uint32_t m, uint32_t k, void* act, cudaStream_t st) {
   const uint32_t groups = m * (k / 32u);
   if (groups == 0) return cudaSuccess;
-  prefill_act_split_kernel<<<(groups + 7u) / 8u, 256, 0, st>>>(a, groups, static_cast<__nv_bfloat16*>(hi),
-                                                               static_cast<__nv_bfloat16*>(lo));
+  int8_t* aq = static_cast<int8_t*>(act);
+  float* asc = reinterpret_cast<float*>(static_cast<uint8_t*>(act) + qg_align1024((size_t)m * k));
+  prefill_act_pack_kernel<<<(groups + 7u) / 8u, 256, 0, st>>>(a, m, k, aq, asc);
   return cudaGetLastError();
 }
 
-cudaError_t launch_prefill_w_split(const uint8_t* w, uint32_t n, uint32_t k, void* hi, void* lo, cudaStream_t st) {
-  const uint32_t sub = n * (k / 32u);
-  if (sub == 0) return cudaSuccess;
-  prefill_w_split_kernel<<<(sub + 255u) / 256u, 256, 0, st>>>(w, sub, static_cast<__nv_bfloat16*>(hi),
-                                                              static_cast<__nv_bfloat16*>(lo));
+cudaError_t launch_prefill_w_prep(const uint8_t* w, uint32_t n, uint32_t k, void* wprep, cudaStream_t st) {
+  const uint64_t threads = (uint64_t)n * (k / Q4K_ELEMS);
+  if (threads == 0) return cudaSuccess;
+  int8_t* wq = static_cast<int8_t*>(wprep);
+  float* wsc = reinterpret_cast<float*>(static_cast<uint8_t*>(wprep) + qg_align1024((size_t)n * k));
+  prefill_w_prep_kernel<<<(uint32_t)((threads + 255u) / 256u), 256, 0, st>>>(w, n, k, wq, wsc);
   return cudaGetLastError();
 }
 
-// C[m,n] from split operands (bf16 row-major [m][k] and [n][k], all 16-byte
-// aligned, k % 64 == 0).  out_status: EOS_E_UNSUPPORTED when the tensor maps
-// cannot be built.
-cudaError_t launch_prefill_gemm(const void* a_hi, const void* a_lo, const void* w_hi, const void* w_lo, float* c,
-                                uint32_t m, uint32_t n, uint32_t k, uint32_t* err, cudaStream_t st, int* out_status) {
+// C[m,n] (or C += with `accumulate`) from prepared operands (layouts above;
+// k % 256 == 0, base pointers 1024-byte aligned).  out_status:
+// EOS_E_UNSUPPORTED when the tensor maps cannot be built.
+cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, uint32_t m, uint32_t n, uint32_t k,
+                                uint32_t* err, cudaStream_t st, int* out_status, bool accumulate) {
   *out_status = EOS_OK;
   if (m == 0 || n == 0) return cudaSuccess;
-  CUtensorMap ma_hi, ma_lo, mb_hi, mb_lo;
-  if (!make_map(&ma_hi, a_hi, m, k, PG_BM) || !make_map(&ma_lo, a_lo, m, k, PG_BM) ||
-      !make_map(&mb_hi, w_hi, n, k, PG_BN) || !make_map(&mb_lo, w_lo, n, k, PG_BN)) {
+  const uint8_t* ab = static_cast<const uint8_t*>(act);
+  const uint8_t* wb = static_cast<const uint8_t*>(wprep);
+  CUtensorMap ma, mb, mas, mbs;
+  if (!make_i8_map(&ma, ab, m, k) || !make_i8_map(&mb, wb, n, k) ||
+      !make_scale_map(&mas, ab + qg_align1024((size_t)m * k), m, k) ||
+      !make_scale_map(&mbs, wb + qg_align1024((size_t)n * k), n, k)) {
     *out_status = EOS_E_UNSUPPORTED;
     return cudaSuccess;
   }
   static bool attr_set = false;
   if (!attr_set) {
-    const cudaError_t e = cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               (int)PG_SMEM);
+    const cudaError_t e =
+        cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QG_SMEM);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  const dim3 grid((n + PG_BN - 1) / PG_BN, (m + PG_BM - 1) / PG_BM);
-  PrefillParams prm{c, m, n, k, err};
-  prefill_gemm_kernel<<<grid, 128, PG_SMEM, st>>>(ma_hi, ma_lo, mb_hi, mb_lo, prm);
+  const dim3 grid((n + QG_BN - 1) / QG_BN, (m + QG_BM - 1) / QG_BM);
+  PrefillParams prm{c, m, n, k, err, accumulate ? 1u : 0u};
+  prefill_gemm_kernel<<<grid, QG_THREADS, QG_SMEM, st>>>(ma, mb, mas, mbs, prm);
   return cudaGetLastError();
 }
 

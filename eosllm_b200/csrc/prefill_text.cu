@@ -1,0 +1,380 @@
+// prefill_text.cu -- batched prompt processing for the device-resident
+// decoder (decoder.cu): the KV-cache rows of a block of prompt tokens in one
+// pass per layer, every linear on the tcgen05 GEMM (prefill_gemm.cu) instead
+// of one GEMV step per token.  The reference feeds a prompt one token at a
+// time (src/core/session.c:231-236 -> eosi_text_step, text.c:267-436); this
+// pass computes the same per-token quantities for m tokens at once:
+//
+//   pf_norm_pack    embedding (layer 0), rmsnorm (rmsnorm.c:14-37, the step's
+//                   own summation order), quantize_sub32 packing per 32
+//                   (matmul_q4_k_int8.c:98-154) into the GEMM's int8 layout
+//   GEMM            [q; k; v] = A . Wqkv^T                      (text.c:349-352)
+//   pf_rope_kv      RoPE on q and k (rope.c:16-38), k/v rows into the cache
+//                   at pos0 + row                               (text.c:359-362)
+//   pf_attn         causal softmax attention with the GQA head map
+//                   (text.c:364-401), packed for the O GEMM
+//   GEMM            x += attn . Wo^T                            (text.c:404-406)
+//   pf_norm_pack    ffn_norm
+//   GEMM            [gate | up] = A . Wgu^T                      (text.c:413-415)
+//   pf_silu_pack    silu(gate) * up (silu.c:17, text.c:417), packed
+//   GEMM            x += h . Wd^T                                (text.c:420-421)
+//
+// Numerics: every linear is bit-exact with the reference's int8 kernel (and
+// so with the step path's GEMV) given the same input vector; rmsnorm, RoPE
+// and SiLU use the step kernels' device arithmetic and order; attention is a
+// streaming softmax over 32-position chunks, where the step path merges
+// 64-position chunk softmaxes.  K/V rows therefore agree with the step path
+// to the rounding of the attention sums, not bit for bit.
+#include <cmath>
+
+#include "decoder_internal.h"
+#include "eos_common.cuh"
+#include "eos_kernels.h"
+
+namespace eos {
+
+constexpr uint32_t kPfNormChunks = 16;  // float4 chunks per thread: n <= 16384
+constexpr uint32_t kPfQ = 16;           // query rows per attention CTA (4 per warp)
+constexpr uint32_t kPfKC = 32;          // cache positions per staged chunk (one per lane)
+
+// ---------------------------------------------------------------------------
+// Residual row -> rmsnorm -> packed activation
+// ---------------------------------------------------------------------------
+struct PfNormParams {
+  float* x;                  // [m][n] residual rows
+  const uint32_t* tokens;    // embedding mode: token of each row (else nullptr)
+  const uint16_t* tok_embd;  // F16 [n_vocab][n]
+  const float* w;            // norm weight
+  float eps;
+  uint32_t n, pitch;         // pitch: pad4(m), the scale pairs' row pitch
+  int8_t* aq;                // GEMM activation layout (pf_pack_group)
+  float* asc;
+};
+
+// One CTA (256 threads) per row.  Thread t holds float4 chunks t, t + 256, ...
+// and the mean square is reduced in the same order as norm_pack_kernel, so a
+// row normalises exactly as the step path normalises the same vector.
+__global__ void __launch_bounds__(256) pf_norm_pack_kernel(const PfNormParams p) {
+  extern __shared__ __align__(16) float ys[];  // [n]
+  __shared__ float red[8];
+  const uint32_t row = blockIdx.x, tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const uint32_t nch = p.n >> 2;
+  float4* xr = reinterpret_cast<float4*>(p.x + (size_t)row * p.n);
+  float4 v[kPfNormChunks];
+  if (p.tokens != nullptr) {
+    const uint2* emb = reinterpret_cast<const uint2*>(p.tok_embd + (size_t)p.tokens[row] * p.n);
+#pragma unroll
+    for (uint32_t j = 0; j < kPfNormChunks; ++j) {
+      const uint32_t c = tid + 256u * j;
+      if (c < nch) {
+        const uint2 h = emb[c];  // F16 -> F32 is exact
+        v[j] = make_float4(f16_bits_to_f32(h.x), f16_bits_to_f32(h.x >> 16), f16_bits_to_f32(h.y),
+                           f16_bits_to_f32(h.y >> 16));
+        xr[c] = v[j];
+      }
+    }
+  } else {
+#pragma unroll
+    for (uint32_t j = 0; j < kPfNormChunks; ++j) {
+      const uint32_t c = tid + 256u * j;
+      if (c < nch) v[j] = xr[c];
+    }
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (uint32_t j = 0; j < kPfNormChunks; ++j) {
+    if (tid + 256u * j < nch) {
+      ss = __fadd_rn(ss, __fmul_rn(v[j].x, v[j].x));
+      ss = __fadd_rn(ss, __fmul_rn(v[j].y, v[j].y));
+      ss = __fadd_rn(ss, __fmul_rn(v[j].z, v[j].z));
+      ss = __fadd_rn(ss, __fmul_rn(v[j].w, v[j].w));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) tot = __fadd_rn(tot, red[w]);
+  const float ms = __fdiv_rn(tot, (float)p.n);
+  const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.eps)));
+  const float4* w4 = reinterpret_cast<const float4*>(p.w);
+#pragma unroll
+  for (uint32_t j = 0; j < kPfNormChunks; ++j) {
+    const uint32_t c = tid + 256u * j;
+    if (c < nch) {
+      const float4 wv = w4[c];
+      ys[4u * c] = __fmul_rn(__fmul_rn(v[j].x, sc), wv.x);
+      ys[4u * c + 1u] = __fmul_rn(__fmul_rn(v[j].y, sc), wv.y);
+      ys[4u * c + 2u] = __fmul_rn(__fmul_rn(v[j].z, sc), wv.z);
+      ys[4u * c + 3u] = __fmul_rn(__fmul_rn(v[j].w, sc), wv.w);
+    }
+  }
+  __syncthreads();
+  for (uint32_t g = warp; g < (p.n >> 5); g += 8u)  // warp-uniform
+    pf_pack_group(ys[g * 32u + lane], row, g, lane, p.n, p.pitch, p.aq, p.asc);
+}
+
+// ---------------------------------------------------------------------------
+// RoPE + KV-cache rows
+// ---------------------------------------------------------------------------
+struct PfRopeParams {
+  float* qkv;  // [m][(hl + 2 kvl) HD]: q heads, k heads, v heads
+  float* kc;   // this layer's caches [max_ctx][kvl HD]
+  float* vc;
+  uint32_t hl, kvl, pos0;
+  float base;
+};
+
+// One CTA per row: thread t rotates pairs t, t + 256, ... of the q and k
+// heads (k heads follow the q heads, so pair t of head h sits at h*HD + 2i).
+template <int HD>
+__global__ void __launch_bounds__(256) pf_rope_kv_kernel(const PfRopeParams p) {
+  const uint32_t row = blockIdx.x, pos = p.pos0 + row;
+  const uint32_t nqkv = (p.hl + 2u * p.kvl) * HD;
+  float* r = p.qkv + (size_t)row * nqkv;
+  const size_t crow = (size_t)pos * p.kvl * HD;
+  const uint32_t pairs = (p.hl + p.kvl) * (HD / 2u);
+  for (uint32_t t = threadIdx.x; t < pairs; t += 256u) {
+    const uint32_t head = t / (HD / 2u), i = 2u * (t % (HD / 2u));
+    float x0 = r[head * HD + i], x1 = r[head * HD + i + 1u];
+    rope_pair<HD>(x0, x1, i, pos, p.base);
+    if (head < p.hl) {
+      r[head * HD + i] = x0;
+      r[head * HD + i + 1u] = x1;
+    } else {
+      const uint32_t kh = head - p.hl;
+      p.kc[crow + kh * HD + i] = x0;
+      p.kc[crow + kh * HD + i + 1u] = x1;
+    }
+  }
+  const float* vr = r + (p.hl + p.kvl) * HD;
+  for (uint32_t t = threadIdx.x; t < p.kvl * HD; t += 256u) p.vc[crow + t] = vr[t];
+}
+
+// ---------------------------------------------------------------------------
+// Causal attention over the cache
+// ---------------------------------------------------------------------------
+struct PfAttnParams {
+  const float* qkv;  // q rotated
+  const float* kc;
+  const float* vc;
+  int8_t* aq;  // GEMM activation layout, k = hl HD
+  float* asc;
+  uint32_t m, hl, kvl, h0, kv0, n_head, n_kv_head, pos0;
+  float scale;
+};
+
+template <int E>
+__host__ __device__ constexpr uint32_t pf_attn_smem_bytes() {
+  // q rows, K chunk (rows padded by 4 floats: conflict-free 16-byte loads
+  // with one row per lane), V chunk, per-warp output row
+  return 4u * (kPfQ * 32u * E + kPfKC * (32u * E + 4u) + kPfKC * 32u * E + 4u * 32u * E);
+}
+
+// Grid (hl, ceil(m / 16)), 128 threads.  CTA (h, b) owns query rows
+// [16 b, 16 b + 16) of local head h; warp w owns four of them.  Cache
+// positions stream through shared memory 32 at a time (K and V rows of the
+// head's KV group); lane j scores position c0 + j for the warp's four
+// queries (q from shared memory by broadcast, K row per lane), then a
+// streaming softmax update (running max, rescaled sum and output) and the
+// weighted V rows (lane = E dims).  At the end each query row is normalised
+// and packed per 32 dims for the O GEMM.
+template <int E>
+__global__ void __launch_bounds__(128) pf_attn_kernel(const PfAttnParams p) {
+  constexpr uint32_t HD = 32u * E, KP = HD + 4u;
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                 // [kPfQ][HD]
+  float* ks = qs + kPfQ * HD;     // [kPfKC][KP]
+  float* vs = ks + kPfKC * KP;    // [kPfKC][HD]
+  float* so = vs + kPfKC * HD;    // [4][HD]
+  const uint32_t hloc = blockIdx.x, i0 = blockIdx.y * kPfQ;
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const uint32_t gh = p.h0 + hloc;
+  const uint32_t gkv = (gh * p.n_kv_head) / p.n_head;  // GQA map (text.c:367)
+  const uint32_t kvi = gkv - p.kv0;
+  const uint32_t nqkv = (p.hl + 2u * p.kvl) * HD;
+  const uint32_t crow = p.kvl * HD;
+  const uint32_t nq = (p.m - i0) < kPfQ ? (p.m - i0) : kPfQ;
+  for (uint32_t t = tid; t < nq * (HD / 4u); t += 128u) {
+    const uint32_t r = t / (HD / 4u), c4 = t % (HD / 4u);
+    reinterpret_cast<float4*>(qs + r * HD)[c4] =
+        reinterpret_cast<const float4*>(p.qkv + (size_t)(i0 + r) * nqkv + hloc * HD)[c4];
+  }
+  float o[4][E], mx[4], l[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    mx[r] = -INFINITY;
+    l[r] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[r][e] = 0.0f;
+  }
+  const uint32_t qpos0 = p.pos0 + i0 + warp * 4u;  // position of the warp's first query
+  const uint32_t last = p.pos0 + i0 + nq - 1u;      // largest query position of the CTA
+  const uint64_t pol = l2_policy_evict_last();      // the layer's cache rows are re-read by every query block
+  for (uint32_t c0 = 0; c0 <= last; c0 += kPfKC) {
+    const uint32_t np = (last + 1u - c0) < kPfKC ? (last + 1u - c0) : kPfKC;
+    __syncthreads();  // the previous chunk (and, first time, q staging) is done
+    const float* kg = p.kc + (size_t)c0 * crow + kvi * HD;
+    const float* vg = p.vc + (size_t)c0 * crow + kvi * HD;
+    for (uint32_t t = tid; t < np * (HD / 4u); t += 128u) {
+      const uint32_t r = t / (HD / 4u), c4 = (t % (HD / 4u)) * 4u;
+      cp_async16(ks + r * KP + c4, kg + (size_t)r * crow + c4, pol);
+      cp_async16(vs + r * HD + c4, vg + (size_t)r * crow + c4, pol);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    // scores of position c0 + lane for the warp's four queries (rows >= np
+    // of the chunk hold stale values; they are masked)
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const float* kr = ks + lane * KP;
+#pragma unroll 4
+    for (uint32_t d = 0; d < HD; d += 4u) {
+      const float4 k4 = *reinterpret_cast<const float4*>(kr + d);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float4 q4 = *reinterpret_cast<const float4*>(qs + (warp * 4u + r) * HD + d);
+        acc[r] = __fmaf_rn(q4.x, k4.x, acc[r]);
+        acc[r] = __fmaf_rn(q4.y, k4.y, acc[r]);
+        acc[r] = __fmaf_rn(q4.z, k4.z, acc[r]);
+        acc[r] = __fmaf_rn(q4.w, k4.w, acc[r]);
+      }
+    }
+    float pw[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      pw[r] = 0.0f;
+      const uint32_t qi = warp * 4u + r;
+      if (qi >= nq || qpos0 + r < c0) continue;  // warp-uniform: no position of this chunk is visible
+      const bool valid = lane < np && c0 + lane <= qpos0 + r;
+      const float s = valid ? __fmul_rn(acc[r], p.scale) : -INFINITY;
+      float cm = s;
+#pragma unroll
+      for (int sh = 16; sh > 0; sh >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, sh));
+      const float nm = fmaxf(mx[r], cm);            // finite: position c0 is visible
+      const float alpha = expf(mx[r] - nm);         // 0 on the first chunk
+      const float e = valid ? expf(s - nm) : 0.0f;
+      float ls = e;
+#pragma unroll
+      for (int sh = 16; sh > 0; sh >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, sh);
+      l[r] = __fmaf_rn(l[r], alpha, ls);
+#pragma unroll
+      for (int ee = 0; ee < E; ++ee) o[r][ee] *= alpha;
+      mx[r] = nm;
+      pw[r] = e;
+    }
+    for (uint32_t j = 0; j < np; ++j) {
+      float vv[E];
+#pragma unroll
+      for (int ee = 0; ee < E; ++ee) vv[ee] = vs[j * HD + lane * E + ee];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float a = __shfl_sync(0xffffffffu, pw[r], j);
+#pragma unroll
+        for (int ee = 0; ee < E; ++ee) o[r][ee] = __fmaf_rn(a, vv[ee], o[r][ee]);
+      }
+    }
+  }
+  // normalise, pack per 32 dims
+  const uint32_t kq = p.hl * HD, pitch = pf_pad4(p.m);
+  float* sw = so + warp * HD;
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const uint32_t qi = warp * 4u + r;
+    if (qi >= nq) break;  // warp-uniform
+    const float inv = 1.0f / l[r];
+#pragma unroll
+    for (int ee = 0; ee < E; ++ee) sw[lane * E + ee] = o[r][ee] * inv;
+    __syncwarp();
+#pragma unroll
+    for (int g = 0; g < E; ++g)
+      pf_pack_group(sw[g * 32 + lane], i0 + qi, hloc * E + g, lane, kq, pitch, p.aq, p.asc);
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// silu(gate) * up -> packed
+// ---------------------------------------------------------------------------
+// Grid (ffl / 256, m), 256 threads; ffl % 32 == 0, so every warp is one group.
+__global__ void __launch_bounds__(256) pf_silu_pack_kernel(const float* __restrict__ gu, uint32_t ffl,
+                                                           uint32_t pitch, int8_t* __restrict__ aq,
+                                                           float* __restrict__ asc) {
+  const uint32_t row = blockIdx.y, i = blockIdx.x * 256u + threadIdx.x;
+  if (i >= ffl) return;  // warp-uniform
+  const float* r = gu + (size_t)row * 2u * ffl;
+  const float g = r[i], u = r[ffl + i];
+  // x * (1 / (1 + expf(-x))) (silu.c:17), then gate * up (text.c:417)
+  const float h = __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), u);
+  pf_pack_group(h, row, i >> 5, threadIdx.x & 31u, ffl, pitch, aq, asc);
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+namespace {
+int8_t* act_q(void* act) { return static_cast<int8_t*>(act); }
+float* act_sc(void* act, uint32_t m, uint32_t k) {
+  return reinterpret_cast<float*>(static_cast<uint8_t*>(act) + pf_scale_offset(m, k));
+}
+}  // namespace
+
+cudaError_t launch_pf_norm_pack(float* x, const uint32_t* tokens, const uint16_t* tok_embd, const float* w, float eps,
+                                uint32_t m, uint32_t n, void* act, cudaStream_t st) {
+  if (m == 0) return cudaSuccess;
+  if (n % 256u || n > 256u * 4u * kPfNormChunks) return cudaErrorInvalidValue;
+  const uint32_t smem = 4u * n;
+  cudaError_t e = cudaFuncSetAttribute(pf_norm_pack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  PfNormParams p{x, tokens, tok_embd, w, eps, n, pf_pad4(m), act_q(act), act_sc(act, m, n)};
+  pf_norm_pack_kernel<<<m, 256, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pf_rope_kv(float* qkv, float* kc, float* vc, uint32_t m, uint32_t hl, uint32_t kvl, uint32_t hd,
+                              uint32_t pos0, float base, cudaStream_t st) {
+  if (m == 0) return cudaSuccess;
+  PfRopeParams p{qkv, kc, vc, hl, kvl, pos0, base};
+  if (hd == 64) pf_rope_kv_kernel<64><<<m, 256, 0, st>>>(p);
+  else if (hd == 128) pf_rope_kv_kernel<128><<<m, 256, 0, st>>>(p);
+  else if (hd == 256) pf_rope_kv_kernel<256><<<m, 256, 0, st>>>(p);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+namespace {
+template <int E>
+cudaError_t attn_launch(const PfAttnParams& p, cudaStream_t st) {
+  constexpr uint32_t smem = pf_attn_smem_bytes<E>();
+  const cudaError_t e = cudaFuncSetAttribute(pf_attn_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+  if (e != cudaSuccess) return e;
+  const dim3 grid(p.hl, (p.m + kPfQ - 1u) / kPfQ);
+  pf_attn_kernel<E><<<grid, 128, smem, st>>>(p);
+  return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_pf_attn(const float* qkv, const float* kc, const float* vc, void* act, uint32_t m, uint32_t hl,
+                           uint32_t kvl, uint32_t h0, uint32_t kv0, uint32_t n_head, uint32_t n_kv_head,
+                           uint32_t hd, uint32_t pos0, float scale, cudaStream_t st) {
+  if (m == 0 || hl == 0) return cudaSuccess;
+  PfAttnParams p{qkv, kc, vc, act_q(act), act_sc(act, m, hl * hd), m, hl, kvl, h0, kv0, n_head, n_kv_head,
+                 pos0, scale};
+  if (hd == 64) return attn_launch<2>(p, st);
+  if (hd == 128) return attn_launch<4>(p, st);
+  if (hd == 256) return attn_launch<8>(p, st);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_pf_silu_pack(const float* gu, uint32_t m, uint32_t ffl, void* act, cudaStream_t st) {
+  if (m == 0 || ffl == 0) return cudaSuccess;
+  if (ffl % 32u) return cudaErrorInvalidValue;
+  pf_silu_pack_kernel<<<dim3((ffl + 255u) / 256u, m), 256, 0, st>>>(gu, ffl, pf_pad4(m), act_q(act),
+                                                                      act_sc(act, m, ffl));
+  return cudaGetLastError();
+}
+
+}  // namespace eos

@@ -116,6 +116,20 @@ class TextDecoder:
                 "eosi_cuda_text_generate")
         return out[:n_gen]
 
+    def prefill(self, tokens) -> None:
+        """Feed `tokens` in one batched pass on the tensor cores (KV cache
+        rows, no logits); one GPU and Q4_K linears (EOS_E_UNSUPPORTED
+        otherwise)."""
+        p = np.ascontiguousarray(tokens, dtype=np.uint32)
+        B.check(self.lib.eosi_cuda_text_prefill(self.handle, p.ctypes.data if p.size else None, p.size),
+                "eosi_cuda_text_prefill")
+
+    def set_prefill_min(self, min_tokens: int) -> None:
+        """generate() prefills in batch when at least `min_tokens` prompt
+        tokens precede the last one (0: always token by token)."""
+        B.check(self.lib.eosi_cuda_text_set_prefill_min(self.handle, int(min_tokens)),
+                "eosi_cuda_text_set_prefill_min")
+
     def reset(self) -> None:
         B.check(self.lib.eosi_cuda_text_reset(self.handle), "eosi_cuda_text_reset")
 

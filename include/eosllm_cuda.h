@@ -182,23 +182,22 @@ EOSLLM_CUDA_API int eosi_cuda_q4_k_from_gauss_dev(void *dst, size_t n_elements, 
                                   void *stream);
 
 /* ---- tensor-core prefill (m > 1) ----------------------------------------------
- * C[m,n] = A[m,k] . deq(W)[n,k]^T on the sm_100a tensor cores (tcgen05): no
- * counterpart in the reference, which processes a prompt one token at a time
- * through the same int8 kernel (src/core/session.c:231-236).  Activations
- * are packed exactly as quantize_sub32 (matmul_q4_k_int8.c:98-154) does,
- * weights dequantized as (d*sc)*q - dmin*m; both are split into bf16 hi+lo
- * parts and multiplied as hi*hi + lo*hi + hi*lo with f32 accumulation, so C
- * agrees with eosi_cuda_matmul_q4_k (the int8 reference) to ~1e-5 relative
- * (not bit for bit).  Weights are split once (a resident prefill copy of
- * 2 * eosi_cuda_q4_k_prefill_weight_bytes bytes); each call needs
- * eosi_cuda_q4_k_prefill_scratch_bytes of scratch.  All pointers device,
+ * C[m,n] = A[m,k] . deq(W)[n,k]^T on the sm_100a tensor cores (tcgen05),
+ * bit-exact with eosi_cuda_matmul_q4_k and with the reference's int8 kernel
+ * (src/kernels/avx2/matmul_q4_k_int8.c:164-269), which the reference applies
+ * to one prompt token at a time (src/core/session.c:231-236).  Activations
+ * are packed per 32 exactly as quantize_sub32 does; every sub-block's integer
+ * dot is one int8 tensor-core MMA, rescaled and summed in the reference's f32
+ * order.  Weights are prepared once into eosi_cuda_q4_k_prefill_weight_bytes
+ * bytes (the 4-bit values as int8 plus per-32 (d*sc, dmin*m) pairs); each call
+ * needs eosi_cuda_q4_k_prefill_scratch_bytes of scratch.  All pointers device,
  * 16-byte aligned; k % 256 == 0. */
 EOSLLM_CUDA_API size_t eosi_cuda_q4_k_prefill_weight_bytes(uint32_t n, uint32_t k);
 EOSLLM_CUDA_API size_t eosi_cuda_q4_k_prefill_scratch_bytes(uint32_t m, uint32_t k);
-EOSLLM_CUDA_API int eosi_cuda_q4_k_prefill_split_weights_dev(const void *w, uint32_t n, uint32_t k, void *w_hi,
-                                                             void *w_lo, void *stream);
-EOSLLM_CUDA_API int eosi_cuda_q4_k_prefill_dev(const float *a, const void *w_hi, const void *w_lo, float *c,
-                                               uint32_t m, uint32_t n, uint32_t k, void *scratch, void *stream);
+EOSLLM_CUDA_API int eosi_cuda_q4_k_prefill_prepare_weights_dev(const void *w, uint32_t n, uint32_t k, void *w_prep,
+                                                               void *stream);
+EOSLLM_CUDA_API int eosi_cuda_q4_k_prefill_dev(const float *a, const void *w_prep, float *c, uint32_t m, uint32_t n,
+                                               uint32_t k, void *scratch, void *stream);
 
 /* ---- device-resident Llama decoder ------------------------------------------
  * The work of eosi_text_open / eosi_text_step / eosi_text_close
@@ -251,6 +250,17 @@ EOSLLM_CUDA_API int eosi_cuda_text_step(eosi_cuda_text_t *t, uint32_t token, flo
  * do (src/core/session.c:211-262, src/sched/greedy.c:48-73). */
 EOSLLM_CUDA_API int eosi_cuda_text_generate(eosi_cuda_text_t *t, const uint32_t *prompt, uint32_t n_prompt,
                                             uint32_t n_gen, uint32_t *out_tokens);
+/* Batched prefill: feeds tokens[0, n) from the current position in one pass
+ * per layer on the tensor cores (the KV cache rows of all n tokens), with no
+ * logits; position + n.  The reference feeds a prompt token by token
+ * (src/core/session.c:231-236); the cache rows agree with that to f32
+ * summation level.  One GPU (world 1) and Q4_K linears only, else
+ * EOS_E_UNSUPPORTED (feed the tokens with eosi_cuda_text_step instead).
+ * eosi_cuda_text_generate uses it for all prompt tokens but the last when at
+ * least `min_tokens` precede the last (eosi_cuda_text_set_prefill_min; default
+ * 16, 0 = never). */
+EOSLLM_CUDA_API int eosi_cuda_text_prefill(eosi_cuda_text_t *t, const uint32_t *tokens, uint32_t n);
+EOSLLM_CUDA_API int eosi_cuda_text_set_prefill_min(eosi_cuda_text_t *t, uint32_t min_tokens);
 /* Position back to 0 (the KV cache is overwritten as steps proceed). */
 EOSLLM_CUDA_API int eosi_cuda_text_reset(eosi_cuda_text_t *t);
 EOSLLM_CUDA_API uint32_t eosi_cuda_text_pos(const eosi_cuda_text_t *t);
@@ -260,8 +270,9 @@ EOSLLM_CUDA_API uint32_t eosi_cuda_text_pos(const eosi_cuda_text_t *t);
  * all-gather over the process group) and passes them to
  * eosi_cuda_text_attach_peers, which maps the peers' buffers and builds the
  * step.  Per layer the ranks exchange the O-projection and down-projection
- * partial sums (each rank reads every rank's partial over NVLink and sums
- * them in rank order, so all ranks hold the same residual stream) and at the
+ * partial sums (each rank's GEMV writes its partial into every rank's
+ * receive slot over NVLink; each rank sums the slots in rank order, so all
+ * ranks hold the same residual stream) and at the
  * end their slice's greedy pick; every exchange is a flag handshake with a
  * one-second bound (EOS_E_INTERNAL when a rank never arrives).  Every rank
  * must make the same calls in the same order (step / generate / reset). */

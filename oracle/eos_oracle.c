@@ -20,6 +20,11 @@
 /* binary16 <-> binary32: restates src/util/f16.h:17-82                */
 /* ------------------------------------------------------------------ */
 
+/* Summation-order switch (orc_set_sum_order): 0 is the reference's order
+ * everywhere; the other bits exist only to measure how far the reference's
+ * algorithm itself moves under a rounding-level reordering of its sums. */
+static int g_orc_sum_order = 0;
+
 float orc_f16_to_f32(uint16_t h) {
     uint32_t sign = ((uint32_t)(h & 0x8000u)) << 16;
     uint32_t exp = (h >> 10) & 0x1Fu;
@@ -246,12 +251,14 @@ int orc_matmul_q4_k_int8(const float *a, const void *bq, float *c,
             float as[8];
             int32_t sa[8];
             int sub;
+            /* order bit 2: super-blocks (and below, sub-blocks) accumulated last to first */
+            const uint32_t bo = (g_orc_sum_order & 2) ? nb - 1u - b : b;
             for (sub = 0; sub < 8; ++sub) /* :208-211 */
-                orc_quantize_sub32(ar + (size_t)b * 256u + 32u * sub, aq + 32 * sub, &as[sub], &sa[sub]);
+                orc_quantize_sub32(ar + (size_t)bo * 256u + 32u * sub, aq + 32 * sub, &as[sub], &sa[sub]);
             for (j = 0; j < n; ++j) {
-                const uint8_t *br = bb + ((size_t)j * nb + b) * 144u;
+                const uint8_t *br = bb + ((size_t)j * nb + bo) * 144u;
                 const uint8_t *qs = br + 16;
-                float d, dmin, partial = 0.0f;
+                float d, dmin, partial = 0.0f, term[8];
                 q4k_header(br, &d, &dmin);
                 for (sub = 0; sub < 8; sub += 2, qs += 32) {
                     uint8_t sl, ml, sh, mh;
@@ -264,11 +271,13 @@ int orc_matmul_q4_k_int8(const float *a, const void *bq, float *c,
                         dh += (int32_t)(qs[l] >> 4) * aq[32 * (sub + 1) + l];
                     }
                     /* rescale in the reference's evaluation order (:254-261) */
-                    partial += d * (float)sl * as[sub] * (float)dl
-                             - dmin * (float)ml * as[sub] * (float)sa[sub];
-                    partial += d * (float)sh * as[sub + 1] * (float)dh
-                             - dmin * (float)mh * as[sub + 1] * (float)sa[sub + 1];
+                    term[sub] = d * (float)sl * as[sub] * (float)dl
+                              - dmin * (float)ml * as[sub] * (float)sa[sub];
+                    term[sub + 1] = d * (float)sh * as[sub + 1] * (float)dh
+                                  - dmin * (float)mh * as[sub + 1] * (float)sa[sub + 1];
                 }
+                /* partial += term, sub-block by sub-block (order bit 2: last to first) */
+                for (sub = 0; sub < 8; ++sub) partial += term[(g_orc_sum_order & 2) ? 7 - sub : sub];
                 cr[j] += partial; /* :264 */
             }
         }
@@ -337,14 +346,19 @@ int orc_matmul_q8_0(const float *a, const void *bq, float *c,
         for (j = 0; j < n; ++j) {
             const uint8_t *br = bb + (size_t)j * nb * 34u;
             float acc = 0.0f;
-            for (b = 0; b < nb; ++b, br += 34) {
+            for (b = 0; b < nb; ++b) {
+                /* order bit 2: blocks and their products accumulated last to first */
+                const uint32_t bo = (g_orc_sum_order & 2) ? nb - 1u - b : b;
+                const uint8_t *blk = br + (size_t)bo * 34u;
                 uint16_t sh;
                 float scale;
                 int p;
-                memcpy(&sh, br, 2);
+                memcpy(&sh, blk, 2);
                 scale = orc_f16_to_f32(sh);
-                for (p = 0; p < 32; ++p)
-                    acc += ar[32u * b + (uint32_t)p] * ((float)(int8_t)br[2 + p] * scale);
+                for (p = 0; p < 32; ++p) {
+                    const int pe = (g_orc_sum_order & 2) ? 31 - p : p;
+                    acc += ar[32u * bo + (uint32_t)pe] * ((float)(int8_t)blk[2 + pe] * scale);
+                }
             }
             c[(size_t)i * n + j] = acc;
         }
@@ -643,8 +657,6 @@ float orc_xs_rand_unit(uint32_t *st) {
 /* Decoder ops                                                         */
 /* ------------------------------------------------------------------ */
 
-static int g_orc_sum_order = 0;
-
 void orc_set_sum_order(int order) { g_orc_sum_order = order; }
 
 /* Sum of squares in the order of a 256-thread reduction: thread t sums
@@ -675,7 +687,7 @@ int orc_rmsnorm(const float *x, const float *w, float eps, float *y,
         const float *xr = x + (size_t)i * cols;
         float *yr = y + (size_t)i * cols;
         float ms = 0.0f, s;
-        if (g_orc_sum_order == 1)
+        if (g_orc_sum_order & 1)
             ms = orc_sumsq_strided256(xr, cols);
         else
             for (j = 0; j < cols; ++j) ms += xr[j] * xr[j];

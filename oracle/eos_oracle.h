@@ -113,12 +113,14 @@ uint32_t orc_xorshift32(uint32_t *state);
 float    orc_xs_rand_unit(uint32_t *state);
 
 /* --- decoder ops (src/kernels/scalar/{rmsnorm,rope,silu}.c) -------------- */
-/* Summation order of rmsnorm's mean square: 0 (default) = the reference's
- * sequential loop; 1 = a 256-wide strided reduction (per-thread partials,
- * warp butterfly, warps in order).  Order 1 exists only to MEASURE how much
- * the reference algorithm itself moves under a rounding-level change of one
- * sum: decoder tests bound the GPU's deviation by that envelope.  Parity
- * results always use order 0. */
+/* Summation orders, a bit mask; 0 (default) = the reference's order
+ * everywhere.  Bit 1: rmsnorm's mean square as a 256-wide strided reduction
+ * (per-thread partials, warp butterfly, warps in order) instead of the
+ * sequential loop.  Bit 2: the quantized matmuls (orc_matmul_q4_k_int8,
+ * orc_matmul_q8_0) accumulate their blocks last to first.  The non-zero
+ * orders exist only to MEASURE how much the reference algorithm itself moves
+ * under a rounding-level reordering of its sums: decoder tests bound the
+ * GPU's deviation by that envelope.  Parity results always use order 0. */
 void orc_set_sum_order(int order);
 int orc_rmsnorm(const float *x, const float *w, float eps, float *y,
                 uint32_t rows, uint32_t cols);

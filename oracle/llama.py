@@ -61,9 +61,10 @@ class _OrcLlama(C.Structure):
 
 
 class OracleDecoder:
-    """orc_text_step on `model`.  sum_order 1 runs rmsnorm's mean square in
-    a 256-wide strided order (orc_set_sum_order) to measure the reference
-    algorithm's own sensitivity; 0 is the reference's order."""
+    """orc_text_step on `model`.  sum_order (orc_set_sum_order, a bit mask)
+    measures the reference algorithm's own sensitivity to summation order:
+    1 runs rmsnorm's mean square in a 256-wide strided order, 2 accumulates
+    the quantized matmuls' blocks last to first; 0 is the reference's order."""
 
     def __init__(self, o: Oracle, model: dict, sum_order: int = 0):
         self.o, self.model, self.sum_order = o, model, sum_order
