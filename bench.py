@@ -652,6 +652,11 @@ def run_decode(args, dev, world, rank) -> dict:
         # (eosi_cuda_text_prefill), the last through the step graph; tensor
         # parallel: every prompt token through the step graph
         "prefill_mode": "batched_tcgen05" if world == 1 else "steps",
+        # the batched prefill's GEMM layout of every layer (bf16 4-bit values
+        # + per-32 scales), prepared once at the warm-up prefill and kept
+        "prefill_weights_gb": round(sum(B.prefill_weight_bytes(nn, kk) for nn, kk in (
+            (3 * cfg["n_embd"], cfg["n_embd"]), (cfg["n_embd"], cfg["n_embd"]), (2 * cfg["n_ff"], cfg["n_embd"]),
+            (cfg["n_embd"], cfg["n_ff"]))) * cfg["n_layer"] / 1e9, 2) if world == 1 else None,
         "config": dict(cfg, wdtype="Q4_K", out_dtype="Q4_K", kv_cache="f32", parallelism=f"tp{world}"),
         "e2e": {"value": round(G / wall_decode, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},

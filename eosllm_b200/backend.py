@@ -85,6 +85,7 @@ _SIGNATURES = {
     "eosi_cuda_text_reset": (C.c_int, [_vp]),
     "eosi_cuda_text_prefill": (C.c_int, [_vp, _vp, _u32]),
     "eosi_cuda_text_set_prefill_min": (C.c_int, [_vp, _u32]),
+    "eosi_cuda_text_set_prefill_resident": (C.c_int, [_vp, C.c_int]),
     "eosi_cuda_text_pos": (_u32, [_vp]),
     "eosi_cuda_text_stream": (_vp, [_vp]),
     "eosi_cuda_text_ipc_handle": (C.c_int, [_vp, _vp, _sz]),

@@ -674,6 +674,11 @@ struct TextDecoder {
   uint32_t pf_rows = 0;
   float *pf_x = nullptr, *pf_qkv = nullptr, *pf_gu = nullptr;
   void *pf_act = nullptr, *pf_w = nullptr;  // GEMM operand buffers (activations, prepared weights)
+  // every layer's four matrices in the GEMM layout, prepared once at the
+  // first prefill when they fit in half of the free device memory (a
+  // load-time repack; empty: each matrix is prepared into pf_w before use)
+  std::vector<void*> pf_wres;
+  bool pf_resident = true;  // allow pf_wres (eosi_cuda_text_set_prefill_resident)
   uint32_t prefill_min = 16;
 
   template <typename T>
@@ -1059,10 +1064,41 @@ cudaError_t TextDecoder::prefill(uint32_t n) {
     pf_rows = rows;
   }
   int status = EOS_OK;
-  // C (+)= A . deq(W)^T, W prepared on the fly into the weight buffer
-  auto gemm = [&](const uint8_t* w, uint32_t nn, uint32_t kk, float* c, uint32_t mm, bool acc) {
-    if (e == cudaSuccess) e = launch_prefill_w_prep(w, nn, kk, pf_w, st);
-    if (e == cudaSuccess) e = launch_prefill_gemm(pf_act, pf_w, c, mm, nn, kk, gemv_err, st, &status, acc);
+  const uint32_t mat_n[4] = {nqkv, E, 2u * ffl, E}, mat_k[4] = {E, kq, E, ffl};  // qkv, o, gate|up, down
+  auto mat_w = [&](uint32_t L, int i) -> const uint8_t* {
+    const DecLayer& d = layers[L];
+    return i == 0 ? d.wqkv : (i == 1 ? d.wo : (i == 2 ? d.wgu : d.wd));
+  };
+  if (pf_wres.empty() && pf_resident) {
+    size_t need = 0;
+    for (int i = 0; i < 4; ++i) need += prefill_operand_bytes(mat_n[i], mat_k[i]);
+    need *= m.n_layer;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) == cudaSuccess && need <= free_b / 2) {
+      std::vector<void*> res(4u * m.n_layer, nullptr);
+      cudaError_t r = cudaSuccess;
+      for (uint32_t L = 0; L < m.n_layer && r == cudaSuccess; ++L)
+        for (int i = 0; i < 4 && r == cudaSuccess; ++i) {
+          r = cudaMalloc(&res[4u * L + i], prefill_operand_bytes(mat_n[i], mat_k[i]));
+          if (r == cudaSuccess) r = launch_prefill_w_prep(mat_w(L, i), mat_n[i], mat_k[i], res[4u * L + i], st);
+        }
+      if (r == cudaSuccess) {
+        pf_wres = res;
+        for (void* q : res) allocs.push_back(q);
+      } else {
+        for (void* q : res)
+          if (q) cudaFree(q);
+        cudaGetLastError();  // not fatal: prepare per layer instead
+      }
+    }
+  }
+  // C (+)= A . deq(W)^T with W resident in the GEMM layout, or prepared on the fly
+  auto gemm = [&](uint32_t L, int i, float* c, uint32_t mm, bool acc) {
+    const uint32_t nn = mat_n[i], kk = mat_k[i];
+    const bool res = pf_resident && !pf_wres.empty();
+    const void* wp = res ? pf_wres[4u * L + i] : pf_w;
+    if (e == cudaSuccess && !res) e = launch_prefill_w_prep(mat_w(L, i), nn, kk, pf_w, st);
+    if (e == cudaSuccess) e = launch_prefill_gemm(pf_act, wp, c, mm, nn, kk, gemv_err, st, &status, acc);
     if (e == cudaSuccess && status != EOS_OK) e = cudaErrorNotSupported;
   };
   const float scale = 1.0f / sqrtf((float)hd);  // text.c:365
@@ -1075,18 +1111,18 @@ cudaError_t TextDecoder::prefill(uint32_t n) {
       float* vcl = vc + (size_t)L * m.max_ctx * kvl * hd;
       e = launch_pf_norm_pack(pf_x, L == 0 ? prompt + pos0 : nullptr, tok_embd, d.attn_norm, m.rms_eps, mm, E,
                               pf_act, st);
-      gemm(d.wqkv, nqkv, E, pf_qkv, mm, false);
+      gemm(L, 0, pf_qkv, mm, false);
       if (e == cudaSuccess) e = launch_pf_rope_kv(pf_qkv, kcl, vcl, mm, hl, kvl, hd, pos0, m.rope_base, st);
       if (L + 1u == m.n_layer) break;  // the cache needs nothing more of the last layer
       if (e == cudaSuccess)
         e = launch_pf_attn(pf_qkv, kcl, vcl, pf_act, mm, hl, kvl, h0, kv0, m.n_head, m.n_kv_head, hd, pos0,
                            scale, st);
-      gemm(d.wo, E, kq, pf_x, mm, true);
+      gemm(L, 1, pf_x, mm, true);
       if (e == cudaSuccess)
         e = launch_pf_norm_pack(pf_x, nullptr, tok_embd, d.ffn_norm, m.rms_eps, mm, E, pf_act, st);
-      gemm(d.wgu, 2u * ffl, E, pf_gu, mm, false);
+      gemm(L, 2, pf_gu, mm, false);
       if (e == cudaSuccess) e = launch_pf_silu_pack(pf_gu, mm, ffl, pf_act, st);
-      gemm(d.wd, E, ffl, pf_x, mm, true);
+      gemm(L, 3, pf_x, mm, true);
     }
   }
   return e;
@@ -1284,6 +1320,12 @@ EOSLLM_CUDA_API int eosi_cuda_text_prefill(eosi_cuda_text_t* t, const uint32_t* 
 EOSLLM_CUDA_API int eosi_cuda_text_set_prefill_min(eosi_cuda_text_t* t, uint32_t min_tokens) {
   if (t == nullptr) return EOS_E_INVALID_ARG;
   t->d.prefill_min = min_tokens;
+  return EOS_OK;
+}
+
+EOSLLM_CUDA_API int eosi_cuda_text_set_prefill_resident(eosi_cuda_text_t* t, int resident) {
+  if (t == nullptr) return EOS_E_INVALID_ARG;
+  t->d.pf_resident = resident != 0;
   return EOS_OK;
 }
 

@@ -3,6 +3,7 @@
 // (TMA 1-D) copies, programmatic dependent launch, bounded waits.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -238,22 +239,22 @@ __device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
   return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xffffu)));
 }
 
-// Activation layout of the tensor-core prefill GEMM (prefill_gemm.cu): int8
-// values [rows][k], then at pf_scale_offset per 32-group s two f32 rows of
-// pad4(rows): the scales [2s][row] and the sums [2s + 1][row].
+// Activation layout of the tensor-core prefill GEMM (prefill_gemm.cu): the
+// int8 values as bf16 [rows][k], then at pf_scale_offset per 32-group s two
+// f32 rows of pad4(rows): the scales [2s][row] and the sums [2s + 1][row].
 __host__ __device__ constexpr uint32_t pf_pad4(uint32_t x) { return (x + 3u) & ~3u; }
 __host__ __device__ constexpr size_t pf_scale_offset(uint32_t rows, uint32_t k) {
-  return ((size_t)rows * k + 1023u) & ~(size_t)1023u;
+  return ((size_t)rows * k * 2u + 1023u) & ~(size_t)1023u;
 }
 
 // Packs the warp's 32-group s of row `row` (lane i holds element i) into that
 // layout: the same quantize_sub32 values as pack_group_to_record.
 __device__ __forceinline__ void pf_pack_group(float v, uint32_t row, uint32_t s, uint32_t lane, uint32_t k,
-                                              uint32_t pitch, int8_t* aq, float* asc) {
+                                              uint32_t pitch, uint16_t* aq, float* asc) {
   float scale;
   int32_t sum;
   const int8_t q = quant_group32(v, scale, sum);
-  aq[(size_t)row * k + s * 32u + lane] = q;
+  aq[(size_t)row * k + s * 32u + lane] = __bfloat16_as_ushort(__float2bfloat16_rn((float)q));  // exact
   if (lane == 0) {
     asc[(size_t)(2u * s) * pitch + row] = scale;
     asc[(size_t)(2u * s + 1u) * pitch + row] = (float)sum;

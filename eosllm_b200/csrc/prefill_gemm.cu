@@ -11,32 +11,36 @@
 //     t_s = ((d*sc_s)*as_s)*dot_s - ((dmin*m_s)*as_s)*sum_s
 // where dot_s = sum_l q_l a_q,l over the sub-block's 32 elements is an exact
 // integer (4-bit weights times int8 activations).  Here every dot_s of a
-// 128 x 128 output tile is one tcgen05.mma kind::i8 (M128 N128 K32, both
-// operands signed 8-bit -- the 4-bit weights are stored as int8 0..15 -- with
-// exact s32 accumulation into TMEM), and the epilogue warps apply t_s, the
-// partial and the row sum in exactly that f32 order (IEEE round-to-nearest,
-// no FMA contraction).  So C equals the reference bit for bit, like the GEMV.
+// 128 x 128 output tile comes from two tcgen05.mma kind::f16 (M128 N128 K16,
+// A and B bf16) into an f32 TMEM accumulator: the 4-bit weights (0..15) and
+// the int8 activations are exact in bf16, every product and every partial
+// sum is an integer of magnitude below 2^16, so the f32 accumulation is exact
+// whatever its order -- and the epilogue reads dot_s as a float, with no
+// integer conversion.  The epilogue warps then apply t_s, the partial and the
+// row sum in exactly the reference's f32 order (IEEE round-to-nearest, no
+// FMA contraction).  So C equals the reference bit for bit, like the GEMV.
 //
 // Operand layouts (prepared by prefill_w_prep_kernel / the packers):
-//   weights  wq  int8 [n][k] (the 4-bit values), then at byte offset
-//                align1024(n*k) per sub-block s two f32 rows of pad4(n):
-//                d*sc_s at [2s][col], -(dmin*m_s) at [2s + 1][col]
-//   activ.   aq  int8 [m][k], then at align1024(m*k) per sub-block s two f32
-//                rows of pad4(m): as_s at [2s][row], sum_s at [2s + 1][row]
+//   weights  wq  bf16 [n][k] (the 4-bit values), then at byte offset
+//                pf_scale_offset(n, k) per sub-block s two f32 rows of
+//                pad4(n): d*sc_s at [2s][col], -(dmin*m_s) at [2s + 1][col]
+//   activ.   aq  bf16 [m][k] (the int8 values), then at pf_scale_offset(m, k)
+//                per sub-block s two f32 rows of pad4(m): as_s at [2s][row],
+//                sum_s at [2s + 1][row]
 // (the min term is stored negated: t = t1 + (-t2) is exactly t1 - t2).
 //
 // Kernel: one CTA per 128 x 128 output tile, 576 threads.  Warp 0 lane 0 is
 // the TMA producer, warp 1 lane 0 the MMA issuer, warps 2..17 the epilogue
 // (warp w reads TMEM lanes 32(w % 4) .. +31 = tile rows, columns
 // 32((w - 2) / 4) .. +31; four epilogue warps per SM sub-partition hide the
-// TMEM-load and shared-memory latencies).  A stage holds a 128-byte K slice
-// (four sub-blocks): the A and B tiles (128B-swizzled, K-major) and the four
-// sub-blocks' scale rows of the tile's rows and columns = 40 KB; four
-// stages.  TMEM holds four s32 accumulators of 128 columns (512 columns), one
-// per sub-block of a stage: the MMA of sub-block s of stage kb waits until the
-// epilogue has read accumulator s of stage kb-1, so tensor core and epilogue
-// overlap.  A stage is released when its MMAs have completed (tcgen05.commit)
-// and all sixteen epilogue warps have read its scales.  The row sums c live
+// TMEM-load and shared-memory latencies).  A stage holds a 64-element K
+// slice (two sub-blocks): the A and B tiles (128B-swizzled, K-major) and the
+// two sub-blocks' scale rows of the tile's rows and columns = 36 KB; four
+// stages.  TMEM holds four f32 accumulators of 128 columns (512 columns),
+// used by sub-blocks in turn: the MMAs of sub-block g wait until the
+// epilogue has read accumulator g % 4 for sub-block g - 4, so tensor core
+// and epilogue overlap.  A stage is released when its MMAs have completed
+// (tcgen05.commit) and all sixteen epilogue warps have read its scales.  The row sums c live
 // in shared memory (updated once per super-block), the partials in
 // registers; every operation is a scalar IEEE round-to-nearest multiply or
 // add (__fmul_rn / __fadd_rn are never contracted into FMAs).  Packed f32x2
@@ -51,6 +55,7 @@
 // offsets that are multiples of 128, so every x coordinate is 16-byte
 // aligned; no multicast.
 #include <cuda.h>
+#include <cuda_bf16.h>
 
 #include "eos_common.cuh"
 #include "eos_kernels.h"
@@ -58,14 +63,15 @@
 
 namespace eos {
 
-constexpr uint32_t QG_BM = 128, QG_BN = 128, QG_BK = 128;  // BK in bytes = int8 elements
-constexpr uint32_t QG_SUBS = QG_BK / 32u;                  // sub-blocks per stage
+constexpr uint32_t QG_BM = 128, QG_BN = 128, QG_BK = 64;  // BK in bf16 elements: 128-byte rows
+constexpr uint32_t QG_SUBS = QG_BK / 32u;                 // sub-blocks per stage (2)
+constexpr uint32_t QG_ACCS = 4;                           // TMEM accumulators of QG_BN f32 columns
 constexpr uint32_t QG_STAGES = 4;
-constexpr uint32_t QG_A_BYTES = QG_BM * QG_BK;                                   // 16 KB
-constexpr uint32_t QG_B_BYTES = QG_BN * QG_BK;                                   // 16 KB
-constexpr uint32_t QG_AS_BYTES = QG_SUBS * QG_BM * 8u;                           // 4 KB
-constexpr uint32_t QG_BS_BYTES = QG_SUBS * QG_BN * 8u;                           // 4 KB
-constexpr uint32_t QG_STAGE_BYTES = QG_A_BYTES + QG_B_BYTES + QG_AS_BYTES + QG_BS_BYTES;  // 40 KB
+constexpr uint32_t QG_A_BYTES = QG_BM * QG_BK * 2u;                              // 16 KB
+constexpr uint32_t QG_B_BYTES = QG_BN * QG_BK * 2u;                              // 16 KB
+constexpr uint32_t QG_AS_BYTES = 2u * QG_SUBS * QG_BM * 4u;                      // 2 KB
+constexpr uint32_t QG_BS_BYTES = 2u * QG_SUBS * QG_BN * 4u;                      // 2 KB
+constexpr uint32_t QG_STAGE_BYTES = QG_A_BYTES + QG_B_BYTES + QG_AS_BYTES + QG_BS_BYTES;  // 36 KB
 constexpr uint32_t QG_EPI_WARPS = 16;
 constexpr uint32_t QG_COLS = QG_BN * 4u / QG_EPI_WARPS;  // columns per epilogue thread (32)
 constexpr uint32_t QG_THREADS = 32u * (2u + QG_EPI_WARPS);
@@ -73,54 +79,52 @@ constexpr uint32_t QG_ACC_BYTES = QG_EPI_WARPS * 32u * QG_COLS * 4u;  // row sum
 constexpr uint32_t QG_SMEM = QG_STAGES * QG_STAGE_BYTES + QG_ACC_BYTES + 1024u + 256u;
 constexpr uint32_t QG_TMEM_COLS = 512;
 
-__host__ __device__ constexpr size_t qg_align1024(size_t x) { return (x + 1023u) & ~(size_t)1023u; }
-
 // ---------------------------------------------------------------------------
 // Operand preparation
 // ---------------------------------------------------------------------------
-// One thread per (row n, super-block b); consecutive threads take consecutive
-// rows of the same super-block, so the scale stores are coalesced.  Values:
-// q (0..15) as int8 at [n][256 b + 32 s + l]; d*sc_s and -(dmin*m_s) with the
-// reference's rounding of d*sc and dmin*m (both __fmul_rn).
+// bf16 bit patterns of the integers 0..15 (exact), two per word.
+__device__ __forceinline__ uint32_t bf16_pair(uint32_t lo, uint32_t hi) {
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn((float)lo)) |
+         ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn((float)hi)) << 16);
+}
+// Eight 4-bit values of the word pair (x, y) (bytes b0..b7, nibble `sh`) as
+// eight bf16 in a 16-byte vector.
+__device__ __forceinline__ uint4 nib8_bf16(uint32_t x, uint32_t y, uint32_t sh) {
+  return make_uint4(bf16_pair((x >> sh) & 15u, (x >> (8 + sh)) & 15u), bf16_pair((x >> (16 + sh)) & 15u, (x >> (24 + sh)) & 15u),
+                    bf16_pair((y >> sh) & 15u, (y >> (8 + sh)) & 15u), bf16_pair((y >> (16 + sh)) & 15u, (y >> (24 + sh)) & 15u));
+}
+
+// One warp per super-block (row-major order: row * k/256 + b).  Lane l writes
+// elements 8l .. 8l+7 (sub-block l/4) as bf16 -- the warp's 512 bytes are
+// contiguous -- from the 8 bytes of qs that hold them (sub-block pair p =
+// s/2 at bytes 32p .. 32p+31: low nibbles = sub-block 2p, high = 2p+1);
+// lanes 0..7 write sub-block l's d*sc and -(dmin*m) with the reference's
+// rounding (both __fmul_rn).
 __global__ void __launch_bounds__(256) prefill_w_prep_kernel(const uint8_t* __restrict__ w, uint32_t n, uint32_t k,
-                                                             int8_t* __restrict__ wq, float* __restrict__ wsc) {
-  const uint32_t nb = k / Q4K_ELEMS;
-  const uint64_t t = (uint64_t)blockIdx.x * 256u + threadIdx.x;
-  if (t >= (uint64_t)n * nb) return;
-  const uint32_t b = (uint32_t)(t / n), row = (uint32_t)(t % n);
-  const uint8_t* blk = w + ((size_t)row * nb + b) * Q4K_BYTES;
-  const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-  const float d = f16_bits_to_f32(hdr.x), dmin = f16_bits_to_f32(hdr.x >> 16);
-  const uint32_t npad = pf_pad4(n);
-  const uint32_t sc8[3] = {hdr.y, hdr.z, hdr.w};
-  const uint8_t* scb = reinterpret_cast<const uint8_t*>(sc8);
-#pragma unroll
-  for (int s = 0; s < 8; ++s) {
+                                                             uint16_t* __restrict__ wq, float* __restrict__ wsc) {
+  const uint32_t nb = k / Q4K_ELEMS, lane = threadIdx.x & 31u;
+  const uint64_t wi = (uint64_t)blockIdx.x * 8u + (threadIdx.x >> 5);
+  if (wi >= (uint64_t)n * nb) return;  // warp-uniform
+  const uint32_t row = (uint32_t)(wi / nb), b = (uint32_t)(wi % nb);
+  const uint8_t* blk = w + wi * Q4K_BYTES;
+  const uint32_t s = lane >> 2, p = s >> 1;
+  const uint2 x = *reinterpret_cast<const uint2*>(blk + 16u + 32u * p + 8u * (lane & 3u));
+  reinterpret_cast<uint4*>(wq + (size_t)row * k + (size_t)b * Q4K_ELEMS)[lane] = nib8_bf16(x.x, x.y, 4u * (s & 1u));
+  if (lane < 8u) {
+    const uint32_t h = *reinterpret_cast<const uint32_t*>(blk);
+    const float d = f16_bits_to_f32(h), dmin = f16_bits_to_f32(h >> 16);
     uint32_t sc, m;
-    q4k_scale_min(s, scb, sc, m);
-    wsc[(size_t)(2u * (b * 8u + s)) * npad + row] = __fmul_rn(d, (float)sc);
-    wsc[(size_t)(2u * (b * 8u + s) + 1u) * npad + row] = -__fmul_rn(dmin, (float)m);
-  }
-  // sub-block pair p: bytes 32p .. 32p+31 of qs; low nibbles = sub-block 2p,
-  // high nibbles = sub-block 2p+1
-  uint4* out = reinterpret_cast<uint4*>(wq + (size_t)row * k + (size_t)b * Q4K_ELEMS);
-  const uint4* qs = reinterpret_cast<const uint4*>(blk + 16);
-  constexpr uint32_t LO = 0x0F0F0F0Fu;
-#pragma unroll
-  for (int p = 0; p < 4; ++p) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint4 x = qs[2 * p + h];
-      out[4 * p + h] = make_uint4(x.x & LO, x.y & LO, x.z & LO, x.w & LO);
-      out[4 * p + 2 + h] = make_uint4((x.x >> 4) & LO, (x.y >> 4) & LO, (x.z >> 4) & LO, (x.w >> 4) & LO);
-    }
+    q4k_scale_min((int)lane, blk + 4, sc, m);
+    const uint32_t npad = pf_pad4(n);
+    wsc[(size_t)(2u * (b * 8u + lane)) * npad + row] = __fmul_rn(d, (float)sc);
+    wsc[(size_t)(2u * (b * 8u + lane) + 1u) * npad + row] = -__fmul_rn(dmin, (float)m);
   }
 }
 
 // quantize_sub32 per 32 activations (matmul_q4_k_int8.c:98-154), one warp
 // per group: int8 values, the scale and the sum.
 __global__ void __launch_bounds__(256) prefill_act_pack_kernel(const float* __restrict__ a, uint32_t m, uint32_t k,
-                                                               int8_t* __restrict__ aq, float* __restrict__ asc) {
+                                                               uint16_t* __restrict__ aq, float* __restrict__ asc) {
   const uint32_t groups = m * (k / 32u);
   const uint32_t g = blockIdx.x * 8u + (threadIdx.x >> 5), lane = threadIdx.x & 31u;
   if (g >= groups) return;  // warp-uniform
@@ -144,17 +148,17 @@ __device__ __forceinline__ uint64_t qg_sw128_desc(uint32_t smem_addr) {
   return dsc;
 }
 
-// Instruction descriptor, kind::i8: D s32 (2 << 4), A and B signed 8-bit
-// (1 << 7, 1 << 10), both K-major, N = 128, M = 128.
-constexpr uint32_t QG_IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((QG_BN >> 3) << 17) | ((QG_BM >> 4) << 24);
+// Instruction descriptor, kind::f16: D f32 (1 << 4), A and B bf16 (1 << 7,
+// 1 << 10, the same type), both K-major, N = 128, M = 128.
+constexpr uint32_t QG_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((QG_BN >> 3) << 17) | ((QG_BM >> 4) << 24);
 
-// D = A . B^T into a fresh accumulator (enable-input-d false)
-__device__ __forceinline__ void qg_mma(uint32_t tmem_d, uint64_t da, uint64_t db) {
+// D (+)= A . B^T over K = 16 (accumulate: enable-input-d)
+__device__ __forceinline__ void qg_mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(QG_IDESC), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(QG_IDESC), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
       : "memory");
 }
 
@@ -174,8 +178,8 @@ __device__ __forceinline__ void qg_tma_2d(void* dst, const CUtensorMap* map, uin
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 32 consecutive s32 accumulator columns of this thread's TMEM lane.
-__device__ __forceinline__ void qg_ld32(uint32_t taddr, int32_t (&r)[32]) {
+// 32 consecutive accumulator columns (f32 bits) of this thread's TMEM lane.
+__device__ __forceinline__ void qg_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -210,8 +214,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + QG_STAGES * QG_STAGE_BYTES + QG_ACC_BYTES);
   uint64_t* empty = full + QG_STAGES;
   uint64_t* tfull = empty + QG_STAGES;
-  uint64_t* tempty = tfull + QG_SUBS;
-  uint64_t* done = tempty + QG_SUBS;
+  uint64_t* tempty = tfull + QG_ACCS;
+  uint64_t* done = tempty + QG_ACCS;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
@@ -223,14 +227,14 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1 + QG_EPI_WARPS);
     }
-    for (uint32_t j = 0; j < QG_SUBS; ++j) {
+    for (uint32_t j = 0; j < QG_ACCS; ++j) {
       mbar_init(&tfull[j], 1);
       mbar_init(&tempty[j], QG_EPI_WARPS);
     }
     mbar_init(done, 1);
     fence_barrier_init();
   }
-  if (warp == 0) {  // TMEM: 128 lanes x 512 s32 columns = four 128-column accumulators
+  if (warp == 0) {  // TMEM: 128 lanes x 512 f32 columns = four 128-column accumulators
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(QG_TMEM_COLS)
                  : "memory");
@@ -277,15 +281,19 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         uint8_t* base = smem + s * QG_STAGE_BYTES;
         const uint64_t da = qg_sw128_desc(smem_u32(base)), db = qg_sw128_desc(smem_u32(base + QG_A_BYTES));
         for (uint32_t j = 0; j < QG_SUBS; ++j) {
-          // accumulator j is free once the epilogue has read it for stage kb-1
-          if (kb > 0 && !mbar_wait(&tempty[j], (kb - 1u) & 1u)) {
+          const uint32_t g = kb * QG_SUBS + j, a = g % QG_ACCS, u = g / QG_ACCS;
+          // accumulator a is free once the epilogue has read sub-block g - 4
+          if (u > 0 && !mbar_wait(&tempty[a], (u - 1u) & 1u)) {
             report(p.err, EOS_DEVERR_WAIT_EMPTY);
             ok = false;
             break;
           }
           tc_fence_after();
-          qg_mma(tmem + j * QG_BN, da + 2u * j, db + 2u * j);  // K offset 32 j bytes
-          qg_commit(&tfull[j]);
+          // elements 32 j .. 32 j + 31 of the 64-element slice: byte offsets
+          // 64 j and 64 j + 32 (descriptor start in 16-byte units)
+          qg_mma(tmem + a * QG_BN, da + 4u * j, db + 4u * j, 0u);
+          qg_mma(tmem + a * QG_BN, da + 4u * j + 2u, db + 4u * j + 2u, 1u);
+          qg_commit(&tfull[a]);
         }
         qg_commit(&empty[s]);  // the stage's A/B tiles are consumed once these MMAs complete
       }
@@ -296,16 +304,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     const uint32_t e = warp - 2u, quad = warp & 3u, cg = e >> 2;
     const uint32_t lrow = quad * 32u + lane;  // tile row of this thread
     const uint32_t col0 = cg * QG_COLS;       // first tile column of this thread
-    // row sums c (updated once per super-block) in shared memory, column pair
-    // c2 at acc[32 c2]; super-block partials (updated every sub-block) in
-    // registers
-    float2* acc = reinterpret_cast<float2*>(acc_s) + e * (QG_COLS / 2u) * 32u + lane;
-    float2 part[QG_COLS / 2];
+    // row sums c (updated once per super-block) in shared memory, columns
+    // 4 c4 .. 4 c4 + 3 at acc[32 c4]; super-block partials (updated every
+    // sub-block) in registers, reset to 0 after each super-block
+    float4* acc = reinterpret_cast<float4*>(acc_s) + e * (QG_COLS / 4u) * 32u + lane;
+    float part[QG_COLS];
 #pragma unroll
-    for (uint32_t c2 = 0; c2 < QG_COLS / 2; ++c2) {
-      acc[32 * c2] = make_float2(0.0f, 0.0f);  // c = 0 (:194)
-      part[c2] = make_float2(0.0f, 0.0f);
-    }
+    for (uint32_t c4 = 0; c4 < QG_COLS / 4; ++c4) acc[32 * c4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // c = 0 (:194)
+#pragma unroll
+    for (uint32_t c = 0; c < QG_COLS; ++c) part[c] = 0.0f;  // partial = 0
     bool ok = true;
     for (uint32_t kb = 0; kb < nkb && ok; ++kb) {
       const uint32_t s = kb % QG_STAGES;
@@ -315,36 +322,43 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       const float* as_s = reinterpret_cast<const float*>(base + QG_A_BYTES + QG_B_BYTES);  // [2 j + {0,1}][128]
       const float* bs_s = reinterpret_cast<const float*>(base + QG_A_BYTES + QG_B_BYTES + QG_AS_BYTES);
       for (uint32_t j = 0; j < QG_SUBS && ok; ++j) {
-        const uint32_t sb = (kb * QG_SUBS + j) & 7u;  // sub-block index within its super-block
-        ok = __all_sync(0xffffffffu, mbar_wait(&tfull[j], kb & 1u)) != 0;
+        const uint32_t g = kb * QG_SUBS + j, a = g % QG_ACCS;
+        ok = __all_sync(0xffffffffu, mbar_wait(&tfull[a], (g / QG_ACCS) & 1u)) != 0;
         if (!ok) break;
         tc_fence_after();
-        int32_t r[32];
-        qg_ld32(tmem + ((quad * 32u) << 16) + j * QG_BN + col0, r);
+        uint32_t r[32];
+        qg_ld32(tmem + ((quad * 32u) << 16) + a * QG_BN + col0, r);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[j]);  // accumulator j may be overwritten
+        if (lane == 0) mbar_arrive(&tempty[a]);  // accumulator a may be overwritten
         const float as = as_s[(2u * j) * QG_BM + lrow], sum = as_s[(2u * j + 1u) * QG_BM + lrow];
-        const float2* dsc = reinterpret_cast<const float2*>(bs_s + (2u * j) * QG_BN + col0);       // d*sc
-        const float2* nmn = reinterpret_cast<const float2*>(bs_s + (2u * j + 1u) * QG_BN + col0);  // -(dmin*m)
+        const float4* dsc = reinterpret_cast<const float4*>(bs_s + (2u * j) * QG_BN + col0);       // d*sc
+        const float4* nmn = reinterpret_cast<const float4*>(bs_s + (2u * j + 1u) * QG_BN + col0);  // -(dmin*m)
 #pragma unroll
-        for (uint32_t c2 = 0; c2 < QG_COLS / 2; ++c2) {
-          const float2 dot = make_float2((float)r[2 * c2], (float)r[2 * c2 + 1]);
-          // t = ((d*sc)*as)*dot - ((dmin*m)*as)*sum   (:254-261)
-          const float2 dd = dsc[c2], nn = nmn[c2];
-          // t1 + (-t2): t2 carries the stored sign of -(dmin*m), exactly -t2
-          const float tx = __fadd_rn(__fmul_rn(__fmul_rn(dd.x, as), dot.x), __fmul_rn(__fmul_rn(nn.x, as), sum));
-          const float ty = __fadd_rn(__fmul_rn(__fmul_rn(dd.y, as), dot.y), __fmul_rn(__fmul_rn(nn.y, as), sum));
-          float2 pp = part[c2];
-          pp.x = __fadd_rn(sb == 0 ? 0.0f : pp.x, tx);  // partial = 0; partial += t
-          pp.y = __fadd_rn(sb == 0 ? 0.0f : pp.y, ty);
-          part[c2] = pp;
-          if (sb == 7) {  // c += partial (:264)
-            float2 a2 = acc[32 * c2];
-            a2.x = __fadd_rn(a2.x, pp.x);
-            a2.y = __fadd_rn(a2.y, pp.y);
-            acc[32 * c2] = a2;
+        for (uint32_t c4 = 0; c4 < QG_COLS / 4; ++c4) {
+          const float4 dd = dsc[c4], nn = nmn[c4];  // broadcast
+          const float d4[4] = {dd.x, dd.y, dd.z, dd.w}, n4[4] = {nn.x, nn.y, nn.z, nn.w};
+#pragma unroll
+          for (uint32_t i = 0; i < 4; ++i) {
+            const uint32_t c = 4u * c4 + i;
+            // t = ((d*sc)*as)*dot - ((dmin*m)*as)*sum   (:254-261), as t1 + (-t2)
+            const float t = __fadd_rn(__fmul_rn(__fmul_rn(d4[i], as), __uint_as_float(r[c])),
+                                      __fmul_rn(__fmul_rn(n4[i], as), sum));
+            part[c] = __fadd_rn(part[c], t);  // partial += t
           }
+        }
+        if ((g & 7u) == 7u) {  // super-block complete: c += partial (:264), partial = 0
+#pragma unroll
+          for (uint32_t c4 = 0; c4 < QG_COLS / 4; ++c4) {
+            float4 v = acc[32 * c4];
+            v.x = __fadd_rn(v.x, part[4 * c4]);
+            v.y = __fadd_rn(v.y, part[4 * c4 + 1]);
+            v.z = __fadd_rn(v.z, part[4 * c4 + 2]);
+            v.w = __fadd_rn(v.w, part[4 * c4 + 3]);
+            acc[32 * c4] = v;
+          }
+#pragma unroll
+          for (uint32_t c = 0; c < QG_COLS; ++c) part[c] = 0.0f;
         }
       }
       __syncwarp();
@@ -358,20 +372,19 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         float* crow = p.c + (size_t)row * p.n + gcol;
         if (gcol + QG_COLS <= p.n && (p.n & 3u) == 0) {
 #pragma unroll
-          for (uint32_t c2 = 0; c2 < QG_COLS / 2; c2 += 2) {
-            const float2 v0 = acc[32 * c2], v1 = acc[32 * (c2 + 1)];
-            float4 v = make_float4(v0.x, v0.y, v1.x, v1.y);
+          for (uint32_t c4 = 0; c4 < QG_COLS / 4; ++c4) {
+            float4 v = acc[32 * c4];
             if (p.accumulate) {
-              const float4 o = *reinterpret_cast<const float4*>(crow + 2 * c2);
+              const float4 o = *reinterpret_cast<const float4*>(crow + 4 * c4);
               v = make_float4(__fadd_rn(o.x, v.x), __fadd_rn(o.y, v.y), __fadd_rn(o.z, v.z), __fadd_rn(o.w, v.w));
             }
-            *reinterpret_cast<float4*>(crow + 2 * c2) = v;
+            *reinterpret_cast<float4*>(crow + 4 * c4) = v;
           }
         } else {
 #pragma unroll
           for (uint32_t c = 0; c < QG_COLS; ++c) {
-            const float2 v2 = acc[32 * (c / 2)];
-            const float v = (c & 1u) ? v2.y : v2.x;
+            const float4 v4 = acc[32 * (c / 4)];
+            const float v = (c & 3u) == 0 ? v4.x : ((c & 3u) == 1 ? v4.y : ((c & 3u) == 2 ? v4.z : v4.w));
             if (gcol + c < p.n) crow[c] = p.accumulate ? __fadd_rn(crow[c], v) : v;
           }
         }
@@ -409,15 +422,15 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// rows x k int8 row-major, boxes of 128 rows x 128 bytes with the 128-byte swizzle
-bool make_i8_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t k) {
+// rows x k bf16 row-major, boxes of 128 rows x 64 elements (128 bytes) with the 128-byte swizzle
+bool make_bf16_map(CUtensorMap* map, const void* base, uint32_t rows, uint32_t k) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[2] = {k, rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)k};
+  const cuuint64_t strides[1] = {(cuuint64_t)k * 2u};
   const cuuint32_t box[2] = {QG_BK, 128u};
   const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -437,24 +450,24 @@ bool make_scale_map(CUtensorMap* map, const void* base, uint32_t cols, uint32_t 
 }  // namespace
 
 size_t prefill_operand_bytes(uint32_t rows, uint32_t k) {
-  return qg_align1024((size_t)rows * k) + (size_t)(k / 32u) * 2u * pf_pad4(rows) * 4u;
+  return pf_scale_offset(rows, k) + (size_t)(k / 32u) * 2u * pf_pad4(rows) * 4u;
 }
 
 cudaError_t launch_prefill_act_pack(const float* a, uint32_t m, uint32_t k, void* act, cudaStream_t st) {
   const uint32_t groups = m * (k / 32u);
   if (groups == 0) return cudaSuccess;
-  int8_t* aq = static_cast<int8_t*>(act);
-  float* asc = reinterpret_cast<float*>(static_cast<uint8_t*>(act) + qg_align1024((size_t)m * k));
+  uint16_t* aq = static_cast<uint16_t*>(act);
+  float* asc = reinterpret_cast<float*>(static_cast<uint8_t*>(act) + pf_scale_offset(m, k));
   prefill_act_pack_kernel<<<(groups + 7u) / 8u, 256, 0, st>>>(a, m, k, aq, asc);
   return cudaGetLastError();
 }
 
 cudaError_t launch_prefill_w_prep(const uint8_t* w, uint32_t n, uint32_t k, void* wprep, cudaStream_t st) {
-  const uint64_t threads = (uint64_t)n * (k / Q4K_ELEMS);
-  if (threads == 0) return cudaSuccess;
-  int8_t* wq = static_cast<int8_t*>(wprep);
-  float* wsc = reinterpret_cast<float*>(static_cast<uint8_t*>(wprep) + qg_align1024((size_t)n * k));
-  prefill_w_prep_kernel<<<(uint32_t)((threads + 255u) / 256u), 256, 0, st>>>(w, n, k, wq, wsc);
+  const uint64_t warps = (uint64_t)n * (k / Q4K_ELEMS);
+  if (warps == 0) return cudaSuccess;
+  uint16_t* wq = static_cast<uint16_t*>(wprep);
+  float* wsc = reinterpret_cast<float*>(static_cast<uint8_t*>(wprep) + pf_scale_offset(n, k));
+  prefill_w_prep_kernel<<<(uint32_t)((warps + 7u) / 8u), 256, 0, st>>>(w, n, k, wq, wsc);
   return cudaGetLastError();
 }
 
@@ -468,9 +481,9 @@ cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, ui
   const uint8_t* ab = static_cast<const uint8_t*>(act);
   const uint8_t* wb = static_cast<const uint8_t*>(wprep);
   CUtensorMap ma, mb, mas, mbs;
-  if (!make_i8_map(&ma, ab, m, k) || !make_i8_map(&mb, wb, n, k) ||
-      !make_scale_map(&mas, ab + qg_align1024((size_t)m * k), m, k) ||
-      !make_scale_map(&mbs, wb + qg_align1024((size_t)n * k), n, k)) {
+  if (!make_bf16_map(&ma, ab, m, k) || !make_bf16_map(&mb, wb, n, k) ||
+      !make_scale_map(&mas, ab + pf_scale_offset(m, k), m, k) ||
+      !make_scale_map(&mbs, wb + pf_scale_offset(n, k), n, k)) {
     *out_status = EOS_E_UNSUPPORTED;
     return cudaSuccess;
   }

@@ -47,7 +47,7 @@ struct PfNormParams {
   const float* w;            // norm weight
   float eps;
   uint32_t n, pitch;         // pitch: pad4(m), the scale pairs' row pitch
-  int8_t* aq;                // GEMM activation layout (pf_pack_group)
+  uint16_t* aq;                // GEMM activation layout (pf_pack_group)
   float* asc;
 };
 
@@ -160,7 +160,7 @@ struct PfAttnParams {
   const float* qkv;  // q rotated
   const float* kc;
   const float* vc;
-  int8_t* aq;  // GEMM activation layout, k = hl HD
+  uint16_t* aq;  // GEMM activation layout, k = hl HD
   float* asc;
   uint32_t m, hl, kvl, h0, kv0, n_head, n_kv_head, pos0;
   float scale;
@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(128) pf_attn_kernel(const PfAttnParams p) {
 // ---------------------------------------------------------------------------
 // Grid (ffl / 256, m), 256 threads; ffl % 32 == 0, so every warp is one group.
 __global__ void __launch_bounds__(256) pf_silu_pack_kernel(const float* __restrict__ gu, uint32_t ffl,
-                                                           uint32_t pitch, int8_t* __restrict__ aq,
+                                                           uint32_t pitch, uint16_t* __restrict__ aq,
                                                            float* __restrict__ asc) {
   const uint32_t row = blockIdx.y, i = blockIdx.x * 256u + threadIdx.x;
   if (i >= ffl) return;  // warp-uniform
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(256) pf_silu_pack_kernel(const float* __restri
 // Host launchers
 // ---------------------------------------------------------------------------
 namespace {
-int8_t* act_q(void* act) { return static_cast<int8_t*>(act); }
+uint16_t* act_q(void* act) { return static_cast<uint16_t*>(act); }
 float* act_sc(void* act, uint32_t m, uint32_t k) {
   return reinterpret_cast<float*>(static_cast<uint8_t*>(act) + pf_scale_offset(m, k));
 }

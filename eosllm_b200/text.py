@@ -130,6 +130,13 @@ class TextDecoder:
         B.check(self.lib.eosi_cuda_text_set_prefill_min(self.handle, int(min_tokens)),
                 "eosi_cuda_text_set_prefill_min")
 
+    def set_prefill_resident(self, resident: bool) -> None:
+        """Keep every layer's weights prepared for the prefill GEMM (default,
+        when they fit in half of the free memory) or prepare each matrix just
+        before its GEMM."""
+        B.check(self.lib.eosi_cuda_text_set_prefill_resident(self.handle, int(bool(resident))),
+                "eosi_cuda_text_set_prefill_resident")
+
     def reset(self) -> None:
         B.check(self.lib.eosi_cuda_text_reset(self.handle), "eosi_cuda_text_reset")
 

@@ -261,6 +261,12 @@ EOSLLM_CUDA_API int eosi_cuda_text_generate(eosi_cuda_text_t *t, const uint32_t 
  * 16, 0 = never). */
 EOSLLM_CUDA_API int eosi_cuda_text_prefill(eosi_cuda_text_t *t, const uint32_t *tokens, uint32_t n);
 EOSLLM_CUDA_API int eosi_cuda_text_set_prefill_min(eosi_cuda_text_t *t, uint32_t min_tokens);
+/* The batched prefill's linears read weights prepared into the tensor-core
+ * layout (4-bit values as bf16 plus per-32 scales, 2.25 bytes per weight).
+ * resident != 0 (default): all layers are prepared once, at the first
+ * prefill, when that fits in half of the free device memory, and kept;
+ * 0: each matrix is prepared into a scratch buffer just before its GEMM. */
+EOSLLM_CUDA_API int eosi_cuda_text_set_prefill_resident(eosi_cuda_text_t *t, int resident);
 /* Position back to 0 (the KV cache is overwritten as steps proceed). */
 EOSLLM_CUDA_API int eosi_cuda_text_reset(eosi_cuda_text_t *t);
 EOSLLM_CUDA_API uint32_t eosi_cuda_text_pos(const eosi_cuda_text_t *t);

@@ -1,9 +1,10 @@
 """Tensor-core prefill GEMM (eosllm_b200/csrc/prefill_gemm.cu) against the
 oracle's int8 matmul, which is the reference's own arithmetic
 (eosi_avx2_matmul_q4_k_int8, matmul_q4_k_int8.c:164-269): the bar is bit for
-bit.  Every sub-block dot is an exact int8 tensor-core MMA and the epilogue
-rescales and sums in the reference's f32 order, so the outputs must be
-identical, including at extreme activation scales."""
+bit.  Every sub-block dot is exact on the tensor cores (integers held in bf16,
+f32 accumulation of integers below 2^16) and the epilogue rescales and sums
+in the reference's f32 order, so the outputs must be identical, including
+at extreme activation scales."""
 from __future__ import annotations
 
 import numpy as np
@@ -59,19 +60,19 @@ def test_prefill_zero_and_ragged_rows(gpu, oracle):
 
 
 def test_prefill_weight_layout(gpu, oracle):
-    """The prepared weights hold the 4-bit values as int8 and, per 32, rows of
+    """The prepared weights hold the 4-bit values as bf16 and, per 32, rows of
     d*sc and -(dmin*m) whose combination d*sc*q - dmin*m is the reference's
     dequantization (matmul_q4_k.c:79-98)."""
     n, k = 64, 512
     _, _, wprep, w = _run(gpu, oracle, 128, n, k, seed=5)
     buf = wprep.cpu().numpy()
-    q = buf[:n * k].view(np.int8).reshape(n, k).astype(np.float32)
-    off = (n * k + 1023) // 1024 * 1024
+    q = (buf[:2 * n * k].view(np.uint16).astype(np.uint32) << 16).view(np.float32).reshape(n, k)  # bf16 values
+    off = (2 * n * k + 1023) // 1024 * 1024
     npad = (n + 3) // 4 * 4
     sc = buf[off:off + (k // 32) * 2 * npad * 4].view(np.float32).reshape(k // 32, 2, npad)[:, :, :n]
     dsc = np.repeat(sc[:, 0, :].T, 32, axis=1)
     dmn = -np.repeat(sc[:, 1, :].T, 32, axis=1)
-    assert q.min() >= 0 and q.max() <= 15
+    assert q.min() >= 0 and q.max() <= 15 and np.all(q == np.round(q))
     deq = oracle.q4_k_dequantize(w, n * k).reshape(n, k)
     np.testing.assert_array_equal((dsc * q - dmn).astype(np.float32), deq)
 

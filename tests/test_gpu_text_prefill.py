@@ -26,7 +26,7 @@ pytestmark = pytest.mark.gpu
 ENVELOPE_ORDERS = (1, 2, 3)  # rmsnorm strided, matmul blocks reversed, both
 
 
-def prefill_check(oracle, model, tokens, splits):
+def prefill_check(oracle, model, tokens, splits, resident=True):
     """Oracle: every token stepped, in the reference's order and with its
     sums reordered (orc_set_sum_order 1, 2, 3: rmsnorm strided, matmul blocks
     and products reversed, both -- the kinds of rounding-level change the
@@ -49,6 +49,7 @@ def prefill_check(oracle, model, tokens, splits):
     for a in alts:
         a.close()
     dec = TextDecoder(model)
+    dec.set_prefill_resident(resident)
     for a, b in splits:
         dec.prefill(tokens[a:b])
     assert dec.pos == n_pre
@@ -85,6 +86,14 @@ def test_prefill_in_pieces_and_odd_sizes(gpu, oracle):
     model = make_llama(oracle, max_ctx=160)
     tokens = np.random.default_rng(22).integers(0, model["config"]["n_vocab"], 150).astype(np.uint32)
     prefill_check(oracle, model, tokens, [(0, 1), (1, 18), (18, 53), (53, 141)])
+
+
+def test_prefill_weights_prepared_per_layer(gpu, oracle):
+    """The same pass with each matrix prepared just before its GEMM (the
+    path taken when the prepared weights do not fit)."""
+    model = make_llama(oracle, max_ctx=128, n_kv_head=2, n_layer=3)
+    tokens = np.random.default_rng(25).integers(0, model["config"]["n_vocab"], 100).astype(np.uint32)
+    prefill_check(oracle, model, tokens, [(0, 60), (60, 95)], resident=False)
 
 
 def test_prefill_longer_than_one_block(gpu, oracle):
