@@ -219,7 +219,9 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31u;
-  const uint32_t m0 = blockIdx.y * QG_BM, n0 = blockIdx.x * QG_BN;
+  // M tiles are the fast grid axis: the CTAs that share a weight tile run
+  // together, so the tile is read from HBM once and from L2 by the others
+  const uint32_t m0 = blockIdx.x * QG_BM, n0 = blockIdx.y * QG_BN;
   const uint32_t nkb = p.k / QG_BK;
 
   if (tid == 0) {
@@ -494,7 +496,7 @@ cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, ui
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  const dim3 grid((n + QG_BN - 1) / QG_BN, (m + QG_BM - 1) / QG_BM);
+  const dim3 grid((m + QG_BM - 1) / QG_BM, (n + QG_BN - 1) / QG_BN);
   PrefillParams prm{c, m, n, k, err, accumulate ? 1u : 0u};
   prefill_gemm_kernel<<<grid, QG_THREADS, QG_SMEM, st>>>(ma, mb, mas, mbs, prm);
   return cudaGetLastError();
