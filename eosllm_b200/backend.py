@@ -22,6 +22,9 @@ EOS_OK = 0
 EOS_E_INVALID_ARG = 1
 EOS_E_OUT_OF_MEMORY = 2
 EOS_E_UNSUPPORTED = 3
+EOS_E_FORMAT = 4
+EOS_E_NOT_FOUND = 6
+EOS_E_IO = 8
 EOS_E_INTERNAL = 9
 STATUS_NAMES = {0: "EOS_OK", 1: "EOS_E_INVALID_ARG", 2: "EOS_E_OUT_OF_MEMORY", 3: "EOS_E_UNSUPPORTED",
                 4: "EOS_E_FORMAT", 5: "EOS_E_VERSION_MISMATCH", 6: "EOS_E_NOT_FOUND", 7: "EOS_E_DEADLINE",
@@ -84,6 +87,9 @@ _SIGNATURES = {
     "eosi_cuda_text_generate": (C.c_int, [_vp, _vp, _u32, _u32, _vp]),
     "eosi_cuda_text_reset": (C.c_int, [_vp]),
     "eosi_cuda_text_prefill": (C.c_int, [_vp, _vp, _u32]),
+    "eosi_cuda_gguf_map": (C.c_int, [C.c_char_p, _u32, _vp, _vp]),
+    "eosi_cuda_gguf_unmap": (None, [_vp]),
+    "eosi_cuda_text_open_gguf": (C.c_int, [C.c_char_p, _u32, C.c_int, C.c_int, C.c_int, _vp]),
     "eosi_cuda_text_set_prefill_min": (C.c_int, [_vp, _u32]),
     "eosi_cuda_text_set_prefill_resident": (C.c_int, [_vp, C.c_int]),
     "eosi_cuda_text_pos": (_u32, [_vp]),

@@ -76,6 +76,23 @@ class TextDecoder:
                 "eosi_cuda_text_open")
         self._keep = None  # weights are resident on the device now
 
+    @classmethod
+    def from_gguf(cls, path: str, max_ctx: int = 0, device: int = 0, rank: int = 0, world: int = 1):
+        """eosi_cuda_text_open_gguf: a GGUF v3 Llama file straight to this
+        rank's GPU (only its own slices are read from the mapped file)."""
+        desc, g = gguf_map(path, max_ctx)
+        self = cls.__new__(cls)
+        self.lib = B.load()
+        self.config = {k: getattr(desc, k) for k in ("n_embd", "n_layer", "n_head", "n_kv_head", "n_ff", "n_vocab",
+                                                    "max_ctx", "rms_eps", "rope_base", "wdtype", "out_dtype")}
+        self.lib.eosi_cuda_gguf_unmap(g)
+        self.n_vocab = self.config["n_vocab"]
+        self._keep = None
+        self.handle = C.c_void_p()
+        B.check(self.lib.eosi_cuda_text_open_gguf(path.encode(), max_ctx, device, rank, world,
+                                                  C.byref(self.handle)), "eosi_cuda_text_open_gguf")
+        return self
+
     def ipc_handle(self) -> bytes:
         """This rank's exchange-buffer IPC handle (tensor parallel)."""
         buf = (C.c_ubyte * 64)()
@@ -158,6 +175,15 @@ class TextDecoder:
             self.close()
         except Exception:
             pass
+
+
+def gguf_map(path: str, max_ctx: int = 0):
+    """eosi_cuda_gguf_map (no GPU needed): (LlamaDesc with pointers into the
+    read-only mapping, mapping handle for eosi_cuda_gguf_unmap)."""
+    lib = B.load()
+    desc, g = LlamaDesc(), C.c_void_p()
+    B.check(lib.eosi_cuda_gguf_map(path.encode(), max_ctx, C.byref(g), C.byref(desc)), "eosi_cuda_gguf_map")
+    return desc, g
 
 
 def partition(config: dict, rank: int, world: int) -> dict:

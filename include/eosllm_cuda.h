@@ -293,6 +293,26 @@ EOSLLM_CUDA_API int eosi_cuda_text_partition(const eosi_cuda_llama_t *m, int ran
 EOSLLM_CUDA_API void *eosi_cuda_text_stream(eosi_cuda_text_t *t);
 EOSLLM_CUDA_API void eosi_cuda_text_close(eosi_cuda_text_t *t);
 
+/* ---- GGUF straight to the device -------------------------------------------
+ * eosi_cuda_gguf_map parses a GGUF v3 Llama-family file with the reference's
+ * rules (src/format/gguf/gguf.c; keys and tensors as eosi_text_open reads
+ * them, src/modality/text/text.c:104-215) from a read-only memory mapping,
+ * without reading it into host memory, and fills `desc` with pointers into
+ * the mapping (valid until eosi_cuda_gguf_unmap); no GPU is needed.  Errors
+ * as the reference's: EOS_E_IO (cannot open / map), EOS_E_FORMAT (bad magic,
+ * version, truncation, shapes, missing tensors), EOS_E_NOT_FOUND (a required
+ * key), EOS_E_UNSUPPORTED (tensor types the decoder cannot run: non-F16
+ * embeddings, a tied output, mixed linear types).  max_ctx: 0 keeps the
+ * file's context_length, else min(context_length, max_ctx).
+ * eosi_cuda_text_open_gguf = map + eosi_cuda_text_open + unmap: each rank
+ * copies only its own slices from the file to its GPU. */
+typedef struct eosi_cuda_gguf eosi_cuda_gguf_t;
+EOSLLM_CUDA_API int eosi_cuda_gguf_map(const char *path, uint32_t max_ctx, eosi_cuda_gguf_t **out,
+                                       eosi_cuda_llama_t *desc);
+EOSLLM_CUDA_API void eosi_cuda_gguf_unmap(eosi_cuda_gguf_t *g);
+EOSLLM_CUDA_API int eosi_cuda_text_open_gguf(const char *path, uint32_t max_ctx, int device, int rank, int world,
+                                             eosi_cuda_text_t **out);
+
 /* ---- diagnostics --------------------------------------------------------- */
 
 /* Device-side error bits raised by bounded waits since the last call on the

@@ -61,6 +61,11 @@ def llama_tokens(n_vocab: int) -> list[str]:
 
 def write_llama(path: str, model: dict) -> None:
     """model: dict from oracle.llama.make_llama (numpy arrays + config)."""
+    write_gguf(path, *llama_parts(model))
+
+
+def llama_parts(model: dict):
+    """(metadata, tensors) of write_llama, for tests that alter single items."""
     c = model["config"]
     meta = [("general.architecture", "llama"), ("general.alignment", ALIGN),
             ("llama.embedding_length", c["n_embd"]), ("llama.block_count", c["n_layer"]),
@@ -86,4 +91,4 @@ def write_llama(path: str, model: dict) -> None:
               (f"blk.{L}.ffn_gate.weight", [E, F], wt, lay["wg"].tobytes()),
               (f"blk.{L}.ffn_up.weight", [E, F], wt, lay["wu"].tobytes()),
               (f"blk.{L}.ffn_down.weight", [F, E], wt, lay["wd"].tobytes())]
-    write_gguf(path, meta, t)
+    return meta, t

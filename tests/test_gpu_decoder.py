@@ -217,3 +217,25 @@ def dec_tokens_after_reset(model, prompt, n):
     out = d.generate(prompt, n)
     d.close()
     return out
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(n_kv_head=2, wdtype=DT_Q8_0, out_dtype=DT_Q8_0)])
+def test_open_from_gguf_equals_open_from_arrays(gpu, oracle, tmp_path, kw):
+    """eosi_cuda_text_open_gguf (the file mapped, this rank's slices copied
+    straight to the GPU) steps bit-identically to eosi_cuda_text_open on the
+    same tensors, and matches the oracle like every decoder."""
+    from oracle.gguf_writer import write_llama
+    from eosllm_b200.text import TextDecoder
+    model = make_llama(oracle, max_ctx=48, **kw)
+    path = tmp_path / "m.gguf"
+    write_llama(str(path), model)
+    a, b = TextDecoder(model), TextDecoder.from_gguf(str(path), max_ctx=32)
+    assert b.config["max_ctx"] == 32 and b.n_vocab == model["config"]["n_vocab"]
+    ref = OracleDecoder(oracle, model)
+    for t in np.random.default_rng(13).integers(0, model["config"]["n_vocab"], 12):
+        la, lb = a.step(int(t)), b.step(int(t))
+        np.testing.assert_array_equal(la.view(np.uint32), lb.view(np.uint32))
+        assert logit_err(lb, ref.step(int(t))) <= LOGIT_TOL
+    ref.close()
+    a.close()
+    b.close()
