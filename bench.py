@@ -577,7 +577,9 @@ def run_prefill(args, dev, reps: int = 20) -> dict:
             raise SystemExit("prefill: device-side bounded wait reported an error")
         ms = e0.elapsed_time(e1) / reps
         tf = 2.0 * m * n * k / (ms * 1e-3) / 1e12
-        out["per_m"][str(m)] = {"ms": round(ms, 4), "tflops": round(tf, 1),
+        # tensor_frac: against the measured dense bf16 peak (the MMAs are
+        # bf16 x bf16 -> f32 over exactly 2 M N K operations)
+        out["per_m"][str(m)] = {"ms": round(ms, 4), "tflops": round(tf, 1), "tensor_frac": round(tf / peak, 4),
                                 "epilogue_gops": round(7.0 * m * n * (k // 32) / (ms * 1e-3) / 1e9, 1)}
     clocks.stop()
     cs = clocks.summary()
