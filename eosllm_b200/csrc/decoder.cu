@@ -50,8 +50,11 @@
 namespace eos {
 
 constexpr uint32_t kMaxParts = 8;
-constexpr uint32_t kAttnChunk = 64;     // positions per attention CTA
-constexpr uint32_t kMaxAttnChunks = 256;  // max_ctx <= 16384
+// 32 positions per attention CTA: 32 KB of K/V staging, small enough for an
+// attention CTA to share an SM with the two CTAs of the QKV GEMV before it
+// and start its K/V copies early (programmatic dependent launch)
+constexpr uint32_t kAttnChunk = 32;       // positions per attention CTA
+constexpr uint32_t kMaxAttnChunks = 512;  // max_ctx <= 16384
 constexpr uint32_t kMergeBatch = 16;      // chunks whose o[d] the merge loads in one batch
 constexpr uint32_t kArgmaxBlocks = 64;  // CTAs of the argmax kernel (upper bound)
 
@@ -255,7 +258,7 @@ struct AttnParams {
 __host__ __device__ constexpr uint32_t attn_smem_bytes(uint32_t hd) { return 2u * kAttnChunk * hd * 4u; }
 
 // Grid (hl, max_chunks), 128 threads.  E = dims per lane (head_dim = 32 E).
-// CTA (h, c) covers positions [64 c, 64 c + 64) up to `pos`: it stages the
+// CTA (h, c) covers positions [32 c, 32 c + 32) up to `pos`: it stages the
 // cached K and V rows of the chunk into shared memory with one batch of
 // 16-byte cp.async copies -- issued before the PDL wait, since rows < pos
 // were written by earlier steps -- then computes the scores (one warp per
@@ -306,6 +309,11 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
     }
     cp_async_commit();
   }
+  // the rotation at `pos` does not depend on this step's q and k: computed
+  // while the QKV GEMV still runs
+  float rsn[E / 2], rcs[E / 2];
+#pragma unroll
+  for (int e = 0; e < E; e += 2) rope_factors<HD>(d0 + e, pos, p.base, rsn[e / 2], rcs[e / 2]);
   pdl_wait();  // q, k, v of this step come from the QKV GEMV
 
   float q[E], kn[E], vn[E];
@@ -320,8 +328,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
   }
 #pragma unroll
   for (int e = 0; e < E; e += 2) {
-    rope_pair<HD>(q[e], q[e + 1], d0 + e, pos, p.base);
-    rope_pair<HD>(kn[e], kn[e + 1], d0 + e, pos, p.base);
+    rope_apply(q[e], q[e + 1], rsn[e / 2], rcs[e / 2]);
+    rope_apply(kn[e], kn[e + 1], rsn[e / 2], rcs[e / 2]);
   }
   const bool has_pos = p1 == pos + 1u;
   // the first local head of each KV group appends this step's K and V
@@ -1134,6 +1142,12 @@ int TextDecoder::capture() {
   cudaError_t e = hd == 64    ? cudaFuncSetAttribute(attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm)
                   : hd == 128 ? cudaFuncSetAttribute(attn_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm)
                               : cudaFuncSetAttribute(attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  // the largest shared-memory carveout, so that a kernel's CTAs can share an
+  // SM with the CTAs of the kernel before it (PDL overlap)
+  for (const void* f : {(const void*)attn_kernel<2>, (const void*)attn_kernel<4>, (const void*)attn_kernel<8>,
+                        (const void*)norm_pack_kernel, (const void*)silu_pack_kernel, (const void*)argmax_kernel})
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess) e = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);
   if (e == cudaSuccess) {
     const cudaError_t r = record_step(st);

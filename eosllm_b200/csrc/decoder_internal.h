@@ -43,14 +43,24 @@ struct DecLayer {
 // (rope.c:25-33): th = pos * base^(-i/HD), then the rotation with separately
 // rounded products.  Shared by the step attention and the batched prefill so
 // both rotate identically.
+// The rotation's sine and cosine depend only on (i, pos), so callers that
+// know the position early compute them first (rope_factors) and rotate later
+// (rope_apply); rope_pair does both.
 template <int HD>
-__device__ __forceinline__ void rope_pair(float& x0, float& x1, uint32_t i, uint32_t pos, float base) {
+__device__ __forceinline__ void rope_factors(uint32_t i, uint32_t pos, float base, float& sn, float& cs) {
   const float th = __fmul_rn((float)pos, powf(base, __fdiv_rn(-(float)i, (float)HD)));
-  float sn, cs;
   sincosf(th, &sn, &cs);
+}
+__device__ __forceinline__ void rope_apply(float& x0, float& x1, float sn, float cs) {
   const float p0 = x0, p1 = x1;
   x0 = __fsub_rn(__fmul_rn(p0, cs), __fmul_rn(p1, sn));
   x1 = __fadd_rn(__fmul_rn(p0, sn), __fmul_rn(p1, cs));
+}
+template <int HD>
+__device__ __forceinline__ void rope_pair(float& x0, float& x1, uint32_t i, uint32_t pos, float base) {
+  float sn, cs;
+  rope_factors<HD>(i, pos, base, sn, cs);
+  rope_apply(x0, x1, sn, cs);
 }
 
 // Batched prefill kernels (prefill_text.cu).  `act`: the prefill GEMM's

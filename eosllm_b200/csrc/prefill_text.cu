@@ -23,7 +23,7 @@
 // so with the step path's GEMV) given the same input vector; rmsnorm, RoPE
 // and SiLU use the step kernels' device arithmetic and order; attention is a
 // streaming softmax over 32-position chunks, where the step path merges
-// 64-position chunk softmaxes.  K/V rows therefore agree with the step path
+// 32-position chunk softmaxes.  K/V rows therefore agree with the step path
 // to the rounding of the attention sums, not bit for bit.
 #include <cmath>
 

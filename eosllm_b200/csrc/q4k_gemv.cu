@@ -454,6 +454,9 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   }
   if ((int)smem > cfg.smem_set) {
     cudaError_t e = cudaFuncSetAttribute(cfg.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // largest carveout: the next kernel's CTAs can share the SM (PDL overlap)
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(cfg.fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
     cfg.smem_set = (int)smem;
   }
