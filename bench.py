@@ -650,15 +650,15 @@ def run_decode(args, dev, world, rank) -> dict:
         "metric": "7B-shape Q4_K greedy decode tokens/s", "value": round(G / (decode_ms * 1e-3), 2),
         "unit": "tok/s", "ms_per_token": round(ms_tok, 4), "n_gpus": world,
         "prefill_tok_s": round(P / (prefill_ms * 1e-3), 2), "prompt": P, "generated": G,
-        # one GPU: prompt tokens 0..P-2 in one batched pass on the tensor cores
-        # (eosi_cuda_text_prefill), the last through the step graph; tensor
-        # parallel: every prompt token through the step graph
-        "prefill_mode": "batched_tcgen05" if world == 1 else "steps",
+        # prompt tokens 0..P-2 in one batched pass on the tensor cores
+        # (eosi_cuda_text_prefill; tensor parallel: each rank its slices, the
+        # partial rows pushed over NVLink), the last through the step graph
+        "prefill_mode": "batched_tcgen05",
         # the batched prefill's GEMM layout of every layer (bf16 4-bit values
         # + per-32 scales), prepared once at the warm-up prefill and kept
         "prefill_weights_gb": round(sum(B.prefill_weight_bytes(nn, kk) for nn, kk in (
             (3 * cfg["n_embd"], cfg["n_embd"]), (cfg["n_embd"], cfg["n_embd"]), (2 * cfg["n_ff"], cfg["n_embd"]),
-            (cfg["n_embd"], cfg["n_ff"]))) * cfg["n_layer"] / 1e9, 2) if world == 1 else None,
+            (cfg["n_embd"], cfg["n_ff"]))) * cfg["n_layer"] / world / 1e9, 2),  # per rank
         "config": dict(cfg, wdtype="Q4_K", out_dtype="Q4_K", kv_cache="f32", parallelism=f"tp{world}"),
         "e2e": {"value": round(G / wall_decode, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4},

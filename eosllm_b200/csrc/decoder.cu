@@ -57,6 +57,7 @@ constexpr uint32_t kAttnChunk = 32;       // positions per attention CTA
 constexpr uint32_t kMaxAttnChunks = 512;  // max_ctx <= 16384
 constexpr uint32_t kMergeBatch = 16;      // chunks whose o[d] the merge loads in one batch
 constexpr uint32_t kArgmaxBlocks = 64;  // CTAs of the argmax kernel (upper bound)
+constexpr uint32_t kPrefillRows = 1024;  // tokens per batched-prefill block
 
 // ---------------------------------------------------------------------------
 // Residual + rmsnorm + activation packing
@@ -84,14 +85,6 @@ struct NormPackParams {
   uint32_t xchg_per_step;
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // Tensor-parallel handshake of exchange `epoch`: thread 0 of the publishing
 // CTA raises this rank's flag in every rank's receive words with release
@@ -668,6 +661,10 @@ struct TextDecoder {
   // ranks write (push) into it through CUDA IPC mappings
   uint8_t* xbuf = nullptr;
   size_t xoff_po = 0, xoff_pd = 0, xoff_lg = 0, xoff_fl = 0, xbytes = 0;
+  // batched prefill (world > 1): receive slots [source rank][xpf_rows][n_embd]
+  // for the O and down partial rows, and the prefill's exchange counter
+  size_t xoff_pfo = 0, xoff_pfd = 0;
+  uint32_t xpf_rows = 0, pf_epoch = 0;
   uint8_t* xpeer[kMaxParts] = {};  // every rank's exchange buffer (own included)
   bool peer_opened[kMaxParts] = {};
   float* push_o[kMaxParts] = {};   // where this rank's O partial goes on the other ranks
@@ -726,7 +723,7 @@ struct TextDecoder {
   int open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws);
   int attach(const uint8_t* handles);
   // the batched path serves one GPU with Q4_K linears
-  bool prefill_ok() const { return world == 1 && m.wdtype == EOS_DT_Q4_K && m.n_layer > 0; }
+  bool prefill_ok() const { return m.wdtype == EOS_DT_Q4_K && m.n_layer > 0 && (world == 1 || xpf_rows > 0); }
   cudaError_t prefill(uint32_t n);  // tokens at prompt[host_pos, host_pos + n)
   XRecv* xrecv(int q) const { return reinterpret_cast<XRecv*>(xpeer[q] + xoff_fl); }
   cudaError_t record_step(cudaStream_t s);
@@ -858,6 +855,12 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
     xoff_lg = xoff_pd + up(4ull * E * ws);
     xoff_fl = xoff_lg + up(4ull * vmax);
     xbytes = xoff_fl + up(sizeof(XRecv));
+    if (ws > 1 && wdt == EOS_DT_Q4_K) {  // batched-prefill receive slots (allocated with the handles)
+      xpf_rows = m.max_ctx < kPrefillRows ? m.max_ctx : kPrefillRows;
+      xoff_pfo = xbytes;
+      xoff_pfd = xoff_pfo + up(4ull * ws * xpf_rows * E);
+      xbytes = xoff_pfd + up(4ull * ws * xpf_rows * E);
+    }
     chk(alloc(&xbuf, xbytes));
     part_o = reinterpret_cast<float*>(xbuf + xoff_po) + (size_t)E * rk;  // own slot
     part_d = reinterpret_cast<float*>(xbuf + xoff_pd) + (size_t)E * rk;
@@ -1041,8 +1044,6 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
   return e;
 }
 
-constexpr uint32_t kPrefillRows = 1024;  // tokens per batched-prefill block
-
 // Batched prefill of the n tokens at prompt[host_pos ...]: per block of up to
 // pf_rows tokens and per layer, the block's rows go through the GEMMs and
 // the prefill kernels, which write their K/V rows into the cache; the next
@@ -1101,13 +1102,38 @@ cudaError_t TextDecoder::prefill(uint32_t n) {
     }
   }
   // C (+)= A . deq(W)^T with W resident in the GEMM layout, or prepared on the fly
-  auto gemm = [&](uint32_t L, int i, float* c, uint32_t mm, bool acc) {
+  auto gemm = [&](uint32_t L, int i, float* c, uint32_t mm, bool acc, float* const* extra = nullptr,
+                  uint32_t n_extra = 0) {
     const uint32_t nn = mat_n[i], kk = mat_k[i];
     const bool res = pf_resident && !pf_wres.empty();
     const void* wp = res ? pf_wres[4u * L + i] : pf_w;
     if (e == cudaSuccess && !res) e = launch_prefill_w_prep(mat_w(L, i), nn, kk, pf_w, st);
-    if (e == cudaSuccess) e = launch_prefill_gemm(pf_act, wp, c, mm, nn, kk, gemv_err, st, &status, acc);
+    if (e == cudaSuccess)
+      e = launch_prefill_gemm(pf_act, wp, c, mm, nn, kk, gemv_err, st, &status, acc, extra, n_extra);
     if (e == cudaSuccess && status != EOS_OK) e = cudaErrorNotSupported;
+  };
+  // tensor parallel: this rank's O / down partial rows go to its own slot and,
+  // over NVLink, to its slot at every other rank; pf_xchg_add then sums the
+  // slots into the residual rows (identical on every rank)
+  const size_t slot_floats = (size_t)xpf_rows * E;
+  auto slot = [&](int q, int type) {
+    return reinterpret_cast<float*>(xpeer[q] + (type == 0 ? xoff_pfo : xoff_pfd)) + slot_floats * rank;
+  };
+  float* push[2][kMaxParts] = {};
+  uint32_t n_push_pf = 0;
+  uint32_t* pub[2][kMaxParts] = {};
+  for (int q = 0; q < world && world > 1; ++q) {
+    for (int t = 0; t < 2; ++t) pub[t][q] = &xrecv(q)->pf_flag[t][rank];
+    if (q == rank) continue;
+    push[0][n_push_pf] = slot(q, 0);
+    push[1][n_push_pf] = slot(q, 1);
+    ++n_push_pf;
+  }
+  auto exchange = [&](int type, uint32_t mm) {
+    if (e != cudaSuccess) return;
+    const float* mine = reinterpret_cast<const float*>(xbuf + (type == 0 ? xoff_pfo : xoff_pfd));
+    e = launch_pf_xchg_add(pf_x, mine, slot_floats, mm, E, (uint32_t)world, pub[type], &xrecv(rank)->pf_flag[type][0],
+                           ++pf_epoch, &state->err, st);
   };
   const float scale = 1.0f / sqrtf((float)hd);  // text.c:365
   for (uint32_t b0 = 0; b0 < n && e == cudaSuccess; b0 += pf_rows) {
@@ -1125,12 +1151,22 @@ cudaError_t TextDecoder::prefill(uint32_t n) {
       if (e == cudaSuccess)
         e = launch_pf_attn(pf_qkv, kcl, vcl, pf_act, mm, hl, kvl, h0, kv0, m.n_head, m.n_kv_head, hd, pos0,
                            scale, st);
-      gemm(L, 1, pf_x, mm, true);
+      if (world == 1) {
+        gemm(L, 1, pf_x, mm, true);
+      } else {
+        gemm(L, 1, slot(rank, 0), mm, false, push[0], n_push_pf);
+        exchange(0, mm);
+      }
       if (e == cudaSuccess)
         e = launch_pf_norm_pack(pf_x, nullptr, tok_embd, d.ffn_norm, m.rms_eps, mm, E, pf_act, st);
       gemm(L, 2, pf_gu, mm, false);
       if (e == cudaSuccess) e = launch_pf_silu_pack(pf_gu, mm, ffl, pf_act, st);
-      gemm(L, 3, pf_x, mm, true);
+      if (world == 1) {
+        gemm(L, 3, pf_x, mm, true);
+      } else {
+        gemm(L, 3, slot(rank, 1), mm, false, push[1], n_push_pf);
+        exchange(1, mm);
+      }
     }
   }
   return e;
@@ -1307,8 +1343,12 @@ EOSLLM_CUDA_API int eosi_cuda_text_prefill(eosi_cuda_text_t* t, const uint32_t* 
   if (t == nullptr || (tokens == nullptr && n > 0)) return EOS_E_INVALID_ARG;
   TextDecoder& d = t->d;
   if (!d.prefill_ok()) {
-    eos::set_error_message("cuda text: batched prefill needs one GPU and Q4_K linears");
+    eos::set_error_message("cuda text: batched prefill needs Q4_K linears");
     return EOS_E_UNSUPPORTED;
+  }
+  if (d.graph == nullptr) {
+    eos::set_error_message("cuda text: tensor-parallel decoder not attached to its peers");
+    return EOS_E_INVALID_ARG;
   }
   for (uint32_t i = 0; i < n; ++i)
     if (tokens[i] >= d.m.n_vocab) {

@@ -7,6 +7,17 @@
 
 namespace eos {
 
+// System-scope release store / acquire load of a flag word (tensor-parallel
+// handshakes through CUDA IPC mappings).
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Words the step kernels share in device memory.
 struct DecState {
   uint32_t pos;         // position of the next step == tokens consumed
@@ -27,6 +38,9 @@ struct XRecv {
   uint32_t arg_i[8];    // its global vocabulary index
   uint32_t first_nan;   // from rank 0: logits[0] is NaN
   uint32_t pad[7];
+  // batched prefill: [0] O partial rows, [1] down partial rows, [.][q] written
+  // by rank q; values are the prefill's own exchange counter (1, 2, ...)
+  uint32_t pf_flag[2][8];
 };
 
 // One layer's resident weights (this rank's slices).
@@ -81,5 +95,13 @@ cudaError_t launch_pf_attn(const float* qkv, const float* kc, const float* vc, v
                            uint32_t hd, uint32_t pos0, float scale, cudaStream_t st);
 // silu(gate) * up of gu[m][2 ffl] (gate | up), packed (k = ffl).
 cudaError_t launch_pf_silu_pack(const float* gu, uint32_t m, uint32_t ffl, void* act, cudaStream_t st);
+// Tensor-parallel exchange of the prefill: raise this rank's flag (epoch) in
+// every rank's words (pub_flag[q]), wait -- bounded -- for every source's
+// flag in this rank's words (wait_flag[0..world)), then
+// x[i] += ((s_0[i] + s_1[i]) + ...) over the sources' partial rows, which
+// their GEMMs pushed into this rank's slots (source q at slots + q * stride).
+cudaError_t launch_pf_xchg_add(float* x, const float* slots, size_t stride, uint32_t m, uint32_t n, uint32_t world,
+                               uint32_t* const* pub_flag, const uint32_t* wait_flag, uint32_t epoch, uint32_t* err,
+                               cudaStream_t st);
 
 }  // namespace eos

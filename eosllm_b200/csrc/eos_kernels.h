@@ -40,9 +40,12 @@ cudaError_t launch_q4k_f32_small_n(const float* a, const uint8_t* w, float* c, u
 size_t prefill_operand_bytes(uint32_t rows, uint32_t k);
 cudaError_t launch_prefill_act_pack(const float* a, uint32_t m, uint32_t k, void* act, cudaStream_t st);
 cudaError_t launch_prefill_w_prep(const uint8_t* w, uint32_t n, uint32_t k, void* wprep, cudaStream_t st);
-// accumulate: C = C_old + A.W^T (the decoder's residual adds).
+// accumulate: C = C_old + A.W^T (the decoder's residual adds).  c_extra /
+// n_extra (<= 7, not with accumulate): further destinations of C (tensor-
+// parallel push into other GPUs' IPC-mapped receive slots).
 cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, uint32_t m, uint32_t n, uint32_t k,
-                                uint32_t* err, cudaStream_t st, int* out_status, bool accumulate = false);
+                                uint32_t* err, cudaStream_t st, int* out_status, bool accumulate = false,
+                                float* const* c_extra = nullptr, uint32_t n_extra = 0);
 
 cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t n, uint32_t k, uint32_t* err,
                             int num_sms, int max_smem, cudaStream_t st, int* out_status,

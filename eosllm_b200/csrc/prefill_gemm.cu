@@ -201,6 +201,11 @@ struct PrefillParams {
   uint32_t m, n, k;
   uint32_t* err;
   uint32_t accumulate;  // C = C_old + A.W^T (residual add, old value first)
+  // tensor parallel: further destinations of C (other GPUs' receive slots,
+  // same [m][n] layout), plain stores over NVLink, performed when the grid
+  // completes; not combined with `accumulate`
+  float* c_extra[7];
+  uint32_t n_extra;
 };
 
 __global__ void __launch_bounds__(QG_THREADS, 1)
@@ -381,13 +386,18 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
               v = make_float4(__fadd_rn(o.x, v.x), __fadd_rn(o.y, v.y), __fadd_rn(o.z, v.z), __fadd_rn(o.w, v.w));
             }
             *reinterpret_cast<float4*>(crow + 4 * c4) = v;
+            for (uint32_t x = 0; x < p.n_extra; ++x)
+              *reinterpret_cast<float4*>(p.c_extra[x] + (size_t)row * p.n + gcol + 4 * c4) = v;
           }
         } else {
 #pragma unroll
           for (uint32_t c = 0; c < QG_COLS; ++c) {
             const float4 v4 = acc[32 * (c / 4)];
             const float v = (c & 3u) == 0 ? v4.x : ((c & 3u) == 1 ? v4.y : ((c & 3u) == 2 ? v4.z : v4.w));
-            if (gcol + c < p.n) crow[c] = p.accumulate ? __fadd_rn(crow[c], v) : v;
+            if (gcol + c < p.n) {
+              crow[c] = p.accumulate ? __fadd_rn(crow[c], v) : v;
+              for (uint32_t x = 0; x < p.n_extra; ++x) p.c_extra[x][(size_t)row * p.n + gcol + c] = v;
+            }
           }
         }
       }
@@ -477,9 +487,14 @@ cudaError_t launch_prefill_w_prep(const uint8_t* w, uint32_t n, uint32_t k, void
 // k % 256 == 0, base pointers 1024-byte aligned).  out_status:
 // EOS_E_UNSUPPORTED when the tensor maps cannot be built.
 cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, uint32_t m, uint32_t n, uint32_t k,
-                                uint32_t* err, cudaStream_t st, int* out_status, bool accumulate) {
+                                uint32_t* err, cudaStream_t st, int* out_status, bool accumulate,
+                                float* const* c_extra, uint32_t n_extra) {
   *out_status = EOS_OK;
   if (m == 0 || n == 0) return cudaSuccess;
+  if (n_extra > 7 || (n_extra > 0 && accumulate)) {
+    *out_status = EOS_E_INVALID_ARG;
+    return cudaSuccess;
+  }
   const uint8_t* ab = static_cast<const uint8_t*>(act);
   const uint8_t* wb = static_cast<const uint8_t*>(wprep);
   CUtensorMap ma, mb, mas, mbs;
@@ -497,7 +512,8 @@ cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, ui
     attr_set = true;
   }
   const dim3 grid((m + QG_BM - 1) / QG_BM, (n + QG_BN - 1) / QG_BN);
-  PrefillParams prm{c, m, n, k, err, accumulate ? 1u : 0u};
+  PrefillParams prm{c, m, n, k, err, accumulate ? 1u : 0u, {}, n_extra};
+  for (uint32_t x = 0; x < n_extra; ++x) prm.c_extra[x] = c_extra[x];
   prefill_gemm_kernel<<<grid, QG_THREADS, QG_SMEM, st>>>(ma, mb, mas, mbs, prm);
   return cudaGetLastError();
 }

@@ -312,6 +312,60 @@ __global__ void __launch_bounds__(256) pf_silu_pack_kernel(const float* __restri
 }
 
 // ---------------------------------------------------------------------------
+// Tensor-parallel partial-sum exchange (push model, like the decode step's)
+// ---------------------------------------------------------------------------
+struct PfXchgParams {
+  float* x;              // [m][n] residual rows of this rank
+  const float* slots;    // this rank's receive slots; source q at slots + q * stride
+  size_t stride;         // floats
+  uint32_t m, n, world, epoch;
+  uint32_t* pub_flag[8];
+  const uint32_t* wait_flag;
+  uint32_t* err;
+};
+
+// The sources' GEMMs wrote their partial rows into this rank's slots with
+// plain stores and completed before this kernel started (stream order);
+// CTA 0's system-scope fence and release stores announce this rank's own
+// push, every CTA waits for all sources, then adds the slots in rank order
+// (the decode step's order: x + ((p_0 + p_1) + ...)).
+__global__ void __launch_bounds__(256) pf_xchg_add_kernel(const PfXchgParams p) {
+  __shared__ uint32_t s_ok;
+  if (threadIdx.x == 0) s_ok = 1u;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    __threadfence_system();
+    for (uint32_t q = 0; q < p.world; ++q) st_release_sys(p.pub_flag[q], p.epoch);
+  }
+  __syncthreads();
+  if (threadIdx.x < p.world) {
+    const uint32_t* f = p.wait_flag + threadIdx.x;
+    if (ld_acquire_sys(f) < p.epoch) {
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(f) < p.epoch) {
+        if (global_timer_ns() - t0 > EOS_WAIT_LIMIT_NS) {
+          report(p.err, EOS_DEVERR_PEER);
+          s_ok = 0u;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (!s_ok) return;  // a peer never arrived: the error bit is set
+  const size_t n4 = (size_t)p.m * p.n / 4u;
+  float4* x4 = reinterpret_cast<float4*>(p.x);
+  for (size_t i = (size_t)blockIdx.x * 256u + threadIdx.x; i < n4; i += (size_t)gridDim.x * 256u) {
+    float4 t = __ldcg(reinterpret_cast<const float4*>(p.slots) + i);
+    for (uint32_t q = 1; q < p.world; ++q) {
+      const float4 u = __ldcg(reinterpret_cast<const float4*>(p.slots + q * p.stride) + i);
+      t = make_float4(__fadd_rn(t.x, u.x), __fadd_rn(t.y, u.y), __fadd_rn(t.z, u.z), __fadd_rn(t.w, u.w));
+    }
+    const float4 v = x4[i];
+    x4[i] = make_float4(__fadd_rn(v.x, t.x), __fadd_rn(v.y, t.y), __fadd_rn(v.z, t.z), __fadd_rn(v.w, t.w));
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host launchers
 // ---------------------------------------------------------------------------
 namespace {
@@ -367,6 +421,19 @@ cudaError_t launch_pf_attn(const float* qkv, const float* kc, const float* vc, v
   if (hd == 128) return attn_launch<4>(p, st);
   if (hd == 256) return attn_launch<8>(p, st);
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_pf_xchg_add(float* x, const float* slots, size_t stride, uint32_t m, uint32_t n, uint32_t world,
+                               uint32_t* const* pub_flag, const uint32_t* wait_flag, uint32_t epoch, uint32_t* err,
+                               cudaStream_t st) {
+  if (m == 0 || world < 2 || world > 8 || n % 4u) return cudaErrorInvalidValue;
+  PfXchgParams p{x, slots, stride, m, n, world, epoch, {}, wait_flag, err};
+  for (uint32_t q = 0; q < world; ++q) p.pub_flag[q] = pub_flag[q];
+  const size_t n4 = (size_t)m * n / 4u;
+  size_t blocks = (n4 + 255u) / 256u;
+  if (blocks > 1184u) blocks = 1184u;  // grid-stride beyond 148 SMs x 8
+  pf_xchg_add_kernel<<<(uint32_t)blocks, 256, 0, st>>>(p);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_pf_silu_pack(const float* gu, uint32_t m, uint32_t ffl, void* act, cudaStream_t st) {

@@ -253,9 +253,10 @@ EOSLLM_CUDA_API int eosi_cuda_text_generate(eosi_cuda_text_t *t, const uint32_t 
 /* Batched prefill: feeds tokens[0, n) from the current position in one pass
  * per layer on the tensor cores (the KV cache rows of all n tokens), with no
  * logits; position + n.  The reference feeds a prompt token by token
- * (src/core/session.c:231-236); the cache rows agree with that to f32
- * summation level.  One GPU (world 1) and Q4_K linears only, else
- * EOS_E_UNSUPPORTED (feed the tokens with eosi_cuda_text_step instead).
+ * (src/core/session.c:231-236); the linears here are bit-exact with it and
+ * the cache rows differ only by the attention sums' rounding.  Q4_K linears only, else EOS_E_UNSUPPORTED (feed the
+ * tokens with eosi_cuda_text_step instead); tensor parallel, every rank
+ * makes the same call (the partial sums are exchanged like the step's).
  * eosi_cuda_text_generate uses it for all prompt tokens but the last when at
  * least `min_tokens` precede the last (eosi_cuda_text_set_prefill_min; default
  * 16, 0 = never). */

@@ -14,6 +14,7 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
+N_PREFILL = 33  # tokens fed by the batched prefill in the prefill check
 CASES = [dict(n_embd=512, n_head=4, n_kv_head=2, n_ff=768, n_vocab=1000, n_layer=2),
          dict(n_embd=512, n_head=8, n_kv_head=2, n_ff=512, n_vocab=77, n_layer=2, wdtype=32, out_dtype=32),
          dict(n_embd=4096, n_head=32, n_kv_head=32, n_ff=11008, n_vocab=512, n_layer=1, seed=9)]
@@ -38,12 +39,22 @@ def _tp_worker(rank: int, world: int, port: int, kw: dict, tokens, prompt, n_gen
         dist.barrier()
         dec.reset()
         dist.barrier()
-        picks = dec.generate(prompt, n_gen)
+        picks = dec.generate(prompt, n_gen)  # Q4_K: the prompt through the batched prefill
         all_picks = [None] * world
         dist.all_gather_object(all_picks, picks.tolist())
         dist.barrier()
+        # the batched prefill of the first tokens, then steps for the rest
+        dec.reset()
+        dist.barrier()
+        pf_logits = []
+        if kw.get("wdtype", 33) == 33:
+            dec.prefill(np.asarray(tokens[:N_PREFILL], np.uint32))
+            for t in tokens[N_PREFILL:]:
+                dist.barrier()
+                pf_logits.append(dec.step(int(t)))
+        dist.barrier()
         dec.close()
-        q.put((rank, np.stack(logits), all_picks))
+        q.put((rank, (np.stack(logits), np.stack(pf_logits) if pf_logits else None), all_picks))
     except Exception as e:  # report, never hang the parent
         q.put((rank, None, repr(e)))
     finally:
@@ -55,7 +66,7 @@ def test_two_gpu_decoder_matches_oracle(gpu, oracle, kw):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     from oracle.llama import OracleDecoder, make_llama
-    from test_gpu_decoder import ENVELOPE_FACTOR, LOGIT_TOL, envelope_check, pick_agrees
+    from test_gpu_decoder import ENVELOPE_FACTOR, LOGIT_TOL, envelope_check, logit_err, pick_agrees
     world = 2
     rng = np.random.default_rng(21)
     tokens = rng.integers(0, kw["n_vocab"], 40)
@@ -74,6 +85,9 @@ def test_two_gpu_decoder_matches_oracle(gpu, oracle, kw):
         p.join(timeout=120)
     for r in range(world):
         assert res[r][0] is not None, res[r][1]
+    pf = [res[r][0][1] for r in range(world)]
+    for r in range(world):
+        res[r] = (res[r][0][0], res[r][1])
     np.testing.assert_array_equal(res[0][0].view(np.uint32), res[1][0].view(np.uint32))  # same logits on both ranks
     picks = res[0][1]
     assert picks[0] == picks[1]  # both ranks generated the same tokens
@@ -81,6 +95,15 @@ def test_two_gpu_decoder_matches_oracle(gpu, oracle, kw):
     it = iter(res[0][0])
     _, e_env = envelope_check(oracle, model, tokens, lambda t: next(it))
     band = max(LOGIT_TOL, ENVELOPE_FACTOR * max(e_env))
+    if pf[0] is not None:
+        # tensor-parallel batched prefill: identical on both ranks, and the
+        # steps after it agree with the oracle like the stepped ones
+        np.testing.assert_array_equal(pf[0].view(np.uint32), pf[1].view(np.uint32))
+        ref = OracleDecoder(oracle, model)
+        want = [ref.step(int(t)) for t in tokens][N_PREFILL:]
+        ref.close()
+        errs = [logit_err(g, w) for g, w in zip(pf[0], want)]
+        assert max(errs) <= band, (errs, band)
     od = OracleDecoder(oracle, model)
     logits = None
     for t in prompt:
