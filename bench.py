@@ -495,7 +495,7 @@ def run_ours(args):
                        "weights": "Q4_K, ~N(0,0.02) (Irwin-Hall), own quantizer", "activations": "~N(0,1)",
                        "l2": f"{R} rotating weight copies ({R * sum(q4k_bytes(n, k) for n, k in SHAPES) / 1e6:.1f}"
                              " MB) > 126 MB L2",
-                       "timing": "CUDA graph of K steps (4 packs + 4 PDL-chained GEMVs each), CUDA events, max over ranks",
+                       "timing": "CUDA graph of K steps (2 packing launches, one per distinct k, + 4 PDL-chained GEMVs each), CUDA events, max over ranks",
                        "parallelism": f"row shards x{world}, no collective"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,

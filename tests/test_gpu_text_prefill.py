@@ -151,3 +151,30 @@ def test_prefill_errors(gpu, oracle):
         q8.prefill(np.arange(4, dtype=np.uint32))  # Q8_0 linears: feed token by token
     assert q8.pos == 0
     q8.close()
+
+
+def test_decoder_layer_at_position_1024(gpu, oracle):
+    """The one-decoder-layer configuration (dim 4096, 32 heads of 128, FFN
+    11008, f32 KV, ctx 2048, decode at position 1024): the cache filled by a
+    1024-token batched prefill, then steps at positions 1024..1031, against
+    the same steps after feeding all 1024 tokens one by one (the step path
+    is itself checked against the oracle at model width).  The bound is the
+    reference's envelope measured at this layer shape."""
+    from eosllm_b200.text import TextDecoder
+    model = make_llama(oracle, n_embd=4096, n_layer=1, n_head=32, n_kv_head=32, n_ff=11008, n_vocab=512,
+                       max_ctx=2048, seed=3)
+    tokens = np.random.default_rng(3).integers(0, 512, 1032).astype(np.uint32)
+    a, b = TextDecoder(model), TextDecoder(model)
+    a.set_prefill_min(0)
+    a.generate(tokens[:1024], 0)  # token by token
+    b.prefill(tokens[:1024])
+    assert a.pos == b.pos == 1024
+    errs = []
+    for t in tokens[1024:]:
+        la, lb = a.step(int(t)), b.step(int(t))
+        errs.append(float(np.max(np.abs(la.astype(np.float64) - lb)) / np.sqrt(np.mean(la.astype(np.float64) ** 2))))
+    a.close()
+    b.close()
+    # 3x the 7B-layer envelope measured on the oracle (3.23e-2, test_gpu_decoder.py)
+    print("position 1024: max logit diff / rms %.2e" % max(errs))
+    assert max(errs) <= ENVELOPE_FACTOR * 3.23e-2, errs
