@@ -16,6 +16,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -88,11 +89,6 @@ int device_info(int dev, DevInfo** out) {
   return EOS_OK;
 }
 
-int current_info(DevInfo** out) {
-  int dev = 0;
-  EOS_CK(cudaGetDevice(&dev), "cudaGetDevice");
-  return device_info(dev, out);
-}
 
 // ---- host-pointer layer state ---------------------------------------------
 struct WeightEntry {
@@ -164,7 +160,10 @@ void release_shard(Shard& s) {
 }
 
 void release_all() {
+  int prev = 0;
+  const bool had = cudaGetDevice(&prev) == cudaSuccess;
   for (auto& s : g_shards) release_shard(s);
+  if (had) cudaSetDevice(prev);  // the caller's current device, as found
   g_shards.clear();
   if (g_h_a) cudaFreeHost(g_h_a);
   if (g_h_c) cudaFreeHost(g_h_c);
@@ -396,9 +395,34 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
   return EOS_OK;
 }
 
-int dev_prologue(DevInfo** info) {
+// A *_dev entry point runs on the caller's current device, so every pointer
+// it is given must be device (or managed) memory of that device: a host
+// pointer or another GPU's memory is rejected here instead of being handed
+// to a kernel.
+int check_on_device(const void* p, int dev) {
+  if (p == nullptr) return EOS_OK;
+  cudaPointerAttributes at;
+  const cudaError_t e = cudaPointerGetAttributes(&at, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(EOS_E_INVALID_ARG, "pointer %p is not CUDA memory", p);
+  }
+  if (at.type == cudaMemoryTypeManaged) return EOS_OK;
+  if (at.type != cudaMemoryTypeDevice)
+    return fail(EOS_E_INVALID_ARG, "pointer %p is host memory; the *_dev entry points take device pointers", p);
+  if (at.device != dev)
+    return fail(EOS_E_INVALID_ARG, "pointer %p is on device %d, the current device is %d", p, at.device, dev);
+  return EOS_OK;
+}
+
+int dev_prologue(DevInfo** info, std::initializer_list<const void*> ptrs = {}) {
   if (eosi_cuda_probe() != EOS_OK) return fail(EOS_E_UNSUPPORTED, "no usable sm_100 GPU");
-  return current_info(info);
+  int dev = 0;
+  EOS_CK(cudaGetDevice(&dev), "cudaGetDevice");
+  int rc = device_info(dev, info);
+  for (const void* p : ptrs)
+    if (rc == EOS_OK) rc = check_on_device(p, dev);
+  return rc;
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -407,6 +431,13 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 namespace eos {
 void set_error_message(const char* msg) { fail(EOS_OK, "%s", msg); }
+int pointers_on_device(std::initializer_list<const void*> ptrs, int dev) {
+  for (const void* p : ptrs) {
+    const int rc = check_on_device(p, dev);
+    if (rc != EOS_OK) return rc;
+  }
+  return EOS_OK;
+}
 }  // namespace eos
 
 // ===========================================================================
@@ -544,7 +575,7 @@ int eosi_cuda_matmul_q4_k_dev(const float* a, const void* w, float* c, uint32_t 
     return fail(EOS_E_INVALID_ARG, "device pointers must be 16-byte aligned");
   if (m == 0 || n == 0) return EOS_OK;
   DevInfo* info = nullptr;
-  rc = dev_prologue(&info);
+  rc = dev_prologue(&info, {a, w, c, scratch});
   if (rc != EOS_OK) return rc;
   return enqueue_matmul(info, EOS_DT_Q4_K, a, (const uint8_t*)w, c, m, n, n, k, (uint8_t*)scratch,
                         (cudaStream_t)stream);
@@ -555,7 +586,7 @@ int eosi_cuda_q4_k_pack_act_dev(const float* a, uint32_t m, uint32_t k, void* ac
   if (k % Q4K_ELEMS) return fail(EOS_E_INVALID_ARG, "q4_k: k=%u is not a multiple of 256", k);
   if (!al16(act)) return fail(EOS_E_INVALID_ARG, "act must be 16-byte aligned");
   DevInfo* info = nullptr;
-  int rc = dev_prologue(&info);
+  int rc = dev_prologue(&info, {a, act});
   if (rc != EOS_OK) return rc;
   EOS_CK(eos::launch_act_pack(a, m, k, (uint8_t*)act, EOS_ACT_LAYOUT_GEMV, (cudaStream_t)stream),
          "activation pack kernel");
@@ -567,7 +598,7 @@ int eosi_cuda_q4_k_gemv_dev(const void* act, const void* w, float* c, uint32_t n
   if (rc != EOS_OK) return rc;
   if (!al16(act) || !al16(w)) return fail(EOS_E_INVALID_ARG, "device pointers must be 16-byte aligned");
   DevInfo* info = nullptr;
-  rc = dev_prologue(&info);
+  rc = dev_prologue(&info, {act, w, c});
   if (rc != EOS_OK) return rc;
   int status = EOS_OK;
   EOS_CK(eos::launch_q4k_gemv((const uint8_t*)w, (const uint8_t*)act, nullptr, c, n, k, info->err_d, info->num_sms,
@@ -586,7 +617,7 @@ int eosi_cuda_q4_k_prefill_prepare_weights_dev(const void* w, uint32_t n, uint32
   if (rc != EOS_OK) return rc;
   if (!al16(w) || !al16(w_prep)) return fail(EOS_E_INVALID_ARG, "prefill weights must be 16-byte aligned");
   DevInfo* info = nullptr;
-  rc = dev_prologue(&info);
+  rc = dev_prologue(&info, {w, w_prep});
   if (rc != EOS_OK) return rc;
   EOS_CK(eos::launch_prefill_w_prep((const uint8_t*)w, n, k, w_prep, (cudaStream_t)stream), "prefill weight prep");
   return EOS_OK;
@@ -601,7 +632,7 @@ int eosi_cuda_q4_k_prefill_dev(const float* a, const void* w_prep, float* c, uin
     return fail(EOS_E_INVALID_ARG, "prefill pointers must be 16-byte aligned");
   if (m == 0 || n == 0) return EOS_OK;
   DevInfo* info = nullptr;
-  rc = dev_prologue(&info);
+  rc = dev_prologue(&info, {a, w_prep, c, scratch});
   if (rc != EOS_OK) return rc;
   EOS_CK(eos::launch_prefill_act_pack(a, m, k, scratch, (cudaStream_t)stream), "prefill activation packing");
   int status = EOS_OK;
@@ -618,7 +649,7 @@ int eosi_cuda_matmul_q8_0_dev(const float* a, const void* w, float* c, uint32_t 
   if (!al16(a)) return fail(EOS_E_INVALID_ARG, "activations must be 16-byte aligned");
   if (m == 0 || n == 0) return EOS_OK;
   DevInfo* info = nullptr;
-  rc = dev_prologue(&info);
+  rc = dev_prologue(&info, {a, w, c});
   if (rc != EOS_OK) return rc;
   return enqueue_matmul(info, EOS_DT_Q8_0, a, (const uint8_t*)w, c, m, n, n, k, nullptr, (cudaStream_t)stream);
 }
@@ -628,7 +659,7 @@ int eosi_cuda_quantize_act_dev(const float* a, uint32_t m, uint32_t k, int8_t* a
   if (!a || !aq || !scales || !sums) return fail(EOS_E_INVALID_ARG, "NULL pointer argument");
   if (k % 32u) return fail(EOS_E_INVALID_ARG, "k=%u is not a multiple of 32", k);
   DevInfo* info = nullptr;
-  int rc = dev_prologue(&info);
+  int rc = dev_prologue(&info, {a, aq, scales, sums});
   if (rc != EOS_OK) return rc;
   if (m == 0 || k == 0) return EOS_OK;
   // Pack into a temporary source-order buffer, then scatter to the caller's arrays.
@@ -651,7 +682,7 @@ int eosi_cuda_unpack_scale_min_dev(const uint8_t* scales12, uint32_t count, uint
                                    void* stream) {
   if (!scales12 || !sc || !m) return fail(EOS_E_INVALID_ARG, "NULL pointer argument");
   DevInfo* info = nullptr;
-  int rc = dev_prologue(&info);
+  int rc = dev_prologue(&info, {scales12, sc, m});
   if (rc != EOS_OK) return rc;
   EOS_CK(eos::launch_unpack_scale_min(scales12, count, sc, m, (cudaStream_t)stream), "unpack kernel");
   return EOS_OK;
@@ -661,7 +692,7 @@ int eosi_cuda_q8_0_quantize_dev(const float* src, void* dst, size_t n_elements, 
   if (!src || !dst) return fail(EOS_E_INVALID_ARG, "NULL pointer argument");
   if (n_elements % 32u) return fail(EOS_E_INVALID_ARG, "n_elements not a multiple of 32");
   DevInfo* info = nullptr;
-  int rc = dev_prologue(&info);
+  int rc = dev_prologue(&info, {src, dst});
   if (rc != EOS_OK) return rc;
   EOS_CK(eos::launch_q80_quantize(src, (uint8_t*)dst, n_elements, (cudaStream_t)stream), "q8_0 quantize kernel");
   return EOS_OK;
@@ -672,7 +703,7 @@ int eosi_cuda_q4_k_quantize_dev(const float* src, void* dst, size_t n_elements, 
   if (n_elements % 256u) return fail(EOS_E_INVALID_ARG, "n_elements not a multiple of 256");
   if (!al16(dst)) return fail(EOS_E_INVALID_ARG, "dst must be 16-byte aligned");
   DevInfo* info = nullptr;
-  int rc = dev_prologue(&info);
+  int rc = dev_prologue(&info, {src, dst});
   if (rc != EOS_OK) return rc;
   EOS_CK(eos::launch_q4k_quantize(src, (uint8_t*)dst, n_elements, (cudaStream_t)stream), "q4_k quantize kernel");
   return EOS_OK;
@@ -681,7 +712,7 @@ int eosi_cuda_q4_k_quantize_dev(const float* src, void* dst, size_t n_elements, 
 int eosi_cuda_fill_gauss_dev(float* dst, size_t n, uint64_t seed, uint64_t offset, float sigma, void* stream) {
   if (!dst) return fail(EOS_E_INVALID_ARG, "NULL pointer argument");
   DevInfo* info = nullptr;
-  int rc = dev_prologue(&info);
+  int rc = dev_prologue(&info, {dst});
   if (rc != EOS_OK) return rc;
   EOS_CK(eos::launch_fill_gauss(dst, n, seed, offset, sigma, (cudaStream_t)stream), "gauss kernel");
   return EOS_OK;
@@ -692,7 +723,7 @@ int eosi_cuda_q4_k_from_gauss_dev(void* dst, size_t n_elements, uint64_t seed, f
   if (n_elements % 256u) return fail(EOS_E_INVALID_ARG, "n_elements not a multiple of 256");
   if (!al16(dst)) return fail(EOS_E_INVALID_ARG, "dst must be 16-byte aligned");
   DevInfo* info = nullptr;
-  int rc = dev_prologue(&info);
+  int rc = dev_prologue(&info, {dst});
   if (rc != EOS_OK) return rc;
   EOS_CK(eos::launch_q4k_from_gauss((uint8_t*)dst, n_elements / 256u, seed, 0, sigma, (cudaStream_t)stream),
          "q4_k generator kernel");

@@ -261,4 +261,26 @@ __device__ __forceinline__ void pf_pack_group(float v, uint32_t row, uint32_t s,
   }
 }
 
+// Kernel attributes belong to a device, not to the process: a kernel that
+// needs more than 48 KB of dynamic shared memory must be allowed it on every
+// device it runs on.  SmemAttr remembers, per device ordinal, the largest
+// amount already allowed; ensure_smem_attr sets the attribute (and the
+// largest shared-memory carveout) for the current device when needed.
+constexpr int kMaxDevices = 64;
+struct SmemAttr {
+  int set[kMaxDevices] = {};
+};
+inline cudaError_t ensure_smem_attr(const void* fn, int bytes, SmemAttr& a, bool max_carveout = true) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (bytes <= __atomic_load_n(&a.set[dev], __ATOMIC_ACQUIRE)) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && max_carveout)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess) __atomic_store_n(&a.set[dev], bytes, __ATOMIC_RELEASE);
+  return e;
+}
+
 }  // namespace eos

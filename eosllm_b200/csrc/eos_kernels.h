@@ -7,6 +7,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <initializer_list>
+
 // Layouts the activation packer can write.
 enum { EOS_ACT_LAYOUT_GEMV = 0, EOS_ACT_LAYOUT_SOURCE = 1 };
 
@@ -14,6 +16,9 @@ namespace eos {
 
 // Sets the calling thread's message returned by eosi_cuda_last_error().
 void set_error_message(const char* msg);
+// EOS_OK when every non-null pointer is device (or managed) memory of device
+// `dev`; else EOS_E_INVALID_ARG with the message set.  No allocation.
+int pointers_on_device(std::initializer_list<const void*> ptrs, int dev);
 
 size_t act_layout_bytes(uint32_t m, uint32_t k, int layout);
 cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out, int layout, cudaStream_t st);

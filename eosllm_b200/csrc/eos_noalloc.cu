@@ -98,6 +98,9 @@ EOSLLM_CUDA_API int eosi_cuda_matmul_q4_k_noalloc(const float* a, const void* w,
   NoAllocDevice* d = nullptr;
   const int rc = noalloc_device(&d);
   if (rc != EOS_OK) return noalloc_fail(rc, "no usable sm_100 device for the no-alloc entry point");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (eos::pointers_on_device({a, w, c}, dev) != EOS_OK) return EOS_E_INVALID_ARG;  // message already set
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (n < 4) {  // the reference's f32-dequant path for n < 4 needs no scratch

@@ -504,12 +504,10 @@ cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, ui
     *out_status = EOS_E_UNSUPPORTED;
     return cudaSuccess;
   }
-  static bool attr_set = false;
-  if (!attr_set) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QG_SMEM);
+  static SmemAttr attr;  // per device
+  {
+    const cudaError_t e = ensure_smem_attr((const void*)prefill_gemm_kernel, (int)QG_SMEM, attr, false);
     if (e != cudaSuccess) return e;
-    attr_set = true;
   }
   const dim3 grid((m + QG_BM - 1) / QG_BM, (n + QG_BN - 1) / QG_BN);
   PrefillParams prm{c, m, n, k, err, accumulate ? 1u : 0u, {}, n_extra};

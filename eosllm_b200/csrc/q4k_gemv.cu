@@ -367,19 +367,19 @@ struct GemvConfig {
   void (*fn)(const Q4kGemvParams);
   int nw, d;
   int cols;      // 0: q4k_gemv_kernel (rows per stage chosen at launch); R: q4k_gemv_cols_kernel<., ., R>
-  int smem_set;  // largest dynamic shared memory already allowed
+  SmemAttr attr;  // dynamic shared memory allowed so far, per device
 };
 GemvConfig g_cfgs[] = {
-    {q4k_gemv_kernel<16, 4>, 16, 4, 0, 0},      {q4k_gemv_kernel<16, 3>, 16, 3, 0, 0},
-    {q4k_gemv_kernel<16, 2>, 16, 2, 0, 0},      {q4k_gemv_kernel<20, 3>, 20, 3, 0, 0},
-    {q4k_gemv_kernel<8, 4>, 8, 4, 0, 0},        {q4k_gemv_kernel<12, 4>, 12, 4, 0, 0},
-    {q4k_gemv_kernel<24, 2>, 24, 2, 0, 0},      {q4k_gemv_kernel<8, 6>, 8, 6, 0, 0},
-    {q4k_gemv_kernel<20, 2>, 20, 2, 0, 0},      {q4k_gemv_kernel<12, 3>, 12, 3, 0, 0},
-    {q4k_gemv_kernel<16, 2>, 16, 2, 0, 0},      {q4k_gemv_kernel<10, 4>, 10, 4, 0, 0},
-    {q4k_gemv_cols_kernel<12, 2, 4>, 12, 2, 4, 0}, {q4k_gemv_cols_kernel<16, 3, 2>, 16, 3, 2, 0},
-    {q4k_gemv_cols_kernel<8, 3, 4>, 8, 3, 4, 0},   {q4k_gemv_cols_kernel<16, 2, 2>, 16, 2, 2, 0},
-    {q4k_gemv_cols_kernel<8, 2, 2>, 8, 2, 2, 0},   {q4k_gemv_cols_kernel<12, 3, 2>, 12, 3, 2, 0},
-    {q4k_gemv_cols_kernel<16, 2, 1>, 16, 2, 1, 0}, {q4k_gemv_cols_kernel<8, 4, 2>, 8, 4, 2, 0}};
+    {q4k_gemv_kernel<16, 4>, 16, 4, 0, {}},      {q4k_gemv_kernel<16, 3>, 16, 3, 0, {}},
+    {q4k_gemv_kernel<16, 2>, 16, 2, 0, {}},      {q4k_gemv_kernel<20, 3>, 20, 3, 0, {}},
+    {q4k_gemv_kernel<8, 4>, 8, 4, 0, {}},        {q4k_gemv_kernel<12, 4>, 12, 4, 0, {}},
+    {q4k_gemv_kernel<24, 2>, 24, 2, 0, {}},      {q4k_gemv_kernel<8, 6>, 8, 6, 0, {}},
+    {q4k_gemv_kernel<20, 2>, 20, 2, 0, {}},      {q4k_gemv_kernel<12, 3>, 12, 3, 0, {}},
+    {q4k_gemv_kernel<16, 2>, 16, 2, 0, {}},      {q4k_gemv_kernel<10, 4>, 10, 4, 0, {}},
+    {q4k_gemv_cols_kernel<12, 2, 4>, 12, 2, 4, {}}, {q4k_gemv_cols_kernel<16, 3, 2>, 16, 3, 2, {}},
+    {q4k_gemv_cols_kernel<8, 3, 4>, 8, 3, 4, {}},   {q4k_gemv_cols_kernel<16, 2, 2>, 16, 2, 2, {}},
+    {q4k_gemv_cols_kernel<8, 2, 2>, 8, 2, 2, {}},   {q4k_gemv_cols_kernel<12, 3, 2>, 12, 3, 2, {}},
+    {q4k_gemv_cols_kernel<16, 2, 1>, 16, 2, 1, {}}, {q4k_gemv_cols_kernel<8, 4, 2>, 8, 4, 2, {}}};
 constexpr int kNumCfgs = sizeof(g_cfgs) / sizeof(g_cfgs[0]);
 int g_q4k_variant = -1;  // kernel config override (-1: automatic)
 int g_q4k_rows = 0;      // rows-per-stage override (0: automatic)
@@ -452,13 +452,11 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
     q4k_gemv_simple_kernel<<<(n + 7u) / 8u, 256, 0, st>>>(w, act, c, n, k);
     return cudaGetLastError();
   }
-  if ((int)smem > cfg.smem_set) {
-    cudaError_t e = cudaFuncSetAttribute(cfg.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    // largest carveout: the next kernel's CTAs can share the SM (PDL overlap)
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(cfg.fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  {
+    // on this device; largest carveout so the next kernel's CTAs can share
+    // the SM (PDL overlap)
+    const cudaError_t e = ensure_smem_attr((const void*)cfg.fn, (int)smem, cfg.attr);
     if (e != cudaSuccess) return e;
-    cfg.smem_set = (int)smem;
   }
   uint32_t cps = (uint32_t)(max_smem + 1024) / (smem + 1024);
   if (cps > 4u) cps = 4u;

@@ -206,11 +206,11 @@ namespace {
 struct Q80Config {
   void (*fn)(const Q80GemvParams);
   int nw, d;
-  int smem_set;
+  SmemAttr attr;  // dynamic shared memory allowed so far, per device
 };
-Q80Config g_q80_cfgs[] = {{q80_gemv_kernel<16, 4>, 16, 4, 0}, {q80_gemv_kernel<16, 3>, 16, 3, 0},
-                          {q80_gemv_kernel<16, 2>, 16, 2, 0}, {q80_gemv_kernel<8, 4>, 8, 4, 0},
-                          {q80_gemv_kernel<24, 2>, 24, 2, 0}, {q80_gemv_kernel<12, 3>, 12, 3, 0}};
+Q80Config g_q80_cfgs[] = {{q80_gemv_kernel<16, 4>, 16, 4, {}}, {q80_gemv_kernel<16, 3>, 16, 3, {}},
+                          {q80_gemv_kernel<16, 2>, 16, 2, {}}, {q80_gemv_kernel<8, 4>, 8, 4, {}},
+                          {q80_gemv_kernel<24, 2>, 24, 2, {}}, {q80_gemv_kernel<12, 3>, 12, 3, {}}};
 constexpr int kNumQ80Cfgs = sizeof(g_q80_cfgs) / sizeof(g_q80_cfgs[0]);
 int g_q80_variant = -1;
 }  // namespace
@@ -258,10 +258,9 @@ cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t
   }
   Q80Config& cfg = g_q80_cfgs[pick];
   const uint32_t smem = act_region + (uint32_t)(cfg.nw * cfg.d) * pitch;
-  if ((int)smem > cfg.smem_set) {
-    cudaError_t e = cudaFuncSetAttribute(cfg.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  {
+    const cudaError_t e = ensure_smem_attr((const void*)cfg.fn, (int)smem, cfg.attr);  // on this device
     if (e != cudaSuccess) return e;
-    cfg.smem_set = (int)smem;
   }
   uint32_t cps = (uint32_t)(max_smem + 1024) / (smem + 1024);
   if (cps > 4u) cps = 4u;

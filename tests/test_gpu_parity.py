@@ -324,11 +324,36 @@ def test_row_sharding_two_gpus(gpu, oracle):
     w = oracle.q4_k_quantize(oracle.gauss(n * k, 6, 0.02))
     a = oracle.gauss(k, 7, 1.0)
     ref = oracle.matmul_q(a, w, DT_Q4_K, 1, n, k, threads=0)[1]
+    before = torch.cuda.current_device()
     try:
         gpu.set_devices(list(range(torch.cuda.device_count())))
         assert same_bits(gpu.matmul_q(a, w, DT_Q4_K, 1, n, k), ref)
     finally:
         gpu.set_devices(None)
+    # the caller's current device is left as it was (the *_dev entry points
+    # run on it)
+    assert torch.cuda.current_device() == before
+
+
+def test_dev_entry_points_reject_foreign_pointers(gpu):
+    """A *_dev call runs on the current device: host memory or another GPU's
+    memory is rejected before any kernel is launched."""
+    from eosllm_b200 import backend as B
+    n, k = 256, 512
+    w = torch.zeros(n * (k // 256) * 144, dtype=torch.uint8, device="cuda:0")
+    act = torch.zeros(B.q4_k_scratch_bytes(1, k), dtype=torch.uint8, device="cuda:0")
+    c = torch.zeros(n, dtype=torch.float32, device="cuda:0")
+    host = np.zeros(n * (k // 256) * 144, np.uint8)
+    with pytest.raises(B.CudaBackendError) as ei:
+        gpu.q4_k_gemv_dev(act, host, c, n, k)
+    assert ei.value.status == B.EOS_E_INVALID_ARG
+    if torch.cuda.device_count() > 1:
+        w1 = torch.zeros_like(w, device="cuda:1")
+        with pytest.raises(B.CudaBackendError) as ei:
+            gpu.q4_k_gemv_dev(act, w1, c, n, k)
+        assert ei.value.status == B.EOS_E_INVALID_ARG
+    gpu.q4_k_gemv_dev(act, w, c, n, k)  # same-device pointers still work
+    torch.cuda.synchronize()
 
 
 def test_no_device_errors_raised(gpu):
