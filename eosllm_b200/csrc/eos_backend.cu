@@ -59,13 +59,14 @@ struct DevInfo {
 };
 
 std::mutex g_info_mu;
-std::vector<DevInfo> g_info;
+// One entry per device ordinal, never moved: shards and callers keep
+// pointers to their device's entry.
+DevInfo g_info[eos::kMaxDevices];
 
 int device_info(int dev, DevInfo** out) {
   std::lock_guard<std::mutex> lk(g_info_mu);
-  if (dev < 0) return fail(EOS_E_INVALID_ARG, "bad device %d", dev);
-  if ((size_t)dev >= g_info.size()) g_info.resize((size_t)dev + 1);
-  DevInfo& d = g_info[(size_t)dev];
+  if (dev < 0 || dev >= eos::kMaxDevices) return fail(EOS_E_INVALID_ARG, "bad device %d", dev);
+  DevInfo& d = g_info[dev];
   if (!d.ready) {
     int major = 0, minor = 0;
     EOS_CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev), "cudaDeviceGetAttribute");
@@ -493,12 +494,15 @@ void eosi_cuda_shutdown(void) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   release_all();
   std::lock_guard<std::mutex> lk2(g_info_mu);
-  for (size_t d = 0; d < g_info.size(); ++d)
+  int prev = 0;
+  const bool had = cudaGetDevice(&prev) == cudaSuccess;
+  for (int d = 0; d < eos::kMaxDevices; ++d)
     if (g_info[d].err_d) {
-      cudaSetDevice((int)d);
+      cudaSetDevice(d);
       cudaFree(g_info[d].err_d);
+      g_info[d] = DevInfo();
     }
-  g_info.clear();
+  if (had) cudaSetDevice(prev);
 }
 
 const char* eosi_cuda_last_error(void) { return g_err; }
