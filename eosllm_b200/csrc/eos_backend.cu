@@ -121,6 +121,8 @@ struct Shard {
   uint8_t* d_act = nullptr;
   size_t cap_act = 0;
   uint32_t* h_err = nullptr;  // pinned copy of the error word
+  uint8_t* h_blk = nullptr;   // pinned: Q4_K path's status header + outputs, one D2H
+  size_t cap_blk = 0;
   std::unordered_map<Key, WeightEntry, KeyHash> cache;
 };
 
@@ -156,6 +158,7 @@ void release_shard(Shard& s) {
   cudaFree(s.d_c);
   cudaFree(s.d_act);
   if (s.h_err) cudaFreeHost(s.h_err);
+  if (s.h_blk) cudaFreeHost(s.h_blk);
   if (s.stream) cudaStreamDestroy(s.stream);
   s = Shard();
 }
@@ -243,7 +246,9 @@ int ensure_pinned(float** p, size_t* cap, size_t bytes) {
   *p = nullptr;
   *cap = 0;
   size_t want = std::max(bytes, (size_t)65536);
-  EOS_CK(cudaHostAlloc((void**)p, want, cudaHostAllocPortable), "pinned staging");
+  // portable (every device's context treats it as pinned) and mapped (a
+  // kernel may read it directly: the Q4_K path's activations)
+  EOS_CK(cudaHostAlloc((void**)p, want, cudaHostAllocPortable | cudaHostAllocMapped), "pinned staging");
   *cap = want;
   return EOS_OK;
 }
@@ -347,6 +352,14 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
   cudaGetDevice(&prev);
   memcpy(g_h_a, a, (size_t)m * k * 4u);
   std::vector<char> used(G, 0);
+  // Q4_K with n >= 4 (the int8 path): zero-copy activations, one D2H
+  const bool q4k_fast = dtype == EOS_DT_Q4_K && n >= 4;
+  const float* d_a_mapped = nullptr;
+  if (q4k_fast) {
+    void* dp = nullptr;
+    EOS_CK(cudaHostGetDevicePointer(&dp, g_h_a, 0), "mapped activations");
+    d_a_mapped = static_cast<const float*>(dp);
+  }
   for (uint32_t gi = 0; gi < G && rc == EOS_OK; ++gi) {
     Shard& s = g_shards[gi];
     const uint32_t row0 = (uint32_t)(((uint64_t)n * gi) / G), row1 = (uint32_t)(((uint64_t)n * (gi + 1)) / G);
@@ -363,6 +376,42 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
     if (rc == EOS_OK && dtype == EOS_DT_Q4_K)
       rc = ensure_dev(&s.d_act, &s.cap_act, eos::act_layout_bytes(m, k, EOS_ACT_LAYOUT_GEMV), "act scratch");
     if (rc != EOS_OK) break;
+    if (q4k_fast) {
+      // Q4_K: the packing kernel reads the activations straight from the
+      // mapped pinned staging buffer (no H2D copy) and zeroes a status word
+      // the GEMVs report into; status word + outputs come back in one D2H
+      const size_t blk = 16u + (size_t)m * rows * 4u;
+      rc = ensure_dev(&s.d_c, &s.cap_c, blk, "output buffer");
+      if (rc == EOS_OK && s.cap_blk < blk) {
+        if (s.h_blk) cudaFreeHost(s.h_blk);
+        s.h_blk = nullptr;
+        s.cap_blk = 0;
+        const cudaError_t ae = cudaHostAlloc((void**)&s.h_blk, std::max(blk, (size_t)65536), cudaHostAllocPortable);
+        if (ae != cudaSuccess) rc = cuda_fail(ae, "pinned output staging");
+        else s.cap_blk = std::max(blk, (size_t)65536);
+      }
+      if (rc != EOS_OK) break;
+      used[gi] = 1;
+      uint32_t* status = reinterpret_cast<uint32_t*>(s.d_c);
+      float* d_out = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d_c) + 16);
+      cudaError_t e = eos::launch_act_pack(d_a_mapped, m, k, s.d_act, EOS_ACT_LAYOUT_GEMV, s.stream, status);
+      if (e != cudaSuccess) {
+        rc = cuda_fail(e, "activation pack kernel");
+        break;
+      }
+      const size_t act_stride = eos::act_layout_bytes(1, k, EOS_ACT_LAYOUT_GEMV);
+      for (uint32_t i = 0; i < m && rc == EOS_OK; ++i) {
+        int st2 = EOS_OK;
+        e = eos::launch_q4k_gemv(d_w, s.d_act + i * act_stride, nullptr, d_out + (size_t)i * rows, rows, k, status,
+                                 s.info->num_sms, s.info->max_smem, true, s.stream, &st2);
+        if (e != cudaSuccess) rc = cuda_fail(e, "q4_k gemv kernel");
+        else if (st2 != EOS_OK) rc = fail(st2, "q4_k gemv: shape %u x %u not supported", rows, k);
+      }
+      if (rc != EOS_OK) break;
+      e = cudaMemcpyAsync(s.h_blk, s.d_c, blk, cudaMemcpyDeviceToHost, s.stream);
+      if (e != cudaSuccess) rc = cuda_fail(e, "D2H outputs");
+      continue;
+    }
     cudaError_t e = cudaMemcpyAsync(s.d_a, g_h_a, (size_t)m * k * 4u, cudaMemcpyHostToDevice, s.stream);
     if (e != cudaSuccess) {
       rc = cuda_fail(e, "H2D activations");
@@ -383,15 +432,27 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
     cudaSetDevice(s.dev);
     cudaError_t e = cudaStreamSynchronize(s.stream);
     if (e != cudaSuccess && rc == EOS_OK) rc = cuda_fail(e, "kernel execution");
-    if (rc == EOS_OK && *s.h_err != 0) {
-      const uint32_t bits = *s.h_err;
-      *s.h_err = 0;
-      cudaMemset(s.info->err_d, 0, 4);
+    const uint32_t bits = q4k_fast ? *reinterpret_cast<const uint32_t*>(s.h_blk) : *s.h_err;
+    if (rc == EOS_OK && bits != 0) {
+      if (!q4k_fast) {
+        *s.h_err = 0;
+        cudaMemset(s.info->err_d, 0, 4);
+      }
       rc = fail(EOS_E_INTERNAL, "device %d: bounded wait gave up (error bits 0x%x)", s.dev, bits);
     }
   }
   cudaSetDevice(prev);
   if (rc != EOS_OK) return rc;
+  if (q4k_fast) {  // each shard's rows into c (written only on success)
+    for (uint32_t gi = 0; gi < G; ++gi) {
+      if (!used[gi]) continue;
+      const uint32_t row0 = (uint32_t)(((uint64_t)n * gi) / G), row1 = (uint32_t)(((uint64_t)n * (gi + 1)) / G);
+      const uint32_t rows = row1 - row0;
+      const float* src = reinterpret_cast<const float*>(g_shards[gi].h_blk + 16);
+      for (uint32_t i = 0; i < m; ++i) memcpy(c + (size_t)i * n + row0, src + (size_t)i * rows, (size_t)rows * 4u);
+    }
+    return EOS_OK;
+  }
   memcpy(c, g_h_c, (size_t)m * n * 4u);
   return EOS_OK;
 }

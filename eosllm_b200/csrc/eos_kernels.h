@@ -21,7 +21,10 @@ void set_error_message(const char* msg);
 int pointers_on_device(std::initializer_list<const void*> ptrs, int dev);
 
 size_t act_layout_bytes(uint32_t m, uint32_t k, int layout);
-cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out, int layout, cudaStream_t st);
+// zero_word (optional): set to 0 by the kernel, for the GEMVs that follow to
+// report into (the host path reads it back with their outputs).
+cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out, int layout, cudaStream_t st,
+                            uint32_t* zero_word = nullptr);
 
 // Exactly one of `act` (packed activations, GEMV layout) and `a` (f32
 // activations, packed inside the kernel) is non-null.  out_status: EOS_OK, or

@@ -46,9 +46,12 @@ namespace eos {
 // Activation packing kernel: one warp per 32-group.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) act_pack_kernel(const float* __restrict__ a, uint32_t m, uint32_t k,
-                                                       uint8_t* __restrict__ out, int layout) {
+                                                       uint8_t* __restrict__ out, int layout, uint32_t* zero_word) {
   pdl_trigger();  // let the dependent GEMV start streaming its weights
   pdl_wait();     // `a` may be the previous kernel's output
+  // the error word of the GEMVs that follow starts at 0 (they report into it
+  // only after their own PDL wait, i.e. after this grid has completed)
+  if (zero_word != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *zero_word = 0u;
   const uint32_t groups_per_row = k >> 5;
   const uint32_t gid = blockIdx.x * 8u + (threadIdx.x >> 5);
   const uint32_t lane = threadIdx.x & 31u;
@@ -346,7 +349,8 @@ size_t act_layout_bytes(uint32_t m, uint32_t k, int layout) {
   return (size_t)m * k + (size_t)m * (k >> 5) * 8u;
 }
 
-cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out, int layout, cudaStream_t st) {
+cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out, int layout, cudaStream_t st,
+                            uint32_t* zero_word) {
   const uint32_t groups = m * (k >> 5);
   const uint32_t blocks = (groups + 7u) / 8u;
   if (blocks == 0) return cudaSuccess;
@@ -359,7 +363,7 @@ cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = 1;
-  return cudaLaunchKernelEx(&lc, act_pack_kernel, a, m, k, out, layout);
+  return cudaLaunchKernelEx(&lc, act_pack_kernel, a, m, k, out, layout, zero_word);
 }
 
 namespace {
