@@ -168,15 +168,16 @@ struct PfAttnParams {
 
 template <int E>
 __host__ __device__ constexpr uint32_t pf_attn_smem_bytes() {
-  // q rows, K chunk (rows padded by 4 floats: conflict-free 16-byte loads
-  // with one row per lane), V chunk, per-warp output row
-  return 4u * (kPfQ * 32u * E + kPfKC * (32u * E + 4u) + kPfKC * 32u * E + 4u * 32u * E);
+  // q rows, two buffers of (K chunk -- rows padded by 4 floats: conflict-free
+  // 16-byte loads with one row per lane -- and V chunk), per-warp output row
+  return 4u * (kPfQ * 32u * E + 2u * (kPfKC * (32u * E + 4u) + kPfKC * 32u * E) + 4u * 32u * E);
 }
 
 // Grid (hl, ceil(m / 16)), 128 threads.  CTA (h, b) owns query rows
 // [16 b, 16 b + 16) of local head h; warp w owns four of them.  Cache
 // positions stream through shared memory 32 at a time (K and V rows of the
-// head's KV group); lane j scores position c0 + j for the warp's four
+// head's KV group, double-buffered: the next chunk's copies fly while this
+// one is used); lane j scores position c0 + j for the warp's four
 // queries (q from shared memory by broadcast, K row per lane), then a
 // streaming softmax update (running max, rescaled sum and output) and the
 // weighted V rows (lane = E dims).  At the end each query row is normalised
@@ -185,10 +186,9 @@ template <int E>
 __global__ void __launch_bounds__(128) pf_attn_kernel(const PfAttnParams p) {
   constexpr uint32_t HD = 32u * E, KP = HD + 4u;
   extern __shared__ __align__(16) float sm[];
-  float* qs = sm;                 // [kPfQ][HD]
-  float* ks = qs + kPfQ * HD;     // [kPfKC][KP]
-  float* vs = ks + kPfKC * KP;    // [kPfKC][HD]
-  float* so = vs + kPfKC * HD;    // [4][HD]
+  float* qs = sm;                          // [kPfQ][HD]
+  float* kv0 = qs + kPfQ * HD;  // buffer b: K [kPfKC][KP] at kv0 + b (KP + HD) kPfKC, then V [kPfKC][HD]
+  float* so = kv0 + 2u * kPfKC * (KP + HD);  // [4][HD]
   const uint32_t hloc = blockIdx.x, i0 = blockIdx.y * kPfQ;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   const uint32_t gh = p.h0 + hloc;
@@ -213,19 +213,34 @@ __global__ void __launch_bounds__(128) pf_attn_kernel(const PfAttnParams p) {
   const uint32_t qpos0 = p.pos0 + i0 + warp * 4u;  // position of the warp's first query
   const uint32_t last = p.pos0 + i0 + nq - 1u;      // largest query position of the CTA
   const uint64_t pol = l2_policy_evict_last();      // the layer's cache rows are re-read by every query block
-  for (uint32_t c0 = 0; c0 <= last; c0 += kPfKC) {
+  // K and V rows [c0, c0 + 32) (up to `last`) into buffer b; one commit group
+  auto stage = [&](uint32_t c0, int b) {
     const uint32_t np = (last + 1u - c0) < kPfKC ? (last + 1u - c0) : kPfKC;
-    __syncthreads();  // the previous chunk (and, first time, q staging) is done
     const float* kg = p.kc + (size_t)c0 * crow + kvi * HD;
     const float* vg = p.vc + (size_t)c0 * crow + kvi * HD;
     for (uint32_t t = tid; t < np * (HD / 4u); t += 128u) {
       const uint32_t r = t / (HD / 4u), c4 = (t % (HD / 4u)) * 4u;
-      cp_async16(ks + r * KP + c4, kg + (size_t)r * crow + c4, pol);
-      cp_async16(vs + r * HD + c4, vg + (size_t)r * crow + c4, pol);
+      float* kb = kv0 + (uint32_t)b * kPfKC * (KP + HD);
+      cp_async16(kb + r * KP + c4, kg + (size_t)r * crow + c4, pol);
+      cp_async16(kb + kPfKC * KP + r * HD + c4, vg + (size_t)r * crow + c4, pol);
     }
     cp_async_commit();
-    cp_async_wait<0>();
-    __syncthreads();
+  };
+  stage(0u, 0);
+  int cur = 0;
+  for (uint32_t c0 = 0; c0 <= last; c0 += kPfKC, cur ^= 1) {
+    const uint32_t np = (last + 1u - c0) < kPfKC ? (last + 1u - c0) : kPfKC;
+    // the other buffer was last read in the previous iteration, which ended
+    // with a barrier: refill it with the next chunk, then wait for this one
+    if (c0 + kPfKC <= last) {
+      stage(c0 + kPfKC, cur ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // this chunk (and, first time, q staging) visible to all
+    const float* ks = kv0 + (uint32_t)cur * kPfKC * (KP + HD);
+    const float* vs = ks + kPfKC * KP;
     // scores of position c0 + lane for the warp's four queries (rows >= np
     // of the chunk hold stale values; they are masked)
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -276,6 +291,7 @@ __global__ void __launch_bounds__(128) pf_attn_kernel(const PfAttnParams p) {
         for (int ee = 0; ee < E; ++ee) o[r][ee] = __fmaf_rn(a, vv[ee], o[r][ee]);
       }
     }
+    __syncthreads();  // every warp is done with buffer `cur` before it is refilled
   }
   // normalise, pack per 32 dims
   const uint32_t kq = p.hl * HD, pitch = pf_pad4(p.m);
