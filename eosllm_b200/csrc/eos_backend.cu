@@ -121,7 +121,8 @@ struct Shard {
   uint8_t* d_act = nullptr;
   size_t cap_act = 0;
   uint32_t* h_err = nullptr;  // pinned copy of the error word
-  uint8_t* h_blk = nullptr;   // pinned: Q4_K path's status header + outputs, one D2H
+  uint8_t* h_blk = nullptr;      // mapped pinned: Q4_K path's status header + outputs
+  uint8_t* h_blk_dev = nullptr;  // its device alias, written by copy_out_kernel
   size_t cap_blk = 0;
   std::unordered_map<Key, WeightEntry, KeyHash> cache;
 };
@@ -352,7 +353,7 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
   cudaGetDevice(&prev);
   memcpy(g_h_a, a, (size_t)m * k * 4u);
   std::vector<char> used(G, 0);
-  // Q4_K with n >= 4 (the int8 path): zero-copy activations, one D2H
+  // Q4_K with n >= 4 (the int8 path): zero-copy activations and outputs
   const bool q4k_fast = dtype == EOS_DT_Q4_K && n >= 4;
   const float* d_a_mapped = nullptr;
   if (q4k_fast) {
@@ -379,16 +380,27 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
     if (q4k_fast) {
       // Q4_K: the packing kernel reads the activations straight from the
       // mapped pinned staging buffer (no H2D copy) and zeroes a status word
-      // the GEMVs report into; status word + outputs come back in one D2H
-      const size_t blk = 16u + (size_t)m * rows * 4u;
+      // the GEMVs report into; a copy kernel chained behind the GEMVs writes
+      // status word + outputs into mapped pinned memory (no copy engine)
+      const size_t blk = 16u + (((size_t)m * rows * 4u + 15u) & ~(size_t)15u);
       rc = ensure_dev(&s.d_c, &s.cap_c, blk, "output buffer");
       if (rc == EOS_OK && s.cap_blk < blk) {
         if (s.h_blk) cudaFreeHost(s.h_blk);
         s.h_blk = nullptr;
+        s.h_blk_dev = nullptr;
         s.cap_blk = 0;
-        const cudaError_t ae = cudaHostAlloc((void**)&s.h_blk, std::max(blk, (size_t)65536), cudaHostAllocPortable);
-        if (ae != cudaSuccess) rc = cuda_fail(ae, "pinned output staging");
-        else s.cap_blk = std::max(blk, (size_t)65536);
+        const size_t want = std::max(blk, (size_t)65536);
+        cudaError_t ae = cudaHostAlloc((void**)&s.h_blk, want, cudaHostAllocPortable | cudaHostAllocMapped);
+        void* dp = nullptr;
+        if (ae == cudaSuccess) ae = cudaHostGetDevicePointer(&dp, s.h_blk, 0);
+        if (ae != cudaSuccess) {
+          if (s.h_blk) cudaFreeHost(s.h_blk);
+          s.h_blk = nullptr;
+          rc = cuda_fail(ae, "pinned output staging");
+        } else {
+          s.h_blk_dev = static_cast<uint8_t*>(dp);
+          s.cap_blk = want;
+        }
       }
       if (rc != EOS_OK) break;
       used[gi] = 1;
@@ -408,8 +420,8 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
         else if (st2 != EOS_OK) rc = fail(st2, "q4_k gemv: shape %u x %u not supported", rows, k);
       }
       if (rc != EOS_OK) break;
-      e = cudaMemcpyAsync(s.h_blk, s.d_c, blk, cudaMemcpyDeviceToHost, s.stream);
-      if (e != cudaSuccess) rc = cuda_fail(e, "D2H outputs");
+      e = eos::launch_copy_out(s.d_c, s.h_blk_dev, blk, s.stream);
+      if (e != cudaSuccess) rc = cuda_fail(e, "outputs to host (copy kernel)");
       continue;
     }
     cudaError_t e = cudaMemcpyAsync(s.d_a, g_h_a, (size_t)m * k * 4u, cudaMemcpyHostToDevice, s.stream);

@@ -38,6 +38,12 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
                             uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status,
                             float* const* c_extra = nullptr, uint32_t n_extra = 0);
 void set_q4k_gemv_variant(int v);
+// Copies `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// device memory written by the previous kernel on `st` to `dst`, typically
+// the device alias of mapped pinned host memory.  Launched with programmatic
+// dependent launch, so it replaces a device-to-host copy-engine transfer
+// behind that kernel without waiting for a copy engine.
+cudaError_t launch_copy_out(const void* src, void* dst, size_t bytes, cudaStream_t st);
 // n < 4 Q4_K: the reference's f32-dequant path, bit for bit.
 cudaError_t launch_q4k_f32_small_n(const float* a, const uint8_t* w, float* c, uint32_t m, uint32_t n, uint32_t k,
                                    cudaStream_t st);

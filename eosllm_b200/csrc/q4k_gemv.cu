@@ -77,6 +77,33 @@ __global__ void __launch_bounds__(256) act_pack_kernel(const float* __restrict__
 }
 
 // ---------------------------------------------------------------------------
+// Results to the host: 16-byte stores into mapped pinned memory, coalesced
+// per warp into whole 128-byte lines on the PCIe link.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) copy_out_kernel(const uint4* src, uint4* dst, uint32_t n16) {
+  pdl_wait();  // src is the previous grid's output
+  for (uint32_t i = blockIdx.x * 256u + threadIdx.x; i < n16; i += gridDim.x * 256u) dst[i] = src[i];
+}
+
+cudaError_t launch_copy_out(const void* src, void* dst, size_t bytes, cudaStream_t st) {
+  const uint32_t n16 = (uint32_t)(bytes >> 4);
+  if (n16 == 0) return cudaSuccess;
+  uint32_t blocks = (n16 + 255u) / 256u;
+  if (blocks > 64u) blocks = 64u;
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(blocks);
+  lc.blockDim = dim3(256);
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, copy_out_kernel, reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst),
+                            n16);
+}
+
+// ---------------------------------------------------------------------------
 // In-CTA activation packing into shared memory (fused path)
 // ---------------------------------------------------------------------------
 template <int NW>
@@ -100,6 +127,30 @@ __device__ __forceinline__ void pack_into_smem(const float* __restrict__ a, uint
         act_s[rec_aq_offset(g) + lane] = static_cast<uint8_t>(q);
         if (lane == 0) *reinterpret_cast<float2*>(act_s + rec_st_offset(g)) = make_float2(scale, (float)sum);
       }
+    }
+  }
+}
+
+// Packed activation records global -> shared memory with every load of a
+// round in flight before the first store: one L2 round trip per 8 x 16
+// bytes a thread instead of one per 16 bytes (the records of a k = 11008
+// row are 20.6 KB, five 16-byte rounds for 256 threads).
+template <int NT>
+__device__ __forceinline__ void copy_act_to_smem(const uint8_t* __restrict__ src, uint8_t* dst, uint32_t bytes) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  const uint32_t n16 = bytes >> 4;
+  for (uint32_t base = 0; base < n16; base += 8u * NT) {
+    uint4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t t = base + (uint32_t)j * NT + threadIdx.x;
+      if (t < n16) v[j] = s[t];  // coherent loads: the previous grid wrote `src`
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t t = base + (uint32_t)j * NT + threadIdx.x;
+      if (t < n16) d[t] = v[j];
     }
   }
 }
@@ -172,9 +223,7 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParam
   if (p.a != nullptr) {
     pack_into_smem<NW>(p.a, p.k, act_s, warp, lane);
   } else {
-    const uint4* src = reinterpret_cast<const uint4*>(p.act);
-    uint4* dst = reinterpret_cast<uint4*>(act_s);
-    for (uint32_t t = threadIdx.x; t < (p.act_bytes >> 4); t += NW * 32) dst[t] = src[t];
+    copy_act_to_smem<NW * 32>(p.act, act_s, p.act_bytes);
   }
   __syncthreads();
   pdl_trigger();  // every CTA holds its activations: the next kernel may start
@@ -272,9 +321,7 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_cols_kernel(const Q4kGemv
   if (p.a != nullptr) {
     pack_into_smem<NW>(p.a, p.k, act_s, warp, lane);
   } else {
-    const uint4* src = reinterpret_cast<const uint4*>(p.act);
-    uint4* dst = reinterpret_cast<uint4*>(act_s);
-    for (uint32_t t = threadIdx.x; t < (p.act_bytes >> 4); t += NW * 32) dst[t] = src[t];
+    copy_act_to_smem<NW * 32>(p.act, act_s, p.act_bytes);
   }
   __syncthreads();
   pdl_trigger();
