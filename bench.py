@@ -503,7 +503,8 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic,
-                         "kernel": "q4k_gemv_cols_kernel<8,2,2>: mean launch time of a 100+-launch train per shape "
+                         "kernel": "q4k_gemv_cols_kernel<8,2,2> (rows of k = 11008 staged in 16-super-block chunks): "
+                                   "mean launch time of a 100+-launch train per shape "
                                    "(rotating copies), bytes = weights + 4k + 4n per launch, summed over the sweep",
                          "per_shape_us": {f"{n}x{k}": round(ms * 1e3, 3) for (n, k), ms in zip(SHAPES, per_shape_ms)},
                          "per_shape_frac": {f"{n}x{k}": round(algo_bytes(n, k) / (ms * 1e-3) / 1e9 / peak, 4)

@@ -164,6 +164,7 @@ struct Q4kGemvParams {
   const float* a;      // f32 activations, k (fused path)
   float* c;            // n outputs
   uint32_t n, k, nb, row_bytes, pitch, R, act_bytes;
+  uint32_t cb, nch;  // column-major kernel: super-blocks per staged row chunk, chunks per row
   uint32_t* err;
   // further copies of every output (tensor-parallel push: other GPUs'
   // receive buffers, mapped through CUDA IPC), written after c
@@ -280,15 +281,23 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParam
 // Column-major variant: a warp stage is R rows; a lane PAIR owns one
 // super-block column b (16 columns per pass) and computes all R rows of it,
 // so each activation half-record is read from shared memory once per stage
-// instead of once per row.  Same terms, partials and ordered row sums as
-// q4k_gemv_kernel, so outputs are bit-identical.
-template <int NW, int D, int R>
+// instead of once per row.  Long rows are streamed in chunks of p.cb
+// super-blocks (p.nch chunks a row; p.nch == 1: whole rows): a warp takes
+// row groups warp, warp + NW, ... and runs through the chunks of each in
+// order, parking every super-block partial; after the last chunk one lane
+// per row adds them in order.  Chunking keeps the staging buffers -- hence
+// the CTA's shared memory -- independent of k, so long rows still fit two
+// CTAs per SM.  Same terms, partials and ordered row sums as q4k_gemv_kernel,
+// so outputs are bit-identical.  CHUNKED = false is the whole-row form
+// (nch = 1, cb = nb known at compile time, no chunk bookkeeping).
+template <int NW, int D, int R, bool CHUNKED>
 __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_cols_kernel(const Q4kGemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t act_region = (p.act_bytes + 127u) & ~127u;
   uint8_t* act_s = smem;
   const uint32_t nb = p.nb, pitch = p.pitch, row_bytes = p.row_bytes;
-  const uint32_t buf_bytes = R * pitch;
+  const uint32_t cb = CHUNKED ? p.cb : nb, nch = CHUNKED ? p.nch : 1u;
+  const uint32_t buf_bytes = R * pitch;  // pitch = cb * Q4K_BYTES
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t pstride = (R * nb + 3u) & ~3u;
   const uint32_t part_region = (NW * pstride * 4u + 127u) & ~127u;
@@ -298,24 +307,30 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_cols_kernel(const Q4kGemv
   const uint32_t r0 = (uint32_t)(((uint64_t)p.n * blockIdx.x) / gridDim.x);
   const uint32_t r1 = (uint32_t)(((uint64_t)p.n * (blockIdx.x + 1)) / gridDim.x);
   const uint32_t nrows = r1 - r0;
-  const uint32_t nst = (nrows + R - 1) / R;
-  const uint32_t cpr = row_bytes >> 4;
+  const uint32_t nst = (nrows + R - 1) / R;  // row groups of this CTA
   const uint64_t pol_w = l2_policy_evict_first();
-
-  auto issue = [&](uint32_t s, uint32_t slot) {
-    if (s < nst) {
-      const uint32_t rows = (nrows - s * R) < R ? (nrows - s * R) : R;
-      const uint8_t* src = p.w + (size_t)(r0 + s * R) * row_bytes;
+  // this warp's stages in order: row groups warp, warp + NW, ..., each
+  // through chunks 0 .. nch - 1.  Cursor (ig, ic) is the next stage to stage.
+  uint32_t ig = warp, ic = 0;
+  auto issue = [&](uint32_t slot) {
+    if (ig < nst) {
+      const uint32_t rows = (nrows - ig * R) < R ? (nrows - ig * R) : R;
+      const uint32_t b0 = ic * cb, cpr = ((nb - b0) < cb ? (nb - b0) : cb) * (Q4K_BYTES / 16u);
+      const uint8_t* src = p.w + (size_t)(r0 + ig * R) * row_bytes + (size_t)b0 * Q4K_BYTES;
       uint8_t* dst = wbuf + slot * buf_bytes;
       for (uint32_t r = 0; r < rows; ++r)
-        for (uint32_t t = lane; t < cpr; t += 32)
-          cp_async16(dst + r * pitch + (t << 4), src + (size_t)r * row_bytes + (t << 4), pol_w);
+        for (uint32_t q = lane; q < cpr; q += 32)
+          cp_async16(dst + r * pitch + (q << 4), src + (size_t)r * row_bytes + (q << 4), pol_w);
+      if (++ic == nch) {
+        ic = 0;
+        ig += NW;
+      }
     }
-    cp_async_commit();
+    cp_async_commit();  // one group per call, empty or not, keeps the counting uniform
   };
 
 #pragma unroll
-  for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(warp + d * NW, d);
+  for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(d);
 
   pdl_wait();
   if (p.a != nullptr) {
@@ -327,41 +342,47 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_cols_kernel(const Q4kGemv
   pdl_trigger();
 
   const uint32_t h = lane & 1u;
-  uint32_t i = 0;
-  for (uint32_t s = warp; s < nst; s += NW, ++i) {
-    const uint32_t slot = i % D;
+  uint32_t g = warp, ch = 0;  // the stage computed now: row group g, chunk ch
+  for (uint32_t t = 0; g < nst; ++t) {
+    const uint32_t slot = t % D;
     cp_async_wait<D - 1>();
     __syncwarp();
-    const uint32_t rows = (nrows - s * R) < R ? (nrows - s * R) : R;
+    const uint32_t rows = (nrows - g * R) < R ? (nrows - g * R) : R;
+    const uint32_t b0 = ch * cb, bn = (nb - b0) < cb ? (nb - b0) : cb;  // super-blocks of this chunk
     const uint8_t* stage = wbuf + slot * buf_bytes;
-    for (uint32_t b0 = 0; b0 < nb; b0 += 16u) {
-      const uint32_t b = b0 + (lane >> 1);
-      const uint32_t bc = b < nb ? b : nb - 1u;
-      float t[R][4];
-      q4k_half_terms_rows<R>(stage + bc * Q4K_BYTES, pitch, act_s + bc * kActRec + h * kActHalf, h, t, rows);
+    for (uint32_t j0 = 0; j0 < bn; j0 += 16u) {
+      const uint32_t j = j0 + (lane >> 1);
+      const uint32_t jc = j < bn ? j : bn - 1u;
+      float tr[R][4];
+      q4k_half_terms_rows<R>(stage + jc * Q4K_BYTES, pitch, act_s + (b0 + jc) * kActRec + h * kActHalf, h, tr,
+                             rows);
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        const float part = pair_partial(t[r], lane);
-        if (h && b < nb && (uint32_t)r < rows) part_w[r * nb + b] = part;
+        const float part = pair_partial(tr[r], lane);
+        if (h && j < bn && (uint32_t)r < rows) part_w[r * nb + b0 + j] = part;
       }
     }
     __syncwarp();
-    issue(s + D * NW, slot);
-    if (lane < rows) {
+    issue(slot);
+    if (ch == nch - 1u && lane < rows) {
       const float* pr = part_w + lane * nb;
       float acc = 0.0f;  // c = 0; c += partial_b in order (:194, :264)
       uint32_t b = 0;
       for (; b + 8u <= nb; b += 8u) {
         float v8[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v8[j] = pr[b + j];
+        for (int q = 0; q < 8; ++q) v8[q] = pr[b + q];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc = __fadd_rn(acc, v8[j]);
+        for (int q = 0; q < 8; ++q) acc = __fadd_rn(acc, v8[q]);
       }
       for (; b < nb; ++b) acc = __fadd_rn(acc, pr[b]);
-      gemv_store(p, r0 + s * R + lane, acc);
+      gemv_store(p, r0 + g * R + lane, acc);
     }
     __syncwarp();
+    if (++ch == nch) {
+      ch = 0;
+      g += NW;
+    }
   }
   cp_async_wait<0>();
 }
@@ -400,7 +421,7 @@ cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out
                             uint32_t* zero_word) {
   const uint32_t groups = m * (k >> 5);
   const uint32_t blocks = (groups + 7u) / 8u;
-  if (blocks == 0) return cudaSuccess;
+  if (blocks == 0) return zero_word != nullptr ? cudaMemsetAsync(zero_word, 0, 4, st) : cudaSuccess;
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(blocks);
   lc.blockDim = dim3(256);
@@ -417,32 +438,39 @@ namespace {
 struct GemvConfig {
   void (*fn)(const Q4kGemvParams);
   int nw, d;
-  int cols;      // 0: q4k_gemv_kernel (rows per stage chosen at launch); R: q4k_gemv_cols_kernel<., ., R>
+  int cols;      // 0: q4k_gemv_kernel (rows per stage chosen at launch); R: q4k_gemv_cols_kernel<., ., R, .>
   SmemAttr attr;  // dynamic shared memory allowed so far, per device
+  void (*fn_chunked)(const Q4kGemvParams);  // column-major: rows staged in chunks
+  SmemAttr attr_chunked;
 };
+#define EOS_COLS_CFG(NW, D, R) \
+  { q4k_gemv_cols_kernel<NW, D, R, false>, NW, D, R, {}, q4k_gemv_cols_kernel<NW, D, R, true>, {} }
 GemvConfig g_cfgs[] = {
-    {q4k_gemv_kernel<16, 4>, 16, 4, 0, {}},      {q4k_gemv_kernel<16, 3>, 16, 3, 0, {}},
-    {q4k_gemv_kernel<16, 2>, 16, 2, 0, {}},      {q4k_gemv_kernel<20, 3>, 20, 3, 0, {}},
-    {q4k_gemv_kernel<8, 4>, 8, 4, 0, {}},        {q4k_gemv_kernel<12, 4>, 12, 4, 0, {}},
-    {q4k_gemv_kernel<24, 2>, 24, 2, 0, {}},      {q4k_gemv_kernel<8, 6>, 8, 6, 0, {}},
-    {q4k_gemv_kernel<20, 2>, 20, 2, 0, {}},      {q4k_gemv_kernel<12, 3>, 12, 3, 0, {}},
-    {q4k_gemv_kernel<16, 2>, 16, 2, 0, {}},      {q4k_gemv_kernel<10, 4>, 10, 4, 0, {}},
-    {q4k_gemv_cols_kernel<12, 2, 4>, 12, 2, 4, {}}, {q4k_gemv_cols_kernel<16, 3, 2>, 16, 3, 2, {}},
-    {q4k_gemv_cols_kernel<8, 3, 4>, 8, 3, 4, {}},   {q4k_gemv_cols_kernel<16, 2, 2>, 16, 2, 2, {}},
-    {q4k_gemv_cols_kernel<8, 2, 2>, 8, 2, 2, {}},   {q4k_gemv_cols_kernel<12, 3, 2>, 12, 3, 2, {}},
-    {q4k_gemv_cols_kernel<16, 2, 1>, 16, 2, 1, {}}, {q4k_gemv_cols_kernel<8, 4, 2>, 8, 4, 2, {}}};
+    {q4k_gemv_kernel<16, 4>, 16, 4, 0, {}, nullptr, {}}, {q4k_gemv_kernel<16, 3>, 16, 3, 0, {}, nullptr, {}},
+    {q4k_gemv_kernel<16, 2>, 16, 2, 0, {}, nullptr, {}}, {q4k_gemv_kernel<20, 3>, 20, 3, 0, {}, nullptr, {}},
+    {q4k_gemv_kernel<8, 4>, 8, 4, 0, {}, nullptr, {}},   {q4k_gemv_kernel<12, 4>, 12, 4, 0, {}, nullptr, {}},
+    {q4k_gemv_kernel<24, 2>, 24, 2, 0, {}, nullptr, {}}, {q4k_gemv_kernel<8, 6>, 8, 6, 0, {}, nullptr, {}},
+    {q4k_gemv_kernel<20, 2>, 20, 2, 0, {}, nullptr, {}}, {q4k_gemv_kernel<12, 3>, 12, 3, 0, {}, nullptr, {}},
+    {q4k_gemv_kernel<16, 2>, 16, 2, 0, {}, nullptr, {}}, {q4k_gemv_kernel<10, 4>, 10, 4, 0, {}, nullptr, {}},
+    EOS_COLS_CFG(12, 2, 4), EOS_COLS_CFG(16, 3, 2), EOS_COLS_CFG(8, 3, 4),  EOS_COLS_CFG(16, 2, 2),
+    EOS_COLS_CFG(8, 2, 2),  EOS_COLS_CFG(12, 3, 2), EOS_COLS_CFG(16, 2, 1), EOS_COLS_CFG(8, 4, 2)};
+#undef EOS_COLS_CFG
 constexpr int kNumCfgs = sizeof(g_cfgs) / sizeof(g_cfgs[0]);
 int g_q4k_variant = -1;  // kernel config override (-1: automatic)
 int g_q4k_rows = 0;      // rows-per-stage override (0: automatic)
 int g_q4k_ctas = 0;      // CTAs-per-SM override (0: automatic)
+int g_q4k_chunk = 0;     // column-major row chunking override (0: automatic)
 }  // namespace
 
 void set_q4k_gemv_variant(int v) {
-  // v < 0: automatic.  Else v = cfg + 32 * rows + 512 * ctas_per_sm, each
-  // field 0 = automatic (rows applies to the row-major kernels only).
+  // v < 0: automatic.  Else v = cfg + 32 * rows + 512 * ctas_per_sm +
+  // 4096 * chunk, each field 0 = automatic (rows applies to the row-major
+  // kernels only; chunk to the column-major ones: 1 = whole rows, c >= 2 =
+  // chunks of 8 (c - 1) super-blocks).
   g_q4k_variant = v < 0 ? -1 : (v % 32);
   g_q4k_rows = v < 0 ? 0 : ((v / 32) % 16);
-  g_q4k_ctas = v < 0 ? 0 : (v / 512);
+  g_q4k_ctas = v < 0 ? 0 : ((v / 512) % 8);
+  g_q4k_chunk = v < 0 ? 0 : (v / 4096);
 }
 
 cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
@@ -466,16 +494,32 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   const uint32_t target = R_rm == 1 ? 0u : (R_rm == 2 ? 32u : 16u);
   const uint32_t pitch_rm = row_bytes + ((target - (row_bytes & 127u)) & 127u);
   // column-major kernels: R rows per stage, unpadded (a load phase spans
-  // four columns of one row, always distinct banks)
-  auto geom = [&](const GemvConfig& g, uint32_t& R, uint32_t& pitch) {
-    R = g.cols ? (uint32_t)g.cols : R_rm;
-    pitch = g.cols ? row_bytes : pitch_rm;
-  };
-  auto smem_of = [&](const GemvConfig& g) -> uint32_t {
-    uint32_t R, pitch;
-    geom(g, R, pitch);
+  // four columns of one row, always distinct banks), staged whole -- or,
+  // when whole rows would leave room for one CTA per SM only, in chunks of
+  // 16 super-blocks, so that two CTAs (and the next kernel's) fit an SM
+  auto smem_with = [&](const GemvConfig& g, uint32_t R, uint32_t pitch) -> uint32_t {
     const uint32_t part = ((uint32_t)g.nw * ((R * nb + 3u) & ~3u) * 4u + 127u) & ~127u;
     return act_region + part + (uint32_t)(g.nw * g.d) * R * pitch;
+  };
+  auto geom = [&](const GemvConfig& g, uint32_t& R, uint32_t& pitch, uint32_t& cb) {
+    R = g.cols ? (uint32_t)g.cols : R_rm;
+    cb = nb;
+    pitch = g.cols ? row_bytes : pitch_rm;
+    if (!g.cols) return;
+    if (g_q4k_chunk >= 2) {
+      cb = 8u * (uint32_t)(g_q4k_chunk - 1);
+    } else if (g_q4k_chunk == 0 && nb > 16u &&
+               (uint32_t)(max_smem + 1024) / (smem_with(g, R, row_bytes) + 1024u) < 2u) {
+      cb = 16u;
+    }
+    if (cb > nb) cb = nb;
+    if (cb == 0) cb = 1;  // k = 0: no super-blocks, every output is c = 0
+    pitch = cb * Q4K_BYTES;
+  };
+  auto smem_of = [&](const GemvConfig& g) -> uint32_t {
+    uint32_t R, pitch, cb;
+    geom(g, R, pitch, cb);
+    return smem_with(g, R, pitch);
   };
   // first configuration that fits: column-major with activation reuse over
   // several rows, then the row-major pipelines
@@ -492,8 +536,8 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
     if (pick < 0) pick = 2;
   }
   GemvConfig& cfg = g_cfgs[pick];
-  uint32_t R, pitch;
-  geom(cfg, R, pitch);
+  uint32_t R, pitch, cb;
+  geom(cfg, R, pitch, cb);
   const uint32_t smem = smem_of(cfg);
   if (smem > (uint32_t)max_smem) {  // rows too long to stage: unstaged kernel
     if (act == nullptr || n_extra != 0) {  // it reads packed activations, writes one destination
@@ -503,10 +547,13 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
     q4k_gemv_simple_kernel<<<(n + 7u) / 8u, 256, 0, st>>>(w, act, c, n, k);
     return cudaGetLastError();
   }
+  const uint32_t nch = nb == 0 ? 1u : (nb + cb - 1u) / cb;
+  const bool chunked = nch > 1u;  // only column-major configs ever split rows
+  void (*fn)(const Q4kGemvParams) = chunked ? cfg.fn_chunked : cfg.fn;
   {
     // on this device; largest carveout so the next kernel's CTAs can share
     // the SM (PDL overlap)
-    const cudaError_t e = ensure_smem_attr((const void*)cfg.fn, (int)smem, cfg.attr);
+    const cudaError_t e = ensure_smem_attr((const void*)fn, (int)smem, chunked ? cfg.attr_chunked : cfg.attr);
     if (e != cudaSuccess) return e;
   }
   uint32_t cps = (uint32_t)(max_smem + 1024) / (smem + 1024);
@@ -516,7 +563,7 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   uint32_t grid = (uint32_t)num_sms * cps;
   const uint32_t max_grid = (n + R - 1) / R;
   if (grid > max_grid) grid = max_grid;
-  Q4kGemvParams prm{w, act, a, c, n, k, nb, row_bytes, pitch, R, act_bytes, err, {}, n_extra};
+  Q4kGemvParams prm{w, act, a, c, n, k, nb, row_bytes, pitch, R, act_bytes, cb, nch, err, {}, n_extra};
   for (uint32_t j = 0; j < n_extra; ++j) prm.c_extra[j] = c_extra[j];
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
@@ -528,7 +575,7 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   lc.attrs = attr;
   lc.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&lc, cfg.fn, prm);
+  return cudaLaunchKernelEx(&lc, fn, prm);
 }
 
 }  // namespace eos

@@ -169,10 +169,14 @@ def test_q4k_model_shapes_bitexact(gpu, oracle, n, k):
     assert same_bits(host(dc), ref[0])
 
 
-# variant = config + 32 * rows_per_stage + 512 * ctas_per_sm; configs 0-11 are
-# the row-major kernel, 12-19 the column-major one (rows reuse activations)
+# variant = config + 32 * rows_per_stage + 512 * ctas_per_sm + 4096 * chunk;
+# configs 0-11 are the row-major kernel, 12-19 the column-major one (rows
+# reuse activations), whose rows are staged whole (chunk 1) or in chunks of
+# 8 (c - 1) super-blocks (chunk c >= 2; the last chunk of a row may be short)
 @pytest.mark.parametrize("variant", [0, 1, 2, 3, 4, 5, 6, 7, 32, 64, 128, 256, 5 + 32 * 4, 2 * 512 + 2 + 32 * 2,
-                                     12, 13, 14, 15, 16, 17, 18, 19, 2 * 512 + 15])
+                                     12, 13, 14, 15, 16, 17, 18, 19, 2 * 512 + 15,
+                                     16 + 4096 * 1, 16 + 4096 * 2, 16 + 4096 * 3, 19 + 4096 * 2, 18 + 4096 * 2,
+                                     12 + 4096 * 5, 14 + 4096 * 3, 13 + 4096 * 2 + 512 * 1])
 def test_q4k_kernel_variants_bitexact(gpu, oracle, variant):
     try:
         gpu.set_kernel_variant(DT_Q4_K, variant)
@@ -183,6 +187,25 @@ def test_q4k_kernel_variants_bitexact(gpu, oracle, variant):
             assert same_bits(gpu.matmul_q(a, w, DT_Q4_K, 1, n, k), ref), (variant, n, k)
     finally:
         gpu.set_kernel_variant(DT_Q4_K, -1)
+
+
+def test_q4k_empty_k_gives_zeros(gpu, oracle):
+    """k = 0: no super-blocks, so every output is the reference's c = 0
+    (matmul_q4_k_int8.c:194) -- through the host slot and the device path."""
+    import torch
+    w = np.zeros(16, np.uint8)
+    a = np.zeros(4, np.float32)
+    ref = oracle.matmul_q(a, w, DT_Q4_K, 2, 40, 0)[1]
+    assert np.array_equal(ref, np.zeros((2, 40), np.float32))
+    got = gpu.matmul_q(a, w, DT_Q4_K, 2, 40, 0)
+    assert same_bits(got, ref)
+    dw = torch.zeros(16, dtype=torch.uint8, device="cuda")
+    da = torch.zeros(4, dtype=torch.float32, device="cuda")
+    dc = torch.full((40,), float("nan"), dtype=torch.float32, device="cuda")
+    scratch = torch.zeros(64, dtype=torch.uint8, device="cuda")
+    gpu.matmul_q4_k_dev(da, dw, dc, 1, 40, 0, scratch)
+    torch.cuda.synchronize()
+    assert same_bits(dc.cpu().numpy(), ref[0])
 
 
 @pytest.mark.parametrize("m,n,k", [(2, 64, 4096), (3, 257, 1024), (5, 4, 512), (2, 3, 768), (4, 1, 256)])
