@@ -320,7 +320,12 @@ EOSLLM_CUDA_API int eosi_cuda_text_open_gguf(const char *path, uint32_t max_ctx,
  * current device (0 = none); clears them. */
 EOSLLM_CUDA_API int eosi_cuda_take_device_errors(uint32_t *bits);
 
-/* Kernel variant override for tuning (-1 = automatic). */
+/* Kernel variant override for tuning (-1 = automatic).  Q4_K GEMV:
+ * variant = config + 32 * rows_per_stage + 512 * ctas_per_sm + 4096 * chunk,
+ * every field 0 = automatic; configs 0..11 are the row-major kernel (rows per
+ * stage 1, 2, 4 or 8), 12..19 the column-major one, whose rows are staged
+ * whole (chunk 1) or in pieces of 8 * (chunk - 1) super-blocks (chunk >= 2).
+ * Every variant gives bit-identical results. */
 EOSLLM_CUDA_API int eosi_cuda_set_kernel_variant(int b_dtype, int variant);
 
 #ifdef __cplusplus
