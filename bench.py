@@ -58,6 +58,16 @@ def algo_bytes(n: int, k: int) -> int:
 
 
 STEP_BYTES = sum(algo_bytes(n, k) for n, k in SHAPES)
+DT_Q8_0 = 32
+
+
+def q80_bytes(n: int, k: int) -> int:
+    return n * (k // 32) * 34
+
+
+def algo_bytes_q80(n: int, k: int) -> int:
+    """Algorithmic bytes of one Q8_0 GEMV: weights + f32 activations + f32 outputs."""
+    return q80_bytes(n, k) + 4 * k + 4 * n
 
 
 def parse():
@@ -70,6 +80,7 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample length")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-q8", action="store_true", help="skip the Q8_0 half of the sweep")
     p.add_argument("--workload", choices=["all", "sweep", "decode", "prefill"], default="all",
                    help="sweep: the GEMV sweep line only; decode: the 7B decode line; prefill: the GEMM line")
     p.add_argument("--no-prefill", action="store_true", help="skip the tensor-core prefill measurement")
@@ -207,7 +218,7 @@ class CpuSweep:
     reference build is absent) over the sweep, rows split across threads;
     ctypes releases the GIL so the threads run in parallel."""
 
-    def __init__(self, threads: int | None = None, row_fraction: float = 1.0):
+    def __init__(self, threads: int | None = None, row_fraction: float = 1.0, dtype: int = DT_Q4_K):
         from oracle.oracle import REF_KERNELS, Oracle, RefKernels
         if RefKernels.available():
             self.kind = "reference"
@@ -218,21 +229,24 @@ class CpuSweep:
             lib = Oracle().lib
             self.fn = lib.orc_matmul_q
         self.oracle = Oracle()
+        self.dtype = dtype
         self.threads = threads or os.cpu_count() or 1
         self.pool = cf.ThreadPoolExecutor(self.threads)
         self.data = []
+        quant = self.oracle.q4_k_quantize if dtype == DT_Q4_K else self.oracle.q8_0_quantize
         for s, (n, k) in enumerate(SHAPES):
             rows = max(self.threads, int(n * row_fraction))
-            w = self.oracle.q4_k_quantize(self.oracle.gauss(rows * k, s, 0.02))
+            w = quant(self.oracle.gauss(rows * k, s, 0.02))
             x = self.oracle.gauss(k, 10 + s, 1.0)
             c = np.empty(rows, np.float32)
             self.data.append((rows, k, w, x, c))
-        self.step_bytes = sum(algo_bytes(rows, k) for rows, k, *_ in self.data)
+        ab = algo_bytes if dtype == DT_Q4_K else algo_bytes_q80
+        self.step_bytes = sum(ab(rows, k) for rows, k, *_ in self.data)
         self.row_fraction = row_fraction
 
     def _part(self, rows, k, w, x, c, lo, hi):
-        rb = (k // 256) * 144
-        rc = self.fn(x.ctypes.data, w.ctypes.data + lo * rb, DT_Q4_K, c.ctypes.data + 4 * lo, 1, hi - lo, k)
+        rb = (k // 256) * 144 if self.dtype == DT_Q4_K else (k // 32) * 34
+        rc = self.fn(x.ctypes.data, w.ctypes.data + lo * rb, self.dtype, c.ctypes.data + 4 * lo, 1, hi - lo, k)
         if rc != 0:
             raise RuntimeError(f"reference matmul_q failed: {rc}")
 
@@ -251,17 +265,22 @@ class CpuSweep:
         return f"{sample}, batch 1, {self.threads} threads over output rows"
 
 
-def cpu_baseline(seconds: float) -> dict:
-    cpu = CpuSweep()
+def cpu_baseline(seconds: float, threads: int | None = None, dtype: int = DT_Q4_K,
+                 row_fraction: float = 1.0) -> dict:
+    """The reference's matmul_q slot on the host cores for `seconds`: Q4_K
+    goes to its int8 AVX2 kernel, Q8_0 to its scalar kernel (the x86
+    backend's dispatch, src/kernels/avx2/matmul_q4_k.c:155-171)."""
+    cpu = CpuSweep(threads=threads, dtype=dtype, row_fraction=row_fraction)
     cpu.step()
     steps, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds:
         cpu.step()
         steps += 1
     dt = time.perf_counter() - t0
+    path = "Q4_K -> int8 AVX2 path" if dtype == DT_Q4_K else "Q8_0 -> scalar path"
     return {"value": round(cpu.step_bytes * steps / dt / 1e9, 3), "unit": "GB/s", "cores": cpu.threads,
             "kind": cpu.kind, "sample": f"{steps} sweeps ({cpu.describe()}) in {dt:.1f} s, "
-                                        f"eosi_avx2_matmul_q (Q4_K -> int8 AVX2 path)"}
+                                        f"eosi_avx2_matmul_q ({path})"}
 
 
 def run_reference(args):
@@ -472,9 +491,17 @@ def run_ours(args):
                "h2d_bytes_per_step": sum(4 * k for _, k in SHAPES),
                "d2h_bytes_per_step": sum(4 * n for n, _ in SHAPES)}
 
-    cpu = None
+    q80 = None
+    if not args.no_q8:
+        q80 = run_q80_sweep(args, dev, world, rank, R)
+
+    cpu = cpu_1core = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.cpu_seconds)
+        # one core, on an eighth of each matrix's rows (rows are independent)
+        cpu_1core = cpu_baseline(args.cpu_seconds / 2, threads=1, row_fraction=0.125)
+        if q80 is not None:  # the reference's scalar Q8_0 kernel on every host core, a quarter of the rows
+            q80["cpu_baseline"] = cpu_baseline(args.cpu_seconds / 2, dtype=DT_Q8_0, row_fraction=0.25)
 
     prefill = None
     if args.workload == "all" and not args.no_prefill:
@@ -511,6 +538,8 @@ def run_ours(args):
                                             for (n, k), ms in zip(SHAPES, per_shape_ms)}},
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "cpu_baseline_1core": cpu_1core,
+            "q8_0_sweep": q80,
             "gpu_launches": args.steps * (len(ks) + len(SHAPES)),
             "clocks": clocks.summary(),
             "decode_7b": decode,
@@ -523,6 +552,102 @@ def run_ours(args):
 LLAMA_7B = dict(n_embd=4096, n_layer=32, n_head=32, n_kv_head=32, n_ff=11008, n_vocab=32000)
 PREFILL_M = (128, 512, 2048)
 PREFILL_NK = (11008, 4096)
+
+
+def run_q80_sweep(args, dev, world, rank, R: int) -> dict:
+    """The Q8_0 half of the reference's matvec sweep on the same four shapes:
+    weights ~N(0, 0.02) quantized on the device by the reference's Q8_0
+    quantizer (q8_0.c:58-93, bit for bit), activations ~N(0, 1); one step =
+    one eosi_cuda_matmul_q8_0_dev GEMV per shape, K steps replayed from one
+    CUDA graph, R rotating weight copies (> L2), CUDA events on the replay
+    stream, max over ranks.  The per-shape trains give the kernel's mean
+    launch time for the roofline."""
+    import torch
+
+    from eosllm_b200 import backend as B
+    tmp = torch.empty(max(n * k for n, k in SHAPES), dtype=torch.float32, device=dev)
+    weights, acts, outs = [], [], []
+    for s, (n, k) in enumerate(SHAPES):
+        copies = []
+        for r in range(R):
+            w = torch.empty(q80_bytes(n, k), dtype=torch.uint8, device=dev)
+            B.fill_gauss_dev(tmp, n * k, 5000 + 1000 * rank + 100 * r + s, 0, 0.02)
+            B.q8_0_quantize_dev(tmp, w, n * k)
+            copies.append(w)
+        weights.append(copies)
+        x = torch.empty(k, dtype=torch.float32, device=dev)
+        B.fill_gauss_dev(x, k, 10 + s, 0, 1.0)
+        acts.append(x)
+        outs.append(torch.empty(n, dtype=torch.float32, device=dev))
+    torch.cuda.synchronize()
+    del tmp
+
+    def graph(launch, count):
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(device=dev)
+        with torch.cuda.graph(g, stream=side, capture_error_mode="relaxed"):
+            st = torch.cuda.current_stream().cuda_stream
+            for i in range(count):
+                launch(i, st)
+        return g
+
+    def gemv(s, i, st):
+        n, k = SHAPES[s]
+        B.matmul_q8_0_dev(acts[s], weights[s][i % R], outs[s], 1, n, k, st)
+
+    def step(i, st):
+        for s in range(len(SHAPES)):
+            gemv(s, i, st)
+
+    train_n = max(args.steps, 100)
+    g_warm, g_timed = graph(step, max(args.warmup, 3)), graph(step, args.steps)
+    trains = [graph(lambda i, st, s=s: gemv(s, i, st), train_n) for s in range(len(SHAPES))]
+    g_warm.replay()
+    g_timed.replay()  # the graph's upload, untimed
+    for g in trains:
+        g.replay()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.start()
+    t0.record()
+    g_timed.replay()
+    t1.record()
+    torch.cuda.synchronize()
+    clocks.stop()
+    barrier(world)
+    per_shape_ms = []
+    for g in trains:
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        g.replay()
+        a1.record()
+        torch.cuda.synchronize()
+        per_shape_ms.append(a0.elapsed_time(a1) / train_n)
+    if B.take_device_errors() != 0:
+        raise SystemExit("q8_0 sweep: device-side error bits set")
+    t_max = max_over_ranks(t0.elapsed_time(t1), world, dev)
+    step_bytes = sum(algo_bytes_q80(n, k) for n, k in SHAPES)
+    peak, peak_kind = measured_hbm_peak()
+    achieved = step_bytes / (sum(per_shape_ms) * 1e-3) / 1e9
+    return {
+        "metric": "Q8_0 GEMV HBM GB/s (same batch-1 sweep)", "unit": "GB/s",
+        "value": round(world * step_bytes * args.steps / (t_max * 1e-3) / 1e9, 2),
+        "ms_per_step": round(t_max / args.steps, 5), "steps": args.steps, "dtype": "f32 (int8 weights)",
+        "gpu_launches": args.steps * len(SHAPES),
+        "config": {"workload": "q80_gemv_sweep", "shapes": SHAPES, "batch": 1,
+                   "weights": "Q8_0 by the reference's quantizer (on the device), ~N(0,0.02)",
+                   "l2": f"{R} rotating weight copies ({R * sum(q80_bytes(n, k) for n, k in SHAPES) / 1e6:.1f} MB)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "kernel": "q80_gemv_kernel: mean launch time of a 100+-launch train per shape",
+                     "per_shape_us": {f"{n}x{k}": round(ms * 1e3, 3) for (n, k), ms in zip(SHAPES, per_shape_ms)},
+                     "per_shape_frac": {f"{n}x{k}": round(algo_bytes_q80(n, k) / (ms * 1e-3) / 1e9 / peak, 4)
+                                        for (n, k), ms in zip(SHAPES, per_shape_ms)}},
+        "clocks": clocks.summary(),
+    }
 
 
 def measured_bf16_peak():
