@@ -17,7 +17,10 @@ GEMV per shape, activation packing included.  Weights rotate over R copies
   roofline  per-launch CUDA-event times of the GEMV (+ its packing kernel)
           inside the timed graph vs the measured HBM copy bandwidth.
   cpu_baseline  the reference's own x86 kernel (compiled from its sources
-          into oracle/_ref) on the host cores, same workload.
+          into oracle/_ref) on the host cores, same workload;
+          cpu_baseline_1core the same on one core.
+  q8_0_sweep  the Q8_0 half of the sweep (same shapes, the reference's Q8_0
+          weight format), with its own roofline and CPU baseline.
 
 Multi-GPU (torchrun): weak scaling -- every rank streams its own row shard
 of N-times-taller matrices (rows are independent; no collective on the data
