@@ -595,6 +595,8 @@ int eosi_cuda_matmul_q8_0(const float* a, const void* b_q8, float* c, uint32_t m
 
 int eosi_cuda_cache_evict(const void* b_quant) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
+  int prev = 0;  // the caller's device is current again on return
+  const bool had = cudaGetDevice(&prev) == cudaSuccess;
   for (auto& s : g_shards) {
     cudaSetDevice(s.dev);
     for (auto it = s.cache.begin(); it != s.cache.end();) {
@@ -606,16 +608,20 @@ int eosi_cuda_cache_evict(const void* b_quant) {
       }
     }
   }
+  if (had) cudaSetDevice(prev);
   return EOS_OK;
 }
 
 int eosi_cuda_cache_clear(void) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
+  int prev = 0;  // the caller's device is current again on return
+  const bool had = cudaGetDevice(&prev) == cudaSuccess;
   for (auto& s : g_shards) {
     cudaSetDevice(s.dev);
     for (auto& kv : s.cache) cudaFree(kv.second.dev);
     s.cache.clear();
   }
+  if (had) cudaSetDevice(prev);
   return EOS_OK;
 }
 

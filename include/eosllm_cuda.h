@@ -138,8 +138,14 @@ EOSLLM_CUDA_API int eosi_cuda_q4_k_gemv_dev(const void *act, const void *w, floa
  *     overlaps on that GPU (other streams, other host threads) race and
  *     corrupt each other's results -- serialise them;
  *   - no cudaMalloc, cudaFree or other allocating call is made, and the
- *     kernels' one-second bounded waits have no error word to report to
- *     here (they still return; a timed-out call's outputs are invalid).
+ *     kernels this entry point launches contain no waits that could time
+ *     out, so there is no device-side error to report;
+ *   - under CUDA's default lazy module loading the driver itself loads each
+ *     kernel on its first launch, and loading takes device memory: a host
+ *     that must see no allocation on its serving path makes one warm-up
+ *     call per (m, n, k) shape class it will use at start-up (n < 4, k whose
+ *     packed row fits in shared memory, longer k) or runs with
+ *     CUDA_MODULE_LOADING=EAGER.
  * a, w, c are device pointers on the current device (a and w 16-byte
  * aligned); `stream` is a cudaStream_t as void*; asynchronous. */
 EOSLLM_CUDA_API int eosi_cuda_matmul_q4_k_noalloc(const float *a, const void *w, float *c, uint32_t m, uint32_t n,
@@ -186,10 +192,13 @@ EOSLLM_CUDA_API int eosi_cuda_q4_k_from_gauss_dev(void *dst, size_t n_elements, 
  * bit-exact with eosi_cuda_matmul_q4_k and with the reference's int8 kernel
  * (src/kernels/avx2/matmul_q4_k_int8.c:164-269), which the reference applies
  * to one prompt token at a time (src/core/session.c:231-236).  Activations
- * are packed per 32 exactly as quantize_sub32 does; every sub-block's integer
- * dot is one int8 tensor-core MMA, rescaled and summed in the reference's f32
- * order.  Weights are prepared once into eosi_cuda_q4_k_prefill_weight_bytes
- * bytes (the 4-bit values as int8 plus per-32 (d*sc, dmin*m) pairs); each call
+ * are packed per 32 exactly as quantize_sub32 does (the int8 values held as
+ * bf16, which is exact); every sub-block's integer dot is two bf16 x bf16
+ * tensor-core MMAs (tcgen05 kind::f16, K = 16 each) into an f32 TMEM
+ * accumulator -- exact, since every product and partial sum is an integer
+ * below 2^16 -- then rescaled and summed in the reference's f32 order.
+ * Weights are prepared once into eosi_cuda_q4_k_prefill_weight_bytes bytes
+ * (the 4-bit values as bf16 plus per-32 (d*sc, -(dmin*m)) pairs); each call
  * needs eosi_cuda_q4_k_prefill_scratch_bytes of scratch.  All pointers device,
  * 16-byte aligned; k % 256 == 0. */
 EOSLLM_CUDA_API size_t eosi_cuda_q4_k_prefill_weight_bytes(uint32_t n, uint32_t k);

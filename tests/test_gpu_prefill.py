@@ -41,6 +41,29 @@ def test_prefill_bit_exact_with_int8_reference(gpu, oracle, m, n, k):
     np.testing.assert_array_equal(got.view(np.uint32), ref.reshape(m, n).view(np.uint32))
 
 
+@pytest.mark.parametrize("m", [128, 512, 2048])
+def test_prefill_bit_exact_at_benchmark_shapes(gpu, oracle, m):
+    """The timed prefill configurations, with the benchmark's own inputs:
+    W 11008 x 4096 ~N(0, 0.02) from stream seed 2 (Q4_K on the device), A
+    M x 4096 ~N(0, 1) from stream 1000 + M."""
+    import torch
+    n, k = 11008, 4096
+    dev = torch.device("cuda", 0)
+    dw = torch.empty(n * (k // 256) * 144, dtype=torch.uint8, device=dev)
+    gpu.q4_k_from_gauss_dev(dw, n * k, 2, 0.02)
+    da = torch.empty(m * k, dtype=torch.float32, device=dev)
+    gpu.fill_gauss_dev(da, m * k, 1000 + m, 0, 1.0)
+    wprep = torch.empty(gpu.prefill_weight_bytes(n, k), dtype=torch.uint8, device=dev)
+    gpu.prefill_prepare_weights_dev(dw, n, k, wprep)
+    scratch = torch.empty(gpu.prefill_scratch_bytes(m, k), dtype=torch.uint8, device=dev)
+    dc = torch.full((m, n), float("nan"), dtype=torch.float32, device=dev)
+    gpu.prefill_dev(da, wprep, dc, m, n, k, scratch)
+    torch.cuda.synchronize()
+    assert gpu.take_device_errors() == 0
+    ref = oracle.matmul_q(da.cpu().numpy(), dw.cpu().numpy(), DT_Q4_K, m, n, k, threads=0)[1]
+    np.testing.assert_array_equal(dc.cpu().numpy().view(np.uint32), ref.reshape(m, n).view(np.uint32))
+
+
 def test_prefill_extreme_activation_scales(gpu, oracle):
     for s in (1e-30, 1e-3, 1e3, 1e30):
         got, ref, *_ = _run(gpu, oracle, 128, 256, 512, seed=3, a_scale=s)

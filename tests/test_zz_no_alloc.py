@@ -34,10 +34,26 @@ def _call_reference_entry(lib, a, w, c, m, n, k, scratch):
                                          C.c_void_p(st))
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (1, 4096, 11008), (3, 1000, 4096), (1, 2, 512)])
+# (1, 64, 131072): rows too long to stage in shared memory, the unstaged kernel
+@pytest.mark.parametrize("m,n,k", [(1, 4096, 4096), (1, 4096, 11008), (3, 1000, 4096), (1, 2, 512),
+                                   (1, 64, 131072)])
 def test_noalloc_matches_allocating_entry_point(gpu, m, n, k):
+    _compare_on_device(gpu, 0, m, n, k)
+
+
+def test_noalloc_on_a_second_device(gpu):
+    """The array's address is looked up per device: a call on device 1 must
+    use device 1's copy."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    with torch.cuda.device(1):
+        _compare_on_device(gpu, 1, 1, 4096, 4096)
+    _compare_on_device(gpu, 0, 1, 4096, 4096)  # and device 0 still uses its own
+
+
+def _compare_on_device(gpu, index, m, n, k):
     lib = gpu.load()
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", index)
     w = torch.empty(n * (k // 256) * 144, dtype=torch.uint8, device=dev)
     gpu.q4_k_from_gauss_dev(w, n * k, 11, 0.02)
     scratch = torch.empty(gpu.q4_k_scratch_bytes(m, k), dtype=torch.uint8, device=dev)
@@ -71,18 +87,25 @@ def test_noalloc_rejects_sizes_beyond_its_array(gpu):
 
 
 def test_noalloc_leaves_free_device_memory_unchanged(gpu):
+    """After one warm-up call per shape class (the driver loads each kernel
+    on its first launch under lazy module loading), calls of every class
+    leave free device memory unchanged."""
     lib = gpu.load()
     dev = torch.device("cuda", 0)
-    n, k = 2048, 4096
-    w = torch.empty(n * (k // 256) * 144, dtype=torch.uint8, device=dev)
-    gpu.q4_k_from_gauss_dev(w, n * k, 5, 0.02)
-    a = torch.ones(k, dtype=torch.float32, device=dev)
-    c = torch.empty(n, dtype=torch.float32, device=dev)
-    assert _call_noalloc(lib, a, w, c, 1, n, k) == gpu.EOS_OK  # first call does the per-device set-up
+    shapes = [(1, 2048, 4096), (2, 1024, 11008), (1, 2, 4096)]  # short rows, long rows, n < 4
+    bufs = []
+    for m, n, k in shapes:
+        w = torch.empty(n * (k // 256) * 144, dtype=torch.uint8, device=dev)
+        gpu.q4_k_from_gauss_dev(w, n * k, 5, 0.02)
+        a = torch.ones(m * k, dtype=torch.float32, device=dev)
+        c = torch.empty(m * n, dtype=torch.float32, device=dev)
+        bufs.append((a, w, c, m, n, k))
+        assert _call_noalloc(lib, a, w, c, m, n, k) == gpu.EOS_OK  # warm-up (the first also sets the device up)
     torch.cuda.synchronize()
     free_before, _ = torch.cuda.mem_get_info(dev)
-    for _ in range(20):
-        assert _call_noalloc(lib, a, w, c, 1, n, k) == gpu.EOS_OK
+    for _ in range(10):
+        for a, w, c, m, n, k in bufs:
+            assert _call_noalloc(lib, a, w, c, m, n, k) == gpu.EOS_OK
     torch.cuda.synchronize()
     free_after, _ = torch.cuda.mem_get_info(dev)
     assert free_after == free_before
