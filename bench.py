@@ -725,6 +725,36 @@ def run_prefill(args, dev, reps: int = 20) -> dict:
     return out
 
 
+GREEDY_FIXTURE = os.path.join(os.path.dirname(os.path.abspath(__file__)), "tests", "golden", "greedy_7b.npz")
+
+
+def token_hash(tokens) -> str:
+    """sha256 of the generated token ids as little-endian uint32, first 16 hex digits."""
+    import hashlib
+    return hashlib.sha256(np.asarray(tokens, dtype="<u4").tobytes()).hexdigest()[:16]
+
+
+def fixture_agreement(tokens, prompt_len: int):
+    """Free-running picks against the reference engine's own greedy picks on
+    the same model and prompt (tests/golden/greedy_7b.npz, written by
+    tests/golden/make_greedy_7b.py from the reference compiled from its
+    sources): picks equal position by position, and the length of the
+    common prefix (after the first difference the two runs feed different
+    tokens, so later positions are not comparable)."""
+    if not os.path.exists(GREEDY_FIXTURE):
+        return None
+    g = np.load(GREEDY_FIXTURE)
+    ref = g["tokens"].astype(np.int64)
+    if int(g["prompt"].size) != prompt_len:
+        return None
+    got = np.asarray(tokens, dtype=np.int64)
+    n = min(ref.size, got.size)
+    eq = got[:n] == ref[:n]
+    prefix = int(n if eq.all() else np.argmin(eq))
+    return {"compared": int(n), "equal": int(eq.sum()), "common_prefix": prefix,
+            "reference_sha256": token_hash(ref[:n])}
+
+
 def run_decode(args, dev, world, rank) -> dict:
     """7B-shape Q4_K greedy decoding through the device-resident decoder:
     random-init Llama-architecture model generated on the device (weights
@@ -803,6 +833,10 @@ def run_decode(args, dev, world, rank) -> dict:
                      "tok_s_weight_only_at_peak": round(world * peak * 1e9 / wbytes, 1)},
         "launches_per_token": 8 * cfg["n_layer"] + 3,
         "first_tokens": [int(x) for x in toks[:8]],
+        # all P.. greedy picks (the one after the prompt, then G more), the
+        # same on every GPU count when tensor parallelism is exact
+        "tokens_sha256": token_hash(np.concatenate([first, toks])),
+        "reference_agreement": fixture_agreement(np.concatenate([first, toks]), P),
         "clocks": clocks.summary(),
     }
     if host_model is not None:

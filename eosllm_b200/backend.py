@@ -64,6 +64,7 @@ _SIGNATURES = {
     "eosi_cuda_cache_evict": (C.c_int, [_vp]),
     "eosi_cuda_cache_clear": (C.c_int, []),
     "eosi_cuda_cache_preload": (C.c_int, [_vp, C.c_int, _u32, _u32]),
+    "eosi_cuda_host_stats": (C.c_int, [_vp, _vp, _vp]),
     "eosi_cuda_q4_k_scratch_bytes": (_sz, [_u32, _u32]),
     "eosi_cuda_matmul_q4_k_dev": (C.c_int, [_vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp]),
     "eosi_cuda_q4_k_pack_act_dev": (C.c_int, [_vp, _u32, _u32, _vp, _vp]),
@@ -96,6 +97,8 @@ _SIGNATURES = {
     "eosi_cuda_text_stream": (_vp, [_vp]),
     "eosi_cuda_text_ipc_handle": (C.c_int, [_vp, _vp, _sz]),
     "eosi_cuda_text_attach_peers": (C.c_int, [_vp, _vp, _sz]),
+    "eosi_cuda_text_attach_local": (C.c_int, [_vp, C.c_int]),
+    "eosi_cuda_text_set_wait_limit": (C.c_int, [_vp, _u32]),
     "eosi_cuda_text_partition": (C.c_int, [_vp, C.c_int, C.c_int, _vp]),
     "eosi_cuda_text_close": (None, [_vp]),
 }

@@ -63,9 +63,8 @@ constexpr uint32_t kPrefillRows = 1024;  // tokens per batched-prefill block
 // Residual + rmsnorm + activation packing
 // ---------------------------------------------------------------------------
 struct NormPackParams {
-  const float* x_in;              // residual stream; nullptr: embedding lookup
-  const float* parts[kMaxParts];  // partial sums added to x_in, in rank order
-  uint32_t nparts;
+  const float* x_in;         // residual stream; nullptr: embedding lookup
+  const float* part;         // t added to x_in (nullptr: none)
   const uint16_t* tok_embd;  // F16 [n_vocab][n]      (embedding mode)
   const uint32_t* prompt;    // token of step pos when pos < n_prompt
   const DecState* state;
@@ -75,51 +74,10 @@ struct NormPackParams {
   uint32_t n;
   uint8_t* act;     // Q4_K consumers: packed records for k = n
   float* act_f32;   // Q8_0 consumers: the normalised vector
-  // tensor parallel: before reading parts[] (this rank's receive slots, one
-  // per source rank, filled by the sources' GEMVs), announce this rank's
-  // partial in every rank's flag slot and wait for every source's flag
-  uint32_t world;
-  uint32_t* pub_flag[kMaxParts];  // flag slot of this rank at rank q (IPC-mapped; own local)
-  const uint32_t* wait_flag;      // this rank's slots [q], q < world
-  uint32_t xchg;                  // exchange index within the step
-  uint32_t xchg_per_step;
+  // tensor parallel: `part` holds every rank's output rows, pushed by their
+  // GEMVs; handshake before reading it
+  XchgSync xs;
 };
-
-
-// Tensor-parallel handshake of exchange `epoch`: thread 0 of the publishing
-// CTA raises this rank's flag in every rank's receive words with release
-// stores after a system-scope fence.  What it announces -- partial sums the
-// previous GEMV pushed into the peers' receive slots (that grid completed
-// before this kernel's griddepcontrol.wait returned), or values this CTA
-// wrote -- is then visible to a peer that acquires the flag;
-// threads t < world wait for source t's flag in this rank's own words
-// (local polling; bounded: EOS_DEVERR_PEER after EOS_WAIT_LIMIT_NS).
-// Returns false when a wait ran out.
-__device__ __forceinline__ bool xchg_sync(uint32_t world, uint32_t* const* pub_flag, const uint32_t* wait_flag,
-                                          uint32_t epoch, uint32_t* err, bool publish) {
-  __shared__ uint32_t s_ok;
-  if (threadIdx.x == 0) s_ok = 1u;
-  if (publish && threadIdx.x == 0) {
-    __threadfence_system();
-    for (uint32_t q = 0; q < world; ++q) st_release_sys(pub_flag[q], epoch);
-  }
-  __syncthreads();
-  if (threadIdx.x < world) {
-    const uint32_t* f = wait_flag + threadIdx.x;
-    if (ld_acquire_sys(f) < epoch) {
-      const uint64_t t0 = global_timer_ns();
-      while (ld_acquire_sys(f) < epoch) {
-        if (global_timer_ns() - t0 > EOS_WAIT_LIMIT_NS) {
-          report(err, EOS_DEVERR_PEER);
-          s_ok = 0u;
-          break;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  return s_ok != 0u;
-}
 
 constexpr uint32_t kNormMaxChunks = 16;  // float4 chunks per thread: n <= 16384
 
@@ -133,19 +91,15 @@ __device__ __forceinline__ float4 add4(float4 a, float4 b) {
 // the mean square of the whole vector (the same fixed order in every CTA, so
 // all agree bit for bit) and then normalises and packs its own 256 elements
 // (CTA b: chunks [64 b, 64 b + 64), held by threads 64 (b % 4) + q at
-// iteration b / 4).  Residual element i is x_in[i] + (((p_0 + p_1) + ...)):
-// the reference adds one full-length result (x[i] += t[i], text.c:406),
-// which is the nparts == 1 case.
+// iteration b / 4).  Residual element i is x_in[i] + t[i], the reference's
+// x[i] += t[i] (text.c:406).
 __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) {
   __shared__ float red[8];
   __shared__ __align__(16) float ys[256];
   pdl_trigger();
   pdl_wait();
-  if (p.world > 1 && p.nparts > 0) {
-    const uint32_t epoch = p.state->epoch * p.xchg_per_step + p.xchg + 1u;
-    if (!xchg_sync(p.world, p.pub_flag, p.wait_flag, epoch, const_cast<uint32_t*>(&p.state->err), blockIdx.x == 0))
-      return;  // a peer never arrived: the error bit is set, outputs are invalid
-  }
+  if (p.xs.world > 1 && p.part != nullptr && !xchg_handshake(p.xs, blockIdx.x == 0, true))
+    return;  // a peer never arrived: the error bit is set, outputs are invalid
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   const uint32_t nch = p.n >> 2, b = blockIdx.x;
   const uint32_t jown = b >> 2;
@@ -170,23 +124,12 @@ __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) 
       const uint32_t c = tid + 256u * j;
       if (c < nch) v[j] = ld4(p.x_in, c);
     }
-    if (p.nparts > 0) {
-      float4 t[kNormMaxChunks];
+    if (p.part != nullptr) {
 #pragma unroll
       for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
         const uint32_t c = tid + 256u * j;
-        if (c < nch) t[j] = __ldcg(reinterpret_cast<const float4*>(p.parts[0]) + c);
+        if (c < nch) v[j] = add4(v[j], __ldcg(reinterpret_cast<const float4*>(p.part) + c));
       }
-      for (uint32_t q = 1; q < p.nparts; ++q) {
-#pragma unroll
-        for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
-          const uint32_t c = tid + 256u * j;
-          if (c < nch) t[j] = add4(t[j], __ldcg(reinterpret_cast<const float4*>(p.parts[q]) + c));
-        }
-      }
-#pragma unroll
-      for (uint32_t j = 0; j < kNormMaxChunks; ++j)
-        if (tid + 256u * j < nch) v[j] = add4(v[j], t[j]);
     }
   }
   const float4 w4 = owner ? ld4(p.w, (b << 6) + (tid & 63u)) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -241,11 +184,34 @@ struct AttnParams {
   float* part;       // [hl][max_chunks][hd + 4]: {max, sum, -, -, o[hd]}
   uint32_t* count;   // [hl] chunk arrivals, reset by the merging CTA
   const DecState* state;
-  uint8_t* act;      // Q4_K: packed records of the O-projection input (k = hl*hd)
-  float* act_f32;    // Q8_0: the attention output itself
+  // the O projection's input, all n_head heads (head h at h * hd): Q4_K packed
+  // records, or (Q8_0) the attention output itself; tensor parallel, the
+  // same positions in the other ranks' copies too (act_x / actf_x, n_x)
+  uint8_t* act;
+  float* act_f32;
+  uint8_t* act_x[kMaxParts - 1];
+  float* actf_x[kMaxParts - 1];
+  uint32_t n_x;
   uint32_t hl, h0, kvl, kv0, n_head, n_kv_head, max_chunks;
   float base, scale;
 };
+
+// pack_group_to_record into this rank's records and n_x further copies: the
+// same quantize_sub32 values everywhere.
+__device__ __forceinline__ void pack_group_to_records(float v, uint32_t g, uint32_t lane, uint8_t* rec,
+                                                      uint8_t* const* rec_x, uint32_t n_x) {
+  float scale;
+  int32_t sum;
+  const int8_t q = quant_group32(v, scale, sum);
+  const uint32_t oq = rec_aq_offset(g) + lane, os = rec_st_offset(g);
+  const float2 st = make_float2(scale, (float)sum);
+  rec[oq] = static_cast<uint8_t>(q);
+  if (lane == 0) *reinterpret_cast<float2*>(rec + os) = st;
+  for (uint32_t j = 0; j < n_x; ++j) {
+    rec_x[j][oq] = static_cast<uint8_t>(q);
+    if (lane == 0) *reinterpret_cast<float2*>(rec_x[j] + os) = st;
+  }
+}
 
 // Dynamic shared memory of attn_kernel<E>: the K and V rows of one chunk.
 __host__ __device__ constexpr uint32_t attn_smem_bytes(uint32_t hd) { return 2u * kAttnChunk * hd * 4u; }
@@ -433,28 +399,47 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
   if (tid == 0) p.count[hloc] = 0u;
   __syncthreads();
   if (p.act != nullptr) {
-    for (uint32_t g = warp; g < E; g += 4u) pack_group_to_record(s_out[g * 32u + lane], hloc * E + g, lane, p.act);
+    for (uint32_t g = warp; g < E; g += 4u)
+      pack_group_to_records(s_out[g * 32u + lane], gh * E + g, lane, p.act, p.act_x, p.n_x);
   } else {
-    for (uint32_t d = tid; d < HD; d += 128u) p.act_f32[hloc * HD + d] = s_out[d];
+    for (uint32_t d = tid; d < HD; d += 128u) {
+      p.act_f32[gh * HD + d] = s_out[d];
+      for (uint32_t j = 0; j < p.n_x; ++j) p.actf_x[j][gh * HD + d] = s_out[d];
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
 // silu(gate) * up, packed for the down projection
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) silu_pack_kernel(const float* __restrict__ gu, uint32_t ffl,
-                                                        uint8_t* __restrict__ act, float* __restrict__ act_f32) {
+struct SiluParams {
+  const float* gu;  // [gate | up] of this rank's FFN slice, ffl each
+  uint32_t ffl, ff0;
+  // the down projection's input, all n_ff units (unit ff0 + i of this rank's
+  // i): Q4_K packed records, or (Q8_0) the values; tensor parallel, the other
+  // ranks' copies too
+  uint8_t* act;
+  float* act_f32;
+  uint8_t* act_x[kMaxParts - 1];
+  float* actf_x[kMaxParts - 1];
+  uint32_t n_x;
+};
+
+__global__ void __launch_bounds__(256) silu_pack_kernel(const SiluParams p) {
   pdl_trigger();
   pdl_wait();
   const uint32_t i = blockIdx.x * 256u + threadIdx.x;
-  if (i >= ffl) return;  // warp-uniform: ffl % 32 == 0
-  const float g = gu[i], u = gu[ffl + i];
+  if (i >= p.ffl) return;  // warp-uniform: ffl % 32 == 0
+  const float g = p.gu[i], u = p.gu[p.ffl + i];
   // x * (1 / (1 + expf(-x))) (silu.c:17), then gate * up (text.c:417)
   const float h = __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), u);
-  if (act != nullptr)
-    pack_group_to_record(h, i >> 5, threadIdx.x & 31u, act);
-  else
-    act_f32[i] = h;
+  const uint32_t gi = p.ff0 + i;
+  if (p.act != nullptr) {
+    pack_group_to_records(h, gi >> 5, threadIdx.x & 31u, p.act, p.act_x, p.n_x);
+  } else {
+    p.act_f32[gi] = h;
+    for (uint32_t j = 0; j < p.n_x; ++j) p.actf_x[j][gi] = h;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -473,7 +458,7 @@ struct ArgmaxParams {
   uint32_t world, rank, v0;  // v0: global index of logits[0]
   XRecv* recv[kMaxParts];    // rank q's receive words (IPC-mapped; own local)
   XRecv* own;
-  uint32_t xchg, xchg_per_step;
+  XchgSync xs;               // the pick's handshake (flags kXArgmax)
 };
 
 __device__ __forceinline__ bool arg_better(float av, uint32_t ai, float bv, uint32_t bi) {
@@ -549,9 +534,6 @@ __global__ void __launch_bounds__(256) argmax_kernel(const ArgmaxParams p) {
   uint32_t first_nan = (p.rank == 0 && first != first) ? 1u : 0u;
   uint32_t gidx = idx == 0xffffffffu ? idx : p.v0 + idx;
   if (p.world > 1) {
-    uint32_t* pub[kMaxParts];
-#pragma unroll
-    for (uint32_t q = 0; q < kMaxParts; ++q) pub[q] = q < p.world ? &p.recv[q]->flag[2][p.rank] : nullptr;
     if (threadIdx.x == 0) {  // push this slice's result into every rank's words
       for (uint32_t q = 0; q < p.world; ++q) {
         p.recv[q]->arg_v[p.rank] = v;
@@ -559,14 +541,15 @@ __global__ void __launch_bounds__(256) argmax_kernel(const ArgmaxParams p) {
         if (p.rank == 0) p.recv[q]->first_nan = first_nan;
       }
     }
-    const uint32_t epoch = p.state->epoch * p.xchg_per_step + p.xchg + 1u;
-    if (!xchg_sync(p.world, pub, &p.own->flag[2][0], epoch, &p.state->err, true)) return;
+    // this CTA published the pushes itself (stores, then the handshake's
+    // fence and release), so it waits for its own flag too
+    if (!xchg_handshake(p.xs, true, false)) return;
     if (threadIdx.x == 0) {
       v = __int_as_float(0x7fc00000);
       gidx = 0xffffffffu;
       const volatile XRecv* x = p.own;
       for (uint32_t q = 0; q < p.world; ++q) {  // rank order = vocabulary order
-        (void)ld_acquire_sys(&p.own->flag[2][q]);
+        (void)ld_acquire_sys(&p.own->flag[kXArgmax][q]);
         const float qv = x->arg_v[q];
         const uint32_t qi = x->arg_i[q];
         if (arg_better(qv, qi, v, gidx)) {
@@ -633,7 +616,8 @@ uint32_t blk_elems(int dt) { return dt == EOS_DT_Q4_K ? Q4K_ELEMS : Q80_ELEMS; }
 struct TextDecoder {
   eosi_cuda_llama_t m{};
   int device = 0, rank = 0, world = 1;
-  uint32_t hd = 0, hl = 0, h0 = 0, kvl = 0, kv0 = 0, ffl = 0, ff0 = 0, vl = 0, v0 = 0, max_chunks = 0;
+  uint32_t hd = 0, hl = 0, h0 = 0, kvl = 0, kv0 = 0, ffl = 0, ff0 = 0, vl = 0, v0 = 0, el = 0, e0 = 0;
+  uint32_t max_chunks = 0;
   int num_sms = 0, max_smem = 0;
   cudaStream_t st = nullptr;
   std::vector<void*> allocs;
@@ -641,11 +625,10 @@ struct TextDecoder {
   uint16_t* tok_embd = nullptr;
   float* out_norm = nullptr;
   uint8_t* wout = nullptr;
-  // activations
-  float *x0 = nullptr, *x1 = nullptr, *qkv = nullptr, *part_o = nullptr, *part_d = nullptr, *gu = nullptr;
-  float* logits = nullptr;
-  uint8_t *act_e = nullptr, *act_o = nullptr, *act_d = nullptr;  // Q4_K records
-  float *actf_e = nullptr, *actf_o = nullptr, *actf_d = nullptr;  // Q8_0 inputs
+  // activations (local)
+  float *x0 = nullptr, *x1 = nullptr, *qkv = nullptr, *gu = nullptr;
+  uint8_t* act_e = nullptr;  // normalised residual, Q4_K records
+  float* actf_e = nullptr;   // normalised residual for Q8_0 consumers
   float *kc = nullptr, *vc = nullptr;
   float* attn_part = nullptr;
   uint32_t* attn_count = nullptr;
@@ -656,19 +639,32 @@ struct TextDecoder {
   uint32_t* out_tokens = nullptr;
   uint32_t* gemv_err = nullptr;
   uint32_t arg_blocks = 0;
-  // exchange buffer: receive slots [source rank][n_embd] for the O and down
-  // partials, this rank's logits slice and its receive words; the other
-  // ranks write (push) into it through CUDA IPC mappings
+  // Exchange buffer, one per rank; the other ranks write (push) into it
+  // through CUDA IPC mappings.  It holds what every rank reads whole:
+  //   o_full, d_full    O / down projection outputs, all n_embd rows
+  //   logits            this rank's vocabulary slice (read back by the host)
+  //   XRecv             flags and the greedy-pick words
+  //   act_o / actf_o    O projection input, all heads (Q4_K records / Q8_0 f32)
+  //   act_d / actf_d    down projection input, all n_ff units
+  // and, tensor parallel with Q4_K, the batched prefill's counterparts for
+  // xpf_rows rows: output rows [xpf_rows][n_embd] of O and down, and the
+  // GEMM operands of the O and down inputs.
   uint8_t* xbuf = nullptr;
-  size_t xoff_po = 0, xoff_pd = 0, xoff_lg = 0, xoff_fl = 0, xbytes = 0;
-  // batched prefill (world > 1): receive slots [source rank][xpf_rows][n_embd]
-  // for the O and down partial rows, and the prefill's exchange counter
-  size_t xoff_pfo = 0, xoff_pfd = 0;
+  size_t xoff_o = 0, xoff_d = 0, xoff_lg = 0, xoff_fl = 0, xoff_ao = 0, xoff_ad = 0, xbytes = 0;
+  size_t xoff_pfo = 0, xoff_pfd = 0, xoff_pfa = 0, xoff_pfs = 0;
   uint32_t xpf_rows = 0, pf_epoch = 0;
+  float *o_full = nullptr, *d_full = nullptr, *logits = nullptr;
+  uint8_t *act_o = nullptr, *act_d = nullptr;
+  float *actf_o = nullptr, *actf_d = nullptr;
   uint8_t* xpeer[kMaxParts] = {};  // every rank's exchange buffer (own included)
   bool peer_opened[kMaxParts] = {};
-  float* push_o[kMaxParts] = {};   // where this rank's O partial goes on the other ranks
-  float* push_d[kMaxParts] = {};
+  // where this rank's pushes land in the other ranks' exchange buffers
+  float* push_o[kMaxParts] = {};  // O output rows [e0, e0 + el)
+  float* push_d[kMaxParts] = {};  // down output rows
+  uint8_t* push_ao[kMaxParts] = {};  // O input records (the attention kernel writes this rank's heads)
+  uint8_t* push_ad[kMaxParts] = {};  // down input records (this rank's FFN units)
+  float* push_afo[kMaxParts] = {};
+  float* push_afd[kMaxParts] = {};
   uint32_t n_push = 0;
   cudaGraphExec_t graph = nullptr;
   uint32_t host_pos = 0;
@@ -714,15 +710,11 @@ struct TextDecoder {
     const size_t rb = wbytes(dt, 1, k);
     return cudaMemcpyAsync(dst, static_cast<const uint8_t*>(src) + r0 * rb, rows * rb, kind(), st);
   }
-  // all n rows, columns [c0, c0 + cols) (block-aligned) into a dense [n][cols] matrix
-  cudaError_t copy_cols(uint8_t* dst, const void* src, int dt, uint64_t n, uint64_t k, uint64_t c0, uint64_t cols) {
-    const size_t rb = wbytes(dt, 1, k), sb = wbytes(dt, 1, cols), off = wbytes(dt, 1, c0);
-    return cudaMemcpy2DAsync(dst, sb, static_cast<const uint8_t*>(src) + off, rb, sb, n, kind(), st);
-  }
 
   int open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws);
   int attach(const uint8_t* handles);
-  // the batched path serves one GPU with Q4_K linears
+  int attach_buffers(uint8_t* const* bufs);  // every rank's exchange buffer, already mapped
+  // the batched path serves Q4_K linears, on one GPU or tensor parallel
   bool prefill_ok() const { return m.wdtype == EOS_DT_Q4_K && m.n_layer > 0 && (world == 1 || xpf_rows > 0); }
   cudaError_t prefill(uint32_t n);  // tokens at prompt[host_pos, host_pos + n)
   XRecv* xrecv(int q) const { return reinterpret_cast<XRecv*>(xpeer[q] + xoff_fl); }
@@ -731,11 +723,13 @@ struct TextDecoder {
 };
 
 // The slice of the model rank rk of ws owns: heads [h0, h0 + hl) (and their
-// KV heads) for q/k/v and the O projection's columns, FFN units [ff0, ff0 +
-// ffl) for gate/up rows and the down projection's columns, vocabulary rows
-// [v0, v0 + vl) of the LM head.  Host only; returns an eos_status_t.
+// KV heads) for q/k/v rows and attention, FFN units [ff0, ff0 + ffl) for
+// gate/up rows, output rows [e0, e0 + el) of the O and down projections,
+// vocabulary rows [v0, v0 + vl) of the LM head.  Every matrix is split by
+// output rows, so each output element is computed whole on one rank.  Host
+// only; returns an eos_status_t.
 struct Geometry {
-  uint32_t hd, hl, h0, kvl, kv0, ffl, ff0, vl, v0;
+  uint32_t hd, hl, h0, kvl, kv0, ffl, ff0, vl, v0, el, e0;
 };
 int model_geometry(const eosi_cuda_llama_t& m, int rk, int ws, Geometry& g) {
   const int wdt = m.wdtype, odt = m.out_dtype;
@@ -769,14 +763,12 @@ int model_geometry(const eosi_cuda_llama_t& m, int rk, int ws, Geometry& g) {
   g.h0 = g.hl * rk;
   g.kvl = m.n_kv_head / ws;
   g.kv0 = g.kvl * rk;
-  if (wdt == EOS_DT_Q4_K && (g.hl * g.hd) % 256) {
-    set_error_message("cuda text: a rank's head columns must be whole Q4_K super-blocks");
-    return EOS_E_UNSUPPORTED;
-  }
-  // FFN slice in whole blocks of the down projection's k
-  const uint32_t be = blk_elems(wdt), units = m.n_ff / be;
-  g.ff0 = (uint32_t)(((uint64_t)units * rk) / ws) * be;
-  g.ffl = (uint32_t)(((uint64_t)units * (rk + 1)) / ws) * be - g.ff0;
+  g.el = m.n_embd / ws;  // n_head % ws == 0, so n_embd % ws == 0
+  g.e0 = g.el * rk;
+  // FFN units in whole 32-element groups (the activation packing's unit)
+  const uint32_t units = m.n_ff / 32u;
+  g.ff0 = (uint32_t)(((uint64_t)units * rk) / ws) * 32u;
+  g.ffl = (uint32_t)(((uint64_t)units * (rk + 1)) / ws) * 32u - g.ff0;
   g.v0 = (uint32_t)(((uint64_t)m.n_vocab * rk) / ws);
   g.vl = (uint32_t)(((uint64_t)m.n_vocab * (rk + 1)) / ws) - g.v0;
   if (g.ffl == 0 || g.vl == 0) {
@@ -804,6 +796,8 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
   ff0 = g.ff0;
   vl = g.vl;
   v0 = g.v0;
+  el = g.el;
+  e0 = g.e0;
   max_chunks = (m.max_ctx + kAttnChunk - 1) / kAttnChunk;
 
   if (cudaSetDevice(dev) != cudaSuccess) return EOS_E_INTERNAL;
@@ -811,12 +805,12 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return EOS_E_INTERNAL;
 
-  const uint32_t E = m.n_embd;
+  const uint32_t E = m.n_embd, F = m.n_ff;
   cudaError_t e = cudaSuccess;
   auto chk = [&](cudaError_t r) {
     if (e == cudaSuccess) e = r;
   };
-  // ---- resident weights (this rank's slices) ----
+  // ---- resident weights (this rank's rows) ----
   layers.resize(m.n_layer);
   for (uint32_t L = 0; L < m.n_layer; ++L) {
     DecLayer& d = layers[L];
@@ -825,13 +819,13 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
     chk(copy_rows(d.wqkv, m.wq[L], wdt, E, h0 * hd, hl * hd));
     chk(copy_rows(d.wqkv + rb * hl * hd, m.wk[L], wdt, E, kv0 * hd, kvl * hd));
     chk(copy_rows(d.wqkv + rb * (hl * hd + kvl * hd), m.wv[L], wdt, E, kv0 * hd, kvl * hd));
-    chk(alloc(&d.wo, wbytes(wdt, E, hl * hd)));
-    chk(copy_cols(d.wo, m.wo[L], wdt, E, E, h0 * hd, hl * hd));
+    chk(alloc(&d.wo, wbytes(wdt, el, E)));
+    chk(copy_rows(d.wo, m.wo[L], wdt, E, e0, el));
     chk(alloc(&d.wgu, 2 * rb * ffl));
     chk(copy_rows(d.wgu, m.wg[L], wdt, E, ff0, ffl));
     chk(copy_rows(d.wgu + rb * ffl, m.wu[L], wdt, E, ff0, ffl));
-    chk(alloc(&d.wd, wbytes(wdt, E, ffl)));
-    chk(copy_cols(d.wd, m.wd[L], wdt, E, m.n_ff, ff0, ffl));
+    chk(alloc(&d.wd, wbytes(wdt, el, F)));
+    chk(copy_rows(d.wd, m.wd[L], wdt, F, e0, el));
     chk(alloc(&d.attn_norm, 4ull * E));
     chk(cudaMemcpyAsync(d.attn_norm, m.attn_norm[L], 4ull * E, kind(), st));
     chk(alloc(&d.ffn_norm, 4ull * E));
@@ -849,33 +843,37 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
   chk(alloc(&qkv, 4ull * (hl * hd + 2 * kvl * hd)));
   {
     const uint32_t vmax = (m.n_vocab + ws - 1) / ws + 1;
-    auto up = [](size_t x) { return (x + 255) & ~(size_t)255; };
-    xoff_po = 0;
-    xoff_pd = up(4ull * E * ws);
-    xoff_lg = xoff_pd + up(4ull * E * ws);
+    auto up = [](size_t x) { return (x + 4095) & ~(size_t)4095; };  // operand bases: 1024-byte aligned TMA
+    const bool q4 = wdt == EOS_DT_Q4_K;
+    xoff_o = 0;
+    xoff_d = up(4ull * E);
+    xoff_lg = xoff_d + up(4ull * E);
     xoff_fl = xoff_lg + up(4ull * vmax);
-    xbytes = xoff_fl + up(sizeof(XRecv));
-    if (ws > 1 && wdt == EOS_DT_Q4_K) {  // batched-prefill receive slots (allocated with the handles)
+    xoff_ao = xoff_fl + up(sizeof(XRecv));
+    xoff_ad = xoff_ao + up(q4 ? (size_t)(E / 256) * kActRec : 4ull * E);
+    xbytes = xoff_ad + up(q4 ? (size_t)(F / 256) * kActRec : 4ull * F);
+    if (ws > 1 && q4) {  // batched-prefill exchange (allocated with the handles)
       xpf_rows = m.max_ctx < kPrefillRows ? m.max_ctx : kPrefillRows;
       xoff_pfo = xbytes;
-      xoff_pfd = xoff_pfo + up(4ull * ws * xpf_rows * E);
-      xbytes = xoff_pfd + up(4ull * ws * xpf_rows * E);
+      xoff_pfd = xoff_pfo + up(4ull * xpf_rows * E);
+      xoff_pfa = xoff_pfd + up(4ull * xpf_rows * E);
+      xoff_pfs = xoff_pfa + up(prefill_operand_bytes(xpf_rows, E));
+      xbytes = xoff_pfs + up(prefill_operand_bytes(xpf_rows, F));
     }
     chk(alloc(&xbuf, xbytes));
-    part_o = reinterpret_cast<float*>(xbuf + xoff_po) + (size_t)E * rk;  // own slot
-    part_d = reinterpret_cast<float*>(xbuf + xoff_pd) + (size_t)E * rk;
+    o_full = reinterpret_cast<float*>(xbuf + xoff_o);
+    d_full = reinterpret_cast<float*>(xbuf + xoff_d);
     logits = reinterpret_cast<float*>(xbuf + xoff_lg);
+    if (q4) {
+      act_o = xbuf + xoff_ao;
+      act_d = xbuf + xoff_ad;
+    } else {
+      actf_o = reinterpret_cast<float*>(xbuf + xoff_ao);
+      actf_d = reinterpret_cast<float*>(xbuf + xoff_ad);
+    }
     xpeer[rk] = xbuf;
   }
   chk(alloc(&gu, 8ull * ffl));
-
-  if (wdt == EOS_DT_Q4_K) {
-    chk(alloc(&act_o, (size_t)(hl * hd / 256) * kActRec));
-    chk(alloc(&act_d, (size_t)(ffl / 256) * kActRec));
-  } else {
-    chk(alloc(&actf_o, 4ull * hl * hd));
-    chk(alloc(&actf_d, 4ull * ffl));
-  }
   // the normalised residual feeds the block linears (wdtype) and the head (out_dtype)
   if (wdt == EOS_DT_Q4_K || odt == EOS_DT_Q4_K) chk(alloc(&act_e, (size_t)(E / 256) * kActRec));
   if (wdt == EOS_DT_Q8_0 || odt == EOS_DT_Q8_0) chk(alloc(&actf_e, 4ull * E));
@@ -891,6 +889,10 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
   chk(alloc(&arg_v, 4ull * kArgmaxBlocks));
   chk(alloc(&arg_i, 4ull * kArgmaxBlocks));
   chk(alloc(&state, sizeof(DecState)));
+  {
+    const uint32_t limit_us = (uint32_t)(EOS_WAIT_LIMIT_NS / 1000ull);
+    chk(cudaMemcpyAsync(&state->wait_limit_us, &limit_us, 4, cudaMemcpyHostToDevice, st));
+  }
   chk(alloc(&prompt, 4ull * m.max_ctx));
   chk(alloc(&out_tokens, 4ull * m.max_ctx));
   chk(alloc(&gemv_err, 16));
@@ -907,8 +909,12 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
 int TextDecoder::attach(const uint8_t* handles) {
   if (world == 1 || graph != nullptr) return graph != nullptr ? EOS_OK : capture();
   if (cudaSetDevice(device) != cudaSuccess) return EOS_E_INTERNAL;
+  uint8_t* bufs[kMaxParts] = {};
   for (int q = 0; q < world; ++q) {
-    if (q == rank) continue;
+    if (q == rank) {
+      bufs[q] = xbuf;
+      continue;
+    }
     cudaIpcMemHandle_t h;
     memcpy(&h, handles + (size_t)q * sizeof(cudaIpcMemHandle_t), sizeof(h));
     void* ptr = nullptr;
@@ -917,55 +923,68 @@ int TextDecoder::attach(const uint8_t* handles) {
       set_error_message(cudaGetErrorString(e));
       return EOS_E_INTERNAL;
     }
-    xpeer[q] = static_cast<uint8_t*>(ptr);
+    bufs[q] = static_cast<uint8_t*>(ptr);
     peer_opened[q] = true;
   }
+  return attach_buffers(bufs);
+}
+
+int TextDecoder::attach_buffers(uint8_t* const* bufs) {
+  if (world == 1 || graph != nullptr) return graph != nullptr ? EOS_OK : capture();
+  for (int q = 0; q < world; ++q) xpeer[q] = bufs[q];
   n_push = 0;
   for (int q = 0; q < world; ++q) {
     if (q == rank) continue;
-    push_o[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_po) + (size_t)m.n_embd * rank;
-    push_d[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_pd) + (size_t)m.n_embd * rank;
+    push_o[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_o) + e0;
+    push_d[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_d) + e0;
+    push_ao[n_push] = xpeer[q] + xoff_ao;
+    push_ad[n_push] = xpeer[q] + xoff_ad;
+    push_afo[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_ao);
+    push_afd[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_ad);
     ++n_push;
   }
   return capture();
 }
 
 cudaError_t TextDecoder::record_step(cudaStream_t s) {
-  const uint32_t E = m.n_embd;
+  const uint32_t E = m.n_embd, F = m.n_ff;
   const int wdt = m.wdtype, odt = m.out_dtype;
   const uint32_t nqkv = hl * hd + 2 * kvl * hd;
+  const uint32_t xps = 4u * m.n_layer + 1u;  // exchanges per step
   cudaError_t e = cudaSuccess;
   int status = EOS_OK;
-  // push: the O and down partials also go straight into the other ranks'
-  // receive slots (tensor parallel)
+  // handshake of the step's exchange number xk, of kind `type`
+  auto xsync = [&](uint32_t type, uint32_t xk) {
+    XchgSync x{};
+    x.world = (uint32_t)world;
+    x.rank = (uint32_t)rank;
+    for (int q = 0; q < world; ++q) x.pub[q] = &xrecv(q)->flag[type][rank];
+    x.wait = &xrecv(rank)->flag[type][0];
+    x.epoch_word = &state->epoch;
+    x.mul = xps;
+    x.add = xk + 1u;
+    x.limit_us = &state->wait_limit_us;
+    x.err = &state->err;
+    return x;
+  };
+  // `extra`: the other ranks' copies of the output rows (push)
   auto gemv = [&](int dt, const uint8_t* w, const uint8_t* act, const float* actf, float* c, uint32_t n,
-                  uint32_t k, float* const* extra = nullptr, uint32_t n_extra = 0) -> cudaError_t {
+                  uint32_t k, float* const* extra = nullptr, uint32_t n_extra = 0,
+                  const XchgSync* xs = nullptr) -> cudaError_t {
     if (n == 0) return cudaSuccess;
     if (dt == EOS_DT_Q4_K)
       return launch_q4k_gemv(w, act, nullptr, c, n, k, gemv_err, num_sms, max_smem, true, s, &status, extra,
-                             n_extra);
-    return launch_q80_gemv(w, actf, c, n, k, gemv_err, num_sms, max_smem, s, &status, extra, n_extra);
+                             n_extra, xs);
+    return launch_q80_gemv(w, actf, c, n, k, gemv_err, num_sms, max_smem, s, &status, extra, n_extra, xs);
   };
-  const uint32_t xps = 2u * m.n_layer + 1u;  // exchanges per step
-  // `part`: nullptr (no partial), part_o or part_d; xk: exchange index
-  auto norm_pack = [&](const float* x_in, const float* part, float* x_out, const float* w, int dt_a, int dt_b,
-                       uint32_t xk = 0) -> cudaError_t {
+  // x_out = x_in + part (part: d_full / o_full, pushed by every rank), then
+  // rmsnorm and the packing for a consumer of dtype dt_a
+  auto norm_pack = [&](const float* x_in, const float* part, float* x_out, const float* w, int dt_a, uint32_t type,
+                       uint32_t xk) -> cudaError_t {
     NormPackParams p{};
     p.x_in = x_in;
-    p.nparts = 0;
-    if (part != nullptr) {
-      const size_t off = part == part_o ? xoff_po : xoff_pd;
-      const uint32_t type = part == part_o ? 0u : 1u;
-      p.nparts = (uint32_t)world;
-      for (int q = 0; q < world; ++q) {
-        p.parts[q] = reinterpret_cast<const float*>(xbuf + off) + (size_t)E * q;  // local slot of source q
-        p.pub_flag[q] = &xrecv(q)->flag[type][rank];
-      }
-      p.wait_flag = &xrecv(rank)->flag[type][0];
-    }
-    p.world = (uint32_t)world;
-    p.xchg = xk;
-    p.xchg_per_step = xps;
+    p.part = part;
+    p.xs = xsync(type, xk);
     p.tok_embd = tok_embd;
     p.prompt = prompt;
     p.state = state;
@@ -973,16 +992,15 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
     p.w = w;
     p.eps = m.rms_eps;
     p.n = E;
-    // one consumer dtype per launch; the head may differ from the block linears
-    (void)dt_b;
     p.act = dt_a == EOS_DT_Q4_K ? act_e : nullptr;
     p.act_f32 = dt_a == EOS_DT_Q8_0 ? actf_e : nullptr;
     return launch_pdl(norm_pack_kernel, dim3(E / 256u), dim3(256), s, p);
   };
   for (uint32_t L = 0; L < m.n_layer && e == cudaSuccess; ++L) {
     const DecLayer& d = layers[L];
-    // x1 = (L == 0 ? embedding : x0 + down partial); act_e = pack(rmsnorm(x1))
-    e = norm_pack(L == 0 ? nullptr : x0, L == 0 ? nullptr : part_d, x1, d.attn_norm, wdt, wdt, 2u * L - 1u);
+    // x1 = (L == 0 ? embedding : x0 + down output); act_e = pack(rmsnorm(x1))
+    e = norm_pack(L == 0 ? nullptr : x0, L == 0 ? nullptr : d_full, x1, d.attn_norm, wdt, kXDRows,
+                  L == 0 ? 0u : 4u * L - 1u);
     if (e == cudaSuccess) e = gemv(wdt, d.wqkv, act_e, actf_e, qkv, nqkv, E);
     if (e == cudaSuccess) {
       AttnParams a{};
@@ -994,6 +1012,11 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
       a.state = state;
       a.act = act_o;
       a.act_f32 = actf_o;
+      a.n_x = n_push;
+      for (uint32_t j = 0; j < n_push; ++j) {
+        a.act_x[j] = act_o != nullptr ? push_ao[j] : nullptr;
+        a.actf_x[j] = actf_o != nullptr ? push_afo[j] : nullptr;
+      }
       a.hl = hl;
       a.h0 = h0;
       a.kvl = kvl;
@@ -1009,19 +1032,36 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
       else if (hd == 128) e = launch_pdl_smem(attn_kernel<4>, grid, dim3(128), sm, s, a);
       else e = launch_pdl_smem(attn_kernel<8>, grid, dim3(128), sm, s, a);
     }
-    if (e == cudaSuccess) e = gemv(wdt, d.wo, act_o, actf_o, part_o, E, hl * hd, push_o, n_push);
-    // x0 = x1 + O partial; act_e = pack(rmsnorm(x0))
-    if (e == cudaSuccess) e = norm_pack(x1, part_o, x0, d.ffn_norm, wdt, wdt, 2u * L);
+    if (e == cudaSuccess) {  // this rank's O rows of all heads' attention output
+      const XchgSync xs = xsync(kXAttn, 4u * L);
+      e = gemv(wdt, d.wo, act_o, actf_o, o_full + e0, el, E, push_o, n_push, &xs);
+    }
+    // x0 = x1 + O output; act_e = pack(rmsnorm(x0))
+    if (e == cudaSuccess) e = norm_pack(x1, o_full, x0, d.ffn_norm, wdt, kXORows, 4u * L + 1u);
     if (e == cudaSuccess) e = gemv(wdt, d.wgu, act_e, actf_e, gu, 2 * ffl, E);
-    if (e == cudaSuccess)
-      e = launch_pdl(silu_pack_kernel, dim3((ffl + 255u) / 256u), dim3(256), s, (const float*)gu, ffl, act_d,
-                     actf_d);
-    if (e == cudaSuccess) e = gemv(wdt, d.wd, act_d, actf_d, part_d, E, ffl, push_d, n_push);
+    if (e == cudaSuccess) {
+      SiluParams sp{};
+      sp.gu = gu;
+      sp.ffl = ffl;
+      sp.ff0 = ff0;
+      sp.act = act_d;
+      sp.act_f32 = actf_d;
+      sp.n_x = n_push;
+      for (uint32_t j = 0; j < n_push; ++j) {
+        sp.act_x[j] = act_d != nullptr ? push_ad[j] : nullptr;
+        sp.actf_x[j] = actf_d != nullptr ? push_afd[j] : nullptr;
+      }
+      e = launch_pdl(silu_pack_kernel, dim3((ffl + 255u) / 256u), dim3(256), s, sp);
+    }
+    if (e == cudaSuccess) {  // this rank's down rows over all FFN units
+      const XchgSync xs = xsync(kXSilu, 4u * L + 2u);
+      e = gemv(wdt, d.wd, act_d, actf_d, d_full + e0, el, F, push_d, n_push, &xs);
+    }
   }
   // final norm + LM head + greedy pick (text.c:425-432, greedy.c:66-69)
   if (e == cudaSuccess)
-    e = norm_pack(m.n_layer ? x0 : nullptr, m.n_layer ? part_d : nullptr, x1, out_norm, odt, odt,
-                  m.n_layer ? 2u * m.n_layer - 1u : 0u);
+    e = norm_pack(m.n_layer ? x0 : nullptr, m.n_layer ? d_full : nullptr, x1, out_norm, odt, kXDRows,
+                  m.n_layer ? 4u * m.n_layer - 1u : 0u);
   if (e == cudaSuccess) e = gemv(odt, wout, act_e, actf_e, logits, vl, E);
   if (e == cudaSuccess) {
     ArgmaxParams a{};
@@ -1036,8 +1076,7 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
     a.v0 = v0;
     a.own = xrecv(rank);
     for (int q = 0; q < world; ++q) a.recv[q] = xrecv(q);
-    a.xchg = 2u * m.n_layer;
-    a.xchg_per_step = xps;
+    a.xs = xsync(kXArgmax, 4u * m.n_layer);
     e = launch_pdl(argmax_kernel, dim3(arg_blocks), dim3(256), s, a);
   }
   if (e == cudaSuccess && status != EOS_OK) e = cudaErrorNotSupported;
@@ -1049,20 +1088,25 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
 // the prefill kernels, which write their K/V rows into the cache; the next
 // block attends to them.  Only the cache matters afterwards (the next step
 // reads it), so the last layer stops after its K/V rows and no block computes
-// logits.  Leaves state->pos = host_pos + n (not host_pos itself: the caller
-// commits it after its synchronisation).
+// logits.  Tensor parallel, the matrices are split by output rows as in the
+// step: each rank packs its heads' attention output and its FFN units'
+// SiLU output into every rank's copy of the next GEMM's operand, and pushes
+// its O / down output rows into every rank's row buffer, which the exchange
+// kernel then adds to the residual rows -- so every rank holds the one-GPU
+// residual stream bit for bit.  Leaves state->pos = host_pos + n (not
+// host_pos itself: the caller commits it after its synchronisation).
 cudaError_t TextDecoder::prefill(uint32_t n) {
-  const uint32_t E = m.n_embd, nqkv = hl * hd + 2u * kvl * hd, kq = hl * hd;
+  const uint32_t E = m.n_embd, F = m.n_ff, nqkv = hl * hd + 2u * kvl * hd;
   cudaError_t e = cudaSuccess;
   if (pf_rows == 0) {
     const uint32_t rows = m.max_ctx < kPrefillRows ? m.max_ctx : kPrefillRows;
     // the operand size grows with the row count: `rows` bounds every block
     size_t amax = 0;
-    for (const uint32_t kk : {E, kq, ffl})
+    for (const uint32_t kk : {E, F})
       if (prefill_operand_bytes(rows, kk) > amax) amax = prefill_operand_bytes(rows, kk);
     size_t wmax = prefill_operand_bytes(nqkv, E);
-    for (const size_t b : {prefill_operand_bytes(E, kq), prefill_operand_bytes(2u * ffl, E),
-                           prefill_operand_bytes(E, ffl)})
+    for (const size_t b : {prefill_operand_bytes(el, E), prefill_operand_bytes(2u * ffl, E),
+                           prefill_operand_bytes(el, F)})
       if (b > wmax) wmax = b;
     if (e == cudaSuccess) e = alloc(&pf_x, 4ull * rows * E);
     if (e == cudaSuccess) e = alloc(&pf_qkv, 4ull * rows * nqkv);
@@ -1073,7 +1117,7 @@ cudaError_t TextDecoder::prefill(uint32_t n) {
     pf_rows = rows;
   }
   int status = EOS_OK;
-  const uint32_t mat_n[4] = {nqkv, E, 2u * ffl, E}, mat_k[4] = {E, kq, E, ffl};  // qkv, o, gate|up, down
+  const uint32_t mat_n[4] = {nqkv, el, 2u * ffl, el}, mat_k[4] = {E, E, E, F};  // qkv, o, gate|up, down
   auto mat_w = [&](uint32_t L, int i) -> const uint8_t* {
     const DecLayer& d = layers[L];
     return i == 0 ? d.wqkv : (i == 1 ? d.wo : (i == 2 ? d.wgu : d.wd));
@@ -1101,39 +1145,48 @@ cudaError_t TextDecoder::prefill(uint32_t n) {
       }
     }
   }
-  // C (+)= A . deq(W)^T with W resident in the GEMM layout, or prepared on the fly
-  auto gemm = [&](uint32_t L, int i, float* c, uint32_t mm, bool acc, float* const* extra = nullptr,
-                  uint32_t n_extra = 0) {
+  // C (+)= act . deq(W)^T with W resident in the GEMM layout, or prepared on
+  // the fly; rows of C ldc floats apart, pushed into `extra` too
+  auto gemm = [&](uint32_t L, int i, const void* act, float* c, uint32_t mm, bool acc, uint32_t ldc = 0,
+                  float* const* extra = nullptr, uint32_t n_extra = 0) {
     const uint32_t nn = mat_n[i], kk = mat_k[i];
     const bool res = pf_resident && !pf_wres.empty();
     const void* wp = res ? pf_wres[4u * L + i] : pf_w;
     if (e == cudaSuccess && !res) e = launch_prefill_w_prep(mat_w(L, i), nn, kk, pf_w, st);
     if (e == cudaSuccess)
-      e = launch_prefill_gemm(pf_act, wp, c, mm, nn, kk, gemv_err, st, &status, acc, extra, n_extra);
+      e = launch_prefill_gemm(act, wp, c, mm, nn, kk, gemv_err, st, &status, acc, extra, n_extra, ldc);
     if (e == cudaSuccess && status != EOS_OK) e = cudaErrorNotSupported;
   };
-  // tensor parallel: this rank's O / down partial rows go to its own slot and,
-  // over NVLink, to its slot at every other rank; pf_xchg_add then sums the
-  // slots into the residual rows (identical on every rank)
-  const size_t slot_floats = (size_t)xpf_rows * E;
-  auto slot = [&](int q, int type) {
-    return reinterpret_cast<float*>(xpeer[q] + (type == 0 ? xoff_pfo : xoff_pfd)) + slot_floats * rank;
-  };
-  float* push[2][kMaxParts] = {};
-  uint32_t n_push_pf = 0;
-  uint32_t* pub[2][kMaxParts] = {};
+  // tensor parallel: the other ranks' copies of the O / down output rows and
+  // of the O / down operands
+  float* push_rows[2][kMaxParts] = {};
+  void* push_op[2][kMaxParts] = {};
+  uint32_t np = 0;
   for (int q = 0; q < world && world > 1; ++q) {
-    for (int t = 0; t < 2; ++t) pub[t][q] = &xrecv(q)->pf_flag[t][rank];
     if (q == rank) continue;
-    push[0][n_push_pf] = slot(q, 0);
-    push[1][n_push_pf] = slot(q, 1);
-    ++n_push_pf;
+    push_rows[0][np] = reinterpret_cast<float*>(xpeer[q] + xoff_pfo) + e0;
+    push_rows[1][np] = reinterpret_cast<float*>(xpeer[q] + xoff_pfd) + e0;
+    push_op[0][np] = xpeer[q] + xoff_pfa;
+    push_op[1][np] = xpeer[q] + xoff_pfs;
+    ++np;
   }
-  auto exchange = [&](int type, uint32_t mm) {
+  float* rows_o = world > 1 ? reinterpret_cast<float*>(xbuf + xoff_pfo) : nullptr;
+  float* rows_d = world > 1 ? reinterpret_cast<float*>(xbuf + xoff_pfd) : nullptr;
+  void* op_o = world > 1 ? static_cast<void*>(xbuf + xoff_pfa) : pf_act;
+  void* op_d = world > 1 ? static_cast<void*>(xbuf + xoff_pfs) : pf_act;
+  // handshake of one prefill exchange (kind `type`); with src, x += src
+  auto exchange = [&](int type, const float* src, uint32_t mm) {
     if (e != cudaSuccess) return;
-    const float* mine = reinterpret_cast<const float*>(xbuf + (type == 0 ? xoff_pfo : xoff_pfd));
-    e = launch_pf_xchg_add(pf_x, mine, slot_floats, mm, E, (uint32_t)world, pub[type], &xrecv(rank)->pf_flag[type][0],
-                           ++pf_epoch, &state->err, st);
+    XchgSync xs{};
+    xs.world = (uint32_t)world;
+    xs.rank = (uint32_t)rank;
+    for (int q = 0; q < world; ++q) xs.pub[q] = &xrecv(q)->pf_flag[type][rank];
+    xs.wait = &xrecv(rank)->pf_flag[type][0];
+    xs.epoch_word = nullptr;
+    xs.add = ++pf_epoch;
+    xs.limit_us = &state->wait_limit_us;
+    xs.err = &state->err;
+    e = launch_pf_xchg(xs, pf_x, src, mm, E, st);
   };
   const float scale = 1.0f / sqrtf((float)hd);  // text.c:365
   for (uint32_t b0 = 0; b0 < n && e == cudaSuccess; b0 += pf_rows) {
@@ -1145,27 +1198,29 @@ cudaError_t TextDecoder::prefill(uint32_t n) {
       float* vcl = vc + (size_t)L * m.max_ctx * kvl * hd;
       e = launch_pf_norm_pack(pf_x, L == 0 ? prompt + pos0 : nullptr, tok_embd, d.attn_norm, m.rms_eps, mm, E,
                               pf_act, st);
-      gemm(L, 0, pf_qkv, mm, false);
+      gemm(L, 0, pf_act, pf_qkv, mm, false);
       if (e == cudaSuccess) e = launch_pf_rope_kv(pf_qkv, kcl, vcl, mm, hl, kvl, hd, pos0, m.rope_base, st);
       if (L + 1u == m.n_layer) break;  // the cache needs nothing more of the last layer
       if (e == cudaSuccess)
-        e = launch_pf_attn(pf_qkv, kcl, vcl, pf_act, mm, hl, kvl, h0, kv0, m.n_head, m.n_kv_head, hd, pos0,
-                           scale, st);
+        e = launch_pf_attn(pf_qkv, kcl, vcl, op_o, mm, hl, kvl, h0, kv0, m.n_head, m.n_kv_head, hd, pos0, scale,
+                           E, push_op[0], np, st);
       if (world == 1) {
-        gemm(L, 1, pf_x, mm, true);
+        gemm(L, 1, op_o, pf_x, mm, true);
       } else {
-        gemm(L, 1, slot(rank, 0), mm, false, push[0], n_push_pf);
-        exchange(0, mm);
+        exchange(kXAttn, nullptr, mm);
+        gemm(L, 1, op_o, rows_o + e0, mm, false, E, push_rows[0], np);
+        exchange(kXORows, rows_o, mm);
       }
       if (e == cudaSuccess)
         e = launch_pf_norm_pack(pf_x, nullptr, tok_embd, d.ffn_norm, m.rms_eps, mm, E, pf_act, st);
-      gemm(L, 2, pf_gu, mm, false);
-      if (e == cudaSuccess) e = launch_pf_silu_pack(pf_gu, mm, ffl, pf_act, st);
+      gemm(L, 2, pf_act, pf_gu, mm, false);
+      if (e == cudaSuccess) e = launch_pf_silu_pack(pf_gu, mm, ffl, op_d, ff0, F, push_op[1], np, st);
       if (world == 1) {
-        gemm(L, 3, pf_x, mm, true);
+        gemm(L, 3, op_d, pf_x, mm, true);
       } else {
-        gemm(L, 3, slot(rank, 1), mm, false, push[1], n_push_pf);
-        exchange(1, mm);
+        exchange(kXSilu, nullptr, mm);
+        gemm(L, 3, op_d, rows_d + e0, mm, false, E, push_rows[1], np);
+        exchange(kXDRows, rows_d, mm);
       }
     }
   }
@@ -1221,6 +1276,11 @@ int dec_check_device_errors(eosi_cuda_text_t* t) {
   if (e == cudaSuccess) e = cudaMemcpyAsync(&words[1], t->d.gemv_err, 4, cudaMemcpyDeviceToHost, t->d.st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(t->d.st);
   if (e != cudaSuccess) return dec_fail(e);
+  if (words[0] & EOS_DEVERR_PEER) {
+    eos::set_error_message("cuda text: a tensor-parallel peer did not arrive within the wait limit "
+                           "(bounded wait ran out; reset every rank before stepping again)");
+    return EOS_E_INTERNAL;
+  }
   if (words[0] | words[1]) {
     eos::set_error_message("cuda text: a device-side bounded wait ran out");
     return EOS_E_INTERNAL;
@@ -1415,12 +1475,52 @@ EOSLLM_CUDA_API int eosi_cuda_text_attach_peers(eosi_cuda_text_t* t, const void*
   return t->d.attach(static_cast<const uint8_t*>(handles));
 }
 
+EOSLLM_CUDA_API int eosi_cuda_text_attach_local(eosi_cuda_text_t* const* ranks, int world) {
+  if (ranks == nullptr || world < 2 || world > (int)eos::kMaxParts) return EOS_E_INVALID_ARG;
+  uint8_t* bufs[eos::kMaxParts] = {};
+  for (int q = 0; q < world; ++q) {
+    if (ranks[q] == nullptr || ranks[q]->d.world != world || ranks[q]->d.rank != q) {
+      eos::set_error_message("cuda text: attach_local needs every rank's decoder, in rank order");
+      return EOS_E_INVALID_ARG;
+    }
+    bufs[q] = ranks[q]->d.xbuf;
+  }
+  for (int r = 0; r < world; ++r) {
+    TextDecoder& d = ranks[r]->d;
+    if (cudaSetDevice(d.device) != cudaSuccess) return EOS_E_INTERNAL;
+    for (int q = 0; q < world; ++q) {  // stores into the other ranks' buffers need peer access
+      const int pd = ranks[q]->d.device;
+      if (pd == d.device) continue;
+      const cudaError_t e = cudaDeviceEnablePeerAccess(pd, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+      } else if (e != cudaSuccess) {
+        cudaGetLastError();
+        eos::set_error_message("cuda text: attach_local: no peer access between the ranks' devices");
+        return EOS_E_UNSUPPORTED;
+      }
+    }
+    const int s = d.attach_buffers(bufs);
+    if (s != EOS_OK) return s;
+  }
+  return EOS_OK;
+}
+
+EOSLLM_CUDA_API int eosi_cuda_text_set_wait_limit(eosi_cuda_text_t* t, uint32_t limit_us) {
+  if (t == nullptr || limit_us == 0) return EOS_E_INVALID_ARG;
+  TextDecoder& d = t->d;
+  if (cudaSetDevice(d.device) != cudaSuccess) return EOS_E_INTERNAL;
+  cudaError_t e = cudaMemcpyAsync(&d.state->wait_limit_us, &limit_us, 4, cudaMemcpyHostToDevice, d.st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(d.st);
+  return e == cudaSuccess ? EOS_OK : dec_fail(e);
+}
+
 EOSLLM_CUDA_API int eosi_cuda_text_partition(const eosi_cuda_llama_t* m, int rank, int world, uint32_t* out) {
   if (m == nullptr || out == nullptr) return EOS_E_INVALID_ARG;
   eos::Geometry g{};
   const int s = eos::model_geometry(*m, rank, world, g);
   if (s != EOS_OK) return s;
-  const uint32_t v[9] = {g.hd, g.h0, g.hl, g.kv0, g.kvl, g.ff0, g.ffl, g.v0, g.vl};
+  const uint32_t v[11] = {g.hd, g.h0, g.hl, g.kv0, g.kvl, g.ff0, g.ffl, g.v0, g.vl, g.e0, g.el};
   memcpy(out, v, sizeof(v));
   return EOS_OK;
 }

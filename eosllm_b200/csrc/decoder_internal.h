@@ -5,18 +5,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-namespace eos {
+#include "eos_common.cuh"
 
-// System-scope release store / acquire load of a flag word (tensor-parallel
-// handshakes through CUDA IPC mappings).
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+namespace eos {
 
 // Words the step kernels share in device memory.
 struct DecState {
@@ -26,29 +17,37 @@ struct DecState {
   uint32_t arg_count;   // argmax CTA arrivals (reset by the last CTA)
   uint32_t err;         // EOS_DEVERR_* bits
   uint32_t epoch;       // completed steps (never reset): tensor-parallel exchange epochs
-  uint32_t pad[2];
+  uint32_t wait_limit_us;  // bound on every tensor-parallel flag wait
+  uint32_t pad;
 };
+
+// Tensor-parallel exchanges of one decode step, in order, per layer: the
+// attention output (packed for the O projection), the O projection's output
+// rows, the SiLU output (packed for the down projection), the down
+// projection's output rows; after the last layer the greedy pick.
+enum : uint32_t { kXAttn = 0, kXORows = 1, kXSilu = 2, kXDRows = 3, kXArgmax = 4, kXTypes = 5 };
 
 // Tensor-parallel receive words of one rank, in its exchange buffer; the
 // other ranks write them through CUDA IPC mappings (push).  Flag values are
-// epochs: step_epoch * (2 n_layer + 1) + exchange + 1.
+// epochs: step_epoch * (4 n_layer + 1) + exchange + 1.
 struct XRecv {
-  uint32_t flag[3][8];  // [0] O partial, [1] down partial, [2] argmax result; [.][q]: written by rank q
+  uint32_t flag[kXTypes][8];  // [type][q]: written by rank q
   float arg_v[8];       // rank q's best logit
   uint32_t arg_i[8];    // its global vocabulary index
   uint32_t first_nan;   // from rank 0: logits[0] is NaN
   uint32_t pad[7];
-  // batched prefill: [0] O partial rows, [1] down partial rows, [.][q] written
-  // by rank q; values are the prefill's own exchange counter (1, 2, ...)
-  uint32_t pf_flag[2][8];
+  // batched prefill, same four exchange types per layer; values are the
+  // prefill's own exchange counter (1, 2, ...)
+  uint32_t pf_flag[4][8];
 };
 
-// One layer's resident weights (this rank's slices).
+// One layer's resident weights (this rank's slices; tensor parallel shards
+// every matrix by output rows).
 struct DecLayer {
-  uint8_t* wqkv;  // [q rows; k rows; v rows] x n_embd
-  uint8_t* wo;    // n_embd rows x (this rank's head columns)
+  uint8_t* wqkv;  // [q rows; k rows; v rows] of this rank's heads x n_embd
+  uint8_t* wo;    // this rank's n_embd output rows x n_embd
   uint8_t* wgu;   // [gate rows; up rows] of this rank's FFN slice x n_embd
-  uint8_t* wd;    // n_embd rows x (this rank's FFN columns)
+  uint8_t* wd;    // this rank's n_embd output rows x n_ff
   float* attn_norm;
   float* ffn_norm;
 };
@@ -89,19 +88,23 @@ cudaError_t launch_pf_norm_pack(float* x, const uint32_t* tokens, const uint16_t
 cudaError_t launch_pf_rope_kv(float* qkv, float* kc, float* vc, uint32_t m, uint32_t hl, uint32_t kvl, uint32_t hd,
                               uint32_t pos0, float base, cudaStream_t st);
 // Causal attention of query rows [0, m) (positions pos0 + row) over cache
-// positions [0, pos0 + row], packed for the O GEMM (k = hl*hd).
+// positions [0, pos0 + row] of this rank's hl heads, packed into the O GEMM's
+// operand of k = k_total columns (head h0 + h at columns (h0 + h) * hd; one
+// GPU: k_total = hl * hd, h0 = 0) and into the n_extra further operands of
+// the same layout (tensor parallel: the other ranks' copies).
 cudaError_t launch_pf_attn(const float* qkv, const float* kc, const float* vc, void* act, uint32_t m, uint32_t hl,
                            uint32_t kvl, uint32_t h0, uint32_t kv0, uint32_t n_head, uint32_t n_kv_head,
-                           uint32_t hd, uint32_t pos0, float scale, cudaStream_t st);
-// silu(gate) * up of gu[m][2 ffl] (gate | up), packed (k = ffl).
-cudaError_t launch_pf_silu_pack(const float* gu, uint32_t m, uint32_t ffl, void* act, cudaStream_t st);
-// Tensor-parallel exchange of the prefill: raise this rank's flag (epoch) in
-// every rank's words (pub_flag[q]), wait -- bounded -- for every source's
-// flag in this rank's words (wait_flag[0..world)), then
-// x[i] += ((s_0[i] + s_1[i]) + ...) over the sources' partial rows, which
-// their GEMMs pushed into this rank's slots (source q at slots + q * stride).
-cudaError_t launch_pf_xchg_add(float* x, const float* slots, size_t stride, uint32_t m, uint32_t n, uint32_t world,
-                               uint32_t* const* pub_flag, const uint32_t* wait_flag, uint32_t epoch, uint32_t* err,
-                               cudaStream_t st);
+                           uint32_t hd, uint32_t pos0, float scale, uint32_t k_total, void* const* act_extra,
+                           uint32_t n_extra, cudaStream_t st);
+// silu(gate) * up of gu[m][2 ffl] (gate | up) -- FFN units [f0, f0 + ffl) --
+// packed into the down GEMM's operand of k = k_total columns at column f0,
+// and into the n_extra further operands of the same layout.
+cudaError_t launch_pf_silu_pack(const float* gu, uint32_t m, uint32_t ffl, void* act, uint32_t f0, uint32_t k_total,
+                                void* const* act_extra, uint32_t n_extra, cudaStream_t st);
+// Tensor-parallel exchange of the prefill: raise this rank's flag in every
+// rank's words and wait -- bounded -- for every other rank's flag in this
+// rank's words (xs: epoch in xs.add); then, when src != nullptr,
+// x[i] += src[i] over m rows of n (the rows every rank pushed into src).
+cudaError_t launch_pf_xchg(const XchgSync& xs, float* x, const float* src, uint32_t m, uint32_t n, cudaStream_t st);
 
 }  // namespace eos

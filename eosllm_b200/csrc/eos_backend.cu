@@ -138,6 +138,7 @@ size_t g_cap_h_c = 0;
 
 int g_probe = -1;
 int g_ndev = 0;
+uint64_t g_host_calls = 0;  // host-pointer matmuls completed on the GPU
 
 size_t row_bytes_of(int dtype, uint32_t k) {
   return dtype == EOS_DT_Q4_K ? (size_t)(k / Q4K_ELEMS) * Q4K_BYTES : (size_t)(k / Q80_ELEMS) * Q80_BYTES;
@@ -463,9 +464,11 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
       const float* src = reinterpret_cast<const float*>(g_shards[gi].h_blk + 16);
       for (uint32_t i = 0; i < m; ++i) memcpy(c + (size_t)i * n + row0, src + (size_t)i * rows, (size_t)rows * 4u);
     }
+    ++g_host_calls;
     return EOS_OK;
   }
   memcpy(c, g_h_c, (size_t)m * n * 4u);
+  ++g_host_calls;
   return EOS_OK;
 }
 
@@ -622,6 +625,20 @@ int eosi_cuda_cache_clear(void) {
     s.cache.clear();
   }
   if (had) cudaSetDevice(prev);
+  return EOS_OK;
+}
+
+int eosi_cuda_host_stats(uint64_t* calls, uint64_t* cached_weights, uint64_t* cached_bytes) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  uint64_t entries = 0, bytes = 0;
+  for (const auto& s : g_shards)
+    for (const auto& kv : s.cache) {
+      ++entries;
+      bytes += kv.second.bytes;
+    }
+  if (calls) *calls = g_host_calls;
+  if (cached_weights) *cached_weights = entries;
+  if (cached_bytes) *cached_bytes = bytes;
   return EOS_OK;
 }
 

@@ -139,6 +139,73 @@ __device__ __forceinline__ void report(uint32_t* err, uint32_t bits) {
   if (err) atomicOr(err, bits);
 }
 
+// ---- tensor-parallel handshakes (device-resident decoder) ---------------
+// System-scope release store / acquire load of a flag word that other GPUs
+// write through CUDA IPC mappings.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One exchange of the tensor-parallel decoder: the ranks have pushed data
+// into each other's memory (plain stores over NVLink by the kernel before the
+// one that runs the handshake), and the consumer must not read its own copy
+// before every source's push is visible.  Flag values are epochs,
+// *epoch_word * mul + add, that only grow, so flags need no reset.
+struct XchgSync {
+  uint32_t world;              // > 1: the handshake runs
+  uint32_t rank;               // this rank
+  uint32_t* pub[8];            // this rank's flag word in every rank's receive words (own included)
+  const uint32_t* wait;        // this rank's receive words: [q] is raised by rank q
+  const uint32_t* epoch_word;  // completed steps (nullptr: the epoch is `add` itself)
+  uint32_t mul, add;
+  const uint32_t* limit_us;    // bound on the wait, in microseconds
+  uint32_t* err;               // EOS_DEVERR_PEER when a wait runs out
+};
+
+// Every thread of the CTA calls this after griddepcontrol.wait (the pushing
+// grid has completed, and a grid's stores, remote ones included, are
+// performed when it completes).  With `publish`, thread 0 raises this rank's
+// flag in every rank's words after a system-scope fence, so a rank that
+// acquires the flag sees the pushed data; threads q < world then wait for
+// source q's flag in this rank's own memory (local polling, bounded) -- all
+// sources, or all but this rank itself when `skip_own` (a CTA of a large
+// grid need not wait for its own grid's CTA 0).  Returns false when a wait
+// ran out (the error bit is set; the caller leaves its outputs unwritten).
+__device__ __forceinline__ bool xchg_handshake(const XchgSync& x, bool publish, bool skip_own) {
+  __shared__ uint32_t s_xok;
+  const uint32_t epoch = x.epoch_word != nullptr ? *x.epoch_word * x.mul + x.add : x.add;
+  if (threadIdx.x == 0) s_xok = 1u;
+  if (publish && threadIdx.x == 0) {
+    __threadfence_system();
+    for (uint32_t q = 0; q < x.world; ++q) st_release_sys(x.pub[q], epoch);
+  }
+  __syncthreads();
+  if (threadIdx.x < x.world && !(skip_own && threadIdx.x == x.rank)) {
+    const uint32_t* f = x.wait + threadIdx.x;
+    if (ld_acquire_sys(f) < epoch) {
+      const uint64_t limit = (uint64_t)*x.limit_us * 1000ull;
+      const uint64_t t0 = global_timer_ns();
+      while (ld_acquire_sys(f) < epoch) {
+        // give up at the limit, or at once when an earlier handshake of
+        // this step already lost a peer (the step's outputs are invalid)
+        if (global_timer_ns() - t0 > limit ||
+            (x.err != nullptr && (*(volatile const uint32_t*)x.err & EOS_DEVERR_PEER) != 0u)) {
+          report(x.err, EOS_DEVERR_PEER);
+          s_xok = 0u;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return s_xok != 0u;
+}
+
 // ---- exact activation packing: x86 semantics of quantize_sub32 -----------
 // MAXPS/MAXSS: first operand if greater, else second (NaN -> second).
 __device__ __forceinline__ float x86_max(float a, float b) { return a > b ? a : b; }

@@ -9,6 +9,10 @@
 
 #include <initializer_list>
 
+namespace eos {
+struct XchgSync;  // eos_common.cuh
+}
+
 // Layouts the activation packer can write.
 enum { EOS_ACT_LAYOUT_GEMV = 0, EOS_ACT_LAYOUT_SOURCE = 1 };
 
@@ -34,9 +38,12 @@ cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out
 // after c (tensor-parallel push into other GPUs' IPC-mapped buffers; visible
 // to them once the grid has completed); not supported by the unstaged
 // fallback.
+// xs (optional, xs->world > 1): the tensor-parallel handshake every CTA runs
+// after its griddepcontrol.wait and before it reads the activations, which
+// the other ranks pushed into `act` (CTA 0 publishes; see xchg_handshake).
 cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
                             uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status,
-                            float* const* c_extra = nullptr, uint32_t n_extra = 0);
+                            float* const* c_extra = nullptr, uint32_t n_extra = 0, const XchgSync* xs = nullptr);
 void set_q4k_gemv_variant(int v);
 // Copies `bytes` (a multiple of 16; both addresses 16-byte aligned) from
 // device memory written by the previous kernel on `st` to `dst`, typically
@@ -56,14 +63,15 @@ cudaError_t launch_prefill_act_pack(const float* a, uint32_t m, uint32_t k, void
 cudaError_t launch_prefill_w_prep(const uint8_t* w, uint32_t n, uint32_t k, void* wprep, cudaStream_t st);
 // accumulate: C = C_old + A.W^T (the decoder's residual adds).  c_extra /
 // n_extra (<= 7, not with accumulate): further destinations of C (tensor-
-// parallel push into other GPUs' IPC-mapped receive slots).
+// parallel push into other GPUs' IPC-mapped buffers).  ldc: floats between
+// rows of C and of every extra destination (0: n).
 cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, uint32_t m, uint32_t n, uint32_t k,
                                 uint32_t* err, cudaStream_t st, int* out_status, bool accumulate = false,
-                                float* const* c_extra = nullptr, uint32_t n_extra = 0);
+                                float* const* c_extra = nullptr, uint32_t n_extra = 0, uint32_t ldc = 0);
 
 cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t n, uint32_t k, uint32_t* err,
                             int num_sms, int max_smem, cudaStream_t st, int* out_status,
-                            float* const* c_extra = nullptr, uint32_t n_extra = 0);
+                            float* const* c_extra = nullptr, uint32_t n_extra = 0, const XchgSync* xs = nullptr);
 void set_q80_gemv_variant(int v);
 
 // Test/utility kernels (eos_util.cu).

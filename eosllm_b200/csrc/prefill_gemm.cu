@@ -197,8 +197,8 @@ __device__ __forceinline__ void qg_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 // GEMM
 // ---------------------------------------------------------------------------
 struct PrefillParams {
-  float* c;
-  uint32_t m, n, k;
+  float* c;          // row r at c + r * ldc (ldc >= n)
+  uint32_t m, n, k, ldc;
   uint32_t* err;
   uint32_t accumulate;  // C = C_old + A.W^T (residual add, old value first)
   // tensor parallel: further destinations of C (other GPUs' receive slots,
@@ -376,8 +376,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     } else {
       const uint32_t row = m0 + lrow, gcol = n0 + col0;
       if (row < p.m) {
-        float* crow = p.c + (size_t)row * p.n + gcol;
-        if (gcol + QG_COLS <= p.n && (p.n & 3u) == 0) {
+        float* crow = p.c + (size_t)row * p.ldc + gcol;
+        if (gcol + QG_COLS <= p.n && (p.ldc & 3u) == 0) {
 #pragma unroll
           for (uint32_t c4 = 0; c4 < QG_COLS / 4; ++c4) {
             float4 v = acc[32 * c4];
@@ -387,7 +387,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
             }
             *reinterpret_cast<float4*>(crow + 4 * c4) = v;
             for (uint32_t x = 0; x < p.n_extra; ++x)
-              *reinterpret_cast<float4*>(p.c_extra[x] + (size_t)row * p.n + gcol + 4 * c4) = v;
+              *reinterpret_cast<float4*>(p.c_extra[x] + (size_t)row * p.ldc + gcol + 4 * c4) = v;
           }
         } else {
 #pragma unroll
@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
             const float v = (c & 3u) == 0 ? v4.x : ((c & 3u) == 1 ? v4.y : ((c & 3u) == 2 ? v4.z : v4.w));
             if (gcol + c < p.n) {
               crow[c] = p.accumulate ? __fadd_rn(crow[c], v) : v;
-              for (uint32_t x = 0; x < p.n_extra; ++x) p.c_extra[x][(size_t)row * p.n + gcol + c] = v;
+              for (uint32_t x = 0; x < p.n_extra; ++x) p.c_extra[x][(size_t)row * p.ldc + gcol + c] = v;
             }
           }
         }
@@ -484,14 +484,16 @@ cudaError_t launch_prefill_w_prep(const uint8_t* w, uint32_t n, uint32_t k, void
 }
 
 // C[m,n] (or C += with `accumulate`) from prepared operands (layouts above;
-// k % 256 == 0, base pointers 1024-byte aligned).  out_status:
+// k % 256 == 0, base pointers 1024-byte aligned); rows of C (and of every
+// extra destination) ldc floats apart (0: n).  out_status:
 // EOS_E_UNSUPPORTED when the tensor maps cannot be built.
 cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, uint32_t m, uint32_t n, uint32_t k,
                                 uint32_t* err, cudaStream_t st, int* out_status, bool accumulate,
-                                float* const* c_extra, uint32_t n_extra) {
+                                float* const* c_extra, uint32_t n_extra, uint32_t ldc) {
   *out_status = EOS_OK;
   if (m == 0 || n == 0) return cudaSuccess;
-  if (n_extra > 7 || (n_extra > 0 && accumulate)) {
+  if (ldc == 0) ldc = n;
+  if (n_extra > 7 || (n_extra > 0 && accumulate) || ldc < n) {
     *out_status = EOS_E_INVALID_ARG;
     return cudaSuccess;
   }
@@ -510,7 +512,7 @@ cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, ui
     if (e != cudaSuccess) return e;
   }
   const dim3 grid((m + QG_BM - 1) / QG_BM, (n + QG_BN - 1) / QG_BN);
-  PrefillParams prm{c, m, n, k, err, accumulate ? 1u : 0u, {}, n_extra};
+  PrefillParams prm{c, m, n, k, ldc, err, accumulate ? 1u : 0u, {}, n_extra};
   for (uint32_t x = 0; x < n_extra; ++x) prm.c_extra[x] = c_extra[x];
   prefill_gemm_kernel<<<grid, QG_THREADS, QG_SMEM, st>>>(ma, mb, mas, mbs, prm);
   return cudaGetLastError();

@@ -36,6 +36,33 @@ namespace eos {
 constexpr uint32_t kPfNormChunks = 16;  // float4 chunks per thread: n <= 16384
 constexpr uint32_t kPfQ = 16;           // query rows per attention CTA (4 per warp)
 constexpr uint32_t kPfKC = 32;          // cache positions per staged chunk (one per lane)
+constexpr uint32_t kPfMaxDst = 8;       // this rank's operand + up to 7 peers' copies
+
+// Where a packed 32-group goes: this rank's GEMM operand and, tensor
+// parallel, the same position in the other ranks' copies (plain stores over
+// NVLink through CUDA IPC mappings, performed when the grid completes).
+struct PfOperands {
+  uint16_t* aq[kPfMaxDst];  // int8 values as bf16, [rows][k]
+  float* asc[kPfMaxDst];    // per-32 scale pairs, [2 k/32][pitch]
+  uint32_t n;               // destinations
+  uint32_t k, pitch;        // operand columns, scale-row pitch (pad4(rows))
+};
+
+// pf_pack_group into every destination: the same quantize_sub32 values.
+__device__ __forceinline__ void pf_pack_group_to(const PfOperands& d, float v, uint32_t row, uint32_t s,
+                                                 uint32_t lane) {
+  float scale;
+  int32_t sum;
+  const int8_t q = quant_group32(v, scale, sum);
+  const uint16_t b = __bfloat16_as_ushort(__float2bfloat16_rn((float)q));  // exact
+  for (uint32_t j = 0; j < d.n; ++j) {
+    d.aq[j][(size_t)row * d.k + s * 32u + lane] = b;
+    if (lane == 0) {
+      d.asc[j][(size_t)(2u * s) * d.pitch + row] = scale;
+      d.asc[j][(size_t)(2u * s + 1u) * d.pitch + row] = (float)sum;
+    }
+  }
+}
 
 // ---------------------------------------------------------------------------
 // Residual row -> rmsnorm -> packed activation
@@ -160,8 +187,7 @@ struct PfAttnParams {
   const float* qkv;  // q rotated
   const float* kc;
   const float* vc;
-  uint16_t* aq;  // GEMM activation layout, k = hl HD
-  float* asc;
+  PfOperands out;    // the O GEMM's operand(s); head h0 + h at groups (h0 + h) HD / 32
   uint32_t m, hl, kvl, h0, kv0, n_head, n_kv_head, pos0;
   float scale;
 };
@@ -294,7 +320,6 @@ __global__ void __launch_bounds__(128) pf_attn_kernel(const PfAttnParams p) {
     __syncthreads();  // every warp is done with buffer `cur` before it is refilled
   }
   // normalise, pack per 32 dims
-  const uint32_t kq = p.hl * HD, pitch = pf_pad4(p.m);
   float* sw = so + warp * HD;
 #pragma unroll
   for (int r = 0; r < 4; ++r) {
@@ -305,8 +330,7 @@ __global__ void __launch_bounds__(128) pf_attn_kernel(const PfAttnParams p) {
     for (int ee = 0; ee < E; ++ee) sw[lane * E + ee] = o[r][ee] * inv;
     __syncwarp();
 #pragma unroll
-    for (int g = 0; g < E; ++g)
-      pf_pack_group(sw[g * 32 + lane], i0 + qi, hloc * E + g, lane, kq, pitch, p.aq, p.asc);
+    for (int g = 0; g < E; ++g) pf_pack_group_to(p.out, sw[g * 32 + lane], i0 + qi, gh * E + g, lane);
     __syncwarp();
   }
 }
@@ -315,67 +339,41 @@ __global__ void __launch_bounds__(128) pf_attn_kernel(const PfAttnParams p) {
 // silu(gate) * up -> packed
 // ---------------------------------------------------------------------------
 // Grid (ffl / 256, m), 256 threads; ffl % 32 == 0, so every warp is one group.
-__global__ void __launch_bounds__(256) pf_silu_pack_kernel(const float* __restrict__ gu, uint32_t ffl,
-                                                           uint32_t pitch, uint16_t* __restrict__ aq,
-                                                           float* __restrict__ asc) {
+// FFN unit f0 + i goes to operand column f0 + i.
+__global__ void __launch_bounds__(256) pf_silu_pack_kernel(const float* __restrict__ gu, uint32_t ffl, uint32_t f0,
+                                                           const PfOperands out) {
   const uint32_t row = blockIdx.y, i = blockIdx.x * 256u + threadIdx.x;
   if (i >= ffl) return;  // warp-uniform
   const float* r = gu + (size_t)row * 2u * ffl;
   const float g = r[i], u = r[ffl + i];
   // x * (1 / (1 + expf(-x))) (silu.c:17), then gate * up (text.c:417)
   const float h = __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), u);
-  pf_pack_group(h, row, i >> 5, threadIdx.x & 31u, ffl, pitch, aq, asc);
+  pf_pack_group_to(out, h, row, (f0 + i) >> 5, threadIdx.x & 31u);
 }
 
 // ---------------------------------------------------------------------------
-// Tensor-parallel partial-sum exchange (push model, like the decode step's)
+// Tensor-parallel exchange (push model, like the decode step's)
 // ---------------------------------------------------------------------------
 struct PfXchgParams {
-  float* x;              // [m][n] residual rows of this rank
-  const float* slots;    // this rank's receive slots; source q at slots + q * stride
-  size_t stride;         // floats
-  uint32_t m, n, world, epoch;
-  uint32_t* pub_flag[8];
-  const uint32_t* wait_flag;
-  uint32_t* err;
+  XchgSync xs;
+  float* x;         // [m][n] residual rows (identical on every rank)
+  const float* src;  // [m][n] rows every rank pushed its slice of, or nullptr
+  uint32_t m, n;
 };
 
-// The sources' GEMMs wrote their partial rows into this rank's slots with
-// plain stores and completed before this kernel started (stream order);
-// CTA 0's system-scope fence and release stores announce this rank's own
-// push, every CTA waits for all sources, then adds the slots in rank order
-// (the decode step's order: x + ((p_0 + p_1) + ...)).
-__global__ void __launch_bounds__(256) pf_xchg_add_kernel(const PfXchgParams p) {
-  __shared__ uint32_t s_ok;
-  if (threadIdx.x == 0) s_ok = 1u;
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    __threadfence_system();
-    for (uint32_t q = 0; q < p.world; ++q) st_release_sys(p.pub_flag[q], p.epoch);
-  }
-  __syncthreads();
-  if (threadIdx.x < p.world) {
-    const uint32_t* f = p.wait_flag + threadIdx.x;
-    if (ld_acquire_sys(f) < p.epoch) {
-      const uint64_t t0 = global_timer_ns();
-      while (ld_acquire_sys(f) < p.epoch) {
-        if (global_timer_ns() - t0 > EOS_WAIT_LIMIT_NS) {
-          report(p.err, EOS_DEVERR_PEER);
-          s_ok = 0u;
-          break;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  if (!s_ok) return;  // a peer never arrived: the error bit is set
+// The ranks' GEMMs or packing kernels wrote their slices into this rank's
+// buffer with plain stores and completed before this kernel started (stream
+// order); CTA 0 announces this rank's own push, every CTA waits for the other
+// ranks' flags (its own rank's data is local and complete), then, for the
+// residual exchanges, x[i] += src[i] -- the reference's x + t, exactly the
+// single-GPU epilogue's add.
+__global__ void __launch_bounds__(256) pf_xchg_kernel(const PfXchgParams p) {
+  if (!xchg_handshake(p.xs, blockIdx.x == 0, true)) return;  // a peer never arrived: error bit set
+  if (p.src == nullptr) return;
   const size_t n4 = (size_t)p.m * p.n / 4u;
   float4* x4 = reinterpret_cast<float4*>(p.x);
   for (size_t i = (size_t)blockIdx.x * 256u + threadIdx.x; i < n4; i += (size_t)gridDim.x * 256u) {
-    float4 t = __ldcg(reinterpret_cast<const float4*>(p.slots) + i);
-    for (uint32_t q = 1; q < p.world; ++q) {
-      const float4 u = __ldcg(reinterpret_cast<const float4*>(p.slots + q * p.stride) + i);
-      t = make_float4(__fadd_rn(t.x, u.x), __fadd_rn(t.y, u.y), __fadd_rn(t.z, u.z), __fadd_rn(t.w, u.w));
-    }
+    const float4 t = __ldcg(reinterpret_cast<const float4*>(p.src) + i);
     const float4 v = x4[i];
     x4[i] = make_float4(__fadd_rn(v.x, t.x), __fadd_rn(v.y, t.y), __fadd_rn(v.z, t.z), __fadd_rn(v.w, t.w));
   }
@@ -427,36 +425,56 @@ cudaError_t attn_launch(const PfAttnParams& p, cudaStream_t st) {
 }
 }  // namespace
 
+namespace {
+PfOperands operands(void* act, uint32_t m, uint32_t k, void* const* extra, uint32_t n_extra) {
+  PfOperands d{};
+  d.n = 1u + n_extra;
+  d.k = k;
+  d.pitch = pf_pad4(m);
+  d.aq[0] = act_q(act);
+  d.asc[0] = act_sc(act, m, k);
+  for (uint32_t j = 0; j < n_extra; ++j) {
+    d.aq[1 + j] = act_q(extra[j]);
+    d.asc[1 + j] = act_sc(extra[j], m, k);
+  }
+  return d;
+}
+}  // namespace
+
 cudaError_t launch_pf_attn(const float* qkv, const float* kc, const float* vc, void* act, uint32_t m, uint32_t hl,
                            uint32_t kvl, uint32_t h0, uint32_t kv0, uint32_t n_head, uint32_t n_kv_head,
-                           uint32_t hd, uint32_t pos0, float scale, cudaStream_t st) {
+                           uint32_t hd, uint32_t pos0, float scale, uint32_t k_total, void* const* act_extra,
+                           uint32_t n_extra, cudaStream_t st) {
   if (m == 0 || hl == 0) return cudaSuccess;
-  PfAttnParams p{qkv, kc, vc, act_q(act), act_sc(act, m, hl * hd), m, hl, kvl, h0, kv0, n_head, n_kv_head,
-                 pos0, scale};
+  if (n_extra >= kPfMaxDst || (h0 + hl) * hd > k_total) return cudaErrorInvalidValue;
+  PfAttnParams p{qkv, kc, vc, operands(act, m, k_total, act_extra, n_extra), m, hl, kvl, h0, kv0, n_head,
+                 n_kv_head, pos0, scale};
   if (hd == 64) return attn_launch<2>(p, st);
   if (hd == 128) return attn_launch<4>(p, st);
   if (hd == 256) return attn_launch<8>(p, st);
   return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_pf_xchg_add(float* x, const float* slots, size_t stride, uint32_t m, uint32_t n, uint32_t world,
-                               uint32_t* const* pub_flag, const uint32_t* wait_flag, uint32_t epoch, uint32_t* err,
-                               cudaStream_t st) {
-  if (m == 0 || world < 2 || world > 8 || n % 4u) return cudaErrorInvalidValue;
-  PfXchgParams p{x, slots, stride, m, n, world, epoch, {}, wait_flag, err};
-  for (uint32_t q = 0; q < world; ++q) p.pub_flag[q] = pub_flag[q];
-  const size_t n4 = (size_t)m * n / 4u;
-  size_t blocks = (n4 + 255u) / 256u;
-  if (blocks > 1184u) blocks = 1184u;  // grid-stride beyond 148 SMs x 8
-  pf_xchg_add_kernel<<<(uint32_t)blocks, 256, 0, st>>>(p);
+cudaError_t launch_pf_xchg(const XchgSync& xs, float* x, const float* src, uint32_t m, uint32_t n, cudaStream_t st) {
+  if (xs.world < 2 || xs.world > 8 || n % 4u) return cudaErrorInvalidValue;
+  PfXchgParams p{xs, x, src, m, n};
+  size_t blocks = 1;
+  if (src != nullptr) {
+    const size_t n4 = (size_t)m * n / 4u;
+    blocks = (n4 + 255u) / 256u;
+    if (blocks > 1184u) blocks = 1184u;  // grid-stride beyond 148 SMs x 8
+    if (blocks == 0) blocks = 1;
+  }
+  pf_xchg_kernel<<<(uint32_t)blocks, 256, 0, st>>>(p);
   return cudaGetLastError();
 }
 
-cudaError_t launch_pf_silu_pack(const float* gu, uint32_t m, uint32_t ffl, void* act, cudaStream_t st) {
+cudaError_t launch_pf_silu_pack(const float* gu, uint32_t m, uint32_t ffl, void* act, uint32_t f0, uint32_t k_total,
+                                void* const* act_extra, uint32_t n_extra, cudaStream_t st) {
   if (m == 0 || ffl == 0) return cudaSuccess;
-  if (ffl % 32u) return cudaErrorInvalidValue;
-  pf_silu_pack_kernel<<<dim3((ffl + 255u) / 256u, m), 256, 0, st>>>(gu, ffl, pf_pad4(m), act_q(act),
-                                                                      act_sc(act, m, ffl));
+  if (ffl % 32u || f0 % 32u || f0 + ffl > k_total || n_extra >= kPfMaxDst) return cudaErrorInvalidValue;
+  pf_silu_pack_kernel<<<dim3((ffl + 255u) / 256u, m), 256, 0, st>>>(gu, ffl, f0,
+                                                                      operands(act, m, k_total, act_extra, n_extra));
   return cudaGetLastError();
 }
 

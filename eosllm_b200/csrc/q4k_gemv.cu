@@ -170,7 +170,20 @@ struct Q4kGemvParams {
   // receive buffers, mapped through CUDA IPC), written after c
   float* c_extra[7];
   uint32_t n_extra;
+  // tensor parallel (xs.world > 1): the other ranks pushed parts of `act`;
+  // handshake before reading it
+  XchgSync xs;
 };
+
+// The tensor-parallel handshake of a GEMV CTA (no-op on one GPU): after the
+// PDL wait, before the activations are read.  On a timeout the CTA drains its
+// weight copies and leaves (outputs unwritten, error bit set).
+__device__ __forceinline__ bool gemv_handshake(const Q4kGemvParams& p) {
+  if (p.xs.world < 2) return true;
+  if (xchg_handshake(p.xs, blockIdx.x == 0, true)) return true;
+  cp_async_wait<0>();
+  return false;
+}
 
 // c[r] = v and the same value into every extra destination (other GPUs'
 // receive slots, plain stores over NVLink).  No fence here: the consumer
@@ -221,6 +234,7 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParam
   for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(warp + d * NW, d);
 
   pdl_wait();  // the activations are the previous kernel's output
+  if (!gemv_handshake(p)) return;
   if (p.a != nullptr) {
     pack_into_smem<NW>(p.a, p.k, act_s, warp, lane);
   } else {
@@ -333,6 +347,7 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_cols_kernel(const Q4kGemv
   for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(d);
 
   pdl_wait();
+  if (!gemv_handshake(p)) return;
   if (p.a != nullptr) {
     pack_into_smem<NW>(p.a, p.k, act_s, warp, lane);
   } else {
@@ -475,7 +490,7 @@ void set_q4k_gemv_variant(int v) {
 
 cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
                             uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status,
-                            float* const* c_extra, uint32_t n_extra) {
+                            float* const* c_extra, uint32_t n_extra, const XchgSync* xs) {
   if (n_extra > 7) {
     *out_status = EOS_E_INVALID_ARG;
     return cudaSuccess;
@@ -540,7 +555,8 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   geom(cfg, R, pitch, cb);
   const uint32_t smem = smem_of(cfg);
   if (smem > (uint32_t)max_smem) {  // rows too long to stage: unstaged kernel
-    if (act == nullptr || n_extra != 0) {  // it reads packed activations, writes one destination
+    // it reads packed activations, writes one destination, has no handshake
+    if (act == nullptr || n_extra != 0 || (xs != nullptr && xs->world > 1)) {
       *out_status = EOS_E_UNSUPPORTED;
       return cudaSuccess;
     }
@@ -563,8 +579,9 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   uint32_t grid = (uint32_t)num_sms * cps;
   const uint32_t max_grid = (n + R - 1) / R;
   if (grid > max_grid) grid = max_grid;
-  Q4kGemvParams prm{w, act, a, c, n, k, nb, row_bytes, pitch, R, act_bytes, cb, nch, err, {}, n_extra};
+  Q4kGemvParams prm{w, act, a, c, n, k, nb, row_bytes, pitch, R, act_bytes, cb, nch, err, {}, n_extra, {}};
   for (uint32_t j = 0; j < n_extra; ++j) prm.c_extra[j] = c_extra[j];
+  if (xs != nullptr) prm.xs = *xs;
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
   lc.blockDim = dim3(cfg.nw * 32);

@@ -80,6 +80,7 @@ struct Q80GemvParams {
   uint32_t* err;
   float* c_extra[7];  // further copies of every output (tensor-parallel push)
   uint32_t n_extra;
+  XchgSync xs;  // tensor parallel (world > 1): the other ranks pushed parts of `a`
 };
 
 // Four signed bytes -> two float2 of exact values: 2^23 + (b + 128) built by
@@ -160,6 +161,10 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
   for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(d, d);
 
   pdl_wait();  // the activations may be the previous kernel's output
+  if (p.xs.world > 1 && !xchg_handshake(p.xs, blockIdx.x == 0, true)) {
+    cp_async_wait<0>();  // a peer never arrived: drain, leave the outputs unwritten
+    return;
+  }
   {
     const float4* src = reinterpret_cast<const float4*>(p.a);
     for (uint32_t t = threadIdx.x; t < (p.k >> 2); t += NW * 32) {
@@ -219,7 +224,7 @@ void set_q80_gemv_variant(int v) { g_q80_variant = v; }
 
 cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t n, uint32_t k, uint32_t* err,
                             int num_sms, int max_smem, cudaStream_t st, int* out_status, float* const* c_extra,
-                            uint32_t n_extra) {
+                            uint32_t n_extra, const XchgSync* xs) {
   if (n_extra > 7) {
     *out_status = EOS_E_INVALID_ARG;
     return cudaSuccess;
@@ -249,7 +254,7 @@ cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t
   }
   if (!aligned || pick < 0 ||
       act_region + (uint32_t)(g_q80_cfgs[pick].nw * g_q80_cfgs[pick].d) * pitch > (uint32_t)max_smem) {
-    if (n_extra != 0) {  // the unstaged kernel writes one destination
+    if (n_extra != 0 || (xs != nullptr && xs->world > 1)) {  // the unstaged kernel: one destination, no handshake
       *out_status = EOS_E_UNSUPPORTED;
       return cudaSuccess;
     }
@@ -267,8 +272,9 @@ cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t
   if (cps < 1u) cps = 1u;
   uint32_t grid = (uint32_t)num_sms * cps;
   if (grid > n) grid = n;
-  Q80GemvParams prm{w, a, c, n, k, nblk, row_bytes, pitch, cb, chunks, err, {}, n_extra};
+  Q80GemvParams prm{w, a, c, n, k, nblk, row_bytes, pitch, cb, chunks, err, {}, n_extra, {}};
   for (uint32_t j = 0; j < n_extra; ++j) prm.c_extra[j] = c_extra[j];
+  if (xs != nullptr) prm.xs = *xs;
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
   lc.blockDim = dim3(cfg.nw * 32);

@@ -106,6 +106,17 @@ class TextDecoder:
         buf = (C.c_ubyte * len(blob)).from_buffer_copy(blob)
         B.check(self.lib.eosi_cuda_text_attach_peers(self.handle, buf, len(blob)), "eosi_cuda_text_attach_peers")
 
+    @staticmethod
+    def attach_local(ranks: list) -> None:
+        """eosi_cuda_text_attach_local: tensor-parallel ranks opened in this
+        one process (ranks[q] is rank q's decoder)."""
+        arr = (C.c_void_p * len(ranks))(*[r.handle.value for r in ranks])
+        B.check(B.load().eosi_cuda_text_attach_local(arr, len(ranks)), "eosi_cuda_text_attach_local")
+
+    def set_wait_limit(self, limit_us: int) -> None:
+        """Bound on every tensor-parallel flag wait, in microseconds."""
+        B.check(self.lib.eosi_cuda_text_set_wait_limit(self.handle, int(limit_us)), "eosi_cuda_text_set_wait_limit")
+
     def connect(self, group=None) -> None:
         """attach_peers with the handles all-gathered over a torch.distributed
         process group (any backend)."""
@@ -135,8 +146,8 @@ class TextDecoder:
 
     def prefill(self, tokens) -> None:
         """Feed `tokens` in one batched pass on the tensor cores (KV cache
-        rows, no logits); one GPU and Q4_K linears (EOS_E_UNSUPPORTED
-        otherwise)."""
+        rows, no logits); Q4_K linears (EOS_E_UNSUPPORTED otherwise), on one
+        GPU or tensor parallel."""
         p = np.ascontiguousarray(tokens, dtype=np.uint32)
         B.check(self.lib.eosi_cuda_text_prefill(self.handle, p.ctypes.data if p.size else None, p.size),
                 "eosi_cuda_text_prefill")
@@ -192,9 +203,10 @@ def partition(config: dict, rank: int, world: int) -> dict:
     for k in ("n_embd", "n_layer", "n_head", "n_kv_head", "n_ff", "n_vocab", "max_ctx"):
         setattr(d, k, int(config[k]))
     d.wdtype, d.out_dtype = int(config["wdtype"]), int(config["out_dtype"])
-    out = (C.c_uint32 * 9)()
+    out = (C.c_uint32 * 11)()
     B.check(B.load().eosi_cuda_text_partition(C.byref(d), rank, world, out), "eosi_cuda_text_partition")
-    keys = ("head_dim", "head0", "heads", "kv_head0", "kv_heads", "ff0", "ff_len", "vocab0", "vocab_len")
+    keys = ("head_dim", "head0", "heads", "kv_head0", "kv_heads", "ff0", "ff_len", "vocab0", "vocab_len",
+            "out_row0", "out_rows")
     return dict(zip(keys, list(out)))
 
 

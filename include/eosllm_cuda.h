@@ -92,6 +92,13 @@ EOSLLM_CUDA_API int eosi_cuda_matmul_q8_0(const float *a, const void *b_q8, floa
 EOSLLM_CUDA_API int eosi_cuda_cache_evict(const void *b_quant);
 EOSLLM_CUDA_API int eosi_cuda_cache_clear(void);
 
+/* Counters of the host-pointer path (reading them launches nothing): the matmuls completed on
+ * the GPU through eosi_cuda_matmul_q / _q4_k / _q8_0 since the library was
+ * loaded, and the weight-cache entries (one per weight and device) with their
+ * device bytes.  An engine integration reads them to confirm that its
+ * dispatch really routes matmul_q here.  NULL arguments are skipped. */
+EOSLLM_CUDA_API int eosi_cuda_host_stats(uint64_t *calls, uint64_t *cached_weights, uint64_t *cached_bytes);
+
 /* Upload (or refresh) one weight buffer now instead of on first use. */
 EOSLLM_CUDA_API int eosi_cuda_cache_preload(const void *b_quant, int b_dtype, uint32_t n, uint32_t k);
 
@@ -285,19 +292,33 @@ EOSLLM_CUDA_API uint32_t eosi_cuda_text_pos(const eosi_cuda_text_t *t);
  * bytes), the host gathers all ranks' handles in rank order (e.g. an
  * all-gather over the process group) and passes them to
  * eosi_cuda_text_attach_peers, which maps the peers' buffers and builds the
- * step.  Per layer the ranks exchange the O-projection and down-projection
- * partial sums (each rank's GEMV writes its partial into every rank's
- * receive slot over NVLink; each rank sums the slots in rank order, so all
- * ranks hold the same residual stream) and at the
- * end their slice's greedy pick; every exchange is a flag handshake with a
- * one-second bound (EOS_E_INTERNAL when a rank never arrives).  Every rank
- * must make the same calls in the same order (step / generate / reset). */
+ * step.  Every matrix is split by output rows (the q/k/v rows of a rank's
+ * heads, the gate/up rows of its FFN units, a slice of the O and down output
+ * rows, a slice of the vocabulary), so every output element is computed
+ * whole on one rank, exactly as on one GPU.  Per layer the ranks exchange,
+ * by pushing into each other's buffers over NVLink, the attention output
+ * (packed for the O projection), the O output rows, the SiLU output (packed
+ * for the down projection) and the down output rows, and at the end their
+ * slice's greedy pick; every rank therefore holds the one-GPU residual
+ * stream bit for bit and picks the one-GPU tokens.  Every exchange is a flag
+ * handshake with a bounded wait (one second unless
+ * eosi_cuda_text_set_wait_limit says otherwise; EOS_E_INTERNAL when a rank
+ * never arrives).  Every rank must make the same calls in the same order
+ * (step / generate / prefill / reset). */
 #define EOSI_CUDA_IPC_HANDLE_BYTES 64
 EOSLLM_CUDA_API int eosi_cuda_text_ipc_handle(eosi_cuda_text_t *t, void *out, size_t cap);
 EOSLLM_CUDA_API int eosi_cuda_text_attach_peers(eosi_cuda_text_t *t, const void *handles, size_t bytes);
-/* This rank's slice of the model (host only, no GPU needed): out[9] =
+/* The same attachment for ranks opened in ONE process (one host thread
+ * driving every rank; ranks on different devices get peer access enabled):
+ * ranks[q] is rank q's decoder.  Every rank must then be stepped; a rank
+ * that is not makes the others' next exchange run into its bounded wait. */
+EOSLLM_CUDA_API int eosi_cuda_text_attach_local(eosi_cuda_text_t *const *ranks, int world);
+/* Bound on every tensor-parallel flag wait of this decoder, in microseconds
+ * (default 1000000). */
+EOSLLM_CUDA_API int eosi_cuda_text_set_wait_limit(eosi_cuda_text_t *t, uint32_t limit_us);
+/* This rank's slice of the model (host only, no GPU needed): out[11] =
  * {head_dim, head0, heads, kv_head0, kv_heads, ff0, ff_len, vocab0,
- * vocab_len}. */
+ * vocab_len, out_row0, out_rows} (out_row*: the O / down output rows). */
 EOSLLM_CUDA_API int eosi_cuda_text_partition(const eosi_cuda_llama_t *m, int rank, int world, uint32_t *out);
 /* The decoder's cudaStream_t (as void*), for timing with events. */
 EOSLLM_CUDA_API void *eosi_cuda_text_stream(eosi_cuda_text_t *t);

@@ -59,12 +59,20 @@ def llama_tokens(n_vocab: int) -> list[str]:
     return ["<s>", "</s>"] + [f"t{i}" for i in range(n_vocab - 2)]
 
 
-def write_llama(path: str, model: dict) -> None:
-    """model: dict from oracle.llama.make_llama (numpy arrays + config)."""
-    write_gguf(path, *llama_parts(model))
+def byte_fallback_tokens(n_vocab: int) -> list[str]:
+    """A vocabulary the engine's BPE tokenizer can encode any text with: the
+    256 byte tokens <0xNN> (its fallback set) after <s>, </s>, then fillers."""
+    assert n_vocab >= 258
+    return ["<s>", "</s>"] + [f"<0x{b:02X}>" for b in range(256)] + [f"t{i}" for i in range(n_vocab - 258)]
 
 
-def llama_parts(model: dict):
+def write_llama(path: str, model: dict, tokens: list[str] | None = None) -> None:
+    """model: dict from oracle.llama.make_llama (numpy arrays + config);
+    tokens: the vocabulary strings (default llama_tokens)."""
+    write_gguf(path, *llama_parts(model, tokens))
+
+
+def llama_parts(model: dict, tokens: list[str] | None = None):
     """(metadata, tensors) of write_llama, for tests that alter single items."""
     c = model["config"]
     meta = [("general.architecture", "llama"), ("general.alignment", ALIGN),
@@ -73,7 +81,8 @@ def llama_parts(model: dict):
             ("llama.feed_forward_length", c["n_ff"]), ("llama.context_length", c["max_ctx"]),
             ("llama.rope.freq_base", float(c["rope_base"])),
             ("llama.attention.layer_norm_rms_epsilon", float(c["rms_eps"])),
-            ("tokenizer.ggml.model", "llama"), ("tokenizer.ggml.tokens", llama_tokens(c["n_vocab"]))]
+            ("tokenizer.ggml.model", "llama"),
+            ("tokenizer.ggml.tokens", tokens if tokens is not None else llama_tokens(c["n_vocab"]))]
     wt = GGML_Q4_K if c["wdtype"] == 33 else GGML_Q8_0
     ot = GGML_Q4_K if c["out_dtype"] == 33 else GGML_Q8_0
     E, V, F, H = c["n_embd"], c["n_vocab"], c["n_ff"], c["n_embd"] // c["n_head"] * c["n_kv_head"]

@@ -29,10 +29,17 @@ _u32 = C.c_uint32
 
 
 def build(ref: bool = False) -> None:
-    """Compile liboracle.so (and oracle/_ref when the reference tree exists)."""
+    """Compile liboracle.so (and, with ref, oracle/_ref: the recipe builds it
+    where the reference tree exists and leaves it alone elsewhere)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if ref and os.path.isdir(os.environ.get("EOS_REFERENCE_DIR", "/root/reference")):
+    if ref:
         subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+
+
+def reference_dir() -> str:
+    """Where the recipe (oracle/Makefile) looks for the reference tree."""
+    return subprocess.run(["make", "-s", "-C", HERE, "print-ref"], check=True, capture_output=True,
+                          text=True).stdout.strip()
 
 
 def _ptr(a: np.ndarray):

@@ -37,9 +37,10 @@ def test_header_is_plain_c(tmp_path):
 def test_backend_glue_compiles_against_engine_headers(tmp_path):
     """eosllm_b200/host/cuda_backend.c is C99 against the engine's own
     include/eosllm/backend.h (present where the reference tree is)."""
-    ref_inc = os.path.join(os.environ.get("EOS_REFERENCE_DIR", "/root/reference"), "include")
+    from oracle.oracle import reference_dir
+    ref_inc = os.path.join(reference_dir(), "include")
     if not os.path.isdir(ref_inc):
-        pytest.skip("engine headers not present on this machine")
+        pytest.skip(f"engine headers not present on this machine ({ref_inc})")
     src = os.path.join(ROOT, "eosllm_b200", "host", "cuda_backend.c")
     for flag in ("-DEOSLLM_HAVE_KERNEL_CUDA=1", "-DEOSLLM_HAVE_KERNEL_CUDA=0"):
         subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic", flag, "-I", ref_inc,

@@ -1,7 +1,8 @@
 """Tensor-parallel sharding of the decoder, host side: two gloo ranks on the
 CPU query their slice through the C ABI (eosi_cuda_text_partition, no GPU
-needed) and check that the slices tile every dimension exactly once, and that
-the IPC-handle all-gather the decoder uses moves the bytes intact."""
+needed) and check that the slices tile every dimension exactly once -- heads,
+FFN units, vocabulary rows and the O / down output rows -- and that the
+IPC-handle all-gather the decoder uses moves the bytes intact."""
 from __future__ import annotations
 
 import os
@@ -55,16 +56,16 @@ def test_two_rank_partitions_tile_the_model(cuda_lib, world):
         views = results[0][0][ci]
         assert views == results[1][0][ci]  # every rank sees the same table
         for key0, keyl, total in (("head0", "heads", cfg["n_head"]), ("kv_head0", "kv_heads", cfg["n_kv_head"]),
-                                  ("ff0", "ff_len", cfg["n_ff"]), ("vocab0", "vocab_len", cfg["n_vocab"])):
+                                  ("ff0", "ff_len", cfg["n_ff"]), ("vocab0", "vocab_len", cfg["n_vocab"]),
+                                  ("out_row0", "out_rows", cfg["n_embd"])):
             pos = 0
             for r in range(world):
                 assert views[r][key0] == pos, (cfg, key0, r)
                 assert views[r][keyl] > 0
                 pos += views[r][keyl]
             assert pos == total, (cfg, key0)
-        blk = 256 if cfg["wdtype"] == 33 else 32
-        for r in range(world):
-            assert views[r]["ff0"] % blk == 0 and views[r]["ff_len"] % blk == 0
+        for r in range(world):  # FFN units in whole 32-element packing groups
+            assert views[r]["ff0"] % 32 == 0 and views[r]["ff_len"] % 32 == 0
             assert views[r]["head_dim"] == cfg["n_embd"] // cfg["n_head"]
     for r in range(world):
         assert results[r][1] == [bytes((q * 37 + i) % 256 for i in range(64)) for q in range(world)]
