@@ -90,7 +90,7 @@ def parse():
     p.add_argument("--no-decode", action="store_true", help="skip the 7B-shape decode measurement")
     p.add_argument("--decode-prompt", type=int, default=512)
     p.add_argument("--decode-gen", type=int, default=256)
-    p.add_argument("--decode-cpu-steps", type=int, default=2, help="oracle decoder steps timed on the host")
+    p.add_argument("--decode-cpu-steps", type=int, default=2, help="reference-engine decode steps timed on the host (cpu_baseline)")
     return p.parse_args()
 
 
@@ -268,6 +268,30 @@ class CpuSweep:
         return f"{sample}, batch 1, {self.threads} threads over output rows"
 
 
+def host_cpu() -> dict:
+    """The host CPU every CPU number was measured on: model string and the
+    logical cores the OS offers."""
+    name = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"cpu": name, "nproc": os.cpu_count() or 1}
+
+
+def sweep_config(copies: int) -> dict:
+    """The workload of the headline sweep, identical in both arms."""
+    return {"workload": "q4k_gemv_sweep", "shapes": SHAPES, "batch": 1,
+            "weights": "Q4_K, ~N(0,0.02) (Irwin-Hall), own quantizer", "activations": "~N(0,1)",
+            "l2": f"inputs larger than the last-level cache: on the GPU {copies} rotating weight copies "
+                  f"({copies * sum(q4k_bytes(n, k) for n, k in SHAPES) / 1e6:.1f} MB) > 126 MB L2; the host "
+                  f"sweep's {sum(q4k_bytes(n, k) for n, k in SHAPES) / 1e6:.1f} MB > its L3"}
+
+
 def cpu_baseline(seconds: float, threads: int | None = None, dtype: int = DT_Q4_K,
                  row_fraction: float = 1.0) -> dict:
     """The reference's matmul_q slot on the host cores for `seconds`: Q4_K
@@ -282,8 +306,8 @@ def cpu_baseline(seconds: float, threads: int | None = None, dtype: int = DT_Q4_
     dt = time.perf_counter() - t0
     path = "Q4_K -> int8 AVX2 path" if dtype == DT_Q4_K else "Q8_0 -> scalar path"
     return {"value": round(cpu.step_bytes * steps / dt / 1e9, 3), "unit": "GB/s", "cores": cpu.threads,
-            "kind": cpu.kind, "sample": f"{steps} sweeps ({cpu.describe()}) in {dt:.1f} s, "
-                                        f"eosi_avx2_matmul_q ({path})"}
+            "kind": cpu.kind, **host_cpu(), "sample": f"{steps} sweeps ({cpu.describe()}) in {dt:.1f} s, "
+                                                      f"eosi_avx2_matmul_q ({path})"}
 
 
 def run_reference(args):
@@ -309,10 +333,9 @@ def run_reference(args):
         "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "q4k_gemv_sweep", "shapes": SHAPES, "batch": 1, "host_threads": cpu.threads,
-                   "sample": cpu.describe()},
+        "config": sweep_config(max(1, args.copies)),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu.threads, "kind": cpu.kind,
-                         "sample": cpu.describe()},
+                         **host_cpu(), "sample": cpu.describe()},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -524,12 +547,10 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(t_max / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "q4k_gemv_sweep", "shapes": SHAPES, "batch": 1,
-                       "weights": "Q4_K, ~N(0,0.02) (Irwin-Hall), own quantizer", "activations": "~N(0,1)",
-                       "l2": f"{R} rotating weight copies ({R * sum(q4k_bytes(n, k) for n, k in SHAPES) / 1e6:.1f}"
-                             " MB) > 126 MB L2",
-                       "timing": "CUDA graph of K steps (2 packing launches, one per distinct k, + 4 PDL-chained GEMVs each), CUDA events, max over ranks",
-                       "parallelism": f"row shards x{world}, no collective"},
+            "config": sweep_config(R),
+            "timing": f"CUDA graph of K steps (2 packing launches, one per distinct k, + 4 PDL-chained GEMVs "
+                      f"each) over {R} rotating weight copies, CUDA events, max over ranks",
+            "parallelism": f"row shards x{world}, no collective",
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": traffic,
@@ -839,23 +860,50 @@ def run_decode(args, dev, world, rank) -> dict:
         "reference_agreement": fixture_agreement(np.concatenate([first, toks]), P),
         "clocks": clocks.summary(),
     }
-    if host_model is not None:
-        # the reference's algorithm on the host (the C restatement, bit-exact
-        # with the engine): a few steps at position 0.., single thread
-        from oracle.llama import OracleDecoder
-        from oracle.oracle import Oracle
-        od = OracleDecoder(Oracle(), host_model)
-        t0 = time.perf_counter()
-        for t in prompt[:args.decode_cpu_steps]:
-            od.step(int(t))
-        dt = time.perf_counter() - t0
-        od.close()
-        out["cpu_baseline"] = {"value": round(args.decode_cpu_steps / dt, 4), "unit": "tok/s", "cores": 1,
-                               "kind": "port",
-                               "sample": f"{args.decode_cpu_steps} steps of orc_text_step at positions 0.. "
-                                         "(C restatement of eosi_text_step, AVX2-path arithmetic)"}
     dec.close()
+    if host_model is not None:
+        out["cpu_baseline"] = decode_cpu_baseline(host_model, prompt[:args.decode_cpu_steps], P + G)
     return out
+
+
+def decode_cpu_baseline(host_model: dict, tokens, max_ctx: int) -> dict:
+    """The reference engine itself on the host: the same model written as a
+    GGUF file, eos_model_open, then eosi_text_step with the op table the
+    engine's dispatch picks on an AVX2 host (oracle/_ref/libeosllm_ref.so,
+    compiled from the reference's sources; single-threaded, as the engine
+    is), a few steps at positions 0...  Falls back to the C restatement of
+    the same step (bit-exact with the engine) where oracle/_ref is absent."""
+    import tempfile
+
+    from oracle.oracle import REF_ENGINE
+    n = len(tokens)
+    if os.path.exists(REF_ENGINE):
+        from oracle.gguf_writer import write_llama
+        from oracle.llama import RefDecoder
+        with tempfile.TemporaryDirectory() as tmp:
+            path = os.path.join(tmp, "llama7b.gguf")
+            write_llama(path, host_model)
+            n_vocab = host_model["config"]["n_vocab"]
+            host_model.clear()
+            ref = RefDecoder(path, max_ctx, n_vocab)
+            t0 = time.perf_counter()
+            for t in tokens:
+                ref.step(int(t))
+            dt = time.perf_counter() - t0
+            ref.close()
+        return dict(value=round(n / dt, 4), unit="tok/s", cores=1, kind="reference", **host_cpu(),
+                    sample=f"{n} steps of the reference engine's eosi_text_step at positions 0.. "
+                           "(x86_avx2 matmul_q, scalar rmsnorm/rope/silu; the engine is single-threaded)")
+    from oracle.llama import OracleDecoder
+    from oracle.oracle import Oracle
+    od = OracleDecoder(Oracle(), host_model)
+    t0 = time.perf_counter()
+    for t in tokens:
+        od.step(int(t))
+    dt = time.perf_counter() - t0
+    od.close()
+    return dict(value=round(n / dt, 4), unit="tok/s", cores=1, kind="port", **host_cpu(),
+                sample=f"{n} steps of orc_text_step at positions 0.. (C restatement of eosi_text_step)")
 
 
 def main():
