@@ -386,7 +386,11 @@ def run_ours(args):
     # activations with the same k are rows of one matrix, packed in one launch
     ks = sorted({k for _, k in SHAPES})
     xmat = {k: torch.empty((sum(1 for _, kk in SHAPES if kk == k), k), dtype=torch.float32, device=dev) for k in ks}
-    smat = {k: torch.empty(B.q4_k_scratch_bytes(xmat[k].shape[0], k), dtype=torch.uint8, device=dev) for k in ks}
+    # packed activations, double-buffered: step i reads set i % 2 while the
+    # packing of step i + 1 fills the other set
+    smats = [{k: torch.empty(B.q4_k_scratch_bytes(xmat[k].shape[0], k), dtype=torch.uint8, device=dev) for k in ks}
+             for _ in range(2)]
+    smat = smats[0]
     row_of = {}
     for s, (n, k) in enumerate(SHAPES):
         row_of[s] = sum(1 for kk in [kk for _, kk in SHAPES[:s]] if kk == k)
@@ -404,20 +408,43 @@ def run_ours(args):
         scratch.append(smat[k].data_ptr() + row_of[s] * B.q4_k_scratch_bytes(1, k))
     torch.cuda.synchronize()
 
+    def scratch_of(s: int, i: int) -> int:
+        n, k = SHAPES[s]
+        return smats[i % 2][k].data_ptr() + row_of[s] * B.q4_k_scratch_bytes(1, k)
+
     def capture(steps: int):
         """One step: pack the four activation vectors (exact quantize_sub32
         packing; one launch per distinct k, the vectors being rows of one
-        matrix), then the four GEMVs back to back (PDL-chained)."""
+        matrix), then the four GEMVs back to back (PDL-chained).  The
+        packing of step i + 1 runs on a second stream while the GEMVs of step
+        i run (double-buffered packed activations; graph edges order each
+        packing after the GEMVs that last read its buffer and before the
+        GEMVs that read it), so the GEMV chain is not interrupted."""
         g = torch.cuda.CUDAGraph()
-        side = torch.cuda.Stream(device=dev)
-        with torch.cuda.graph(g, stream=side, capture_error_mode="relaxed"):
-            st = torch.cuda.current_stream().cuda_stream
-            for i in range(steps):
-                r = i % R
+        main = torch.cuda.Stream(device=dev)
+        packer = torch.cuda.Stream(device=dev)
+        packed = [torch.cuda.Event() for _ in range(steps + 1)]
+        gemvs_done = [torch.cuda.Event() for _ in range(steps)]
+        with torch.cuda.graph(g, stream=main, capture_error_mode="relaxed"):
+            st, ps = main.cuda_stream, packer.cuda_stream
+            packer.wait_stream(main)  # fork the packing stream into the capture
+
+            def pack(i: int) -> None:
                 for k in ks:
-                    B.q4_k_pack_act_dev(xmat[k], xmat[k].shape[0], k, smat[k], st)
+                    B.q4_k_pack_act_dev(xmat[k], xmat[k].shape[0], k, smats[i % 2][k], ps)
+                packed[i].record(packer)
+
+            pack(0)
+            for i in range(steps):
+                if i + 1 < steps:
+                    if i >= 1:
+                        packer.wait_event(gemvs_done[i - 1])  # step i - 1 read the buffer step i + 1 fills
+                    pack(i + 1)
+                main.wait_event(packed[i])
                 for s, (n, k) in enumerate(SHAPES):
-                    B.q4_k_gemv_dev(scratch[s], weights[s][r], outs[s], n, k, st)
+                    B.q4_k_gemv_dev(scratch_of(s, i), weights[s][i % R], outs[s], n, k, st)
+                gemvs_done[i].record(main)
+            main.wait_stream(packer)  # join
         return g
 
     def capture_train(s: int, launches: int):
@@ -549,7 +576,8 @@ def run_ours(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": sweep_config(R),
             "timing": f"CUDA graph of K steps (2 packing launches, one per distinct k, + 4 PDL-chained GEMVs "
-                      f"each) over {R} rotating weight copies, CUDA events, max over ranks",
+                      f"each; the packing of step i + 1 on a second stream during the GEMVs of step i) over {R} "
+                      "rotating weight copies, CUDA events, max over ranks",
             "parallelism": f"row shards x{world}, no collective",
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,

@@ -99,7 +99,6 @@ _SIGNATURES = {
     "eosi_cuda_text_attach_peers": (C.c_int, [_vp, _vp, _sz]),
     "eosi_cuda_text_attach_local": (C.c_int, [_vp, C.c_int]),
     "eosi_cuda_text_set_wait_limit": (C.c_int, [_vp, _u32]),
-    "eosi_cuda_text_set_l2_warm": (C.c_int, [_vp, C.c_int]),
     "eosi_cuda_text_partition": (C.c_int, [_vp, C.c_int, C.c_int, _vp]),
     "eosi_cuda_text_close": (None, [_vp]),
 }

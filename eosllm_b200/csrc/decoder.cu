@@ -77,8 +77,6 @@ struct NormPackParams {
   // tensor parallel: `part` holds every rank's output rows, pushed by their
   // GEMVs; handshake before reading it
   XchgSync xs;
-  const uint8_t* pf;  // the next GEMV's weights, warmed into L2 (may be nullptr)
-  size_t pf_bytes;
 };
 
 constexpr uint32_t kNormMaxChunks = 16;  // float4 chunks per thread: n <= 16384
@@ -99,7 +97,6 @@ __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) 
   __shared__ float red[8];
   __shared__ __align__(16) float ys[256];
   pdl_trigger();
-  l2_prefetch_share(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);  // weights depend on nothing
   pdl_wait();
   if (p.xs.world > 1 && p.part != nullptr && !xchg_handshake(p.xs, blockIdx.x == 0, true))
     return;  // a peer never arrived: the error bit is set, outputs are invalid
@@ -197,8 +194,6 @@ struct AttnParams {
   uint32_t n_x;
   uint32_t hl, h0, kvl, kv0, n_head, n_kv_head, max_chunks;
   float base, scale;
-  const uint8_t* pf;  // the O projection's weights, warmed into L2 (may be nullptr)
-  size_t pf_bytes;
 };
 
 // pack_group_to_record into this rank's records and n_x further copies: the
@@ -240,7 +235,6 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
   __shared__ float s_lc[kMaxAttnChunks];  // merge: chunk sums
   __shared__ uint32_t s_last;
   pdl_trigger();
-  l2_prefetch_share(p.pf, p.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   const uint32_t hloc = blockIdx.x, c = blockIdx.y;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   // pos was written by the previous step's argmax_kernel, which completed
@@ -429,13 +423,10 @@ struct SiluParams {
   uint8_t* act_x[kMaxParts - 1];
   float* actf_x[kMaxParts - 1];
   uint32_t n_x;
-  const uint8_t* pf;  // the down projection's weights, warmed into L2 (may be nullptr)
-  size_t pf_bytes;
 };
 
 __global__ void __launch_bounds__(256) silu_pack_kernel(const SiluParams p) {
   pdl_trigger();
-  l2_prefetch_share(p.pf, p.pf_bytes, blockIdx.x, gridDim.x);
   pdl_wait();
   const uint32_t i = blockIdx.x * 256u + threadIdx.x;
   if (i >= p.ffl) return;  // warp-uniform: ffl % 32 == 0
@@ -690,9 +681,6 @@ struct TextDecoder {
   std::vector<void*> pf_wres;
   bool pf_resident = true;  // allow pf_wres (eosi_cuda_text_set_prefill_resident)
   uint32_t prefill_min = 16;
-  // the step's latency-bound kernels warm the next GEMV's weights into L2
-  // (eosi_cuda_text_set_l2_warm; on by default)
-  bool l2_warm = true;
 
   template <typename T>
   cudaError_t alloc(T** p, size_t bytes) {
@@ -992,12 +980,8 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
   // x_out = x_in + part (part: d_full / o_full, pushed by every rank), then
   // rmsnorm and the packing for a consumer of dtype dt_a
   auto norm_pack = [&](const float* x_in, const float* part, float* x_out, const float* w, int dt_a, uint32_t type,
-                       uint32_t xk, const uint8_t* pf, size_t pf_bytes) -> cudaError_t {
+                       uint32_t xk) -> cudaError_t {
     NormPackParams p{};
-    if (l2_warm) {
-      p.pf = pf;
-      p.pf_bytes = pf_bytes;
-    }
     p.x_in = x_in;
     p.part = part;
     p.xs = xsync(type, xk);
@@ -1016,7 +1000,7 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
     const DecLayer& d = layers[L];
     // x1 = (L == 0 ? embedding : x0 + down output); act_e = pack(rmsnorm(x1))
     e = norm_pack(L == 0 ? nullptr : x0, L == 0 ? nullptr : d_full, x1, d.attn_norm, wdt, kXDRows,
-                  L == 0 ? 0u : 4u * L - 1u, d.wqkv, wbytes(wdt, nqkv, E));
+                  L == 0 ? 0u : 4u * L - 1u);
     if (e == cudaSuccess) e = gemv(wdt, d.wqkv, act_e, actf_e, qkv, nqkv, E);
     if (e == cudaSuccess) {
       AttnParams a{};
@@ -1042,10 +1026,6 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
       a.max_chunks = max_chunks;
       a.base = m.rope_base;
       a.scale = 1.0f / sqrtf((float)hd);  // text.c:365
-      if (l2_warm) {
-        a.pf = d.wo;
-        a.pf_bytes = wbytes(wdt, el, E);
-      }
       const dim3 grid(hl, max_chunks);
       const uint32_t sm = attn_smem_bytes(hd);
       if (hd == 64) e = launch_pdl_smem(attn_kernel<2>, grid, dim3(128), sm, s, a);
@@ -1057,8 +1037,7 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
       e = gemv(wdt, d.wo, act_o, actf_o, o_full + e0, el, E, push_o, n_push, &xs);
     }
     // x0 = x1 + O output; act_e = pack(rmsnorm(x0))
-    if (e == cudaSuccess)
-      e = norm_pack(x1, o_full, x0, d.ffn_norm, wdt, kXORows, 4u * L + 1u, d.wgu, wbytes(wdt, 2 * ffl, E));
+    if (e == cudaSuccess) e = norm_pack(x1, o_full, x0, d.ffn_norm, wdt, kXORows, 4u * L + 1u);
     if (e == cudaSuccess) e = gemv(wdt, d.wgu, act_e, actf_e, gu, 2 * ffl, E);
     if (e == cudaSuccess) {
       SiluParams sp{};
@@ -1072,10 +1051,6 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
         sp.act_x[j] = act_d != nullptr ? push_ad[j] : nullptr;
         sp.actf_x[j] = actf_d != nullptr ? push_afd[j] : nullptr;
       }
-      if (l2_warm) {
-        sp.pf = d.wd;
-        sp.pf_bytes = wbytes(wdt, el, F);
-      }
       e = launch_pdl(silu_pack_kernel, dim3((ffl + 255u) / 256u), dim3(256), s, sp);
     }
     if (e == cudaSuccess) {  // this rank's down rows over all FFN units
@@ -1086,7 +1061,7 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
   // final norm + LM head + greedy pick (text.c:425-432, greedy.c:66-69)
   if (e == cudaSuccess)
     e = norm_pack(m.n_layer ? x0 : nullptr, m.n_layer ? d_full : nullptr, x1, out_norm, odt, kXDRows,
-                  m.n_layer ? 4u * m.n_layer - 1u : 0u, wout, wbytes(odt, vl, E));
+                  m.n_layer ? 4u * m.n_layer - 1u : 0u);
   if (e == cudaSuccess) e = gemv(odt, wout, act_e, actf_e, logits, vl, E);
   if (e == cudaSuccess) {
     ArgmaxParams a{};
@@ -1529,19 +1504,6 @@ EOSLLM_CUDA_API int eosi_cuda_text_attach_local(eosi_cuda_text_t* const* ranks, 
     if (s != EOS_OK) return s;
   }
   return EOS_OK;
-}
-
-EOSLLM_CUDA_API int eosi_cuda_text_set_l2_warm(eosi_cuda_text_t* t, int on) {
-  if (t == nullptr) return EOS_E_INVALID_ARG;
-  TextDecoder& d = t->d;
-  if (d.l2_warm == (on != 0)) return EOS_OK;
-  d.l2_warm = on != 0;
-  if (d.graph == nullptr) return EOS_OK;  // tensor parallel, not attached yet: capture() will see it
-  if (cudaSetDevice(d.device) != cudaSuccess) return EOS_E_INTERNAL;
-  cudaStreamSynchronize(d.st);
-  cudaGraphExecDestroy(d.graph);
-  d.graph = nullptr;
-  return d.capture();
 }
 
 EOSLLM_CUDA_API int eosi_cuda_text_set_wait_limit(eosi_cuda_text_t* t, uint32_t limit_us) {

@@ -131,28 +131,6 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// ---- L2 prefetch ---------------------------------------------------------
-// This CTA's share of an L2 warm-up of [base, base + bytes) (base 16-byte
-// aligned, bytes a multiple of 16): the range is cut into `nparts`
-// contiguous slices and slice `part` is prefetched into L2 in 16 KB pieces
-// spread over the CTA's threads (cp.async.bulk.prefetch.L2: no data reaches
-// the SM, nothing to wait for).  Latency-bound kernels of the decoder use it
-// to stream the next GEMV's weights while HBM would otherwise idle.
-__device__ __forceinline__ void l2_prefetch_share(const void* base, size_t bytes, uint32_t part, uint32_t nparts) {
-  if (base == nullptr || bytes == 0 || nparts == 0) return;
-  const size_t per = ((bytes + nparts - 1) / nparts + 15u) & ~(size_t)15u;
-  const size_t lo = per * part;
-  if (lo >= bytes) return;
-  const size_t hi = (lo + per) < bytes ? (lo + per) : bytes;
-  constexpr size_t kPiece = 16384;
-  for (size_t off = lo + (size_t)threadIdx.x * kPiece; off < hi; off += (size_t)blockDim.x * kPiece) {
-    const uint32_t n = (uint32_t)(((hi - off) < kPiece ? (hi - off) : kPiece) & ~(size_t)15u);
-    if (n)
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(static_cast<const char*>(base) + off), "r"(n)
-                   : "memory");
-  }
-}
-
 // ---- programmatic dependent launch --------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

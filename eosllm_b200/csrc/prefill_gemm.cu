@@ -42,10 +42,10 @@
 // and epilogue overlap.  A stage is released when its MMAs have completed
 // (tcgen05.commit) and all sixteen epilogue warps have read its scales.  The row sums c live
 // in shared memory (updated once per super-block), the partials in
-// registers; every operation is an IEEE round-to-nearest multiply or add,
-// issued as packed f32x2 instructions over column pairs (__fmul2_rn /
-// __fadd2_rn: per half exactly __fmul_rn / __fadd_rn, never contracted into
-// an FMA), which halves the epilogue's instruction count.
+// registers; every operation is a scalar IEEE round-to-nearest multiply or
+// add (__fmul_rn / __fadd_rn are never contracted into FMAs).  Packed f32x2
+// multiplies and adds were tried here: their results did not match the
+// scalar operations bit for bit, so they are not used.
 //
 // Waits are bounded (EOS_WAIT_LIMIT_NS): on a timeout the waiting role
 // records an error bit and stops; the MMA issuer always commits the "done"
@@ -193,18 +193,6 @@ __device__ __forceinline__ void qg_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// 16 consecutive accumulator columns (f32 bits) of this thread's TMEM lane.
-__device__ __forceinline__ void qg_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 // ---------------------------------------------------------------------------
 // GEMM
 // ---------------------------------------------------------------------------
@@ -327,12 +315,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     // 4 c4 .. 4 c4 + 3 at acc[32 c4]; super-block partials (updated every
     // sub-block) in registers, reset to 0 after each super-block
     float4* acc = reinterpret_cast<float4*>(acc_s) + e * (QG_COLS / 4u) * 32u + lane;
-    // partials of column pairs (2 p, 2 p + 1), for the packed f32x2 operations
-    float2 part[QG_COLS / 2];
+    float part[QG_COLS];
 #pragma unroll
     for (uint32_t c4 = 0; c4 < QG_COLS / 4; ++c4) acc[32 * c4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);  // c = 0 (:194)
 #pragma unroll
-    for (uint32_t c = 0; c < QG_COLS / 2; ++c) part[c] = make_float2(0.0f, 0.0f);  // partial = 0
+    for (uint32_t c = 0; c < QG_COLS; ++c) part[c] = 0.0f;  // partial = 0
     bool ok = true;
     for (uint32_t kb = 0; kb < nkb && ok; ++kb) {
       const uint32_t s = kb % QG_STAGES;
@@ -346,44 +333,39 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&tfull[a], (g / QG_ACCS) & 1u)) != 0;
         if (!ok) break;
         tc_fence_after();
-        const float as = as_s[(2u * j) * QG_BM + lrow], sum = as_s[(2u * j + 1u) * QG_BM + lrow];
-        const float2 as2 = make_float2(as, as), sum2 = make_float2(sum, sum);
-        // d*sc and -(dmin*m) of the thread's columns, as column pairs (broadcast)
-        const float2* dsc = reinterpret_cast<const float2*>(bs_s + (2u * j) * QG_BN + col0);
-        const float2* nmn = reinterpret_cast<const float2*>(bs_s + (2u * j + 1u) * QG_BN + col0);
-        // the thread's 32 accumulator columns in two halves of 16 (fewer live
-        // registers with 18 warps per SM)
-#pragma unroll
-        for (uint32_t hh = 0; hh < 2; ++hh) {
-          uint32_t r[16];
-          qg_ld16(tmem + ((quad * 32u) << 16) + a * QG_BN + col0 + 16u * hh, r);
-#pragma unroll
-          for (uint32_t q2 = 0; q2 < 8; ++q2) {
-            const uint32_t c2 = 8u * hh + q2;
-            // per column, t = ((d*sc)*as)*dot - ((dmin*m)*as)*sum (:254-261) as
-            // t1 + (-t2), then partial += t: the scalar form's IEEE
-            // round-to-nearest multiplies and adds, two columns per f32x2
-            // instruction (__fmul2_rn / __fadd2_rn: per half exactly
-            // __fmul_rn / __fadd_rn, never contracted into an FMA)
-            const float2 dot = make_float2(__uint_as_float(r[2u * q2]), __uint_as_float(r[2u * q2 + 1u]));
-            const float2 t1 = __fmul2_rn(__fmul2_rn(dsc[c2], as2), dot);
-            const float2 t2 = __fmul2_rn(__fmul2_rn(nmn[c2], as2), sum2);
-            part[c2] = __fadd2_rn(part[c2], __fadd2_rn(t1, t2));
-          }
-        }
+        uint32_t r[32];
+        qg_ld32(tmem + ((quad * 32u) << 16) + a * QG_BN + col0, r);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[a]);  // accumulator a may be overwritten
+        const float as = as_s[(2u * j) * QG_BM + lrow], sum = as_s[(2u * j + 1u) * QG_BM + lrow];
+        const float4* dsc = reinterpret_cast<const float4*>(bs_s + (2u * j) * QG_BN + col0);       // d*sc
+        const float4* nmn = reinterpret_cast<const float4*>(bs_s + (2u * j + 1u) * QG_BN + col0);  // -(dmin*m)
+#pragma unroll
+        for (uint32_t c4 = 0; c4 < QG_COLS / 4; ++c4) {
+          const float4 dd = dsc[c4], nn = nmn[c4];  // broadcast
+          const float d4[4] = {dd.x, dd.y, dd.z, dd.w}, n4[4] = {nn.x, nn.y, nn.z, nn.w};
+#pragma unroll
+          for (uint32_t i = 0; i < 4; ++i) {
+            const uint32_t c = 4u * c4 + i;
+            // t = ((d*sc)*as)*dot - ((dmin*m)*as)*sum   (:254-261), as t1 + (-t2)
+            const float t = __fadd_rn(__fmul_rn(__fmul_rn(d4[i], as), __uint_as_float(r[c])),
+                                      __fmul_rn(__fmul_rn(n4[i], as), sum));
+            part[c] = __fadd_rn(part[c], t);  // partial += t
+          }
+        }
         if ((g & 7u) == 7u) {  // super-block complete: c += partial (:264), partial = 0
 #pragma unroll
           for (uint32_t c4 = 0; c4 < QG_COLS / 4; ++c4) {
             float4 v = acc[32 * c4];
-            const float2 lo = __fadd2_rn(make_float2(v.x, v.y), part[2 * c4]);
-            const float2 hi = __fadd2_rn(make_float2(v.z, v.w), part[2 * c4 + 1]);
-            acc[32 * c4] = make_float4(lo.x, lo.y, hi.x, hi.y);
+            v.x = __fadd_rn(v.x, part[4 * c4]);
+            v.y = __fadd_rn(v.y, part[4 * c4 + 1]);
+            v.z = __fadd_rn(v.z, part[4 * c4 + 2]);
+            v.w = __fadd_rn(v.w, part[4 * c4 + 3]);
+            acc[32 * c4] = v;
           }
 #pragma unroll
-          for (uint32_t c = 0; c < QG_COLS / 2; ++c) part[c] = make_float2(0.0f, 0.0f);
+          for (uint32_t c = 0; c < QG_COLS; ++c) part[c] = 0.0f;
         }
       }
       __syncwarp();

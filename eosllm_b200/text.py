@@ -113,11 +113,6 @@ class TextDecoder:
         arr = (C.c_void_p * len(ranks))(*[r.handle.value for r in ranks])
         B.check(B.load().eosi_cuda_text_attach_local(arr, len(ranks)), "eosi_cuda_text_attach_local")
 
-    def set_l2_warm(self, on: bool) -> None:
-        """Warm the next GEMV's weights into L2 during the step's
-        latency-bound kernels (default on)."""
-        B.check(self.lib.eosi_cuda_text_set_l2_warm(self.handle, int(bool(on))), "eosi_cuda_text_set_l2_warm")
-
     def set_wait_limit(self, limit_us: int) -> None:
         """Bound on every tensor-parallel flag wait, in microseconds."""
         B.check(self.lib.eosi_cuda_text_set_wait_limit(self.handle, int(limit_us)), "eosi_cuda_text_set_wait_limit")

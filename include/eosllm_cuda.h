@@ -313,10 +313,6 @@ EOSLLM_CUDA_API int eosi_cuda_text_attach_peers(eosi_cuda_text_t *t, const void 
  * ranks[q] is rank q's decoder.  Every rank must then be stepped; a rank
  * that is not makes the others' next exchange run into its bounded wait. */
 EOSLLM_CUDA_API int eosi_cuda_text_attach_local(eosi_cuda_text_t *const *ranks, int world);
-/* on != 0 (default): the step's latency-bound kernels (rmsnorm + packing,
- * attention, SiLU + packing) warm the next GEMV's weights into L2 with bulk
- * prefetches while they run; 0: they do not (rebuilds the step graph). */
-EOSLLM_CUDA_API int eosi_cuda_text_set_l2_warm(eosi_cuda_text_t *t, int on);
 /* Bound on every tensor-parallel flag wait of this decoder, in microseconds
  * (default 1000000). */
 EOSLLM_CUDA_API int eosi_cuda_text_set_wait_limit(eosi_cuda_text_t *t, uint32_t limit_us);
