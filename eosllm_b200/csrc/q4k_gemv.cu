@@ -468,9 +468,7 @@ GemvConfig g_cfgs[] = {
     {q4k_gemv_kernel<20, 2>, 20, 2, 0, {}, nullptr, {}}, {q4k_gemv_kernel<12, 3>, 12, 3, 0, {}, nullptr, {}},
     {q4k_gemv_kernel<16, 2>, 16, 2, 0, {}, nullptr, {}}, {q4k_gemv_kernel<10, 4>, 10, 4, 0, {}, nullptr, {}},
     EOS_COLS_CFG(12, 2, 4), EOS_COLS_CFG(16, 3, 2), EOS_COLS_CFG(8, 3, 4),  EOS_COLS_CFG(16, 2, 2),
-    EOS_COLS_CFG(8, 2, 2),  EOS_COLS_CFG(12, 3, 2), EOS_COLS_CFG(16, 2, 1), EOS_COLS_CFG(8, 4, 2),
-    EOS_COLS_CFG(4, 2, 2),  EOS_COLS_CFG(4, 3, 2),  EOS_COLS_CFG(4, 4, 2),  EOS_COLS_CFG(6, 2, 2),
-    EOS_COLS_CFG(4, 2, 4)};
+    EOS_COLS_CFG(8, 2, 2),  EOS_COLS_CFG(12, 3, 2), EOS_COLS_CFG(16, 2, 1), EOS_COLS_CFG(8, 4, 2)};
 #undef EOS_COLS_CFG
 constexpr int kNumCfgs = sizeof(g_cfgs) / sizeof(g_cfgs[0]);
 int g_q4k_variant = -1;  // kernel config override (-1: automatic)

@@ -2,25 +2,33 @@
 // with an fp16 scale per 32), the production Q8_0 path of every reference
 // backend: eosi_scalar_matmul_q8_0 (src/kernels/scalar/matmul_q8.c:21-58).
 //
-// Same skeleton as the Q4_K GEMV: each CTA owns a contiguous slab of weight
-// rows; warp w of NW streams rows w, w+NW, ... HBM -> shared memory with
-// coalesced 16-byte cp.async copies through D private buffers.  The f32
-// activation vector is copied once per CTA into shared memory at a 144-byte
-// stride per 32 values (== 16 mod 128), so lanes reading different blocks hit
-// different banks.  One lane takes a whole 32-weight block: block j of a row
-// sits at byte 34j (only 2-byte aligned), so the lane loads the nine aligned
-// words around it and realigns the data with one byte permute per word; each
-// int8 becomes an exact float through the 2^23 magic (prmt + packed subtract),
-// and the products accumulate with packed fp32x2 FMAs.  Per-lane partials
-// are reduced across the warp at the end of the row.  The summation order
-// differs from the reference's sequential loop, so results agree to fp32
-// rounding (the tests bound it), not bit for bit.
+// The reference multiplies every int8 weight, converted to float, by the f32
+// activation.  Converting four bytes at a time to floats costs more integer
+// instructions than the dot itself, so the staged kernel moves the
+// conversion to the activations, once per CTA: each 32-value activation block
+// becomes block-float integers (a power-of-two scale per block, 20-bit signed
+// values, exact scaling, rounding error at most 2^-21 of the block's largest
+// magnitude) held as three signed base-128 digits of int8, and a weight
+// block's dot with it is three exact integer dp4a chains recombined in f32.
+// Results agree with the reference's f32 loop to fp32 rounding (the tests
+// bound it at 1e-3 relative plus 1e-3 rms), not bit for bit -- the summation
+// order differs anyway.
+//
+// Skeleton as the Q4_K GEMV: each CTA owns a contiguous slab of weight rows,
+// which is one contiguous byte range; warp w streams stages w, w + NW, ... of
+// 256 blocks (8704 bytes, 32 groups of 8 blocks) HBM -> shared memory with
+// coalesced 16-byte cp.async copies through D private buffers, issued before
+// the PDL wait.  Lane l of a stage takes group l: 8 consecutive blocks of
+// one row, 272 bytes at a 16-byte aligned offset, so block c of every lane's
+// group starts at the same position mod 16 and the realignment of its 2-byte
+// aligned data is the same compile-time byte permute in every lane (3
+// conflict-free 16-byte loads per block).  Group sums go to shared memory;
+// at the end one thread per row adds its groups in order (deterministic).
 #include "eos_common.cuh"
 #include "eos_kernels.h"
 
 namespace eos {
 
-constexpr uint32_t kQ8ActStride = 36;  // floats per 32-value block in shared memory
 
 // ---------------------------------------------------------------------------
 // Unstaged fallback: any k % 32 == 0 and any alignment of the weights.
@@ -71,140 +79,168 @@ __global__ void __launch_bounds__(256) q80_gemv_simple_kernel(const uint8_t* __r
 // ---------------------------------------------------------------------------
 // Staged kernel
 // ---------------------------------------------------------------------------
+constexpr uint32_t kQ8Group = 8;                            // blocks per lane and stage
+constexpr uint32_t kQ8GroupBytes = kQ8Group * Q80_BYTES;    // 272, a multiple of 16
+constexpr uint32_t kQ8StageBytes = 32u * kQ8GroupBytes;     // 8704: 32 groups per warp stage
+constexpr uint32_t kQ8DigitStride = 112;                    // shared bytes per block: 3 x 32 digits + pad
+
 struct Q80GemvParams {
   const uint8_t* w;  // n rows x row_bytes
   const float* a;    // k floats
   float* c;
-  uint32_t n, k, nblk, row_bytes, pitch;
-  uint32_t cb, chunks;  // blocks per chunk (multiple of 8), chunks per row
+  uint32_t n, k, nblk, row_bytes;
+  uint32_t rows_max;  // rows of the largest CTA slab (the group-sum area)
   uint32_t* err;
   float* c_extra[7];  // further copies of every output (tensor-parallel push)
   uint32_t n_extra;
   XchgSync xs;  // tensor parallel (world > 1): the other ranks pushed parts of `a`
 };
 
-// Four signed bytes -> two float2 of exact values: 2^23 + (b + 128) built by
-// prmt on the biased word, minus 2^23 + 128 with one packed subtract each.
-__device__ __forceinline__ void q8_word_to_f2(uint32_t word, float2& lo, float2& hi) {
-  const uint32_t x = word ^ 0x80808080u;
-  const float2 bias = make_float2(-8388736.0f, -8388736.0f);
-  lo = __fadd2_rn(make_float2(__int_as_float((int)__byte_perm(x, 0x4B000000u, 0x7540u)),
-                              __int_as_float((int)__byte_perm(x, 0x4B000000u, 0x7541u))),
-                  bias);
-  hi = __fadd2_rn(make_float2(__int_as_float((int)__byte_perm(x, 0x4B000000u, 0x7542u)),
-                              __int_as_float((int)__byte_perm(x, 0x4B000000u, 0x7543u))),
-                  bias);
+// Shared-memory layout of the staged kernel (offsets in bytes).
+struct Q80Smem {
+  uint32_t dig, pw2, part, wbuf, total;
+};
+__host__ __device__ inline Q80Smem q80_smem(uint32_t nblk, uint32_t rows_max, uint32_t nw, uint32_t d) {
+  const uint32_t gpr = nblk / kQ8Group;
+  Q80Smem m;
+  m.dig = 0;
+  m.pw2 = (nblk * kQ8DigitStride + 15u) & ~15u;
+  m.part = m.pw2 + ((nblk * 4u + 15u) & ~15u);
+  m.wbuf = m.part + ((rows_max * (gpr + 1u) * 4u + 127u) & ~127u);
+  m.total = m.wbuf + nw * d * kQ8StageBytes;
+  return m;
 }
 
-// One 34-byte block at `blk` (2-byte aligned, shared memory) against the 32
-// activations at `act` (16-byte aligned): scale * sum(a * w).
-__device__ __forceinline__ float q80_block(const uint8_t* blk, const float* act) {
-  const uintptr_t addr = reinterpret_cast<uintptr_t>(blk);
-  const uint32_t* wp = reinterpret_cast<const uint32_t*>(addr & ~(uintptr_t)3);
-  const bool odd = (addr & 2u) != 0;  // block starts in the upper half of its first word
-  uint32_t wd[9];
-#pragma unroll
-  for (int i = 0; i < 9; ++i) wd[i] = wp[i];
-  const float scale = f16_bits_to_f32(odd ? (wd[0] >> 16) : wd[0]);
-  // data starts 2 bytes after the block: bytes 2..5 of (wd[t], wd[t+1]) when
-  // the block is word-aligned, bytes 4..7 (= wd[t+1]) when it is not
-  const uint32_t sel = odd ? 0x7654u : 0x5432u;
-  float2 acc0 = make_float2(0.0f, 0.0f), acc1 = make_float2(0.0f, 0.0f);
-#pragma unroll
-  for (int t = 0; t < 8; ++t) {
-    const uint32_t word = __byte_perm(wd[t], wd[t + 1], sel);
-    float2 lo, hi;
-    q8_word_to_f2(word, lo, hi);
-    const float4 av = *reinterpret_cast<const float4*>(act + 4 * t);
-    acc0 = __ffma2_rn(make_float2(av.x, av.y), lo, acc0);
-    acc1 = __ffma2_rn(make_float2(av.z, av.w), hi, acc1);
-  }
-  return scale * ((acc0.x + acc0.y) + (acc1.x + acc1.y));
-}
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 
 template <int NW, int D>
 __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const uint32_t nblk = p.nblk, row_bytes = p.row_bytes, pitch = p.pitch;
-  float* act_s = reinterpret_cast<float*>(smem);
-  const uint32_t act_region = (nblk * kQ8ActStride * 4u + 127u) & ~127u;
+  const uint32_t nblk = p.nblk, gpr = nblk / kQ8Group;
+  const Q80Smem L = q80_smem(nblk, p.rows_max, NW, D);
+  uint8_t* dig = smem + L.dig;                            // [slot][3][32] int8 digits
+  float* pw2 = reinterpret_cast<float*>(smem + L.pw2);    // [slot] 2^(e - 20)
+  float* part = reinterpret_cast<float*>(smem + L.part);  // [row][gpr + 1] group sums
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  uint8_t* wbuf = smem + act_region + warp * D * pitch;
+  uint8_t* wbuf = smem + L.wbuf + warp * D * kQ8StageBytes;
 
   const uint32_t r0 = (uint32_t)(((uint64_t)p.n * blockIdx.x) / gridDim.x);
   const uint32_t r1 = (uint32_t)(((uint64_t)p.n * (blockIdx.x + 1)) / gridDim.x);
   const uint32_t nrows = r1 - r0;
-  const uint32_t C = p.chunks, cb = p.cb;
+  const uint32_t ngroups = nrows * gpr;  // this CTA's groups, in memory order
+  const uint32_t nst = (ngroups + 31u) / 32u;
+  const uint8_t* slab = p.w + (size_t)r0 * p.row_bytes;
+  const size_t slab_bytes = (size_t)nrows * p.row_bytes;
   const uint64_t pol_w = l2_policy_evict_first();
-  // this warp's stages: rows warp, warp + NW, ..., each as C chunks in order
-  const uint32_t my_rows = nrows > warp ? (nrows - warp + NW - 1) / NW : 0u;
-  const uint32_t T = my_rows * C;
-
-  // (row, chunk) of the next stage to issue, advanced incrementally
-  uint32_t irow = warp, ich = 0;
-  auto issue = [&](uint32_t t, uint32_t slot) {
-    if (t < T) {
-      const uint32_t row = irow, ch = ich;
-      if (++ich == C) {
-        ich = 0;
-        irow += NW;
-      }
-      const uint32_t b0 = ch * cb, nb = (nblk - b0) < cb ? (nblk - b0) : cb;
-      const uint8_t* src = p.w + (size_t)(r0 + row) * row_bytes + b0 * Q80_BYTES;
-      uint8_t* dst = wbuf + slot * pitch;
-      const uint32_t n16 = (nb * Q80_BYTES) >> 4;  // nb is a multiple of 8: 272-byte units
-      for (uint32_t q = lane; q < n16; q += 32) cp_async16(dst + (q << 4), src + (q << 4), pol_w);
+  auto issue = [&](uint32_t s, uint32_t slot) {
+    if (s < nst) {
+      const size_t off = (size_t)s * kQ8StageBytes;
+      const uint32_t bytes = (uint32_t)((slab_bytes - off) < kQ8StageBytes ? (slab_bytes - off) : kQ8StageBytes);
+      const uint8_t* src = slab + off;
+      uint8_t* dst = wbuf + slot * kQ8StageBytes;
+      for (uint32_t q = lane; q < (bytes >> 4); q += 32) cp_async16(dst + (q << 4), src + (q << 4), pol_w);
     }
-    cp_async_commit();
+    cp_async_commit();  // one group per call, empty or not
   };
 #pragma unroll
-  for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(d, d);
+  for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(warp + d * NW, d);
 
   pdl_wait();  // the activations may be the previous kernel's output
   if (p.xs.world > 1 && !xchg_handshake(p.xs, blockIdx.x == 0, true)) {
     cp_async_wait<0>();  // a peer never arrived: drain, leave the outputs unwritten
     return;
   }
-  {
-    const float4* src = reinterpret_cast<const float4*>(p.a);
-    for (uint32_t t = threadIdx.x; t < (p.k >> 2); t += NW * 32) {
-      const uint32_t j = t >> 3, v = t & 7u;
-      *reinterpret_cast<float4*>(act_s + j * kQ8ActStride + 4u * v) = src[t];
+  // activation blocks -> digits.  Block b sits at slot (b % 8) * gpr + b / 8,
+  // so the 8 lanes of a shared-memory phase (groups j .. j + 7, same c) read
+  // consecutive slots, 112 bytes apart: distinct bank groups.
+  for (uint32_t b = warp; b < nblk; b += NW) {
+    const float v = p.a[(b << 5) + lane];
+    const uint32_t mbits = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7fffffffu);
+    int d1 = 0, d2 = 0, d3 = 0;
+    float pw = 0.0f;
+    if (mbits >= 0x7f800000u) {
+      pw = __int_as_float(0x7fc00000);  // Inf or NaN in the block: its contribution is NaN
+    } else if (mbits != 0u) {
+      int e;
+      frexpf(__uint_as_float(mbits), &e);                // max|a| < 2^e
+      const int A = __float2int_rn(ldexpf(v, 20 - e));   // |A| <= 2^20, exact scaling
+      d3 = ((A + 64) & 127) - 64;
+      const int A2 = (A - d3) >> 7;
+      d2 = ((A2 + 64) & 127) - 64;
+      d1 = (A2 - d2) >> 7;  // |d1| <= 64
+      pw = ldexpf(1.0f, e - 20);
     }
+    const uint32_t slot = (b % kQ8Group) * gpr + b / kQ8Group;
+    uint8_t* ds = dig + slot * kQ8DigitStride;
+    ds[lane] = static_cast<uint8_t>(d1);
+    ds[32 + lane] = static_cast<uint8_t>(d2);
+    ds[64 + lane] = static_cast<uint8_t>(d3);
+    if (lane == 0) pw2[slot] = pw;
   }
   __syncthreads();
   pdl_trigger();
 
-  float acc = 0.0f;
-  uint32_t row = warp, ch = 0, slot = 0;  // stage being consumed
-  for (uint32_t t = 0; t < T; ++t) {
+  uint32_t slot = 0;
+  for (uint32_t s = warp; s < nst; s += NW) {
     cp_async_wait<D - 1>();
     __syncwarp();
-    const uint32_t b0 = ch * cb, nb = (nblk - b0) < cb ? (nblk - b0) : cb;
-    const uint8_t* chunk = wbuf + slot * pitch;
-    const float* av = act_s + b0 * kQ8ActStride;
-    for (uint32_t j = lane; j < nb; j += 32) acc += q80_block(chunk + j * Q80_BYTES, av + j * kQ8ActStride);
-    __syncwarp();
-    issue(t + D, slot);
-    if (++slot == (uint32_t)D) slot = 0;
-    if (++ch == C) {  // row complete
-      acc += __shfl_xor_sync(0xffffffffu, acc, 16);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 8);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-      if (lane == 0) {
-        p.c[r0 + row] = acc;
-        // extra destinations: plain remote stores, ordered before the
-        // consumer's flag by grid completion (see gemv_store, q4k_gemv.cu)
-        for (uint32_t j = 0; j < p.n_extra; ++j) p.c_extra[j][r0 + row] = acc;
+    const uint32_t G = s * 32u + lane;
+    if (G < ngroups) {
+      const uint32_t row = G / gpr, j = G - row * gpr;  // group j of the row: blocks 8 j .. 8 j + 7
+      const uint8_t* gb = wbuf + slot * kQ8StageBytes + lane * kQ8GroupBytes;
+      float acc = 0.0f;
+#pragma unroll
+      for (uint32_t c = 0; c < kQ8Group; ++c) {
+        const uint32_t o = (Q80_BYTES * c) & 15u;           // block start mod 16 (even)
+        const uint8_t* wb = gb + ((Q80_BYTES * c) & ~15u);  // 16-byte aligned window of 48 bytes
+        const uint4 v0 = lds128(wb), v1 = lds128(wb + 16), v2 = lds128(wb + 32);
+        const uint32_t win[12] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w, v2.x, v2.y, v2.z, v2.w};
+        const uint32_t hw = win[o >> 2];
+        const uint32_t scale_bits = (o & 2u) ? (hw >> 16) : (hw & 0xffffu);
+        // the 32 weight bytes start at o + 2: whole words, or halves of two
+        const uint32_t ws = (o + 2u) >> 2;
+        uint32_t q[8];
+#pragma unroll
+        for (uint32_t t = 0; t < 8; ++t)
+          q[t] = ((o + 2u) & 2u) ? __byte_perm(win[ws + t], win[ws + t + 1], 0x5432) : win[ws + t];
+        const uint32_t ds_slot = c * gpr + j;
+        const uint8_t* ds = dig + ds_slot * kQ8DigitStride;
+        const int4 a10 = *reinterpret_cast<const int4*>(ds), a11 = *reinterpret_cast<const int4*>(ds + 16);
+        const int4 a20 = *reinterpret_cast<const int4*>(ds + 32), a21 = *reinterpret_cast<const int4*>(ds + 48);
+        const int4 a30 = *reinterpret_cast<const int4*>(ds + 64), a31 = *reinterpret_cast<const int4*>(ds + 80);
+        const int av1[8] = {a10.x, a10.y, a10.z, a10.w, a11.x, a11.y, a11.z, a11.w};
+        const int av2[8] = {a20.x, a20.y, a20.z, a20.w, a21.x, a21.y, a21.z, a21.w};
+        const int av3[8] = {a30.x, a30.y, a30.z, a30.w, a31.x, a31.y, a31.z, a31.w};
+        int D1 = 0, D2 = 0, D3 = 0;
+#pragma unroll
+        for (uint32_t t = 0; t < 8; ++t) {
+          D1 = __dp4a((int)q[t], av1[t], D1);
+          D2 = __dp4a((int)q[t], av2[t], D2);
+          D3 = __dp4a((int)q[t], av3[t], D3);
+        }
+        // |D1|, |D2|, |D3| <= 32 * 128 * 64 = 2^18: exact; the block's dot in
+        // units of 2^(e - 20), then scale_w * dot * 2^(e - 20)
+        const float dot = __fadd_rn(__fmul_rn((float)D1, 16384.0f), (float)(D2 * 128 + D3));
+        acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(f16_bits_to_f32(scale_bits), dot), pw2[ds_slot]));
       }
-      acc = 0.0f;
-      ch = 0;
-      row += NW;
+      part[row * (gpr + 1u) + j] = acc;
     }
+    __syncwarp();  // stage bytes no longer read
+    issue(s + D * NW, slot);
+    if (++slot == (uint32_t)D) slot = 0;
   }
   cp_async_wait<0>();
+  __syncthreads();
+  // row sums: the row's groups in order
+  for (uint32_t row = threadIdx.x; row < nrows; row += NW * 32u) {
+    const float* pr = part + row * (gpr + 1u);
+    float sum = 0.0f;
+    for (uint32_t j = 0; j < gpr; ++j) sum = __fadd_rn(sum, pr[j]);
+    p.c[r0 + row] = sum;
+    // extra destinations: plain remote stores, ordered before the consumer's
+    // flag by grid completion (see gemv_store, q4k_gemv.cu)
+    for (uint32_t x = 0; x < p.n_extra; ++x) p.c_extra[x][r0 + row] = sum;
+  }
 }
 
 namespace {
@@ -213,9 +249,9 @@ struct Q80Config {
   int nw, d;
   SmemAttr attr;  // dynamic shared memory allowed so far, per device
 };
-Q80Config g_q80_cfgs[] = {{q80_gemv_kernel<16, 4>, 16, 4, {}}, {q80_gemv_kernel<16, 3>, 16, 3, {}},
-                          {q80_gemv_kernel<16, 2>, 16, 2, {}}, {q80_gemv_kernel<8, 4>, 8, 4, {}},
-                          {q80_gemv_kernel<24, 2>, 24, 2, {}}, {q80_gemv_kernel<12, 3>, 12, 3, {}}};
+Q80Config g_q80_cfgs[] = {{q80_gemv_kernel<8, 2>, 8, 2, {}}, {q80_gemv_kernel<4, 2>, 4, 2, {}},
+                          {q80_gemv_kernel<8, 3>, 8, 3, {}}, {q80_gemv_kernel<4, 3>, 4, 3, {}},
+                          {q80_gemv_kernel<6, 2>, 6, 2, {}}, {q80_gemv_kernel<12, 2>, 12, 2, {}}};
 constexpr int kNumQ80Cfgs = sizeof(g_q80_cfgs) / sizeof(g_q80_cfgs[0]);
 int g_q80_variant = -1;
 }  // namespace
@@ -233,27 +269,37 @@ cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t
   if (n == 0) return cudaSuccess;
   const uint32_t nblk = k / Q80_ELEMS;
   const uint32_t row_bytes = nblk * Q80_BYTES;
-  const uint32_t act_region = (nblk * kQ8ActStride * 4u + 127u) & ~127u;
-  // rows stream in chunks of at most 128 blocks (4352 bytes); +16: the last
-  // block's nine-word window may reach 2 bytes past the chunk
-  const uint32_t cb = nblk < 128u ? nblk : 128u;
-  const uint32_t chunks = (nblk + cb - 1) / cb;
-  const uint32_t pitch = (cb * Q80_BYTES + 16u + 15u) & ~15u;
-  const bool aligned = (k % 256u) == 0 && (reinterpret_cast<uintptr_t>(w) & 15u) == 0 &&
+  // the staged kernel: groups of 8 blocks (k % 256 == 0), 16-byte aligned
+  // weights and activations
+  const bool aligned = (k % 256u) == 0 && k > 0 && (reinterpret_cast<uintptr_t>(w) & 15u) == 0 &&
                        (reinterpret_cast<uintptr_t>(a) & 15u) == 0;
+  // CTAs per SM and the configuration: the first (in preference order) whose
+  // shared memory fits at the largest CTA count tried
   int pick = -1;
-  if (g_q80_variant >= 0 && g_q80_variant < kNumQ80Cfgs) {
-    pick = g_q80_variant;
-  } else {
-    const int order[] = {4, 2, 1, 0, 3};
-    for (int o : order)
-      if (act_region + (uint32_t)(g_q80_cfgs[o].nw * g_q80_cfgs[o].d) * pitch <= (uint32_t)max_smem) {
-        pick = o;
-        break;
-      }
+  uint32_t cps = 1, smem = 0, rows_max = 0;
+  auto fits = [&](int ci, uint32_t want_cps) -> bool {
+    const Q80Config& g = g_q80_cfgs[ci];
+    const uint32_t grid = (uint32_t)num_sms * want_cps;
+    const uint32_t rmax = (n + grid - 1) / grid + 1u;
+    const Q80Smem m = q80_smem(nblk, rmax, (uint32_t)g.nw, (uint32_t)g.d);
+    if (m.total > (uint32_t)max_smem || want_cps * (m.total + 1024u) > (uint32_t)max_smem + 1024u) return false;
+    pick = ci;
+    cps = want_cps;
+    smem = m.total;
+    rows_max = rmax;
+    return true;
+  };
+  if (aligned) {
+    if (g_q80_variant >= 0 && g_q80_variant < kNumQ80Cfgs) {
+      for (uint32_t want = 4; want >= 1 && pick < 0; --want) fits(g_q80_variant, want);
+    } else {
+      const int order[] = {0, 2, 4, 1, 3};
+      for (uint32_t want = 2; want >= 1 && pick < 0; --want)
+        for (int o : order)
+          if (fits(o, want)) break;
+    }
   }
-  if (!aligned || pick < 0 ||
-      act_region + (uint32_t)(g_q80_cfgs[pick].nw * g_q80_cfgs[pick].d) * pitch > (uint32_t)max_smem) {
+  if (pick < 0) {
     if (n_extra != 0 || (xs != nullptr && xs->world > 1)) {  // the unstaged kernel: one destination, no handshake
       *out_status = EOS_E_UNSUPPORTED;
       return cudaSuccess;
@@ -262,17 +308,13 @@ cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t
     return cudaGetLastError();
   }
   Q80Config& cfg = g_q80_cfgs[pick];
-  const uint32_t smem = act_region + (uint32_t)(cfg.nw * cfg.d) * pitch;
   {
     const cudaError_t e = ensure_smem_attr((const void*)cfg.fn, (int)smem, cfg.attr);  // on this device
     if (e != cudaSuccess) return e;
   }
-  uint32_t cps = (uint32_t)(max_smem + 1024) / (smem + 1024);
-  if (cps > 4u) cps = 4u;
-  if (cps < 1u) cps = 1u;
   uint32_t grid = (uint32_t)num_sms * cps;
   if (grid > n) grid = n;
-  Q80GemvParams prm{w, a, c, n, k, nblk, row_bytes, pitch, cb, chunks, err, {}, n_extra, {}};
+  Q80GemvParams prm{w, a, c, n, k, nblk, row_bytes, rows_max, err, {}, n_extra, {}};
   for (uint32_t j = 0; j < n_extra; ++j) prm.c_extra[j] = c_extra[j];
   if (xs != nullptr) prm.xs = *xs;
   cudaLaunchConfig_t lc = {};
