@@ -7,7 +7,7 @@
 // instructions than the dot itself, so the staged kernel moves the
 // conversion to the activations, once per CTA: each 32-value activation block
 // becomes block-float integers (a power-of-two scale per block, 20-bit signed
-// values, exact scaling, rounding error at most 2^-21 of the block's largest
+// values, exact scaling, rounding error at most 2^-20 of the block's largest
 // magnitude) held as three signed base-128 digits of int8, and a weight
 // block's dot with it is three exact integer dp4a chains recombined in f32.
 // Results agree with the reference's f32 loop to fp32 rounding (the tests
@@ -113,13 +113,49 @@ __host__ __device__ inline Q80Smem q80_smem(uint32_t nblk, uint32_t rows_max, ui
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 
+// One warp converts one 32-value activation block (lane i holds value i):
+// with 2^E <= max|a| < 2^(E+1), every value becomes the integer
+// A = round(a * 2^(19 - E)) (the scaling by a power of two is exact; |A| <=
+// 2^20), written as three signed base-128 digits A = d1 * 2^14 + d2 * 2^7 +
+// d3 (d2, d3 in [-64, 63], |d1| <= 64) into ds[0..31], ds[32..63],
+// ds[64..95]; lane 0 stores the block's unit 2^(E - 19) at *pw.  A block
+// whose largest magnitude is below 2^-100 (or subnormal) takes the slower
+// exact library scaling; a block holding Inf or NaN gets unit NaN.
+__device__ __forceinline__ void q8_act_digits(float v, uint32_t lane, uint8_t* ds, float* pw) {
+  const uint32_t mbits = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7fffffffu);
+  int A = 0;
+  float unit = 0.0f;
+  if (mbits >= 0x7f800000u) {
+    unit = __int_as_float(0x7fc00000);
+  } else if (mbits >= 0x0d800000u) {  // max|a| >= 2^-100: both factors are normal floats
+    const int E = (int)(mbits >> 23) - 127;
+    const float up = __int_as_float((19 - E + 127) << 23);
+    // round to nearest even through the 1.5 * 2^23 magic (|a * up| < 2^20)
+    A = __float_as_int(__fadd_rn(__fmul_rn(v, up), 12582912.0f)) - 0x4B400000;
+    unit = __int_as_float((E - 19 + 127) << 23);
+  } else if (mbits != 0u) {
+    int e;
+    frexpf(__uint_as_float(mbits), &e);  // max|a| < 2^e
+    A = __float2int_rn(ldexpf(v, 20 - e));
+    unit = ldexpf(1.0f, e - 20);
+  }
+  const int d3 = ((A + 64) & 127) - 64;
+  const int A2 = (A - d3) >> 7;
+  const int d2 = ((A2 + 64) & 127) - 64;
+  const int d1 = (A2 - d2) >> 7;
+  ds[lane] = static_cast<uint8_t>(d1);
+  ds[32 + lane] = static_cast<uint8_t>(d2);
+  ds[64 + lane] = static_cast<uint8_t>(d3);
+  if (lane == 0) *pw = unit;
+}
+
 template <int NW, int D>
 __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t nblk = p.nblk, gpr = nblk / kQ8Group;
   const Q80Smem L = q80_smem(nblk, p.rows_max, NW, D);
   uint8_t* dig = smem + L.dig;                            // [slot][3][32] int8 digits
-  float* pw2 = reinterpret_cast<float*>(smem + L.pw2);    // [slot] 2^(e - 20)
+  float* pw2 = reinterpret_cast<float*>(smem + L.pw2);    // [slot] the block unit 2^(E - 19)
   float* part = reinterpret_cast<float*>(smem + L.part);  // [row][gpr + 1] group sums
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   uint8_t* wbuf = smem + L.wbuf + warp * D * kQ8StageBytes;
@@ -152,30 +188,23 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
   }
   // activation blocks -> digits.  Block b sits at slot (b % 8) * gpr + b / 8,
   // so the 8 lanes of a shared-memory phase (groups j .. j + 7, same c) read
-  // consecutive slots, 112 bytes apart: distinct bank groups.
-  for (uint32_t b = warp; b < nblk; b += NW) {
-    const float v = p.a[(b << 5) + lane];
-    const uint32_t mbits = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7fffffffu);
-    int d1 = 0, d2 = 0, d3 = 0;
-    float pw = 0.0f;
-    if (mbits >= 0x7f800000u) {
-      pw = __int_as_float(0x7fc00000);  // Inf or NaN in the block: its contribution is NaN
-    } else if (mbits != 0u) {
-      int e;
-      frexpf(__uint_as_float(mbits), &e);                // max|a| < 2^e
-      const int A = __float2int_rn(ldexpf(v, 20 - e));   // |A| <= 2^20, exact scaling
-      d3 = ((A + 64) & 127) - 64;
-      const int A2 = (A - d3) >> 7;
-      d2 = ((A2 + 64) & 127) - 64;
-      d1 = (A2 - d2) >> 7;  // |d1| <= 64
-      pw = ldexpf(1.0f, e - 20);
+  // consecutive slots, 112 bytes apart: distinct bank groups.  Four blocks
+  // per warp and round, their loads issued together.
+  constexpr uint32_t U = 4;
+  for (uint32_t b0 = warp; b0 < nblk; b0 += U * NW) {
+    float v[U];
+#pragma unroll
+    for (uint32_t u = 0; u < U; ++u) {
+      const uint32_t b = b0 + u * NW;
+      v[u] = b < nblk ? p.a[(b << 5) + lane] : 0.0f;
     }
-    const uint32_t slot = (b % kQ8Group) * gpr + b / kQ8Group;
-    uint8_t* ds = dig + slot * kQ8DigitStride;
-    ds[lane] = static_cast<uint8_t>(d1);
-    ds[32 + lane] = static_cast<uint8_t>(d2);
-    ds[64 + lane] = static_cast<uint8_t>(d3);
-    if (lane == 0) pw2[slot] = pw;
+#pragma unroll
+    for (uint32_t u = 0; u < U; ++u) {
+      const uint32_t b = b0 + u * NW;
+      if (b >= nblk) break;  // warp-uniform
+      q8_act_digits(v[u], lane, dig + ((b % kQ8Group) * gpr + b / kQ8Group) * kQ8DigitStride,
+                    pw2 + (b % kQ8Group) * gpr + b / kQ8Group);
+    }
   }
   __syncthreads();
   pdl_trigger();
@@ -219,7 +248,7 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
           D3 = __dp4a((int)q[t], av3[t], D3);
         }
         // |D1|, |D2|, |D3| <= 32 * 128 * 64 = 2^18: exact; the block's dot in
-        // units of 2^(e - 20), then scale_w * dot * 2^(e - 20)
+        // the block's units, then scale_w * dot * unit
         const float dot = __fadd_rn(__fmul_rn((float)D1, 16384.0f), (float)(D2 * 128 + D3));
         acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(f16_bits_to_f32(scale_bits), dot), pw2[ds_slot]));
       }
@@ -293,10 +322,11 @@ cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t
     if (g_q80_variant >= 0 && g_q80_variant < kNumQ80Cfgs) {
       for (uint32_t want = 4; want >= 1 && pick < 0; --want) fits(g_q80_variant, want);
     } else {
-      const int order[] = {0, 2, 4, 1, 3};
-      for (uint32_t want = 2; want >= 1 && pick < 0; --want)
-        for (int o : order)
-          if (fits(o, want)) break;
+      // measured on a B200 (sweep shapes): 8 warps x 2 buffers, one CTA per
+      // SM, is fastest; smaller configurations for rows too long for it
+      const int order[][2] = {{0, 1}, {4, 1}, {1, 2}, {1, 1}, {3, 1}};
+      for (const auto& o : order)
+        if (fits(o[0], (uint32_t)o[1])) break;
     }
   }
   if (pick < 0) {
