@@ -11,29 +11,43 @@
 // writes or reads, so the GEMVs stream their weights while the small
 // kernels before them run.
 //
-// Per layer (tensor-parallel rank r of G; G == 1 is the whole model):
-//   norm_pack    x = x_prev + sum(partials)   (residual, text.c:404-406 and
-//                :420-421), rmsnorm (src/kernels/scalar/rmsnorm.c:14-37),
-//                then the Q8 activation packing of the next GEMV
+// Per layer (tensor-parallel rank r of G; G == 1 is the whole model; every
+// matrix is sharded by output rows, so every output element is computed
+// whole on one rank, exactly as on one GPU):
+//   norm_pack    x = x_prev + t (residual, text.c:404-406 and :420-421),
+//                rmsnorm (src/kernels/scalar/rmsnorm.c:14-37), then the Q8
+//                activation packing of the next GEMV; every rank normalises
+//                the whole vector
 //   GEMV         [q; k; v] rows of this rank's heads          (text.c:349-352)
 //   attention    RoPE on q and k (src/kernels/scalar/rope.c:16-38), K/V append
 //                at `pos` (text.c:359-362), softmax attention with the GQA
 //                head map (text.c:364-401), split over positions; the last
 //                CTA of a head merges the pieces and packs the head's output
-//   GEMV         O projection on this rank's head columns -> partial x
+//                (tensor parallel: into every rank's copy of the O input)
+//   GEMV         O projection, this rank's output rows (of all n_embd) -> t
 //   norm_pack    ffn_norm
 //   GEMV         [gate; up] rows of this rank's FFN slice     (text.c:413-415)
 //   silu_pack    silu(gate) * up (src/kernels/scalar/silu.c:12-23), packed
-//   GEMV         down projection on this rank's FFN columns -> partial x
-// then norm_pack(output_norm), the LM-head GEMV and argmax_kernel.
+//                (tensor parallel: into every rank's copy of the down input)
+//   GEMV         down projection, this rank's output rows -> t
+// then norm_pack(output_norm), the LM-head GEMV (this rank's vocabulary rows)
+// and argmax_kernel.  A tensor-parallel step makes 4 exchanges per layer plus
+// the pick.  The per-layer ones are low-latency pushes (LLExchange): every
+// 32-bit word goes to every rank together with the exchange's epoch in one
+// 64-bit store, written while the producer runs, and the consumer (the O and
+// down GEMVs, norm_pack) polls the words in its own memory -- bounded --
+// until all carry the epoch.  The pick uses a flag handshake
+// (xchg_handshake) on the (value, index) words.
 //
-// Numerics: every GEMV is the bit-exact reference kernel (q4k_gemv.cu,
-// q80_gemv.cu).  The glue ops use IEEE round-to-nearest arithmetic in the
-// reference's operation order where that is cheap (rmsnorm scaling, RoPE
-// products, SiLU), but sums over a vector (rmsnorm's mean square, attention
-// dot products and softmax sums) are parallel reductions, and expf / powf /
-// sinf / cosf are CUDA's, so logits agree with the CPU engine to a
-// tolerance, not bit for bit.
+// Numerics: every GEMV is the bit-exact reference kernel (q4k_gemv.cu) or
+// (Q8_0) agrees with it to fp32 rounding.  The glue ops use IEEE
+// round-to-nearest arithmetic in the reference's operation order where that
+// is cheap (rmsnorm scaling, RoPE products, SiLU), but sums over a vector
+// (rmsnorm's mean square, attention dot products and softmax sums) are
+// parallel reductions, and expf / powf / sinf / cosf are CUDA's, so logits
+// agree with the CPU engine to a tolerance, not bit for bit.  Those
+// reductions run in the same order on any number of GPUs, so a
+// tensor-parallel run picks exactly the one-GPU tokens.
 #include <cmath>
 #include <cstddef>
 #include <cstdlib>
@@ -74,9 +88,9 @@ struct NormPackParams {
   uint32_t n;
   uint8_t* act;     // Q4_K consumers: packed records for k = n
   float* act_f32;   // Q8_0 consumers: the normalised vector
-  // tensor parallel: `part` holds every rank's output rows, pushed by their
-  // GEMVs; handshake before reading it
-  XchgSync xs;
+  // tensor parallel (ll.epoch_word != nullptr): t comes as the (epoch, word)
+  // pairs every rank's GEMV pushed into ll.in instead of from `part`
+  LLExchange ll;
 };
 
 constexpr uint32_t kNormMaxChunks = 16;  // float4 chunks per thread: n <= 16384
@@ -93,24 +107,23 @@ __device__ __forceinline__ float4 add4(float4 a, float4 b) {
 // (CTA b: chunks [64 b, 64 b + 64), held by threads 64 (b % 4) + q at
 // iteration b / 4).  Residual element i is x_in[i] + t[i], the reference's
 // x[i] += t[i] (text.c:406).
+template <uint32_t NCH>  // float4 chunks per thread: n <= 1024 NCH
 __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) {
   __shared__ float red[8];
   __shared__ __align__(16) float ys[256];
   pdl_trigger();
   pdl_wait();
-  if (p.xs.world > 1 && p.part != nullptr && !xchg_handshake(p.xs, blockIdx.x == 0, true))
-    return;  // a peer never arrived: the error bit is set, outputs are invalid
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   const uint32_t nch = p.n >> 2, b = blockIdx.x;
   const uint32_t jown = b >> 2;
   const bool owner = (tid >> 6) == (b & 3u);
-  float4 v[kNormMaxChunks];
+  float4 v[NCH];
   if (p.x_in == nullptr) {
     const uint32_t pos = p.state->pos;
     const uint32_t tok = pos < p.state->n_prompt ? p.prompt[pos] : p.state->next_token;
     const uint2* emb = reinterpret_cast<const uint2*>(p.tok_embd + (size_t)tok * p.n);
 #pragma unroll
-    for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
+    for (uint32_t j = 0; j < NCH; ++j) {
       const uint32_t c = tid + 256u * j;
       if (c < nch) {
         const uint2 h = emb[c];  // F16 -> F32 is exact (src/util/f16.h)
@@ -120,13 +133,48 @@ __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) 
     }
   } else {
 #pragma unroll
-    for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
+    for (uint32_t j = 0; j < NCH; ++j) {
       const uint32_t c = tid + 256u * j;
       if (c < nch) v[j] = ld4(p.x_in, c);
     }
-    if (p.part != nullptr) {
+    if (p.ll.epoch_word != nullptr) {
+      // tensor parallel: every chunk's four (epoch, word) pairs, all loads in
+      // flight at once, the round reloaded until every pair is there
+      const uint32_t epoch = ll_epoch(p.ll, p.ll.in_add);
+      float4 t[NCH];
+      uint64_t t0 = 0;
+      bool ready, ok = true;
+      do {
+        ready = true;
 #pragma unroll
-      for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
+        for (uint32_t j = 0; j < NCH; ++j) {
+          const uint32_t c = tid + 256u * j;
+          if (c < nch) {
+            uint64_t q0, q1, q2, q3;
+            ll_load2(p.ll.in + 4u * c, q0, q1);
+            ll_load2(p.ll.in + 4u * c + 2u, q2, q3);
+            t[j] = make_float4(__uint_as_float((uint32_t)q0), __uint_as_float((uint32_t)q1),
+                               __uint_as_float((uint32_t)q2), __uint_as_float((uint32_t)q3));
+            if ((uint32_t)(q0 >> 32) != epoch || (uint32_t)(q1 >> 32) != epoch || (uint32_t)(q2 >> 32) != epoch ||
+                (uint32_t)(q3 >> 32) != epoch)
+              ready = false;
+          }
+        }
+        if (!ready && !ll_keep_waiting(p.ll, t0)) {
+          ok = false;
+          break;
+        }
+      } while (!ready);
+      if (!__syncthreads_and(ok)) {
+        if (tid == 0) report(p.ll.err, EOS_DEVERR_PEER);
+        return;  // a peer never arrived: the error bit is set, outputs are invalid
+      }
+#pragma unroll
+      for (uint32_t j = 0; j < NCH; ++j)
+        if (tid + 256u * j < nch) v[j] = add4(v[j], t[j]);
+    } else if (p.part != nullptr) {
+#pragma unroll
+      for (uint32_t j = 0; j < NCH; ++j) {
         const uint32_t c = tid + 256u * j;
         if (c < nch) v[j] = add4(v[j], __ldcg(reinterpret_cast<const float4*>(p.part) + c));
       }
@@ -135,7 +183,7 @@ __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) 
   const float4 w4 = owner ? ld4(p.w, (b << 6) + (tid & 63u)) : make_float4(0.f, 0.f, 0.f, 0.f);
   float ss = 0.0f;
 #pragma unroll
-  for (uint32_t j = 0; j < kNormMaxChunks; ++j) {
+  for (uint32_t j = 0; j < NCH; ++j) {
     if (tid + 256u * j < nch) {
       ss = __fadd_rn(ss, __fmul_rn(v[j].x, v[j].x));
       ss = __fadd_rn(ss, __fmul_rn(v[j].y, v[j].y));
@@ -156,7 +204,7 @@ __global__ void __launch_bounds__(256) norm_pack_kernel(const NormPackParams p) 
   if (owner) {
     float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (uint32_t j = 0; j < kNormMaxChunks; ++j)
+    for (uint32_t j = 0; j < NCH; ++j)
       if (j == jown) x = v[j];
     const uint32_t c = (b << 6) + (tid & 63u);
     if (p.x_out != nullptr) reinterpret_cast<float4*>(p.x_out)[c] = x;
@@ -185,31 +233,35 @@ struct AttnParams {
   uint32_t* count;   // [hl] chunk arrivals, reset by the merging CTA
   const DecState* state;
   // the O projection's input, all n_head heads (head h at h * hd): Q4_K packed
-  // records, or (Q8_0) the attention output itself; tensor parallel, the
-  // same positions in the other ranks' copies too (act_x / actf_x, n_x)
+  // records, or (Q8_0) the attention output itself; tensor parallel, as
+  // (epoch, word) pairs into every rank's buffer (ll.out) instead
   uint8_t* act;
   float* act_f32;
-  uint8_t* act_x[kMaxParts - 1];
-  float* actf_x[kMaxParts - 1];
-  uint32_t n_x;
+  LLExchange ll;
   uint32_t hl, h0, kvl, kv0, n_head, n_kv_head, max_chunks;
   float base, scale;
 };
 
-// pack_group_to_record into this rank's records and n_x further copies: the
-// same quantize_sub32 values everywhere.
-__device__ __forceinline__ void pack_group_to_records(float v, uint32_t g, uint32_t lane, uint8_t* rec,
-                                                      uint8_t* const* rec_x, uint32_t n_x) {
+// The warp's 32-group g (lane i holds element i) packed into records: this
+// rank's (rec), or, tensor parallel, as (epoch, word) pairs into every
+// rank's buffer (word w of the record layout is pair w; four lanes' int8
+// values make one word).
+__device__ __forceinline__ void pack_group_out(float v, uint32_t g, uint32_t lane, uint8_t* rec, const LLExchange& ll,
+                                               uint32_t epoch) {
+  if (ll.epoch_word == nullptr) {
+    pack_group_to_record(v, g, lane, rec);
+    return;
+  }
   float scale;
   int32_t sum;
-  const int8_t q = quant_group32(v, scale, sum);
-  const uint32_t oq = rec_aq_offset(g) + lane, os = rec_st_offset(g);
-  const float2 st = make_float2(scale, (float)sum);
-  rec[oq] = static_cast<uint8_t>(q);
-  if (lane == 0) *reinterpret_cast<float2*>(rec + os) = st;
-  for (uint32_t j = 0; j < n_x; ++j) {
-    rec_x[j][oq] = static_cast<uint8_t>(q);
-    if (lane == 0) *reinterpret_cast<float2*>(rec_x[j] + os) = st;
+  const uint32_t b = static_cast<uint8_t>(quant_group32(v, scale, sum));
+  const unsigned FULL = 0xffffffffu;
+  const uint32_t w = b | (__shfl_down_sync(FULL, b, 1) << 8) | (__shfl_down_sync(FULL, b, 2) << 16) |
+                     (__shfl_down_sync(FULL, b, 3) << 24);
+  if ((lane & 3u) == 0) ll_put(ll, (rec_aq_offset(g) >> 2) + (lane >> 2), w, epoch);
+  if (lane == 0) {
+    ll_put(ll, rec_st_offset(g) >> 2, __float_as_uint(scale), epoch);
+    ll_put(ll, (rec_st_offset(g) >> 2) + 1u, __float_as_uint((float)sum), epoch);
   }
 }
 
@@ -398,13 +450,15 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnParams p) {
   }
   if (tid == 0) p.count[hloc] = 0u;
   __syncthreads();
+  const uint32_t epoch = p.ll.epoch_word != nullptr ? ll_epoch(p.ll, p.ll.out_add) : 0u;
   if (p.act != nullptr) {
-    for (uint32_t g = warp; g < E; g += 4u)
-      pack_group_to_records(s_out[g * 32u + lane], gh * E + g, lane, p.act, p.act_x, p.n_x);
+    for (uint32_t g = warp; g < E; g += 4u) pack_group_out(s_out[g * 32u + lane], gh * E + g, lane, p.act, p.ll, epoch);
   } else {
     for (uint32_t d = tid; d < HD; d += 128u) {
-      p.act_f32[gh * HD + d] = s_out[d];
-      for (uint32_t j = 0; j < p.n_x; ++j) p.actf_x[j][gh * HD + d] = s_out[d];
+      if (p.ll.epoch_word != nullptr)
+        ll_put(p.ll, gh * HD + d, __float_as_uint(s_out[d]), epoch);
+      else
+        p.act_f32[gh * HD + d] = s_out[d];
     }
   }
 }
@@ -416,13 +470,11 @@ struct SiluParams {
   const float* gu;  // [gate | up] of this rank's FFN slice, ffl each
   uint32_t ffl, ff0;
   // the down projection's input, all n_ff units (unit ff0 + i of this rank's
-  // i): Q4_K packed records, or (Q8_0) the values; tensor parallel, the other
-  // ranks' copies too
+  // i): Q4_K packed records, or (Q8_0) the values; tensor parallel, as
+  // (epoch, word) pairs into every rank's buffer (ll.out) instead
   uint8_t* act;
   float* act_f32;
-  uint8_t* act_x[kMaxParts - 1];
-  float* actf_x[kMaxParts - 1];
-  uint32_t n_x;
+  LLExchange ll;
 };
 
 __global__ void __launch_bounds__(256) silu_pack_kernel(const SiluParams p) {
@@ -434,11 +486,13 @@ __global__ void __launch_bounds__(256) silu_pack_kernel(const SiluParams p) {
   // x * (1 / (1 + expf(-x))) (silu.c:17), then gate * up (text.c:417)
   const float h = __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), u);
   const uint32_t gi = p.ff0 + i;
+  const uint32_t epoch = p.ll.epoch_word != nullptr ? ll_epoch(p.ll, p.ll.out_add) : 0u;
   if (p.act != nullptr) {
-    pack_group_to_records(h, gi >> 5, threadIdx.x & 31u, p.act, p.act_x, p.n_x);
+    pack_group_out(h, gi >> 5, threadIdx.x & 31u, p.act, p.ll, epoch);
+  } else if (p.ll.epoch_word != nullptr) {
+    ll_put(p.ll, gi, __float_as_uint(h), epoch);
   } else {
     p.act_f32[gi] = h;
-    for (uint32_t j = 0; j < p.n_x; ++j) p.actf_x[j][gi] = h;
   }
 }
 
@@ -640,7 +694,9 @@ struct TextDecoder {
   uint32_t* gemv_err = nullptr;
   uint32_t arg_blocks = 0;
   // Exchange buffer, one per rank; the other ranks write (push) into it
-  // through CUDA IPC mappings.  It holds what every rank reads whole:
+  // through CUDA IPC mappings.  It holds what every rank reads whole (one
+  // GPU: plain values; tensor parallel: each 32-bit word as an (epoch, word)
+  // pair, see LLExchange, so those regions are sized for twice the bytes):
   //   o_full, d_full    O / down projection outputs, all n_embd rows
   //   logits            this rank's vocabulary slice (read back by the host)
   //   XRecv             flags and the greedy-pick words
@@ -659,13 +715,6 @@ struct TextDecoder {
   uint8_t* xpeer[kMaxParts] = {};  // every rank's exchange buffer (own included)
   bool peer_opened[kMaxParts] = {};
   // where this rank's pushes land in the other ranks' exchange buffers
-  float* push_o[kMaxParts] = {};  // O output rows [e0, e0 + el)
-  float* push_d[kMaxParts] = {};  // down output rows
-  uint8_t* push_ao[kMaxParts] = {};  // O input records (the attention kernel writes this rank's heads)
-  uint8_t* push_ad[kMaxParts] = {};  // down input records (this rank's FFN units)
-  float* push_afo[kMaxParts] = {};
-  float* push_afd[kMaxParts] = {};
-  uint32_t n_push = 0;
   cudaGraphExec_t graph = nullptr;
   uint32_t host_pos = 0;
   bool step_mode = false;  // prompt[] holds every fed token (n_prompt = max_ctx)
@@ -846,12 +895,12 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
     auto up = [](size_t x) { return (x + 4095) & ~(size_t)4095; };  // operand bases: 1024-byte aligned TMA
     const bool q4 = wdt == EOS_DT_Q4_K;
     xoff_o = 0;
-    xoff_d = up(4ull * E);
-    xoff_lg = xoff_d + up(4ull * E);
+    xoff_d = up(8ull * E);
+    xoff_lg = xoff_d + up(8ull * E);
     xoff_fl = xoff_lg + up(4ull * vmax);
     xoff_ao = xoff_fl + up(sizeof(XRecv));
-    xoff_ad = xoff_ao + up(q4 ? (size_t)(E / 256) * kActRec : 4ull * E);
-    xbytes = xoff_ad + up(q4 ? (size_t)(F / 256) * kActRec : 4ull * F);
+    xoff_ad = xoff_ao + up(2ull * (q4 ? (size_t)(E / 256) * kActRec : 4ull * E));
+    xbytes = xoff_ad + up(2ull * (q4 ? (size_t)(F / 256) * kActRec : 4ull * F));
     if (ws > 1 && q4) {  // batched-prefill exchange (allocated with the handles)
       xpf_rows = m.max_ctx < kPrefillRows ? m.max_ctx : kPrefillRows;
       xoff_pfo = xbytes;
@@ -932,17 +981,6 @@ int TextDecoder::attach(const uint8_t* handles) {
 int TextDecoder::attach_buffers(uint8_t* const* bufs) {
   if (world == 1 || graph != nullptr) return graph != nullptr ? EOS_OK : capture();
   for (int q = 0; q < world; ++q) xpeer[q] = bufs[q];
-  n_push = 0;
-  for (int q = 0; q < world; ++q) {
-    if (q == rank) continue;
-    push_o[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_o) + e0;
-    push_d[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_d) + e0;
-    push_ao[n_push] = xpeer[q] + xoff_ao;
-    push_ad[n_push] = xpeer[q] + xoff_ad;
-    push_afo[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_ao);
-    push_afd[n_push] = reinterpret_cast<float*>(xpeer[q] + xoff_ad);
-    ++n_push;
-  }
   return capture();
 }
 
@@ -953,7 +991,8 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
   const uint32_t xps = 4u * m.n_layer + 1u;  // exchanges per step
   cudaError_t e = cudaSuccess;
   int status = EOS_OK;
-  // handshake of the step's exchange number xk, of kind `type`
+  // flag handshake of the step's exchange number xk, of kind `type` (the
+  // greedy pick's)
   auto xsync = [&](uint32_t type, uint32_t xk) {
     XchgSync x{};
     x.world = (uint32_t)world;
@@ -967,24 +1006,42 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
     x.err = &state->err;
     return x;
   };
-  // `extra`: the other ranks' copies of the output rows (push)
+  // Low-latency exchange of a kernel (tensor parallel only; one GPU: plain
+  // buffers): it reads this rank's pairs at xbuf + in_off carrying the
+  // epoch of exchange in_xk, and writes pairs of exchange out_xk into every
+  // rank's buffer at out_off, word 0 at out_word0 (no_off: none).
+  constexpr size_t no_off = ~(size_t)0;
+  auto llx = [&](size_t in_off, uint32_t in_xk, size_t out_off, uint32_t out_xk, uint32_t out_word0) {
+    LLExchange x{};
+    if (world == 1) return x;
+    x.epoch_word = &state->epoch;
+    x.mul = xps;
+    x.in_add = in_xk + 1u;
+    x.out_add = out_xk + 1u;
+    x.in = in_off == no_off ? nullptr : reinterpret_cast<const uint64_t*>(xbuf + in_off);
+    if (out_off != no_off)
+      for (int q = 0; q < world; ++q) x.out[x.n_out++] = reinterpret_cast<uint64_t*>(xpeer[q] + out_off) + out_word0;
+    x.limit_us = &state->wait_limit_us;
+    x.err = &state->err;
+    return x;
+  };
   auto gemv = [&](int dt, const uint8_t* w, const uint8_t* act, const float* actf, float* c, uint32_t n,
-                  uint32_t k, float* const* extra = nullptr, uint32_t n_extra = 0,
-                  const XchgSync* xs = nullptr) -> cudaError_t {
+                  uint32_t k, const LLExchange* ll = nullptr) -> cudaError_t {
     if (n == 0) return cudaSuccess;
     if (dt == EOS_DT_Q4_K)
-      return launch_q4k_gemv(w, act, nullptr, c, n, k, gemv_err, num_sms, max_smem, true, s, &status, extra,
-                             n_extra, xs);
-    return launch_q80_gemv(w, actf, c, n, k, gemv_err, num_sms, max_smem, s, &status, extra, n_extra, xs);
+      return launch_q4k_gemv(w, act, nullptr, c, n, k, gemv_err, num_sms, max_smem, true, s, &status, nullptr, 0,
+                             ll);
+    return launch_q80_gemv(w, actf, c, n, k, gemv_err, num_sms, max_smem, s, &status, nullptr, 0, ll);
   };
-  // x_out = x_in + part (part: d_full / o_full, pushed by every rank), then
-  // rmsnorm and the packing for a consumer of dtype dt_a
-  auto norm_pack = [&](const float* x_in, const float* part, float* x_out, const float* w, int dt_a, uint32_t type,
+  // x_out = x_in + part (part: d_full / o_full, tensor parallel: the pairs
+  // every rank pushed into the same region), then rmsnorm and the packing
+  // for a consumer of dtype dt_a
+  auto norm_pack = [&](const float* x_in, const float* part, float* x_out, const float* w, int dt_a, size_t part_off,
                        uint32_t xk) -> cudaError_t {
     NormPackParams p{};
     p.x_in = x_in;
     p.part = part;
-    p.xs = xsync(type, xk);
+    if (part != nullptr) p.ll = llx(part_off, xk, no_off, 0, 0);
     p.tok_embd = tok_embd;
     p.prompt = prompt;
     p.state = state;
@@ -994,12 +1051,14 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
     p.n = E;
     p.act = dt_a == EOS_DT_Q4_K ? act_e : nullptr;
     p.act_f32 = dt_a == EOS_DT_Q8_0 ? actf_e : nullptr;
-    return launch_pdl(norm_pack_kernel, dim3(E / 256u), dim3(256), s, p);
+    // chunk registers for the model width only (the sums run in the same order)
+    return E <= 4096u ? launch_pdl(norm_pack_kernel<4>, dim3(E / 256u), dim3(256), s, p)
+                      : launch_pdl(norm_pack_kernel<kNormMaxChunks>, dim3(E / 256u), dim3(256), s, p);
   };
   for (uint32_t L = 0; L < m.n_layer && e == cudaSuccess; ++L) {
     const DecLayer& d = layers[L];
     // x1 = (L == 0 ? embedding : x0 + down output); act_e = pack(rmsnorm(x1))
-    e = norm_pack(L == 0 ? nullptr : x0, L == 0 ? nullptr : d_full, x1, d.attn_norm, wdt, kXDRows,
+    e = norm_pack(L == 0 ? nullptr : x0, L == 0 ? nullptr : d_full, x1, d.attn_norm, wdt, xoff_d,
                   L == 0 ? 0u : 4u * L - 1u);
     if (e == cudaSuccess) e = gemv(wdt, d.wqkv, act_e, actf_e, qkv, nqkv, E);
     if (e == cudaSuccess) {
@@ -1012,11 +1071,7 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
       a.state = state;
       a.act = act_o;
       a.act_f32 = actf_o;
-      a.n_x = n_push;
-      for (uint32_t j = 0; j < n_push; ++j) {
-        a.act_x[j] = act_o != nullptr ? push_ao[j] : nullptr;
-        a.actf_x[j] = actf_o != nullptr ? push_afo[j] : nullptr;
-      }
+      a.ll = llx(no_off, 0, xoff_ao, 4u * L, 0);  // exchange 4 L: the attention output
       a.hl = hl;
       a.h0 = h0;
       a.kvl = kvl;
@@ -1032,12 +1087,12 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
       else if (hd == 128) e = launch_pdl_smem(attn_kernel<4>, grid, dim3(128), sm, s, a);
       else e = launch_pdl_smem(attn_kernel<8>, grid, dim3(128), sm, s, a);
     }
-    if (e == cudaSuccess) {  // this rank's O rows of all heads' attention output
-      const XchgSync xs = xsync(kXAttn, 4u * L);
-      e = gemv(wdt, d.wo, act_o, actf_o, o_full + e0, el, E, push_o, n_push, &xs);
+    if (e == cudaSuccess) {  // this rank's O rows of all heads' attention output (exchange 4 L + 1)
+      const LLExchange ll = llx(xoff_ao, 4u * L, xoff_o, 4u * L + 1u, e0);
+      e = gemv(wdt, d.wo, act_o, actf_o, o_full + e0, el, E, &ll);
     }
     // x0 = x1 + O output; act_e = pack(rmsnorm(x0))
-    if (e == cudaSuccess) e = norm_pack(x1, o_full, x0, d.ffn_norm, wdt, kXORows, 4u * L + 1u);
+    if (e == cudaSuccess) e = norm_pack(x1, o_full, x0, d.ffn_norm, wdt, xoff_o, 4u * L + 1u);
     if (e == cudaSuccess) e = gemv(wdt, d.wgu, act_e, actf_e, gu, 2 * ffl, E);
     if (e == cudaSuccess) {
       SiluParams sp{};
@@ -1046,21 +1101,17 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
       sp.ff0 = ff0;
       sp.act = act_d;
       sp.act_f32 = actf_d;
-      sp.n_x = n_push;
-      for (uint32_t j = 0; j < n_push; ++j) {
-        sp.act_x[j] = act_d != nullptr ? push_ad[j] : nullptr;
-        sp.actf_x[j] = actf_d != nullptr ? push_afd[j] : nullptr;
-      }
+      sp.ll = llx(no_off, 0, xoff_ad, 4u * L + 2u, 0);  // exchange 4 L + 2: the SiLU output
       e = launch_pdl(silu_pack_kernel, dim3((ffl + 255u) / 256u), dim3(256), s, sp);
     }
-    if (e == cudaSuccess) {  // this rank's down rows over all FFN units
-      const XchgSync xs = xsync(kXSilu, 4u * L + 2u);
-      e = gemv(wdt, d.wd, act_d, actf_d, d_full + e0, el, F, push_d, n_push, &xs);
+    if (e == cudaSuccess) {  // this rank's down rows over all FFN units (exchange 4 L + 3)
+      const LLExchange ll = llx(xoff_ad, 4u * L + 2u, xoff_d, 4u * L + 3u, e0);
+      e = gemv(wdt, d.wd, act_d, actf_d, d_full + e0, el, F, &ll);
     }
   }
   // final norm + LM head + greedy pick (text.c:425-432, greedy.c:66-69)
   if (e == cudaSuccess)
-    e = norm_pack(m.n_layer ? x0 : nullptr, m.n_layer ? d_full : nullptr, x1, out_norm, odt, kXDRows,
+    e = norm_pack(m.n_layer ? x0 : nullptr, m.n_layer ? d_full : nullptr, x1, out_norm, odt, xoff_d,
                   m.n_layer ? 4u * m.n_layer - 1u : 0u);
   if (e == cudaSuccess) e = gemv(odt, wout, act_e, actf_e, logits, vl, E);
   if (e == cudaSuccess) {
@@ -1236,7 +1287,8 @@ int TextDecoder::capture() {
   // the largest shared-memory carveout, so that a kernel's CTAs can share an
   // SM with the CTAs of the kernel before it (PDL overlap)
   for (const void* f : {(const void*)attn_kernel<2>, (const void*)attn_kernel<4>, (const void*)attn_kernel<8>,
-                        (const void*)norm_pack_kernel, (const void*)silu_pack_kernel, (const void*)argmax_kernel})
+                        (const void*)norm_pack_kernel<4>, (const void*)norm_pack_kernel<kNormMaxChunks>,
+                        (const void*)silu_pack_kernel, (const void*)argmax_kernel})
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess) e = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);

@@ -131,6 +131,56 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// ---- low-latency exchange (tensor-parallel decode) -----------------------
+// Every 32-bit word of an exchanged vector travels together with the epoch
+// of the exchange in ONE aligned 64-bit store (epoch in the high half), so a
+// consumer needs no separate flag: it polls the words themselves, in its own
+// GPU's memory, until each carries the expected epoch.  A 64-bit access is
+// single-copy atomic, so a word is never seen without its epoch, and the
+// producers' stores leave while the producing kernel still runs -- the
+// exchange costs one NVLink trip after the last store instead of a kernel
+// completion, a system fence and a flag trip.  Epochs only grow
+// (step * exchanges_per_step + exchange + 1), so buffers need no clearing;
+// a word is rewritten with the next epoch only after its reader has passed a
+// later exchange that the writer waited for.
+struct LLExchange {
+  const uint32_t* epoch_word;  // completed steps; nullptr: no low-latency exchange (one GPU)
+  uint32_t mul;                // exchanges per step
+  uint32_t in_add, out_add;    // epoch = *epoch_word * mul + add, of what is read / written
+  const uint64_t* in;          // consumer: this rank's buffer of (epoch, word) pairs
+  uint64_t* out[8];            // producer: the same buffer of every rank (own included)
+  uint32_t n_out;
+  const uint32_t* limit_us;    // bound on a consumer's wait, in microseconds
+  uint32_t* err;               // EOS_DEVERR_PEER when a wait runs out
+};
+
+__device__ __forceinline__ uint32_t ll_epoch(const LLExchange& x, uint32_t add) { return *x.epoch_word * x.mul + add; }
+
+// Word i of the exchanged vector, with `epoch`, into every destination.
+__device__ __forceinline__ void ll_put(const LLExchange& x, size_t i, uint32_t word, uint32_t epoch) {
+  const uint64_t v = ((uint64_t)epoch << 32) | word;
+  for (uint32_t j = 0; j < x.n_out; ++j)
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(x.out[j] + i), "l"(v) : "memory");
+}
+
+// Two consecutive pairs (16-byte aligned): each 64-bit half is read atomically.
+__device__ __forceinline__ void ll_load2(const uint64_t* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// A consumer thread's wait budget: false once the limit has passed since its
+// first unsuccessful poll (t0), or once an earlier exchange of the step lost
+// a peer.
+__device__ __forceinline__ bool ll_keep_waiting(const LLExchange& x, uint64_t& t0) {
+  const uint64_t now = global_timer_ns();
+  if (t0 == 0) {
+    t0 = now;
+    return true;
+  }
+  if (now - t0 > (uint64_t)*x.limit_us * 1000ull) return false;
+  return !(x.err != nullptr && (*(volatile const uint32_t*)x.err & EOS_DEVERR_PEER) != 0u);
+}
+
 // ---- programmatic dependent launch --------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

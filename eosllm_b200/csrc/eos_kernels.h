@@ -10,7 +10,7 @@
 #include <initializer_list>
 
 namespace eos {
-struct XchgSync;  // eos_common.cuh
+struct LLExchange;  // eos_common.cuh
 }
 
 // Layouts the activation packer can write.
@@ -38,12 +38,13 @@ cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out
 // after c (tensor-parallel push into other GPUs' IPC-mapped buffers; visible
 // to them once the grid has completed); not supported by the unstaged
 // fallback.
-// xs (optional, xs->world > 1): the tensor-parallel handshake every CTA runs
-// after its griddepcontrol.wait and before it reads the activations, which
-// the other ranks pushed into `act` (CTA 0 publishes; see xchg_handshake).
+// ll (optional, ll->epoch_word != nullptr): tensor parallel -- the packed
+// activation records are read as the (epoch, word) pairs every rank pushed
+// into ll->in (polled, bounded), and every output r goes as a pair to
+// ll->out[j] + r instead of to c (see LLExchange).
 cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
                             uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status,
-                            float* const* c_extra = nullptr, uint32_t n_extra = 0, const XchgSync* xs = nullptr);
+                            float* const* c_extra = nullptr, uint32_t n_extra = 0, const LLExchange* ll = nullptr);
 void set_q4k_gemv_variant(int v);
 // Copies `bytes` (a multiple of 16; both addresses 16-byte aligned) from
 // device memory written by the previous kernel on `st` to `dst`, typically
@@ -71,7 +72,7 @@ cudaError_t launch_prefill_gemm(const void* act, const void* wprep, float* c, ui
 
 cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t n, uint32_t k, uint32_t* err,
                             int num_sms, int max_smem, cudaStream_t st, int* out_status,
-                            float* const* c_extra = nullptr, uint32_t n_extra = 0, const XchgSync* xs = nullptr);
+                            float* const* c_extra = nullptr, uint32_t n_extra = 0, const LLExchange* ll = nullptr);
 void set_q80_gemv_variant(int v);
 
 // Test/utility kernels (eos_util.cu).

@@ -170,28 +170,77 @@ struct Q4kGemvParams {
   // receive buffers, mapped through CUDA IPC), written after c
   float* c_extra[7];
   uint32_t n_extra;
-  // tensor parallel (xs.world > 1): the other ranks pushed parts of `act`;
-  // handshake before reading it
-  XchgSync xs;
+  // tensor parallel (ll.epoch_word != nullptr): the activation records arrive
+  // as (epoch, word) pairs from every rank (ll.in), and every output goes to
+  // every rank as a pair (ll.out) instead of to c
+  LLExchange ll;
 };
 
-// The tensor-parallel handshake of a GEMV CTA (no-op on one GPU): after the
-// PDL wait, before the activations are read.  On a timeout the CTA drains its
-// weight copies and leaves (outputs unwritten, error bit set).
-__device__ __forceinline__ bool gemv_handshake(const Q4kGemvParams& p) {
-  if (p.xs.world < 2) return true;
-  if (xchg_handshake(p.xs, blockIdx.x == 0, true)) return true;
+// Packed activation records from a buffer of (epoch, word) pairs into shared
+// memory (word i of the record layout is pair i), every load of a round in
+// flight at once; a round is reloaded until all its pairs carry `epoch`.
+// Padding words of the records (bytes [160, 272) and [432, 480) of each
+// 480-byte record) are never written by producers and are not waited for.
+// Returns false when the wait ran out.
+template <int NT>
+__device__ __forceinline__ bool copy_act_ll_to_smem(const LLExchange& x, uint32_t epoch, uint8_t* dst,
+                                                    uint32_t bytes) {
+  const uint32_t n16 = bytes >> 3;  // 16-byte units of the pair buffer (two words of the records each)
+  uint64_t t0 = 0;
+  for (uint32_t base = 0; base < n16; base += 8u * NT) {
+    uint64_t lo[8], hi[8];
+    bool ready;
+    do {
+      ready = true;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t t = base + (uint32_t)j * NT + threadIdx.x;
+        if (t < n16) {
+          ll_load2(x.in + 2u * t, lo[j], hi[j]);
+          const uint32_t rw = (2u * t) % (kActRec / 4u);  // word within its record
+          const bool pad = !(rw < 40u || (rw >= kActHalf / 4u && rw < kActHalf / 4u + 40u));
+          if (!pad && ((uint32_t)(lo[j] >> 32) != epoch || (uint32_t)(hi[j] >> 32) != epoch)) ready = false;
+        }
+      }
+      if (!ready && !ll_keep_waiting(x, t0)) return false;
+    } while (!ready);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t t = base + (uint32_t)j * NT + threadIdx.x;
+      if (t < n16) reinterpret_cast<uint2*>(dst)[t] = make_uint2((uint32_t)lo[j], (uint32_t)hi[j]);
+    }
+  }
+  return true;
+}
+
+// After the PDL wait: the activations into shared memory -- packed in the CTA
+// (fused path), copied from the packed records, or, tensor parallel, polled
+// from the (epoch, word) pairs the ranks pushed.  On a timeout the CTA drains
+// its weight copies and leaves (outputs unwritten, error bit set).
+template <int NW>
+__device__ __forceinline__ bool gemv_load_act(const Q4kGemvParams& p, uint8_t* act_s, uint32_t warp, uint32_t lane) {
+  bool ok = true;
+  if (p.ll.epoch_word != nullptr) {
+    ok = copy_act_ll_to_smem<NW * 32>(p.ll, ll_epoch(p.ll, p.ll.in_add), act_s, p.act_bytes);
+  } else if (p.a != nullptr) {
+    pack_into_smem<NW>(p.a, p.k, act_s, warp, lane);
+  } else {
+    copy_act_to_smem<NW * 32>(p.act, act_s, p.act_bytes);
+  }
+  if (__syncthreads_and(ok)) return true;
+  if (threadIdx.x == 0) report(p.ll.err, EOS_DEVERR_PEER);
   cp_async_wait<0>();
   return false;
 }
 
 // c[r] = v and the same value into every extra destination (other GPUs'
-// receive slots, plain stores over NVLink).  No fence here: the consumer
-// learns of the rows through a flag that a later kernel raises after this
-// grid has completed (griddepcontrol.wait) and after its own system-scope
-// fence, and a grid's stores -- remote ones included -- are performed when
-// it completes.  (A fence per writing thread measured ~9 us per exchange.)
-__device__ __forceinline__ void gemv_store(const Q4kGemvParams& p, uint32_t r, float v) {
+// buffers, plain stores over NVLink), or, tensor parallel, the pair
+// (out_epoch, v) into every rank's buffer.
+__device__ __forceinline__ void gemv_store(const Q4kGemvParams& p, uint32_t r, float v, uint32_t out_epoch) {
+  if (p.ll.epoch_word != nullptr) {
+    ll_put(p.ll, r, __float_as_uint(v), out_epoch);
+    return;
+  }
   p.c[r] = v;
   for (uint32_t j = 0; j < p.n_extra; ++j) p.c_extra[j][r] = v;
 }
@@ -234,13 +283,8 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParam
   for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(warp + d * NW, d);
 
   pdl_wait();  // the activations are the previous kernel's output
-  if (!gemv_handshake(p)) return;
-  if (p.a != nullptr) {
-    pack_into_smem<NW>(p.a, p.k, act_s, warp, lane);
-  } else {
-    copy_act_to_smem<NW * 32>(p.act, act_s, p.act_bytes);
-  }
-  __syncthreads();
+  if (!gemv_load_act<NW>(p, act_s, warp, lane)) return;
+  const uint32_t out_epoch = p.ll.epoch_word != nullptr ? ll_epoch(p.ll, p.ll.out_add) : 0u;
   pdl_trigger();  // every CTA holds its activations: the next kernel may start
 
   const uint32_t h = lane & 1u;
@@ -285,7 +329,7 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_kernel(const Q4kGemvParam
         }
       }
       for (; b < nb; ++b) acc = __fadd_rn(acc, pr[b]);
-      gemv_store(p, r0 + s * R + lane, acc);
+      gemv_store(p, r0 + s * R + lane, acc, out_epoch);
     }
     __syncwarp();  // partial buffer free for the next stage
   }
@@ -347,13 +391,8 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_cols_kernel(const Q4kGemv
   for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(d);
 
   pdl_wait();
-  if (!gemv_handshake(p)) return;
-  if (p.a != nullptr) {
-    pack_into_smem<NW>(p.a, p.k, act_s, warp, lane);
-  } else {
-    copy_act_to_smem<NW * 32>(p.act, act_s, p.act_bytes);
-  }
-  __syncthreads();
+  if (!gemv_load_act<NW>(p, act_s, warp, lane)) return;
+  const uint32_t out_epoch = p.ll.epoch_word != nullptr ? ll_epoch(p.ll, p.ll.out_add) : 0u;
   pdl_trigger();
 
   const uint32_t h = lane & 1u;
@@ -391,7 +430,7 @@ __global__ void __launch_bounds__(NW * 32, 1) q4k_gemv_cols_kernel(const Q4kGemv
         for (int q = 0; q < 8; ++q) acc = __fadd_rn(acc, v8[q]);
       }
       for (; b < nb; ++b) acc = __fadd_rn(acc, pr[b]);
-      gemv_store(p, r0 + g * R + lane, acc);
+      gemv_store(p, r0 + g * R + lane, acc, out_epoch);
     }
     __syncwarp();
     if (++ch == nch) {
@@ -490,7 +529,7 @@ void set_q4k_gemv_variant(int v) {
 
 cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
                             uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status,
-                            float* const* c_extra, uint32_t n_extra, const XchgSync* xs) {
+                            float* const* c_extra, uint32_t n_extra, const LLExchange* ll) {
   if (n_extra > 7) {
     *out_status = EOS_E_INVALID_ARG;
     return cudaSuccess;
@@ -555,8 +594,8 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   geom(cfg, R, pitch, cb);
   const uint32_t smem = smem_of(cfg);
   if (smem > (uint32_t)max_smem) {  // rows too long to stage: unstaged kernel
-    // it reads packed activations, writes one destination, has no handshake
-    if (act == nullptr || n_extra != 0 || (xs != nullptr && xs->world > 1)) {
+    // it reads packed activations, writes one destination, exchanges nothing
+    if (act == nullptr || n_extra != 0 || (ll != nullptr && ll->epoch_word != nullptr)) {
       *out_status = EOS_E_UNSUPPORTED;
       return cudaSuccess;
     }
@@ -581,7 +620,7 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   if (grid > max_grid) grid = max_grid;
   Q4kGemvParams prm{w, act, a, c, n, k, nb, row_bytes, pitch, R, act_bytes, cb, nch, err, {}, n_extra, {}};
   for (uint32_t j = 0; j < n_extra; ++j) prm.c_extra[j] = c_extra[j];
-  if (xs != nullptr) prm.xs = *xs;
+  if (ll != nullptr) prm.ll = *ll;
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
   lc.blockDim = dim3(cfg.nw * 32);

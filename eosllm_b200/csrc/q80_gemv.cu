@@ -93,7 +93,10 @@ struct Q80GemvParams {
   uint32_t* err;
   float* c_extra[7];  // further copies of every output (tensor-parallel push)
   uint32_t n_extra;
-  XchgSync xs;  // tensor parallel (world > 1): the other ranks pushed parts of `a`
+  // tensor parallel (ll.epoch_word != nullptr): the activations arrive as
+  // (epoch, word) pairs from every rank (ll.in), and every output goes to
+  // every rank as a pair (ll.out) instead of to c
+  LLExchange ll;
 };
 
 // Shared-memory layout of the staged kernel (offsets in bytes).
@@ -182,10 +185,11 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
   for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(warp + d * NW, d);
 
   pdl_wait();  // the activations may be the previous kernel's output
-  if (p.xs.world > 1 && !xchg_handshake(p.xs, blockIdx.x == 0, true)) {
-    cp_async_wait<0>();  // a peer never arrived: drain, leave the outputs unwritten
-    return;
-  }
+  const bool ll = p.ll.epoch_word != nullptr;
+  const uint32_t in_epoch = ll ? ll_epoch(p.ll, p.ll.in_add) : 0u;
+  const uint32_t out_epoch = ll ? ll_epoch(p.ll, p.ll.out_add) : 0u;
+  bool ok = true;
+  uint64_t t0 = 0;
   // activation blocks -> digits.  Block b sits at slot (b % 8) * gpr + b / 8,
   // so the 8 lanes of a shared-memory phase (groups j .. j + 7, same c) read
   // consecutive slots, 112 bytes apart: distinct bank groups.  Four blocks
@@ -193,10 +197,31 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
   constexpr uint32_t U = 4;
   for (uint32_t b0 = warp; b0 < nblk; b0 += U * NW) {
     float v[U];
+    if (ll) {  // (epoch, word) pairs: reload the round until every pair is there
+      bool ready;
+      do {
+        ready = true;
 #pragma unroll
-    for (uint32_t u = 0; u < U; ++u) {
-      const uint32_t b = b0 + u * NW;
-      v[u] = b < nblk ? p.a[(b << 5) + lane] : 0.0f;
+        for (uint32_t u = 0; u < U; ++u) {
+          const uint32_t b = b0 + u * NW;
+          uint64_t pr = ((uint64_t)in_epoch << 32);
+          if (b < nblk) asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(pr) : "l"(p.ll.in + (b << 5) + lane));
+          v[u] = __uint_as_float((uint32_t)pr);
+          if ((uint32_t)(pr >> 32) != in_epoch) ready = false;
+        }
+        ready = __all_sync(0xffffffffu, ready);
+        if (!ready && !__all_sync(0xffffffffu, ll_keep_waiting(p.ll, t0))) {
+          ok = false;
+          break;
+        }
+      } while (!ready);
+      if (!ok) break;
+    } else {
+#pragma unroll
+      for (uint32_t u = 0; u < U; ++u) {
+        const uint32_t b = b0 + u * NW;
+        v[u] = b < nblk ? p.a[(b << 5) + lane] : 0.0f;
+      }
     }
 #pragma unroll
     for (uint32_t u = 0; u < U; ++u) {
@@ -206,7 +231,11 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
                     pw2 + (b % kQ8Group) * gpr + b / kQ8Group);
     }
   }
-  __syncthreads();
+  if (!__syncthreads_and(ok)) {  // a peer never arrived: drain, leave the outputs unwritten
+    if (threadIdx.x == 0) report(p.ll.err, EOS_DEVERR_PEER);
+    cp_async_wait<0>();
+    return;
+  }
   pdl_trigger();
 
   uint32_t slot = 0;
@@ -265,10 +294,12 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
     const float* pr = part + row * (gpr + 1u);
     float sum = 0.0f;
     for (uint32_t j = 0; j < gpr; ++j) sum = __fadd_rn(sum, pr[j]);
-    p.c[r0 + row] = sum;
-    // extra destinations: plain remote stores, ordered before the consumer's
-    // flag by grid completion (see gemv_store, q4k_gemv.cu)
-    for (uint32_t x = 0; x < p.n_extra; ++x) p.c_extra[x][r0 + row] = sum;
+    if (ll) {
+      ll_put(p.ll, r0 + row, __float_as_uint(sum), out_epoch);
+    } else {
+      p.c[r0 + row] = sum;
+      for (uint32_t x = 0; x < p.n_extra; ++x) p.c_extra[x][r0 + row] = sum;
+    }
   }
 }
 
@@ -289,7 +320,7 @@ void set_q80_gemv_variant(int v) { g_q80_variant = v; }
 
 cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t n, uint32_t k, uint32_t* err,
                             int num_sms, int max_smem, cudaStream_t st, int* out_status, float* const* c_extra,
-                            uint32_t n_extra, const XchgSync* xs) {
+                            uint32_t n_extra, const LLExchange* ll) {
   if (n_extra > 7) {
     *out_status = EOS_E_INVALID_ARG;
     return cudaSuccess;
@@ -330,7 +361,7 @@ cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t
     }
   }
   if (pick < 0) {
-    if (n_extra != 0 || (xs != nullptr && xs->world > 1)) {  // the unstaged kernel: one destination, no handshake
+    if (n_extra != 0 || (ll != nullptr && ll->epoch_word != nullptr)) {  // unstaged: one destination, no exchange
       *out_status = EOS_E_UNSUPPORTED;
       return cudaSuccess;
     }
@@ -346,7 +377,7 @@ cudaError_t launch_q80_gemv(const uint8_t* w, const float* a, float* c, uint32_t
   if (grid > n) grid = n;
   Q80GemvParams prm{w, a, c, n, k, nblk, row_bytes, rows_max, err, {}, n_extra, {}};
   for (uint32_t j = 0; j < n_extra; ++j) prm.c_extra[j] = c_extra[j];
-  if (xs != nullptr) prm.xs = *xs;
+  if (ll != nullptr) prm.ll = *ll;
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
   lc.blockDim = dim3(cfg.nw * 32);
