@@ -880,7 +880,7 @@ def run_decode(args, dev, world, rank) -> dict:
                      "frac": round((wbytes + kv_avg) / world / (ms_tok * 1e-3) / 1e9 / peak, 4),
                      "tok_s_at_peak": round(world * peak * 1e9 / (wbytes + kv_avg), 1),
                      "tok_s_weight_only_at_peak": round(world * peak * 1e9 / wbytes, 1)},
-        "launches_per_token": 8 * cfg["n_layer"] + 3,
+        "launches_per_token": dec.step_kernels,  # counted: the nodes of the step's CUDA graph
         "first_tokens": [int(x) for x in toks[:8]],
         # all P.. greedy picks (the one after the prompt, then G more), the
         # same on every GPU count when tensor parallelism is exact

@@ -173,6 +173,11 @@ class TextDecoder:
         return int(self.lib.eosi_cuda_text_pos(self.handle))
 
     @property
+    def step_kernels(self) -> int:
+        """Kernels one step launches (nodes of the step's CUDA graph)."""
+        return int(self.lib.eosi_cuda_text_step_kernels(self.handle))
+
+    @property
     def stream(self) -> int:
         return int(self.lib.eosi_cuda_text_stream(self.handle) or 0)
 

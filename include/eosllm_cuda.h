@@ -321,6 +321,9 @@ EOSLLM_CUDA_API int eosi_cuda_text_set_wait_limit(eosi_cuda_text_t *t, uint32_t 
  * vocab_len, out_row0, out_rows} (out_row*: the O / down output rows). */
 EOSLLM_CUDA_API int eosi_cuda_text_partition(const eosi_cuda_llama_t *m, int rank, int world, uint32_t *out);
 /* The decoder's cudaStream_t (as void*), for timing with events. */
+/* Kernels one step launches (the nodes of its CUDA graph; 0 before the
+ * step is built). */
+EOSLLM_CUDA_API uint32_t eosi_cuda_text_step_kernels(const eosi_cuda_text_t *t);
 EOSLLM_CUDA_API void *eosi_cuda_text_stream(eosi_cuda_text_t *t);
 EOSLLM_CUDA_API void eosi_cuda_text_close(eosi_cuda_text_t *t);
 
