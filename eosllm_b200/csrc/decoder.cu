@@ -1056,32 +1056,12 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
     return E <= 4096u ? launch_pdl(norm_pack_kernel<4>, dim3(E / 256u), dim3(256), s, p)
                       : launch_pdl(norm_pack_kernel<kNormMaxChunks>, dim3(E / 256u), dim3(256), s, p);
   };
-  // rmsnorm + packing fused into the Q4_K GEMV that consumes it (one kernel
-  // boundary less); false when that GEMV cannot take it (the caller then
-  // launches norm_pack and the plain GEMV)
-  auto fused = [&](int dt, const uint8_t* w, float* c, uint32_t n, const float* x_in, const float* part,
-                   size_t part_off, uint32_t xk, float* x_out, const float* nw) -> bool {
-    if (dt != EOS_DT_Q4_K || E > 4096u || e != cudaSuccess) return false;
-    GemvNorm g{x_in, part, tok_embd, prompt, reinterpret_cast<const uint32_t*>(state), nw, m.rms_eps, x_out};
-    const LLExchange ll = part != nullptr ? llx(part_off, xk, no_off, 0, 0) : LLExchange{};
-    int st = EOS_OK;
-    const cudaError_t r =
-        launch_q4k_gemv(w, nullptr, nullptr, c, n, E, gemv_err, num_sms, max_smem, true, s, &st, nullptr, 0, &ll, &g);
-    if (r == cudaSuccess && st == EOS_E_UNSUPPORTED) return false;
-    e = r;
-    if (st != EOS_OK) status = st;
-    return true;
-  };
   for (uint32_t L = 0; L < m.n_layer && e == cudaSuccess; ++L) {
     const DecLayer& d = layers[L];
     // x1 = (L == 0 ? embedding : x0 + down output); act_e = pack(rmsnorm(x1))
-    if (!fused(wdt, d.wqkv, qkv, nqkv, L == 0 ? nullptr : x0, L == 0 ? nullptr : d_full, xoff_d,
-               L == 0 ? 0u : 4u * L - 1u, x1, d.attn_norm)) {
-      if (e == cudaSuccess)
-        e = norm_pack(L == 0 ? nullptr : x0, L == 0 ? nullptr : d_full, x1, d.attn_norm, wdt, xoff_d,
-                      L == 0 ? 0u : 4u * L - 1u);
-      if (e == cudaSuccess) e = gemv(wdt, d.wqkv, act_e, actf_e, qkv, nqkv, E);
-    }
+    e = norm_pack(L == 0 ? nullptr : x0, L == 0 ? nullptr : d_full, x1, d.attn_norm, wdt, xoff_d,
+                  L == 0 ? 0u : 4u * L - 1u);
+    if (e == cudaSuccess) e = gemv(wdt, d.wqkv, act_e, actf_e, qkv, nqkv, E);
     if (e == cudaSuccess) {
       AttnParams a{};
       a.qkv = qkv;
@@ -1113,10 +1093,8 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
       e = gemv(wdt, d.wo, act_o, actf_o, o_full + e0, el, E, &ll);
     }
     // x0 = x1 + O output; act_e = pack(rmsnorm(x0))
-    if (!fused(wdt, d.wgu, gu, 2 * ffl, x1, o_full, xoff_o, 4u * L + 1u, x0, d.ffn_norm)) {
-      if (e == cudaSuccess) e = norm_pack(x1, o_full, x0, d.ffn_norm, wdt, xoff_o, 4u * L + 1u);
-      if (e == cudaSuccess) e = gemv(wdt, d.wgu, act_e, actf_e, gu, 2 * ffl, E);
-    }
+    if (e == cudaSuccess) e = norm_pack(x1, o_full, x0, d.ffn_norm, wdt, xoff_o, 4u * L + 1u);
+    if (e == cudaSuccess) e = gemv(wdt, d.wgu, act_e, actf_e, gu, 2 * ffl, E);
     if (e == cudaSuccess) {
       SiluParams sp{};
       sp.gu = gu;
@@ -1133,13 +1111,10 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
     }
   }
   // final norm + LM head + greedy pick (text.c:425-432, greedy.c:66-69)
-  if (!fused(odt, wout, logits, vl, m.n_layer ? x0 : nullptr, m.n_layer ? d_full : nullptr, xoff_d,
-             m.n_layer ? 4u * m.n_layer - 1u : 0u, x1, out_norm)) {
-    if (e == cudaSuccess)
-      e = norm_pack(m.n_layer ? x0 : nullptr, m.n_layer ? d_full : nullptr, x1, out_norm, odt, xoff_d,
-                    m.n_layer ? 4u * m.n_layer - 1u : 0u);
-    if (e == cudaSuccess) e = gemv(odt, wout, act_e, actf_e, logits, vl, E);
-  }
+  if (e == cudaSuccess)
+    e = norm_pack(m.n_layer ? x0 : nullptr, m.n_layer ? d_full : nullptr, x1, out_norm, odt, xoff_d,
+                  m.n_layer ? 4u * m.n_layer - 1u : 0u);
+  if (e == cudaSuccess) e = gemv(odt, wout, act_e, actf_e, logits, vl, E);
   if (e == cudaSuccess) {
     ArgmaxParams a{};
     a.logits = logits;

@@ -38,34 +38,13 @@ cudaError_t launch_act_pack(const float* a, uint32_t m, uint32_t k, uint8_t* out
 // after c (tensor-parallel push into other GPUs' IPC-mapped buffers; visible
 // to them once the grid has completed); not supported by the unstaged
 // fallback.
-// The decoder's rmsnorm and Q8 packing of a GEMV's input, fused into the GEMV
-// (launch_q4k_gemv's `norm`): each CTA forms x = x_in + t (t: `part`, or,
-// tensor parallel, the (epoch, word) pairs at ll->in) or the token embedding
-// (x_in == nullptr), normalises it with norm_pack_kernel's arithmetic and
-// summation order and packs it into its own activation records; CTA 0 also
-// writes x to x_out.  k <= 4096, 8-warp configurations only.
-struct GemvNorm {
-  const float* x_in;
-  const float* part;
-  const uint16_t* tok_embd;      // F16 [n_vocab][k] (embedding mode)
-  const uint32_t* prompt;        // token of step pos when pos < n_prompt
-  const uint32_t* state_words;   // the decoder's state: [0] pos, [1] n_prompt, [2] next_token
-  const float* w;                // norm weight
-  float eps;
-  float* x_out;                  // may be nullptr
-};
-
 // ll (optional, ll->epoch_word != nullptr): tensor parallel -- the packed
-// activation records (with `norm`: the vector t) are read as the (epoch,
-// word) pairs every rank pushed into ll->in (polled, bounded), and every
-// output r goes as a pair to ll->out[j] + r instead of to c (see
-// LLExchange).  norm (optional): the input's rmsnorm + packing in the GEMV
-// (act and a unused); out_status EOS_E_UNSUPPORTED when the shape's kernel
-// cannot take it (the caller launches the separate norm kernel instead).
+// activation records are read as the (epoch, word) pairs every rank pushed
+// into ll->in (polled, bounded), and every output r goes as a pair to
+// ll->out[j] + r instead of to c (see LLExchange).
 cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
                             uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status,
-                            float* const* c_extra = nullptr, uint32_t n_extra = 0, const LLExchange* ll = nullptr,
-                            const GemvNorm* norm = nullptr);
+                            float* const* c_extra = nullptr, uint32_t n_extra = 0, const LLExchange* ll = nullptr);
 void set_q4k_gemv_variant(int v);
 // Copies `bytes` (a multiple of 16; both addresses 16-byte aligned) from
 // device memory written by the previous kernel on `st` to `dst`, typically

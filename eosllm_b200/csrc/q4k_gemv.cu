@@ -174,9 +174,6 @@ struct Q4kGemvParams {
   // as (epoch, word) pairs from every rank (ll.in), and every output goes to
   // every rank as a pair (ll.out) instead of to c
   LLExchange ll;
-  uint32_t fuse_norm;  // 1: `norm` forms the activations (8 warps, k <= 4096)
-  uint32_t norm_off;   // dynamic shared-memory offset of the normalised vector
-  GemvNorm norm;
 };
 
 // Packed activation records from a buffer of (epoch, word) pairs into shared
@@ -216,119 +213,6 @@ __device__ __forceinline__ bool copy_act_ll_to_smem(const LLExchange& x, uint32_
   return true;
 }
 
-__device__ __forceinline__ float4 norm_ld4(const float* p, uint32_t c) { return reinterpret_cast<const float4*>(p)[c]; }
-__device__ __forceinline__ float4 norm_add4(float4 a, float4 b) {
-  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
-}
-
-// The decoder's rmsnorm and packing (GemvNorm), for 256 threads: thread t
-// holds float4 chunks t, t + 256, ... (k <= 4096: four), sums their squares
-// in order, then the warp's xor tree and the 8 warp sums in order -- exactly
-// norm_pack_kernel's order, so the result is bit-identical to it.
-// y = (x * s) * w per element (rmsnorm.c:24-33), packed per 32 into this
-// CTA's records.  Returns false when a tensor-parallel wait ran out (the CTA
-// still passes every barrier).
-__device__ __forceinline__ bool gemv_norm_pack(const Q4kGemvParams& p, uint8_t* act_s, float* ys) {
-  constexpr uint32_t NCH = 4;
-  __shared__ float red[8];
-  const GemvNorm& g = p.norm;
-  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-  const uint32_t n = p.k, nch = n >> 2;
-  bool ok = true;
-  float4 v[NCH];
-  if (g.x_in == nullptr) {
-    const uint32_t pos = g.state_words[0];
-    const uint32_t tok = pos < g.state_words[1] ? g.prompt[pos] : g.state_words[2];
-    const uint2* emb = reinterpret_cast<const uint2*>(g.tok_embd + (size_t)tok * n);
-#pragma unroll
-    for (uint32_t j = 0; j < NCH; ++j) {
-      const uint32_t c = tid + 256u * j;
-      if (c < nch) {
-        const uint2 h = emb[c];  // F16 -> F32 is exact
-        v[j] = make_float4(f16_bits_to_f32(h.x), f16_bits_to_f32(h.x >> 16), f16_bits_to_f32(h.y),
-                           f16_bits_to_f32(h.y >> 16));
-      }
-    }
-  } else {
-#pragma unroll
-    for (uint32_t j = 0; j < NCH; ++j) {
-      const uint32_t c = tid + 256u * j;
-      if (c < nch) v[j] = norm_ld4(g.x_in, c);
-    }
-    if (p.ll.epoch_word != nullptr) {  // t as the ranks' (epoch, word) pairs
-      const uint32_t epoch = ll_epoch(p.ll, p.ll.in_add);
-      float4 t[NCH];
-      uint64_t t0 = 0;
-      bool ready;
-      do {
-        ready = true;
-#pragma unroll
-        for (uint32_t j = 0; j < NCH; ++j) {
-          const uint32_t c = tid + 256u * j;
-          if (c < nch) {
-            uint64_t q0, q1, q2, q3;
-            ll_load2(p.ll.in + 4u * c, q0, q1);
-            ll_load2(p.ll.in + 4u * c + 2u, q2, q3);
-            t[j] = make_float4(__uint_as_float((uint32_t)q0), __uint_as_float((uint32_t)q1),
-                               __uint_as_float((uint32_t)q2), __uint_as_float((uint32_t)q3));
-            if ((uint32_t)(q0 >> 32) != epoch || (uint32_t)(q1 >> 32) != epoch ||
-                (uint32_t)(q2 >> 32) != epoch || (uint32_t)(q3 >> 32) != epoch)
-              ready = false;
-          }
-        }
-        if (!ready && !ll_keep_waiting(p.ll, t0)) {
-          ok = false;
-          break;
-        }
-      } while (!ready);
-#pragma unroll
-      for (uint32_t j = 0; j < NCH; ++j)
-        if (tid + 256u * j < nch) v[j] = norm_add4(v[j], t[j]);
-    } else if (g.part != nullptr) {
-#pragma unroll
-      for (uint32_t j = 0; j < NCH; ++j) {
-        const uint32_t c = tid + 256u * j;
-        if (c < nch) v[j] = norm_add4(v[j], __ldcg(reinterpret_cast<const float4*>(g.part) + c));
-      }
-    }
-  }
-  float ss = 0.0f;
-#pragma unroll
-  for (uint32_t j = 0; j < NCH; ++j) {
-    if (tid + 256u * j < nch) {
-      ss = __fadd_rn(ss, __fmul_rn(v[j].x, v[j].x));
-      ss = __fadd_rn(ss, __fmul_rn(v[j].y, v[j].y));
-      ss = __fadd_rn(ss, __fmul_rn(v[j].z, v[j].z));
-      ss = __fadd_rn(ss, __fmul_rn(v[j].w, v[j].w));
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
-  if (lane == 0) red[warp] = ss;
-  __syncthreads();
-  float tot = red[0];
-#pragma unroll
-  for (int w = 1; w < 8; ++w) tot = __fadd_rn(tot, red[w]);
-  // ms /= cols; s = 1 / sqrtf(ms + eps); y = x * s * w  (rmsnorm.c:24-33)
-  const float ms = __fdiv_rn(tot, (float)n);
-  const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, g.eps)));
-#pragma unroll
-  for (uint32_t j = 0; j < NCH; ++j) {
-    const uint32_t c = tid + 256u * j;
-    if (c < nch) {
-      const float4 x = v[j], w4 = norm_ld4(g.w, c);
-      ys[4u * c] = __fmul_rn(__fmul_rn(x.x, sc), w4.x);
-      ys[4u * c + 1u] = __fmul_rn(__fmul_rn(x.y, sc), w4.y);
-      ys[4u * c + 2u] = __fmul_rn(__fmul_rn(x.z, sc), w4.z);
-      ys[4u * c + 3u] = __fmul_rn(__fmul_rn(x.w, sc), w4.w);
-      if (blockIdx.x == 0 && g.x_out != nullptr) reinterpret_cast<float4*>(g.x_out)[c] = x;
-    }
-  }
-  __syncthreads();
-  for (uint32_t gi = warp; gi < (n >> 5); gi += 8u) pack_group_to_record(ys[gi * 32u + lane], gi, lane, act_s);
-  return ok;
-}
-
 // After the PDL wait: the activations into shared memory -- packed in the CTA
 // (fused path), copied from the packed records, or, tensor parallel, polled
 // from the (epoch, word) pairs the ranks pushed.  On a timeout the CTA drains
@@ -336,10 +220,7 @@ __device__ __forceinline__ bool gemv_norm_pack(const Q4kGemvParams& p, uint8_t* 
 template <int NW>
 __device__ __forceinline__ bool gemv_load_act(const Q4kGemvParams& p, uint8_t* act_s, uint32_t warp, uint32_t lane) {
   bool ok = true;
-  if (p.fuse_norm) {
-    extern __shared__ __align__(128) uint8_t gemv_dyn_smem[];
-    if constexpr (NW == 8) ok = gemv_norm_pack(p, act_s, reinterpret_cast<float*>(gemv_dyn_smem + p.norm_off));
-  } else if (p.ll.epoch_word != nullptr) {
+  if (p.ll.epoch_word != nullptr) {
     ok = copy_act_ll_to_smem<NW * 32>(p.ll, ll_epoch(p.ll, p.ll.in_add), act_s, p.act_bytes);
   } else if (p.a != nullptr) {
     pack_into_smem<NW>(p.a, p.k, act_s, warp, lane);
@@ -648,7 +529,7 @@ void set_q4k_gemv_variant(int v) {
 
 cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a, float* c, uint32_t n, uint32_t k,
                             uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status,
-                            float* const* c_extra, uint32_t n_extra, const LLExchange* ll, const GemvNorm* norm) {
+                            float* const* c_extra, uint32_t n_extra, const LLExchange* ll) {
   if (n_extra > 7) {
     *out_status = EOS_E_INVALID_ARG;
     return cudaSuccess;
@@ -711,16 +592,7 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   GemvConfig& cfg = g_cfgs[pick];
   uint32_t R, pitch, cb;
   geom(cfg, R, pitch, cb);
-  uint32_t smem = smem_of(cfg);
-  uint32_t norm_off = 0;
-  if (norm != nullptr) {  // the normalised vector after the staging buffers
-    norm_off = (smem + 15u) & ~15u;
-    smem = norm_off + ((k * 4u + 15u) & ~15u);
-    if (cfg.nw != 8 || k > 4096u || k == 0 || smem > (uint32_t)max_smem) {
-      *out_status = EOS_E_UNSUPPORTED;
-      return cudaSuccess;
-    }
-  }
+  const uint32_t smem = smem_of(cfg);
   if (smem > (uint32_t)max_smem) {  // rows too long to stage: unstaged kernel
     // it reads packed activations, writes one destination, exchanges nothing
     if (act == nullptr || n_extra != 0 || (ll != nullptr && ll->epoch_word != nullptr)) {
@@ -746,14 +618,9 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
   uint32_t grid = (uint32_t)num_sms * cps;
   const uint32_t max_grid = (n + R - 1) / R;
   if (grid > max_grid) grid = max_grid;
-  Q4kGemvParams prm{w, act, a, c, n, k, nb, row_bytes, pitch, R, act_bytes, cb, nch, err, {}, n_extra, {}, 0, 0, {}};
+  Q4kGemvParams prm{w, act, a, c, n, k, nb, row_bytes, pitch, R, act_bytes, cb, nch, err, {}, n_extra, {}};
   for (uint32_t j = 0; j < n_extra; ++j) prm.c_extra[j] = c_extra[j];
   if (ll != nullptr) prm.ll = *ll;
-  if (norm != nullptr) {
-    prm.fuse_norm = 1;
-    prm.norm_off = norm_off;
-    prm.norm = *norm;
-  }
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
   lc.blockDim = dim3(cfg.nw * 32);
