@@ -116,40 +116,58 @@ __host__ __device__ inline Q80Smem q80_smem(uint32_t nblk, uint32_t rows_max, ui
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 
-// One warp converts one 32-value activation block (lane i holds value i):
-// with 2^E <= max|a| < 2^(E+1), every value becomes the integer
-// A = round(a * 2^(19 - E)) (the scaling by a power of two is exact; |A| <=
-// 2^20), written as three signed base-128 digits A = d1 * 2^14 + d2 * 2^7 +
-// d3 (d2, d3 in [-64, 63], |d1| <= 64) into ds[0..31], ds[32..63],
-// ds[64..95]; lane 0 stores the block's unit 2^(E - 19) at *pw.  A block
-// whose largest magnitude is below 2^-100 (or subnormal) takes the slower
-// exact library scaling; a block holding Inf or NaN gets unit NaN.
-__device__ __forceinline__ void q8_act_digits(float v, uint32_t lane, uint8_t* ds, float* pw) {
-  const uint32_t mbits = __reduce_max_sync(0xffffffffu, __float_as_uint(v) & 0x7fffffffu);
-  int A = 0;
+// Eight lanes convert one 32-value activation block, lane i of the eight
+// holding values 4 i .. 4 i + 3: with 2^E <= max|a| < 2^(E+1), every value
+// becomes the integer A = round(a * 2^(19 - E)) (the scaling by a power of
+// two is exact; |A| <= 2^20), written as three signed base-128 digits
+// A = d1 * 2^14 + d2 * 2^7 + d3 (d2, d3 in [-64, 63], |d1| <= 64) -- the
+// lane stores its four d1 bytes as one word at ds + 4 i, its d2 bytes at
+// ds + 32 + 4 i, its d3 bytes at ds + 64 + 4 i; lane 0 of the eight stores the
+// block's unit 2^(E - 19) at *pw.  A block whose largest magnitude is below
+// 2^-100 (or subnormal) takes the slower exact library scaling; a block
+// holding Inf or NaN gets unit NaN.  All 32 lanes of the warp call this.
+__device__ __forceinline__ void q8_act_digits4(float4 v, uint32_t sub, uint8_t* ds, float* pw) {
+  uint32_t mbits = max(max(__float_as_uint(v.x) & 0x7fffffffu, __float_as_uint(v.y) & 0x7fffffffu),
+                       max(__float_as_uint(v.z) & 0x7fffffffu, __float_as_uint(v.w) & 0x7fffffffu));
+  mbits = max(mbits, __shfl_xor_sync(0xffffffffu, mbits, 1));
+  mbits = max(mbits, __shfl_xor_sync(0xffffffffu, mbits, 2));
+  mbits = max(mbits, __shfl_xor_sync(0xffffffffu, mbits, 4));  // the eight lanes of the block
+  const float x[4] = {v.x, v.y, v.z, v.w};
+  int A[4] = {0, 0, 0, 0};
   float unit = 0.0f;
   if (mbits >= 0x7f800000u) {
     unit = __int_as_float(0x7fc00000);
   } else if (mbits >= 0x0d800000u) {  // max|a| >= 2^-100: both factors are normal floats
     const int E = (int)(mbits >> 23) - 127;
     const float up = __int_as_float((19 - E + 127) << 23);
-    // round to nearest even through the 1.5 * 2^23 magic (|a * up| < 2^20)
-    A = __float_as_int(__fadd_rn(__fmul_rn(v, up), 12582912.0f)) - 0x4B400000;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)  // round to nearest even through the 1.5 * 2^23 magic (|a * up| < 2^20)
+      A[q] = __float_as_int(__fadd_rn(__fmul_rn(x[q], up), 12582912.0f)) - 0x4B400000;
     unit = __int_as_float((E - 19 + 127) << 23);
   } else if (mbits != 0u) {
     int e;
     frexpf(__uint_as_float(mbits), &e);  // max|a| < 2^e
-    A = __float2int_rn(ldexpf(v, 20 - e));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) A[q] = __float2int_rn(ldexpf(x[q], 20 - e));
     unit = ldexpf(1.0f, e - 20);
   }
-  const int d3 = ((A + 64) & 127) - 64;
-  const int A2 = (A - d3) >> 7;
-  const int d2 = ((A2 + 64) & 127) - 64;
-  const int d1 = (A2 - d2) >> 7;
-  ds[lane] = static_cast<uint8_t>(d1);
-  ds[32 + lane] = static_cast<uint8_t>(d2);
-  ds[64 + lane] = static_cast<uint8_t>(d3);
-  if (lane == 0) *pw = unit;
+  uint32_t w1 = 0, w2 = 0, w3 = 0;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int d3 = ((A[q] + 64) & 127) - 64;
+    const int A2 = (A[q] - d3) >> 7;
+    const int d2 = ((A2 + 64) & 127) - 64;
+    const int d1 = (A2 - d2) >> 7;
+    w1 |= ((uint32_t)d1 & 0xffu) << (8 * q);
+    w2 |= ((uint32_t)d2 & 0xffu) << (8 * q);
+    w3 |= ((uint32_t)d3 & 0xffu) << (8 * q);
+  }
+  if (ds != nullptr) {
+    reinterpret_cast<uint32_t*>(ds)[sub] = w1;
+    reinterpret_cast<uint32_t*>(ds + 32)[sub] = w2;
+    reinterpret_cast<uint32_t*>(ds + 64)[sub] = w3;
+    if (sub == 0) *pw = unit;
+  }
 }
 
 template <int NW, int D>
@@ -190,24 +208,27 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
   const uint32_t out_epoch = ll ? ll_epoch(p.ll, p.ll.out_add) : 0u;
   bool ok = true;
   uint64_t t0 = 0;
-  // activation blocks -> digits.  Block b sits at slot (b % 8) * gpr + b / 8,
-  // so the 8 lanes of a shared-memory phase (groups j .. j + 7, same c) read
-  // consecutive slots, 112 bytes apart: distinct bank groups.  Four blocks
-  // per warp and round, their loads issued together.
-  constexpr uint32_t U = 4;
-  for (uint32_t b0 = warp; b0 < nblk; b0 += U * NW) {
-    float v[U];
-    if (ll) {  // (epoch, word) pairs: reload the round until every pair is there
+  // activation blocks -> digits, four blocks per warp and round (lane l: block
+  // 4 r + l / 8, values 4 (l % 8) .. 4 (l % 8) + 3).  Block b sits at slot
+  // (b % 8) * gpr + b / 8, so the 8 lanes of a shared-memory phase (groups
+  // j .. j + 7, same c) read consecutive slots, 112 bytes apart: distinct
+  // bank groups.
+  const uint32_t sub = lane & 7u;
+  for (uint32_t b0 = 4u * warp; b0 < nblk; b0 += 4u * NW) {
+    const uint32_t b = b0 + (lane >> 3);
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (ll) {  // (epoch, word) pairs: reload until all four of the lane's are there
       bool ready;
       do {
         ready = true;
-#pragma unroll
-        for (uint32_t u = 0; u < U; ++u) {
-          const uint32_t b = b0 + u * NW;
-          uint64_t pr = ((uint64_t)in_epoch << 32);
-          if (b < nblk) asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(pr) : "l"(p.ll.in + (b << 5) + lane));
-          v[u] = __uint_as_float((uint32_t)pr);
-          if ((uint32_t)(pr >> 32) != in_epoch) ready = false;
+        if (b < nblk) {
+          uint64_t q0, q1, q2, q3;
+          ll_load2(p.ll.in + (b << 5) + 4u * sub, q0, q1);
+          ll_load2(p.ll.in + (b << 5) + 4u * sub + 2u, q2, q3);
+          v = make_float4(__uint_as_float((uint32_t)q0), __uint_as_float((uint32_t)q1),
+                          __uint_as_float((uint32_t)q2), __uint_as_float((uint32_t)q3));
+          ready = (uint32_t)(q0 >> 32) == in_epoch && (uint32_t)(q1 >> 32) == in_epoch &&
+                  (uint32_t)(q2 >> 32) == in_epoch && (uint32_t)(q3 >> 32) == in_epoch;
         }
         ready = __all_sync(0xffffffffu, ready);
         if (!ready && !__all_sync(0xffffffffu, ll_keep_waiting(p.ll, t0))) {
@@ -216,20 +237,13 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
         }
       } while (!ready);
       if (!ok) break;
-    } else {
-#pragma unroll
-      for (uint32_t u = 0; u < U; ++u) {
-        const uint32_t b = b0 + u * NW;
-        v[u] = b < nblk ? p.a[(b << 5) + lane] : 0.0f;
-      }
+    } else if (b < nblk) {
+      v = reinterpret_cast<const float4*>(p.a)[(b << 3) + sub];
     }
-#pragma unroll
-    for (uint32_t u = 0; u < U; ++u) {
-      const uint32_t b = b0 + u * NW;
-      if (b >= nblk) break;  // warp-uniform
-      q8_act_digits(v[u], lane, dig + ((b % kQ8Group) * gpr + b / kQ8Group) * kQ8DigitStride,
-                    pw2 + (b % kQ8Group) * gpr + b / kQ8Group);
-    }
+    // lanes past the last block convert zeros and store nothing (every lane
+    // takes part in the block-max shuffles)
+    const uint32_t slot = (b % kQ8Group) * gpr + b / kQ8Group;
+    q8_act_digits4(v, sub, b < nblk ? dig + slot * kQ8DigitStride : nullptr, pw2 + (b < nblk ? slot : 0u));
   }
   if (!__syncthreads_and(ok)) {  // a peer never arrived: drain, leave the outputs unwritten
     if (threadIdx.x == 0) report(p.ll.err, EOS_DEVERR_PEER);
