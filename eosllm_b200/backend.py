@@ -96,6 +96,8 @@ _SIGNATURES = {
     "eosi_cuda_text_pos": (_u32, [_vp]),
     "eosi_cuda_text_stream": (_vp, [_vp]),
     "eosi_cuda_text_step_kernels": (_u32, [_vp]),
+    "eosi_cuda_text_set_step_mode": (C.c_int, [_vp, C.c_int]),
+    "eosi_cuda_text_step_mode": (C.c_int, [_vp]),
     "eosi_cuda_text_ipc_handle": (C.c_int, [_vp, _vp, _sz]),
     "eosi_cuda_text_attach_peers": (C.c_int, [_vp, _vp, _sz]),
     "eosi_cuda_text_attach_local": (C.c_int, [_vp, C.c_int]),

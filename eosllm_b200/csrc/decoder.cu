@@ -63,15 +63,9 @@
 
 namespace eos {
 
-constexpr uint32_t kMaxParts = 8;
-// 32 positions per attention CTA: 32 KB of K/V staging, small enough for an
-// attention CTA to share an SM with the two CTAs of the QKV GEMV before it
-// and start its K/V copies early (programmatic dependent launch)
-constexpr uint32_t kAttnChunk = 32;       // positions per attention CTA
-constexpr uint32_t kMaxAttnChunks = 512;  // max_ctx <= 16384
-constexpr uint32_t kMergeBatch = 16;      // chunks whose o[d] the merge loads in one batch
 constexpr uint32_t kArgmaxBlocks = 64;  // CTAs of the argmax kernel (upper bound)
 constexpr uint32_t kPrefillRows = 1024;  // tokens per batched-prefill block
+
 
 // ---------------------------------------------------------------------------
 // Residual + rmsnorm + activation packing
@@ -707,6 +701,7 @@ struct TextDecoder {
   // GEMM operands of the O and down inputs.
   uint8_t* xbuf = nullptr;
   size_t xoff_o = 0, xoff_d = 0, xoff_lg = 0, xoff_fl = 0, xoff_ao = 0, xoff_ad = 0, xbytes = 0;
+  size_t xstep_bytes = 0;  // the step's regions: [0, xstep_bytes)
   size_t xoff_pfo = 0, xoff_pfd = 0, xoff_pfa = 0, xoff_pfs = 0;
   uint32_t xpf_rows = 0, pf_epoch = 0;
   float *o_full = nullptr, *d_full = nullptr, *logits = nullptr;
@@ -717,6 +712,14 @@ struct TextDecoder {
   // where this rank's pushes land in the other ranks' exchange buffers
   cudaGraphExec_t graph = nullptr;
   uint32_t step_kernels = 0;  // kernel nodes of the step graph
+  // persistent step (decoder_persistent.cu): one cooperative kernel per
+  // token when the geometry allows (persistent_ok) and the mode asks for it
+  int step_mode_req = EOSI_CUDA_STEP_AUTO;
+  bool persistent_ok = false, persistent = false;
+  PLayer* players = nullptr;                 // device copy of the layer table
+  uint64_t *qkv_x = nullptr, *gu_x = nullptr;  // this rank's q/k/v and gate/up rows as pairs
+  float* parg_v = nullptr;                   // per-CTA greedy candidates
+  uint32_t* parg_i = nullptr;
   uint32_t host_pos = 0;
   bool step_mode = false;  // prompt[] holds every fed token (n_prompt = max_ctx)
   // batched prefill (prefill_text.cu): scratch for pf_rows tokens, allocated
@@ -769,7 +772,9 @@ struct TextDecoder {
   cudaError_t prefill(uint32_t n);  // tokens at prompt[host_pos, host_pos + n)
   XRecv* xrecv(int q) const { return reinterpret_cast<XRecv*>(xpeer[q] + xoff_fl); }
   cudaError_t record_step(cudaStream_t s);
+  cudaError_t record_step_persistent(cudaStream_t s);
   int capture();
+  int set_step_mode(int mode);
 };
 
 // The slice of the model rank rk of ws owns: heads [h0, h0 + hl) (and their
@@ -902,6 +907,7 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
     xoff_ao = xoff_fl + up(sizeof(XRecv));
     xoff_ad = xoff_ao + up(2ull * (q4 ? (size_t)(E / 256) * kActRec : 4ull * E));
     xbytes = xoff_ad + up(2ull * (q4 ? (size_t)(F / 256) * kActRec : 4ull * F));
+    xstep_bytes = xbytes;
     if (ws > 1 && q4) {  // batched-prefill exchange (allocated with the handles)
       xpf_rows = m.max_ctx < kPrefillRows ? m.max_ctx : kPrefillRows;
       xoff_pfo = xbytes;
@@ -946,6 +952,23 @@ int TextDecoder::open(const eosi_cuda_llama_t* desc, int dev, int rk, int ws) {
   chk(alloc(&prompt, 4ull * m.max_ctx));
   chk(alloc(&out_tokens, 4ull * m.max_ctx));
   chk(alloc(&gemv_err, 16));
+  if (e == cudaSuccess && wdt == EOS_DT_Q4_K && odt == EOS_DT_Q4_K &&
+      persistent_step_supported(E, F, hd, max_chunks, m.n_layer, max_smem)) {
+    std::vector<PLayer> tab(m.n_layer);
+    for (uint32_t L = 0; L < m.n_layer; ++L)
+      tab[L] = PLayer{{layers[L].wqkv, layers[L].wo, layers[L].wgu, layers[L].wd}, layers[L].attn_norm,
+                      layers[L].ffn_norm};
+    chk(alloc(&players, sizeof(PLayer) * (m.n_layer ? m.n_layer : 1u)));
+    if (m.n_layer) chk(cudaMemcpyAsync(players, tab.data(), sizeof(PLayer) * m.n_layer, cudaMemcpyHostToDevice, st));
+    chk(alloc(&qkv_x, 8ull * (hl * hd + 2 * kvl * hd)));
+    chk(alloc(&gu_x, 16ull * ffl));
+    chk(alloc(&parg_v, 4ull * num_sms));
+    chk(alloc(&parg_i, 4ull * num_sms));
+    persistent_ok = e == cudaSuccess;
+    // the table must outlive the copy
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  persistent = persistent_ok && step_mode_req == EOSI_CUDA_STEP_PERSISTENT;
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) {
     set_error_message(cudaGetErrorString(e));
@@ -986,6 +1009,7 @@ int TextDecoder::attach_buffers(uint8_t* const* bufs) {
 }
 
 cudaError_t TextDecoder::record_step(cudaStream_t s) {
+  if (persistent) return record_step_persistent(s);
   const uint32_t E = m.n_embd, F = m.n_ff;
   const int wdt = m.wdtype, odt = m.out_dtype;
   const uint32_t nqkv = hl * hd + 2 * kvl * hd;
@@ -1133,6 +1157,108 @@ cudaError_t TextDecoder::record_step(cudaStream_t s) {
   }
   if (e == cudaSuccess && status != EOS_OK) e = cudaErrorNotSupported;
   return e;
+}
+
+// The step as one persistent kernel: every vector that crosses CTAs or ranks
+// as (epoch, word) pairs, 6 exchanges per layer plus the pick's handshake.
+cudaError_t TextDecoder::record_step_persistent(cudaStream_t s) {
+  PStepParams p{};
+  p.layers = players;
+  p.wout = wout;
+  p.out_norm = out_norm;
+  p.tok_embd = tok_embd;
+  p.prompt = prompt;
+  p.state = state;
+  p.out_tokens = out_tokens;
+  p.kc = kc;
+  p.vc = vc;
+  p.attn_part = attn_part;
+  p.attn_count = attn_count;
+  p.logits = logits;
+  p.arg_v = parg_v;
+  p.arg_i = parg_i;
+  p.qkv_x = qkv_x;
+  p.gu_x = gu_x;
+  p.ao_in = reinterpret_cast<const uint64_t*>(xbuf + xoff_ao);
+  p.o_in = reinterpret_cast<const uint64_t*>(xbuf + xoff_o);
+  p.ad_in = reinterpret_cast<const uint64_t*>(xbuf + xoff_ad);
+  p.d_in = reinterpret_cast<const uint64_t*>(xbuf + xoff_d);
+  for (int q = 0; q < world; ++q) {
+    p.ao_out[q] = reinterpret_cast<uint64_t*>(xpeer[q] + xoff_ao);
+    p.o_out[q] = reinterpret_cast<uint64_t*>(xpeer[q] + xoff_o);
+    p.ad_out[q] = reinterpret_cast<uint64_t*>(xpeer[q] + xoff_ad);
+    p.d_out[q] = reinterpret_cast<uint64_t*>(xpeer[q] + xoff_d);
+    p.recv[q] = xrecv(q);
+  }
+  p.own = xrecv(rank);
+  const uint32_t xps = 6u * m.n_layer + 1u;  // exchanges per step
+  p.xs.world = (uint32_t)world;
+  p.xs.rank = (uint32_t)rank;
+  for (int q = 0; q < world; ++q) p.xs.pub[q] = &xrecv(q)->flag[kXArgmax][rank];
+  p.xs.wait = &xrecv(rank)->flag[kXArgmax][0];
+  p.xs.epoch_word = &state->epoch;
+  p.xs.mul = xps;
+  p.xs.add = xps;
+  p.xs.limit_us = &state->wait_limit_us;
+  p.xs.err = &state->err;
+  p.world = (uint32_t)world;
+  p.rank = (uint32_t)rank;
+  p.n_layer = m.n_layer;
+  p.E = m.n_embd;
+  p.F = m.n_ff;
+  p.hl = hl;
+  p.h0 = h0;
+  p.kvl = kvl;
+  p.kv0 = kv0;
+  p.n_head = m.n_head;
+  p.n_kv_head = m.n_kv_head;
+  p.ffl = ffl;
+  p.ff0 = ff0;
+  p.el = el;
+  p.e0 = e0;
+  p.vl = vl;
+  p.v0 = v0;
+  p.max_ctx = m.max_ctx;
+  p.max_chunks = max_chunks;
+  p.eps = m.rms_eps;
+  p.rope_base = m.rope_base;
+  p.attn_scale = 1.0f / sqrtf((float)hd);  // text.c:365
+  return launch_persistent_step(p, hd, (uint32_t)num_sms, s);
+}
+
+// Switches between the persistent and the per-op step and re-records the
+// step graph.  The exchange buffers and the local pair buffers are cleared
+// first: the two steps number their exchanges differently, and a word or
+// flag left by one must not pass for the other's.  Tensor parallel: every
+// rank switches, with no step running.
+int TextDecoder::set_step_mode(int mode) {
+  if (mode != EOSI_CUDA_STEP_AUTO && mode != EOSI_CUDA_STEP_PERSISTENT && mode != EOSI_CUDA_STEP_PER_OP) {
+    set_error_message("cuda text: unknown step mode");
+    return EOS_E_INVALID_ARG;
+  }
+  if (mode == EOSI_CUDA_STEP_PERSISTENT && !persistent_ok) {
+    set_error_message("cuda text: the persistent step needs Q4_K linears and LM head, head_dim 64 or 128 and "
+                      "n_embd <= 4096, with its shared memory on this device");
+    return EOS_E_UNSUPPORTED;
+  }
+  step_mode_req = mode;
+  const bool want = persistent_ok && mode == EOSI_CUDA_STEP_PERSISTENT;
+  if (want == persistent) return EOS_OK;
+  persistent = want;
+  if (graph == nullptr) return EOS_OK;  // tensor parallel, not attached yet: recorded at attach
+  if (cudaSetDevice(device) != cudaSuccess) return EOS_E_INTERNAL;
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess) e = cudaGraphExecDestroy(graph);
+  graph = nullptr;
+  if (e == cudaSuccess) e = cudaMemsetAsync(xbuf, 0, xstep_bytes, st);
+  if (e == cudaSuccess && qkv_x) e = cudaMemsetAsync(qkv_x, 0, 8ull * (hl * hd + 2 * kvl * hd), st);
+  if (e == cudaSuccess && gu_x) e = cudaMemsetAsync(gu_x, 0, 16ull * ffl, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    set_error_message(cudaGetErrorString(e));
+    return EOS_E_INTERNAL;
+  }
+  return capture();
 }
 
 // Batched prefill of the n tokens at prompt[host_pos ...]: per block of up to
@@ -1305,6 +1431,7 @@ int TextDecoder::capture() {
   }
   if (e == cudaSuccess) e = cudaGraphInstantiate(&graph, g, 0);
   if (g) cudaGraphDestroy(g);
+
   if (e != cudaSuccess) {
     set_error_message(cudaGetErrorString(e));
     return EOS_E_INTERNAL;
@@ -1337,6 +1464,11 @@ int dec_check_device_errors(eosi_cuda_text_t* t) {
   if (words[0] & EOS_DEVERR_PEER) {
     eos::set_error_message("cuda text: a tensor-parallel peer did not arrive within the wait limit "
                            "(bounded wait ran out; reset every rank before stepping again)");
+    return EOS_E_INTERNAL;
+  }
+  if (words[0] & EOS_DEVERR_WAIT_ACT) {
+    eos::set_error_message("cuda text: a step's activations did not arrive within the wait limit "
+                           "(bounded wait ran out)");
     return EOS_E_INTERNAL;
   }
   if (words[0] | words[1]) {
@@ -1508,7 +1640,10 @@ EOSLLM_CUDA_API int eosi_cuda_text_reset(eosi_cuda_text_t* t) {
   // position, prompt length, pick, argmax count and error word; the exchange
   // epoch keeps counting (the peers' flags hold earlier epochs)
   cudaError_t e = cudaMemsetAsync(d.state, 0, offsetof(eos::DecState, epoch), d.st);
+  // and the attention chunks' arrival counts (a step that gave up mid-way)
+  if (e == cudaSuccess) e = cudaMemsetAsync(d.attn_count, 0, 4ull * d.hl, d.st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(d.st);
+
   if (e != cudaSuccess) return dec_fail(e);
   d.host_pos = 0;
   d.step_mode = false;
@@ -1586,6 +1721,15 @@ EOSLLM_CUDA_API int eosi_cuda_text_partition(const eosi_cuda_llama_t* m, int ran
 EOSLLM_CUDA_API void* eosi_cuda_text_stream(eosi_cuda_text_t* t) { return t ? (void*)t->d.st : nullptr; }
 
 EOSLLM_CUDA_API uint32_t eosi_cuda_text_step_kernels(const eosi_cuda_text_t* t) { return t ? t->d.step_kernels : 0u; }
+
+EOSLLM_CUDA_API int eosi_cuda_text_set_step_mode(eosi_cuda_text_t* t, int mode) {
+  return t ? t->d.set_step_mode(mode) : EOS_E_INVALID_ARG;
+}
+
+EOSLLM_CUDA_API int eosi_cuda_text_step_mode(const eosi_cuda_text_t* t) {
+  if (t == nullptr) return 0;
+  return t->d.persistent ? EOSI_CUDA_STEP_PERSISTENT : EOSI_CUDA_STEP_PER_OP;
+}
 
 EOSLLM_CUDA_API void eosi_cuda_text_close(eosi_cuda_text_t* t) {
   if (t == nullptr) return;

@@ -9,6 +9,16 @@
 
 namespace eos {
 
+constexpr uint32_t kMaxParts = 8;  // tensor-parallel ranks
+// Attention splits a head's context into chunks of 32 positions (one CTA of
+// the per-op step, one 4-warp group of the persistent step; both reduce in
+// the same order).  32 positions are 32 KB of K/V staging, small enough for
+// an attention CTA to share an SM with the two CTAs of the QKV GEMV before
+// it and start its K/V copies early (programmatic dependent launch).
+constexpr uint32_t kAttnChunk = 32;       // positions per attention chunk
+constexpr uint32_t kMaxAttnChunks = 512;  // max_ctx <= 16384
+constexpr uint32_t kMergeBatch = 16;      // chunks whose o[d] the merge loads in one batch
+
 // Words the step kernels share in device memory.
 struct DecState {
   uint32_t pos;         // position of the next step == tokens consumed
@@ -75,6 +85,59 @@ __device__ __forceinline__ void rope_pair(float& x0, float& x1, uint32_t i, uint
   rope_factors<HD>(i, pos, base, sn, cs);
   rope_apply(x0, x1, sn, cs);
 }
+
+// ---------------------------------------------------------------------------
+// Persistent step (decoder_persistent.cu): one cooperative kernel per token
+// ---------------------------------------------------------------------------
+struct PLayer {
+  const uint8_t* w[4];  // this rank's rows of [q; k; v], O, [gate; up], down
+  const float* attn_norm;
+  const float* ffn_norm;
+};
+
+struct PStepParams {
+  const PLayer* layers;  // [n_layer], device memory
+  const uint8_t* wout;   // this rank's LM-head rows
+  const float* out_norm;
+  const uint16_t* tok_embd;
+  const uint32_t* prompt;
+  DecState* state;
+  uint32_t* out_tokens;
+  float* kc;  // [n_layer][max_ctx][kvl * hd]
+  float* vc;
+  float* attn_part;  // [hl][max_chunks][hd + 4]
+  uint32_t* attn_count;
+  float* logits;     // this rank's vocabulary slice
+  float* arg_v;      // [gridDim.x]
+  uint32_t* arg_i;
+  uint64_t* qkv_x;   // this rank's q/k/v rows as pairs
+  uint64_t* gu_x;    // this rank's gate/up rows as pairs
+  // exchanged: this rank's buffer (in) and every rank's (out, own included)
+  const uint64_t* ao_in;  // attention output, Q4_K records of all heads (word pairs)
+  const uint64_t* o_in;   // O rows, all n_embd
+  const uint64_t* ad_in;  // SiLU output records, all n_ff
+  const uint64_t* d_in;   // down rows, all n_embd
+  uint64_t* ao_out[kMaxParts];
+  uint64_t* o_out[kMaxParts];
+  uint64_t* ad_out[kMaxParts];
+  uint64_t* d_out[kMaxParts];
+  XRecv* recv[kMaxParts];  // the greedy pick's words, as in argmax_kernel
+  XRecv* own;
+  XchgSync xs;
+  uint32_t world, rank;
+  uint32_t n_layer, E, F, hl, h0, kvl, kv0, n_head, n_kv_head, ffl, ff0, el, e0, vl, v0, max_ctx, max_chunks;
+  float eps, rope_base, attn_scale;
+};
+
+// Shared memory of the persistent step for the geometry (bytes).
+uint32_t persistent_step_smem(uint32_t E, uint32_t F, uint32_t hd, uint32_t max_chunks, uint32_t n_layer);
+// Whether this device runs it (one 384-thread CTA per SM, every CTA resident;
+// sets the kernel's shared-memory attribute): Q4_K geometry, head_dim 64 or
+// 128, n_embd <= 4096.
+bool persistent_step_supported(uint32_t E, uint32_t F, uint32_t hd, uint32_t max_chunks, uint32_t n_layer,
+                               int max_smem);
+// One step on `grid` CTAs (the SM count), a cooperative launch.
+cudaError_t launch_persistent_step(const PStepParams& p, uint32_t hd, uint32_t grid, cudaStream_t st);
 
 // Batched prefill kernels (prefill_text.cu).  `act`: the prefill GEMM's
 // activation buffer for m rows of k (int8 values, then the per-32 scale

@@ -272,21 +272,26 @@ __device__ __forceinline__ int32_t x86_cvtps(float x) {
 // Restates src/kernels/avx2/matmul_q4_k_int8.c:98-154 bit for bit: the max
 // tree below is the exact lane pairing of the AVX2 code (two vector maxes,
 // then hmax_ps_8's halves / movehl / lane-1 shuffle).
+// The AVX2 max tree's exact pick of max |v| over the warp's group (lane i's
+// |v| bits in abits) -- needed only when some |v| is a NaN.
+__device__ __forceinline__ uint32_t x86_group_absmax_nan(uint32_t abits) {
+  const unsigned FULL = 0xffffffffu;
+  float t = __uint_as_float(abits);
+  t = x86_max(t, __shfl_down_sync(FULL, t, 8));   // max(ma0, ma1) | max(ma2, ma3)
+  t = x86_max(t, __shfl_down_sync(FULL, t, 16));  // mx = max(.., ..)
+  t = x86_max(t, __shfl_down_sync(FULL, t, 4));   // max_ps(lo, hi)
+  t = x86_max(t, __shfl_down_sync(FULL, t, 2));   // max_ps(m, movehl(m))
+  t = x86_max(t, __shfl_down_sync(FULL, t, 1));   // max_ss(m, lane 1)
+  return __float_as_uint(__shfl_sync(FULL, t, 0));
+}
+
 __device__ __forceinline__ int8_t quant_group32(float v, float& scale, int32_t& sum) {
   const unsigned FULL = 0xffffffffu;
   const uint32_t abits = __float_as_uint(v) & 0x7fffffffu;
   // Without NaNs every max order gives the same value, and |x| bit patterns
   // order like the floats, so one integer max reduction is exact.
   uint32_t mbits = __reduce_max_sync(FULL, abits);
-  if (mbits > 0x7f800000u) {  // a NaN: reproduce the AVX2 tree's exact pick
-    float t = __uint_as_float(abits);
-    t = x86_max(t, __shfl_down_sync(FULL, t, 8));   // max(ma0, ma1) | max(ma2, ma3)
-    t = x86_max(t, __shfl_down_sync(FULL, t, 16));  // mx = max(.., ..)
-    t = x86_max(t, __shfl_down_sync(FULL, t, 4));   // max_ps(lo, hi)
-    t = x86_max(t, __shfl_down_sync(FULL, t, 2));   // max_ps(m, movehl(m))
-    t = x86_max(t, __shfl_down_sync(FULL, t, 1));   // max_ss(m, lane 1)
-    mbits = __float_as_uint(__shfl_sync(FULL, t, 0));
-  }
+  if (mbits > 0x7f800000u) mbits = x86_group_absmax_nan(abits);  // a NaN: the AVX2 tree's exact pick
   const float max_abs = __uint_as_float(mbits);
   float inv;
   if (max_abs > 0.0f) {

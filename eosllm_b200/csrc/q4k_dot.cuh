@@ -95,17 +95,23 @@ namespace eos {
 // blk + r * row_stride.  The activation half-record is loaded once and reused
 // by every row (the single-row form re-reads it per row).  Terms are
 // bit-identical to q4k_half_terms.
-template <int R>
-__device__ __forceinline__ void q4k_half_terms_rows(const uint8_t* blk, uint32_t row_stride, const uint8_t* half,
-                                                    uint32_t h, float (&t)[R][4], uint32_t rows = R) {
-  int4 a[2][4];
-  float4 st[2];
+// The activation half-record in registers: a[p][j] = int8 values 16 j ..
+// 16 j + 15 of qs pair p, st[p] = the pair's {scale, sum} words.
+__device__ __forceinline__ void q4k_load_half(const uint8_t* half, int4 (&a)[2][4], float4 (&st)[2]) {
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) a[p][j] = *reinterpret_cast<const int4*>(half + 64 * p + 16 * j);
     st[p] = *reinterpret_cast<const float4*>(half + 128 + 16 * p);
   }
+}
+
+// q4k_half_terms_rows with the half-record already in registers (a caller
+// that computes many stages of one super-block column loads it once).
+template <int R>
+__device__ __forceinline__ void q4k_half_terms_rows_regs(const uint8_t* blk, uint32_t row_stride,
+                                                         const int4 (&a)[2][4], const float4 (&st)[2], uint32_t h,
+                                                         float (&t)[R][4], uint32_t rows = R) {
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     // rows beyond `rows` recompute the last row (the caller drops them)
@@ -126,6 +132,15 @@ __device__ __forceinline__ void q4k_half_terms_rows(const uint8_t* blk, uint32_t
           sb_term(d, dmin, (scw >> (16 * p + 8)) & 0xFFu, (mw >> (16 * p + 8)) & 0xFFu, st[p].z, st[p].w, dh);
     }
   }
+}
+
+template <int R>
+__device__ __forceinline__ void q4k_half_terms_rows(const uint8_t* blk, uint32_t row_stride, const uint8_t* half,
+                                                    uint32_t h, float (&t)[R][4], uint32_t rows = R) {
+  int4 a[2][4];
+  float4 st[2];
+  q4k_load_half(half, a, st);
+  q4k_half_terms_rows_regs<R>(blk, row_stride, a, st, h, t, rows);
 }
 
 }  // namespace eos

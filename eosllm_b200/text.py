@@ -172,6 +172,21 @@ class TextDecoder:
     def pos(self) -> int:
         return int(self.lib.eosi_cuda_text_pos(self.handle))
 
+    # eosi_cuda_text_set_step_mode: how a step runs
+    STEP_AUTO, STEP_PERSISTENT, STEP_PER_OP = 0, 1, 2
+
+    def set_step_mode(self, mode: int) -> None:
+        """STEP_PER_OP: a graph of one kernel per operation; STEP_PERSISTENT:
+        one cooperative kernel per token (Q4_K, head_dim 64/128, n_embd <=
+        4096); STEP_AUTO (default): per-op, the faster on a B200.  Both give
+        bit-identical logits.  Tensor parallel: every rank, no step running."""
+        B.check(self.lib.eosi_cuda_text_set_step_mode(self.handle, int(mode)), "eosi_cuda_text_set_step_mode")
+
+    @property
+    def step_mode(self) -> int:
+        """The mode in use (STEP_PERSISTENT or STEP_PER_OP)."""
+        return int(self.lib.eosi_cuda_text_step_mode(self.handle))
+
     @property
     def step_kernels(self) -> int:
         """Kernels one step launches (nodes of the step's CUDA graph)."""

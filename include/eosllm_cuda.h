@@ -254,6 +254,23 @@ typedef struct eosi_cuda_text eosi_cuda_text_t;
  * must divide n_head and n_kv_head.  Replaces eosi_text_open (text.c:131-260). */
 EOSLLM_CUDA_API int eosi_cuda_text_open(const eosi_cuda_llama_t *m, int device, int rank, int world,
                                         eosi_cuda_text_t **out);
+/* How a step runs.  PER_OP: a CUDA graph of one kernel per operation,
+ * chained with programmatic dependent launch (any supported model).
+ * PERSISTENT: one cooperative kernel per token, one CTA per SM, every weight
+ * matrix streamed through per-warp TMA rings that run ahead across the
+ * step's phases, every vector that crosses CTAs or ranks as (epoch, word)
+ * pairs (Q4_K linears and LM head, head_dim 64 or 128, n_embd <= 4096).  Both
+ * give bit-identical logits and tokens.  AUTO (the default) is PER_OP, the
+ * faster of the two on a B200 for the 7B shape (about 695 against 470
+ * tokens/s).  Tensor parallel: every rank sets the same mode, with no step
+ * running.  EOS_E_UNSUPPORTED when PERSISTENT is asked for and not
+ * possible. */
+#define EOSI_CUDA_STEP_AUTO 0
+#define EOSI_CUDA_STEP_PERSISTENT 1
+#define EOSI_CUDA_STEP_PER_OP 2
+EOSLLM_CUDA_API int eosi_cuda_text_set_step_mode(eosi_cuda_text_t *t, int mode);
+/* The mode in use: EOSI_CUDA_STEP_PERSISTENT or EOSI_CUDA_STEP_PER_OP. */
+EOSLLM_CUDA_API int eosi_cuda_text_step_mode(const eosi_cuda_text_t *t);
 /* One decoder step at the current position: token -> logits[n_vocab]
  * (host memory), position + 1.  Same contract as eosi_text_step
  * (text.c:267-436): EOS_E_INVALID_ARG for token >= n_vocab,
@@ -300,10 +317,11 @@ EOSLLM_CUDA_API uint32_t eosi_cuda_text_pos(const eosi_cuda_text_t *t);
  * (packed for the O projection), the O output rows, the SiLU output (packed
  * for the down projection) and the down output rows, and at the end their
  * slice's greedy pick; every rank therefore holds the one-GPU residual
- * stream bit for bit and picks the one-GPU tokens.  Every exchange is a flag
- * handshake with a bounded wait (one second unless
- * eosi_cuda_text_set_wait_limit says otherwise; EOS_E_INTERNAL when a rank
- * never arrives).  Every rank must make the same calls in the same order
+ * stream bit for bit and picks the one-GPU tokens.  Every word pushed
+ * carries its exchange's epoch in the same 64-bit store, so a consumer polls
+ * the words themselves in its own memory; the pick is a flag handshake.
+ * Every wait is bounded (one second unless eosi_cuda_text_set_wait_limit
+ * says otherwise; EOS_E_INTERNAL when a rank never arrives).  Every rank must make the same calls in the same order
  * (step / generate / prefill / reset). */
 #define EOSI_CUDA_IPC_HANDLE_BYTES 64
 EOSLLM_CUDA_API int eosi_cuda_text_ipc_handle(eosi_cuda_text_t *t, void *out, size_t cap);
@@ -313,7 +331,8 @@ EOSLLM_CUDA_API int eosi_cuda_text_attach_peers(eosi_cuda_text_t *t, const void 
  * ranks[q] is rank q's decoder.  Every rank must then be stepped; a rank
  * that is not makes the others' next exchange run into its bounded wait. */
 EOSLLM_CUDA_API int eosi_cuda_text_attach_local(eosi_cuda_text_t *const *ranks, int world);
-/* Bound on every tensor-parallel flag wait of this decoder, in microseconds
+/* Bound on every wait of this decoder's steps (tensor-parallel exchanges, and
+ * the persistent step's waits for other CTAs' outputs), in microseconds
  * (default 1000000). */
 EOSLLM_CUDA_API int eosi_cuda_text_set_wait_limit(eosi_cuda_text_t *t, uint32_t limit_us);
 /* This rank's slice of the model (host only, no GPU needed): out[11] =

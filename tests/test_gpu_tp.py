@@ -47,7 +47,7 @@ def _run_decoder(dec, kw, tokens, prompt, barrier=lambda: None):
     return np.stack(logits), picks.tolist(), (np.stack(pf_logits) if pf_logits else None)
 
 
-def _tp_worker(rank: int, world: int, port: int, kw: dict, tokens, prompt, q) -> None:
+def _tp_worker(rank: int, world: int, port: int, kw: dict, tokens, prompt, q, mode: int = 0) -> None:
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -58,6 +58,7 @@ def _tp_worker(rank: int, world: int, port: int, kw: dict, tokens, prompt, q) ->
         from eosllm_b200.text import TextDecoder
         model = make_llama(Oracle(), max_ctx=96, **kw)
         dec = TextDecoder(model, device=rank, rank=rank, world=world)
+        dec.set_step_mode(mode)
         dec.connect()
         out = _run_decoder(dec, kw, tokens, prompt, dist.barrier)
         dec.close()
@@ -72,8 +73,13 @@ def _same(a, b) -> bool:
     return np.array_equal(np.asarray(a, np.float32).view(np.uint32), np.asarray(b, np.float32).view(np.uint32))
 
 
+@pytest.mark.parametrize("mode", [2, 1], ids=["per_op", "persistent"])
 @pytest.mark.parametrize("kw", CASES)
-def test_two_gpu_decoder_is_bit_identical_to_one_gpu(gpu, oracle, kw):
+def test_two_gpu_decoder_is_bit_identical_to_one_gpu(gpu, oracle, kw, mode):
+    """The ranks run the per-op step graph (the default) or the persistent
+    step; the one-GPU reference runs the per-op graph."""
+    if mode == 1 and kw.get("wdtype", 33) != 33:
+        pytest.skip("the persistent step runs Q4_K models")
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     from oracle.llama import OracleDecoder, make_llama
@@ -86,7 +92,8 @@ def test_two_gpu_decoder_is_bit_identical_to_one_gpu(gpu, oracle, kw):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29600 + os.getpid() % 300
-    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, kw, tokens, prompt, q)) for r in range(world)]
+    procs = [ctx.Process(target=_tp_worker, args=(r, world, port, kw, tokens, prompt, q, mode))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -99,6 +106,7 @@ def test_two_gpu_decoder_is_bit_identical_to_one_gpu(gpu, oracle, kw):
         assert res[r][0] is not None, res[r][1]
     model = make_llama(oracle, max_ctx=96, **kw)
     one = TextDecoder(model, device=0)
+    one.set_step_mode(TextDecoder.STEP_PER_OP)
     ref = _run_decoder(one, kw, tokens, prompt)
     one.close()
     for r in range(world):
