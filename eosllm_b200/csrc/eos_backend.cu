@@ -838,7 +838,10 @@ int eosi_cuda_take_device_errors(uint32_t* bits) {
   uint32_t v = 0;
   EOS_CK(cudaMemcpy(&v, info->err_d, 4, cudaMemcpyDeviceToHost), "read error word");
   if (v) EOS_CK(cudaMemset(info->err_d, 0, 4), "clear error word");
-  *bits = v;
+  uint32_t na = 0;  // and the no-alloc entry point's own word
+  rc = eos::noalloc_take_errors(&na);
+  if (rc != EOS_OK) return fail(rc, "read the no-alloc error word");
+  *bits = v | na;
   return EOS_OK;
 }
 

@@ -46,6 +46,9 @@ cudaError_t launch_q4k_gemv(const uint8_t* w, const uint8_t* act, const float* a
                             uint32_t* err, int num_sms, int max_smem, bool pdl, cudaStream_t st, int* out_status,
                             float* const* c_extra = nullptr, uint32_t n_extra = 0, const LLExchange* ll = nullptr);
 void set_q4k_gemv_variant(int v);
+// The device error bits of the most recent eosi_cuda_matmul_q4_k_noalloc call
+// on the current device, then cleared (eos_noalloc.cu).
+int noalloc_take_errors(uint32_t* bits);
 // Copies `bytes` (a multiple of 16; both addresses 16-byte aligned) from
 // device memory written by the previous kernel on `st` to `dst`, typically
 // the device alias of mapped pinned host memory.  Launched with programmatic

@@ -15,7 +15,10 @@
 // process exits.  Host code cannot use the array's name as a device address
 // (on the host it only names a stand-in object), so the first call on each
 // device looks the real address up with cudaGetSymbolAddress, with that
-// device current, and passes it to the kernels.
+// device current, and passes it to the kernels.  A second file-scope word
+// holds the device-side error bits of the most recent call on the device
+// (zeroed by that call's packing kernel; a GEMV whose bounded wait ran out
+// sets a bit): eosi_cuda_take_device_errors reports and clears it.
 #include <mutex>
 
 #include "eosllm_cuda.h"
@@ -27,10 +30,12 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ uint32_t g_noalloc_err;
 
 struct NoAllocDevice {
   bool ready = false;
   uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  uint32_t* err = nullptr;     // device address of g_noalloc_err
   int num_sms = 0;
   int max_smem = 0;
 };
@@ -58,10 +63,13 @@ int noalloc_device(NoAllocDevice** out) {
       return EOS_E_UNSUPPORTED;
     }
     void* ptr = nullptr;
-    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
+    void* eptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr ||
+        cudaGetSymbolAddress(&eptr, g_noalloc_err) != cudaSuccess || eptr == nullptr) {
       cudaGetLastError();
       return EOS_E_INTERNAL;
     }
+    d.err = static_cast<uint32_t*>(eptr);
     if (cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
       cudaGetLastError();
@@ -80,6 +88,33 @@ int noalloc_fail(int status, const char* msg) {
 }
 
 }  // namespace
+
+namespace eos {
+// The error bits of the most recent no-alloc call on the current device, then
+// cleared (0 when the device has made no such call).
+int noalloc_take_errors(uint32_t* bits) {
+  *bits = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return EOS_E_UNSUPPORTED;
+  }
+  uint32_t* err = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_dev[dev].ready) err = g_noalloc_dev[dev].err;
+  }
+  if (err == nullptr) return EOS_OK;
+  uint32_t v = 0;
+  if (cudaMemcpy(&v, err, 4, cudaMemcpyDeviceToHost) != cudaSuccess ||
+      (v != 0 && cudaMemset(err, 0, 4) != cudaSuccess)) {
+    cudaGetLastError();
+    return EOS_E_INTERNAL;
+  }
+  *bits = v;
+  return EOS_OK;
+}
+}  // namespace eos
 
 extern "C" {
 
@@ -111,12 +146,12 @@ EOSLLM_CUDA_API int eosi_cuda_matmul_q4_k_noalloc(const float* a, const void* w,
     }
     return EOS_OK;
   }
-  e = eos::launch_act_pack(a, m, k, d->scratch, EOS_ACT_LAYOUT_GEMV, st);
+  e = eos::launch_act_pack(a, m, k, d->scratch, EOS_ACT_LAYOUT_GEMV, st, d->err);
   const size_t stride = eos::act_layout_bytes(1, k, EOS_ACT_LAYOUT_GEMV);
   for (uint32_t i = 0; i < m && e == cudaSuccess; ++i) {
     int status = EOS_OK;
     e = eos::launch_q4k_gemv(static_cast<const uint8_t*>(w), d->scratch + i * stride, nullptr, c + (size_t)i * n, n,
-                             k, nullptr, d->num_sms, d->max_smem, true, st, &status);
+                             k, d->err, d->num_sms, d->max_smem, true, st, &status);
     if (e == cudaSuccess && status != EOS_OK) return noalloc_fail(status, "q4_k gemv: shape not supported");
   }
   if (e != cudaSuccess) {

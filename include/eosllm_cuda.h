@@ -144,9 +144,11 @@ EOSLLM_CUDA_API int eosi_cuda_q4_k_gemv_dev(const void *act, const void *w, floa
  *   - every call on a device reuses the same array, so calls whose work
  *     overlaps on that GPU (other streams, other host threads) race and
  *     corrupt each other's results -- serialise them;
- *   - no cudaMalloc, cudaFree or other allocating call is made, and the
- *     kernels this entry point launches contain no waits that could time
- *     out, so there is no device-side error to report;
+ *   - no cudaMalloc, cudaFree or other allocating call is made;
+ *   - the GEMV's waits for its staged weights are bounded: one that runs out
+ *     sets a bit in the entry point's own error word (also in the library's
+ *     image, started at 0 by each call), which eosi_cuda_take_device_errors
+ *     reports after the stream has been synchronised;
  *   - under CUDA's default lazy module loading the driver itself loads each
  *     kernel on its first launch, and loading takes device memory: a host
  *     that must see no allocation on its serving path makes one warm-up
@@ -369,7 +371,9 @@ EOSLLM_CUDA_API int eosi_cuda_text_open_gguf(const char *path, uint32_t max_ctx,
 /* ---- diagnostics --------------------------------------------------------- */
 
 /* Device-side error bits raised by bounded waits since the last call on the
- * current device (0 = none); clears them. */
+ * current device (0 = none), together with those of the most recent
+ * eosi_cuda_matmul_q4_k_noalloc call on it (its own word, in the library's
+ * image: each such call starts it at 0); clears them. */
 EOSLLM_CUDA_API int eosi_cuda_take_device_errors(uint32_t *bits);
 
 /* Kernel variant override for tuning (-1 = automatic).  Q4_K GEMV:

@@ -69,6 +69,11 @@ def _compare_on_device(gpu, index, m, n, k):
         torch.cuda.synchronize()
         assert same_bits(c_new.cpu().numpy(), c_ref.cpu().numpy()), (m, n, k, seed)
         assert not np.isnan(c_new.cpu().numpy()).any()
+        # no bounded wait of either entry point ran out (the no-alloc call
+        # reports into its own word, read by the same query)
+        bits = C.c_uint32(0xFFFFFFFF)
+        assert lib.eosi_cuda_take_device_errors(C.byref(bits)) == gpu.EOS_OK, gpu.last_error()
+        assert bits.value == 0
 
 
 def test_noalloc_rejects_sizes_beyond_its_array(gpu):
