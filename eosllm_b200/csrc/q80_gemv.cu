@@ -16,9 +16,10 @@
 //
 // Skeleton as the Q4_K GEMV: each CTA owns a contiguous slab of weight rows,
 // which is one contiguous byte range; warp w streams stages w, w + NW, ... of
-// 256 blocks (8704 bytes, 32 groups of 8 blocks) HBM -> shared memory with
-// coalesced 16-byte cp.async copies through D private buffers, issued before
-// the PDL wait.  Lane l of a stage takes group l: 8 consecutive blocks of
+// 256 blocks (8704 bytes, 32 groups of 8 blocks) HBM -> shared memory, each
+// stage one TMA bulk copy (lane 0, completing on the buffer's mbarrier)
+// through D private buffers, the first D issued before the PDL wait (17
+// cp.async per lane and stage before: sweep 4208 -> 4380 GB/s on a B200).  Lane l of a stage takes group l: 8 consecutive blocks of
 // one row, 272 bytes at a 16-byte aligned offset, so block c of every lane's
 // group starts at the same position mod 16 and the realignment of its 2-byte
 // aligned data is the same compile-time byte permute in every lane (3
@@ -101,7 +102,7 @@ struct Q80GemvParams {
 
 // Shared-memory layout of the staged kernel (offsets in bytes).
 struct Q80Smem {
-  uint32_t dig, pw2, part, wbuf, total;
+  uint32_t dig, pw2, part, wbuf, bars, total;
 };
 __host__ __device__ inline Q80Smem q80_smem(uint32_t nblk, uint32_t rows_max, uint32_t nw, uint32_t d) {
   const uint32_t gpr = nblk / kQ8Group;
@@ -110,7 +111,8 @@ __host__ __device__ inline Q80Smem q80_smem(uint32_t nblk, uint32_t rows_max, ui
   m.pw2 = (nblk * kQ8DigitStride + 15u) & ~15u;
   m.part = m.pw2 + ((nblk * 4u + 15u) & ~15u);
   m.wbuf = m.part + ((rows_max * (gpr + 1u) * 4u + 127u) & ~127u);
-  m.total = m.wbuf + nw * d * kQ8StageBytes;
+  m.bars = m.wbuf + nw * d * kQ8StageBytes;  // one mbarrier per staging slot
+  m.total = m.bars + nw * d * 8u;
   return m;
 }
 
@@ -180,6 +182,7 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
   float* part = reinterpret_cast<float*>(smem + L.part);  // [row][gpr + 1] group sums
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   uint8_t* wbuf = smem + L.wbuf + warp * D * kQ8StageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars) + warp * D;
 
   const uint32_t r0 = (uint32_t)(((uint64_t)p.n * blockIdx.x) / gridDim.x);
   const uint32_t r1 = (uint32_t)(((uint64_t)p.n * (blockIdx.x + 1)) / gridDim.x);
@@ -189,15 +192,31 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
   const uint8_t* slab = p.w + (size_t)r0 * p.row_bytes;
   const size_t slab_bytes = (size_t)nrows * p.row_bytes;
   const uint64_t pol_w = l2_policy_evict_first();
+  if (lane == 0) {
+#pragma unroll
+    for (uint32_t d = 0; d < (uint32_t)D; ++d) mbar_init(bars + d, 1u);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  // lane 0 issues a stage as one TMA bulk copy (a stage is contiguous in the
+  // slab; row_bytes = 34 nblk is a multiple of 272, so every size and address
+  // is a multiple of 16 bytes) completing on the slot's mbarrier
+  uint32_t issued = 0;
   auto issue = [&](uint32_t s, uint32_t slot) {
     if (s < nst) {
-      const size_t off = (size_t)s * kQ8StageBytes;
-      const uint32_t bytes = (uint32_t)((slab_bytes - off) < kQ8StageBytes ? (slab_bytes - off) : kQ8StageBytes);
-      const uint8_t* src = slab + off;
-      uint8_t* dst = wbuf + slot * kQ8StageBytes;
-      for (uint32_t q = lane; q < (bytes >> 4); q += 32) cp_async16(dst + (q << 4), src + (q << 4), pol_w);
+      if (lane == 0) {
+        const size_t off = (size_t)s * kQ8StageBytes;
+        const uint32_t bytes = (uint32_t)((slab_bytes - off) < kQ8StageBytes ? (slab_bytes - off) : kQ8StageBytes);
+        mbar_arrive_expect_tx(bars + slot, bytes);
+        bulk_g2s(wbuf + slot * kQ8StageBytes, slab + off, bytes, bars + slot, pol_w);
+      }
+      ++issued;
     }
-    cp_async_commit();  // one group per call, empty or not
+  };
+  // stages issued and not yet consumed, landed before an early exit
+  auto drain = [&](uint32_t i) {
+    for (; i < issued; ++i)
+      if (!mbar_wait(bars + i % D, (i / D) & 1u) && lane == 0) report(p.err, EOS_DEVERR_DRAIN);
   };
 #pragma unroll
   for (uint32_t d = 0; d < (uint32_t)D; ++d) issue(warp + d * NW, d);
@@ -247,15 +266,20 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
   }
   if (!__syncthreads_and(ok)) {  // a peer never arrived: drain, leave the outputs unwritten
     if (threadIdx.x == 0) report(p.ll.err, EOS_DEVERR_PEER);
-    cp_async_wait<0>();
+    drain(0);
     return;
   }
   pdl_trigger();
 
-  uint32_t slot = 0;
-  for (uint32_t s = warp; s < nst; s += NW) {
-    cp_async_wait<D - 1>();
-    __syncwarp();
+  uint32_t slot = 0, i = 0;
+  bool landed = true;
+  for (uint32_t s = warp; s < nst; s += NW, ++i) {
+    if (!__all_sync(0xffffffffu, mbar_wait(bars + slot, (i / D) & 1u))) {
+      if (lane == 0) report(p.err, EOS_DEVERR_WAIT_FULL);
+      drain(i);
+      landed = false;
+      break;
+    }
     const uint32_t G = s * 32u + lane;
     if (G < ngroups) {
       const uint32_t row = G / gpr, j = G - row * gpr;  // group j of the row: blocks 8 j .. 8 j + 7
@@ -297,12 +321,11 @@ __global__ void __launch_bounds__(NW * 32, 1) q80_gemv_kernel(const Q80GemvParam
       }
       part[row * (gpr + 1u) + j] = acc;
     }
-    __syncwarp();  // stage bytes no longer read
+    __syncwarp();  // every lane's reads of the stage have returned (their values are stored)
     issue(s + D * NW, slot);
     if (++slot == (uint32_t)D) slot = 0;
   }
-  cp_async_wait<0>();
-  __syncthreads();
+  if (!__syncthreads_and(landed)) return;  // a stage never landed: outputs unwritten (error reported)
   // row sums: the row's groups in order
   for (uint32_t row = threadIdx.x; row < nrows; row += NW * 32u) {
     const float* pr = part + row * (gpr + 1u);
