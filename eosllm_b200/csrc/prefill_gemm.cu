@@ -42,10 +42,15 @@
 // and epilogue overlap.  A stage is released when its MMAs have completed
 // (tcgen05.commit) and all sixteen epilogue warps have read its scales.  The row sums c live
 // in shared memory (updated once per super-block), the partials in
-// registers; every operation is a scalar IEEE round-to-nearest multiply or
-// add (__fmul_rn / __fadd_rn are never contracted into FMAs).  Packed f32x2
-// multiplies and adds were tried here: their results did not match the
-// scalar operations bit for bit, so they are not used.
+// registers; every operation is an IEEE round-to-nearest multiply or add,
+// never a fused multiply-add.  The four products of a term and the partial's
+// add run on column pairs (mul.rn.f32x2 / add.rn.f32x2, lane-wise exact:
+// checked against __fmul_rn / __fadd_rn on 2^21 random pairs); the term's
+// own add, t1 + t2, stays two scalar __fadd_rn because ptxas contracts a
+// packed add fed by a packed multiply into a packed FMA even with .rn (on
+// this toolchain the contracted pair equalled fma.rn.f32x2 in every case and
+// differed from multiply-then-add in 27 % of random pairs).  The accumulator
+// is read in two halves of 16 columns (fewer live registers: 96 a thread).
 //
 // Waits are bounded (EOS_WAIT_LIMIT_NS): on a timeout the waiting role
 // records an error bit and stops; the MMA issuer always commits the "done"
@@ -62,6 +67,31 @@
 #include "eosllm_cuda.h"
 
 namespace eos {
+
+// Packed f32 pairs: lane-wise IEEE round-to-nearest multiply and add (no
+// flush-to-zero, no contraction), each lane exactly the scalar operation.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  uint32_t lo, hi;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(__float_as_uint(a.x)), "r"(__float_as_uint(a.y)), "r"(__float_as_uint(b.x)), "r"(__float_as_uint(b.y)));
+  return make_float2(__uint_as_float(lo), __uint_as_float(hi));
+}
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  uint32_t lo, hi;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(__float_as_uint(a.x)), "r"(__float_as_uint(a.y)), "r"(__float_as_uint(b.x)), "r"(__float_as_uint(b.y)));
+  return make_float2(__uint_as_float(lo), __uint_as_float(hi));
+}
 
 constexpr uint32_t QG_BM = 128, QG_BN = 128, QG_BK = 64;  // BK in bf16 elements: 128-byte rows
 constexpr uint32_t QG_SUBS = QG_BK / 32u;                 // sub-blocks per stage (2)
@@ -179,18 +209,16 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // 32 consecutive accumulator columns (f32 bits) of this thread's TMEM lane.
-__device__ __forceinline__ void qg_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 16 consecutive accumulator columns of the warp's 32 TMEM lanes.
+__device__ __forceinline__ void qg_ld16(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr)
       : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -333,25 +361,38 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&tfull[a], (g / QG_ACCS) & 1u)) != 0;
         if (!ok) break;
         tc_fence_after();
-        uint32_t r[32];
-        qg_ld32(tmem + ((quad * 32u) << 16) + a * QG_BN + col0, r);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[a]);  // accumulator a may be overwritten
         const float as = as_s[(2u * j) * QG_BM + lrow], sum = as_s[(2u * j + 1u) * QG_BM + lrow];
-        const float4* dsc = reinterpret_cast<const float4*>(bs_s + (2u * j) * QG_BN + col0);       // d*sc
-        const float4* nmn = reinterpret_cast<const float4*>(bs_s + (2u * j + 1u) * QG_BN + col0);  // -(dmin*m)
+        const float2 as2 = make_float2(as, as), sum2 = make_float2(sum, sum);
+        // the accumulator's 32 columns in two halves of 16 (fewer live registers)
 #pragma unroll
-        for (uint32_t c4 = 0; c4 < QG_COLS / 4; ++c4) {
-          const float4 dd = dsc[c4], nn = nmn[c4];  // broadcast
-          const float d4[4] = {dd.x, dd.y, dd.z, dd.w}, n4[4] = {nn.x, nn.y, nn.z, nn.w};
+        for (uint32_t hh = 0; hh < 2; ++hh) {
+          uint32_t r[16];
+          qg_ld16(tmem + ((quad * 32u) << 16) + a * QG_BN + col0 + 16u * hh, r);
+          if (hh == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[a]);  // accumulator a may be overwritten
+          }
+          const float4* dsc = reinterpret_cast<const float4*>(bs_s + (2u * j) * QG_BN + col0 + 16u * hh);       // d*sc
+          const float4* nmn = reinterpret_cast<const float4*>(bs_s + (2u * j + 1u) * QG_BN + col0 + 16u * hh);  // -(dmin*m)
 #pragma unroll
-          for (uint32_t i = 0; i < 4; ++i) {
-            const uint32_t c = 4u * c4 + i;
-            // t = ((d*sc)*as)*dot - ((dmin*m)*as)*sum   (:254-261), as t1 + (-t2)
-            const float t = __fadd_rn(__fmul_rn(__fmul_rn(d4[i], as), __uint_as_float(r[c])),
-                                      __fmul_rn(__fmul_rn(n4[i], as), sum));
-            part[c] = __fadd_rn(part[c], t);  // partial += t
+          for (uint32_t c4 = 0; c4 < 4; ++c4) {
+            const float4 dd = dsc[c4], nn = nmn[c4];  // broadcast
+            const float2 d2[2] = {make_float2(dd.x, dd.y), make_float2(dd.z, dd.w)};
+            const float2 n2[2] = {make_float2(nn.x, nn.y), make_float2(nn.z, nn.w)};
+#pragma unroll
+            for (uint32_t i = 0; i < 2; ++i) {
+              const uint32_t cl = 4u * c4 + 2u * i, c = 16u * hh + cl;  // columns c, c + 1: the two lanes of a pair
+              const float2 dot = make_float2(__uint_as_float(r[cl]), __uint_as_float(r[cl + 1]));
+              // t = ((d*sc)*as)*dot - ((dmin*m)*as)*sum   (:254-261), as t1 + (-t2): the four
+              // products in pairs, t1 + t2 as two scalar adds (a packed add fed by a
+              // packed multiply is contracted into a fused multiply-add by ptxas)
+              const float2 t1 = mul2_rn(mul2_rn(d2[i], as2), dot), t2 = mul2_rn(mul2_rn(n2[i], as2), sum2);
+              const float2 t = make_float2(__fadd_rn(t1.x, t2.x), __fadd_rn(t1.y, t2.y));
+              const float2 pc = add2_rn(make_float2(part[c], part[c + 1]), t);  // partial += t
+              part[c] = pc.x;
+              part[c + 1] = pc.y;
+            }
           }
         }
         if ((g & 7u) == 7u) {  // super-block complete: c += partial (:264), partial = 0
