@@ -12,6 +12,7 @@
 //
 // Device-pointer layer: enqueue-only wrappers around the same launchers.
 #include <algorithm>
+#include <chrono>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -110,6 +111,28 @@ struct KeyHash {
   }
 };
 
+// The launches of one host-pointer Q4_K call (packing, GEMVs, copy-out,
+// done flag), recorded once as a CUDA graph per weight slice, shape and
+// buffer set: every later call with the same key is one cudaGraphLaunch.
+struct GKey {
+  const void* w;
+  const void* a;
+  const void* act;
+  const void* c;
+  const void* blk;
+  uint32_t m, rows, k;
+  bool operator==(const GKey& o) const {
+    return w == o.w && a == o.a && act == o.act && c == o.c && blk == o.blk && m == o.m && rows == o.rows && k == o.k;
+  }
+};
+struct GKeyHash {
+  size_t operator()(const GKey& x) const {
+    return std::hash<const void*>()(x.w) ^ (std::hash<const void*>()(x.a) << 1) ^ ((size_t)x.m * 131u) ^
+           ((size_t)x.rows * 1000003u) ^ ((size_t)x.k << 24);
+  }
+};
+constexpr size_t kMaxCallGraphs = 1024;
+
 struct Shard {
   int dev = -1;
   DevInfo* info = nullptr;
@@ -125,7 +148,13 @@ struct Shard {
   uint8_t* h_blk_dev = nullptr;  // its device alias, written by copy_out_kernel
   size_t cap_blk = 0;
   std::unordered_map<Key, WeightEntry, KeyHash> cache;
+  std::unordered_map<GKey, cudaGraphExec_t, GKeyHash> graphs;
 };
+
+void drop_graphs(Shard& s) {
+  for (auto& kv : s.graphs) cudaGraphExecDestroy(kv.second);
+  s.graphs.clear();
+}
 
 std::recursive_mutex g_mu;
 std::vector<Shard> g_shards;
@@ -154,6 +183,7 @@ void fingerprint(const void* host, size_t bytes, uint8_t out[128]) {
 void release_shard(Shard& s) {
   if (s.dev < 0) return;
   cudaSetDevice(s.dev);
+  drop_graphs(s);
   for (auto& kv : s.cache) cudaFree(kv.second.dev);
   s.cache.clear();
   cudaFree(s.d_a);
@@ -354,6 +384,7 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
   cudaGetDevice(&prev);
   memcpy(g_h_a, a, (size_t)m * k * 4u);
   std::vector<char> used(G, 0);
+  std::vector<volatile uint32_t*> flags(G, nullptr);  // Q4_K path: each shard's done flag
   // Q4_K with n >= 4 (the int8 path): zero-copy activations and outputs
   const bool q4k_fast = dtype == EOS_DT_Q4_K && n >= 4;
   const float* d_a_mapped = nullptr;
@@ -385,12 +416,13 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
       // status word + outputs into mapped pinned memory (no copy engine)
       const size_t blk = 16u + (((size_t)m * rows * 4u + 15u) & ~(size_t)15u);
       rc = ensure_dev(&s.d_c, &s.cap_c, blk, "output buffer");
-      if (rc == EOS_OK && s.cap_blk < blk) {
+      // the done flag sits just past the copied block (its own 16 bytes)
+      if (rc == EOS_OK && s.cap_blk < blk + 16u) {
         if (s.h_blk) cudaFreeHost(s.h_blk);
         s.h_blk = nullptr;
         s.h_blk_dev = nullptr;
         s.cap_blk = 0;
-        const size_t want = std::max(blk, (size_t)65536);
+        const size_t want = std::max(blk + 16u, (size_t)65536);
         cudaError_t ae = cudaHostAlloc((void**)&s.h_blk, want, cudaHostAllocPortable | cudaHostAllocMapped);
         void* dp = nullptr;
         if (ae == cudaSuccess) ae = cudaHostGetDevicePointer(&dp, s.h_blk, 0);
@@ -407,22 +439,45 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
       used[gi] = 1;
       uint32_t* status = reinterpret_cast<uint32_t*>(s.d_c);
       float* d_out = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(s.d_c) + 16);
-      cudaError_t e = eos::launch_act_pack(d_a_mapped, m, k, s.d_act, EOS_ACT_LAYOUT_GEMV, s.stream, status);
-      if (e != cudaSuccess) {
-        rc = cuda_fail(e, "activation pack kernel");
-        break;
-      }
-      const size_t act_stride = eos::act_layout_bytes(1, k, EOS_ACT_LAYOUT_GEMV);
-      for (uint32_t i = 0; i < m && rc == EOS_OK; ++i) {
+      const GKey gk{d_w, d_a_mapped, s.d_act, s.d_c, s.h_blk_dev, m, rows, k};
+      auto git = s.graphs.find(gk);
+      if (git == s.graphs.end()) {
+        // record the call's launches once: packing (zeroes the status word),
+        // the GEMVs, the copy of status word + outputs into mapped memory,
+        // then the done flag (word 1 of the block)
+        if (s.graphs.size() >= kMaxCallGraphs) drop_graphs(s);
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamBeginCapture(s.stream, cudaStreamCaptureModeRelaxed);
+        cudaError_t le = cudaSuccess;
         int st2 = EOS_OK;
-        e = eos::launch_q4k_gemv(d_w, s.d_act + i * act_stride, nullptr, d_out + (size_t)i * rows, rows, k, status,
-                                 s.info->num_sms, s.info->max_smem, true, s.stream, &st2);
-        if (e != cudaSuccess) rc = cuda_fail(e, "q4_k gemv kernel");
-        else if (st2 != EOS_OK) rc = fail(st2, "q4_k gemv: shape %u x %u not supported", rows, k);
+        if (e == cudaSuccess) {
+          le = eos::launch_act_pack(d_a_mapped, m, k, s.d_act, EOS_ACT_LAYOUT_GEMV, s.stream, status);
+          const size_t act_stride = eos::act_layout_bytes(1, k, EOS_ACT_LAYOUT_GEMV);
+          for (uint32_t i = 0; i < m && le == cudaSuccess && st2 == EOS_OK; ++i)
+            le = eos::launch_q4k_gemv(d_w, s.d_act + i * act_stride, nullptr, d_out + (size_t)i * rows, rows, k,
+                                      status, s.info->num_sms, s.info->max_smem, true, s.stream, &st2);
+          if (le == cudaSuccess) le = eos::launch_copy_out(s.d_c, s.h_blk_dev, blk, s.stream);
+          if (le == cudaSuccess) le = eos::launch_done_flag(reinterpret_cast<uint32_t*>(s.h_blk_dev + blk), s.stream);
+          e = cudaStreamEndCapture(s.stream, &g);
+          if (le != cudaSuccess) e = le;
+        }
+        cudaGraphExec_t ge = nullptr;
+        if (e == cudaSuccess && st2 == EOS_OK) e = cudaGraphInstantiate(&ge, g, 0);
+        if (g) cudaGraphDestroy(g);
+        if (e != cudaSuccess) {
+          rc = cuda_fail(e, "q4_k call graph");
+          break;
+        }
+        if (st2 != EOS_OK) {
+          rc = fail(st2, "q4_k gemv: shape %u x %u not supported", rows, k);
+          break;
+        }
+        git = s.graphs.emplace(gk, ge).first;
       }
-      if (rc != EOS_OK) break;
-      e = eos::launch_copy_out(s.d_c, s.h_blk_dev, blk, s.stream);
-      if (e != cudaSuccess) rc = cuda_fail(e, "outputs to host (copy kernel)");
+      flags[gi] = reinterpret_cast<volatile uint32_t*>(s.h_blk + blk);
+      *flags[gi] = 0u;  // the done flag, raised by the graph's last node
+      const cudaError_t e = cudaGraphLaunch(git->second, s.stream);
+      if (e != cudaSuccess) rc = cuda_fail(e, "q4_k call graph launch");
       continue;
     }
     cudaError_t e = cudaMemcpyAsync(s.d_a, g_h_a, (size_t)m * k * 4u, cudaMemcpyHostToDevice, s.stream);
@@ -438,12 +493,26 @@ int host_matmul(const float* a, const void* b, int dtype, float* c, uint32_t m, 
     if (e == cudaSuccess) e = cudaMemcpyAsync(s.h_err, s.info->err_d, 4, cudaMemcpyDeviceToHost, s.stream);
     if (e != cudaSuccess) rc = cuda_fail(e, "D2H outputs");
   }
-  // Always drain every stream we used, even after a failure.
+  // Always drain every stream we used, even after a failure.  The Q4_K path
+  // waits for its done flag in mapped memory (bounded), and synchronises the
+  // stream only when it does not come (an error then surfaces there).
   for (uint32_t gi = 0; gi < G; ++gi) {
     if (!used[gi]) continue;
     Shard& s = g_shards[gi];
     cudaSetDevice(s.dev);
-    cudaError_t e = cudaStreamSynchronize(s.stream);
+    bool flagged = false;
+    if (q4k_fast && rc == EOS_OK && flags[gi] != nullptr) {
+      const volatile uint32_t* flag = flags[gi];
+      const auto t0 = std::chrono::steady_clock::now();
+      for (uint32_t spin = 0;; ++spin) {
+        if (*flag != 0u) {
+          flagged = true;
+          break;
+        }
+        if ((spin & 1023u) == 1023u && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(2)) break;
+      }
+    }
+    cudaError_t e = flagged ? cudaSuccess : cudaStreamSynchronize(s.stream);
     if (e != cudaSuccess && rc == EOS_OK) rc = cuda_fail(e, "kernel execution");
     const uint32_t bits = q4k_fast ? *reinterpret_cast<const uint32_t*>(s.h_blk) : *s.h_err;
     if (rc == EOS_OK && bits != 0) {
@@ -602,6 +671,7 @@ int eosi_cuda_cache_evict(const void* b_quant) {
   const bool had = cudaGetDevice(&prev) == cudaSuccess;
   for (auto& s : g_shards) {
     cudaSetDevice(s.dev);
+    drop_graphs(s);  // they may reference the evicted weights
     for (auto it = s.cache.begin(); it != s.cache.end();) {
       if (it->first.host == b_quant) {
         cudaFree(it->second.dev);
@@ -621,6 +691,7 @@ int eosi_cuda_cache_clear(void) {
   const bool had = cudaGetDevice(&prev) == cudaSuccess;
   for (auto& s : g_shards) {
     cudaSetDevice(s.dev);
+    drop_graphs(s);
     for (auto& kv : s.cache) cudaFree(kv.second.dev);
     s.cache.clear();
   }

@@ -55,6 +55,9 @@ int noalloc_take_errors(uint32_t* bits);
 // dependent launch, so it replaces a device-to-host copy-engine transfer
 // behind that kernel without waiting for a copy engine.
 cudaError_t launch_copy_out(const void* src, void* dst, size_t bytes, cudaStream_t st);
+// A one-thread kernel that sets *flag = 1 (device alias of mapped host
+// memory) after the stream's earlier kernels.
+cudaError_t launch_done_flag(uint32_t* flag, cudaStream_t st);
 // n < 4 Q4_K: the reference's f32-dequant path, bit for bit.
 cudaError_t launch_q4k_f32_small_n(const float* a, const uint8_t* w, float* c, uint32_t m, uint32_t n, uint32_t k,
                                    cudaStream_t st);

@@ -85,6 +85,19 @@ __global__ void __launch_bounds__(256) copy_out_kernel(const uint4* src, uint4* 
   for (uint32_t i = blockIdx.x * 256u + threadIdx.x; i < n16; i += gridDim.x * 256u) dst[i] = src[i];
 }
 
+// One thread raises *flag (mapped host memory) once every kernel before it on
+// the stream has completed: the host waits for the word instead of for the
+// stream (no synchronisation call on the path of a host-pointer matmul).
+__global__ void done_flag_kernel(uint32_t* flag) {
+  __threadfence_system();
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(1u) : "memory");
+}
+
+cudaError_t launch_done_flag(uint32_t* flag, cudaStream_t st) {
+  done_flag_kernel<<<1, 1, 0, st>>>(flag);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_copy_out(const void* src, void* dst, size_t bytes, cudaStream_t st) {
   const uint32_t n16 = (uint32_t)(bytes >> 4);
   if (n16 == 0) return cudaSuccess;
