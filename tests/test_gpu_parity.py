@@ -322,6 +322,27 @@ def test_weight_cache_tracks_reused_buffers(gpu, oracle):
     assert not same_bits(c1, c2)
 
 
+def test_host_calls_reuse_their_recorded_launches(gpu, oracle):
+    """A host-pointer Q4_K call is a CUDA graph recorded once per weight and
+    shape and then replayed: back-to-back calls with new activations, calls
+    alternating between two weights of one shape (and m = 1 / m = 3), and a
+    call after the weights were evicted (their graphs dropped) each give the
+    oracle's bits."""
+    n, k = 320, 2048
+    w1 = oracle.q4_k_quantize(oracle.gauss(n * k, 31, 0.02))
+    w2 = oracle.q4_k_quantize(oracle.gauss(n * k, 32, 0.02))
+    for i in range(6):
+        w = w1 if i % 2 == 0 else w2
+        m = 1 if i < 4 else 3
+        a = oracle.gauss(m * k, 40 + i, 1.0)
+        c = gpu.matmul_q(a, w, DT_Q4_K, m, n, k)
+        assert same_bits(c, oracle.matmul_q(a, w, DT_Q4_K, m, n, k)[1]), i
+    assert gpu.load().eosi_cuda_cache_evict(w1.ctypes.data) == gpu.EOS_OK
+    a = oracle.gauss(k, 50, 1.0)
+    assert same_bits(gpu.matmul_q(a, w1, DT_Q4_K, 1, n, k), oracle.matmul_q(a, w1, DT_Q4_K, 1, n, k)[1])
+    assert gpu.take_device_errors() == 0
+
+
 def test_row_sharding_across_streams(gpu, oracle):
     # the multi-GPU path with every shard on device 0 (one stream each)
     n, k = 1001, 4096
