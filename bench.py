@@ -889,23 +889,24 @@ def run_decode(args, dev, world, rank) -> dict:
         "clocks": clocks.summary(),
     }
     # the persistent step (one cooperative kernel per token) on the same
-    # decoder: 64 tokens after the same prompt; its picks must be the per-op
-    # step's (bit-identical by construction)
-    if world == 1:
+    # decoder: up to 64 tokens after the same prompt; its picks must be the
+    # per-op step's (bit-identical by construction)
+    n_p = min(64, G)
+    if world == 1 and n_p > 0:
         from eosllm_b200.text import TextDecoder as _TD
         dec.set_step_mode(_TD.STEP_PERSISTENT)
         dec.reset()
         p_first = dec.generate(prompt, 1)
         ev2 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         ev2[0].record(st)
-        p_toks = dec.generate(p_first, 64)
+        p_toks = dec.generate(p_first, n_p)
         ev2[1].record(st)
         torch.cuda.synchronize()
         p_ms = ev2[0].elapsed_time(ev2[1])
-        out["persistent_step"] = {"tok_s": round(64 / (p_ms * 1e-3), 2), "ms_per_token": round(p_ms / 64, 4),
-                                  "launches_per_token": dec.step_kernels,
+        out["persistent_step"] = {"tok_s": round(n_p / (p_ms * 1e-3), 2), "ms_per_token": round(p_ms / n_p, 4),
+                                  "tokens": n_p, "launches_per_token": dec.step_kernels,
                                   "tokens_equal_per_op": bool(np.array_equal(
-                                      np.concatenate([p_first, p_toks]), np.concatenate([first, toks[:64]])))}
+                                      np.concatenate([p_first, p_toks]), np.concatenate([first, toks[:n_p]])))}
         dec.set_step_mode(_TD.STEP_PER_OP)
     dec.close()
     if host_model is not None:
