@@ -32,8 +32,12 @@
 // Kernel: one CTA per 128 x 128 output tile, 576 threads.  Warp 0 lane 0 is
 // the TMA producer, warp 1 lane 0 the MMA issuer, warps 2..17 the epilogue
 // (warp w reads TMEM lanes 32(w % 4) .. +31 = tile rows, columns
-// 32((w - 2) / 4) .. +31; four epilogue warps per SM sub-partition hide the
-// TMEM-load and shared-memory latencies).  A stage holds a 64-element K
+// 32((w - 2) / 4) .. +31, as two 16x256b fragments: a thread holds 4 rows x 4
+// column pairs, so a column pair's scales are one 8-byte load over 4
+// addresses per warp -- a thread per row with 32 columns read every
+// column's scales as warp-uniform 16-byte loads, 4 wavefronts each, and ran
+// 6 % slower; four epilogue warps per SM sub-partition hide the TMEM-load
+// and shared-memory latencies).  A stage holds a 64-element K
 // slice (two sub-blocks): the A and B tiles (128B-swizzled, K-major) and the
 // two sub-blocks' scale rows of the tile's rows and columns = 36 KB; four
 // stages.  TMEM holds four f32 accumulators of 128 columns (512 columns),
@@ -50,7 +54,7 @@
 // packed add fed by a packed multiply into a packed FMA even with .rn (on
 // this toolchain the contracted pair equalled fma.rn.f32x2 in every case and
 // differed from multiply-then-add in 27 % of random pairs).  The accumulator
-// is read in two halves of 16 columns (fewer live registers: 96 a thread).
+// is read one 16-lane fragment at a time (fewer live registers: 95 a thread).
 //
 // Waits are bounded (EOS_WAIT_LIMIT_NS): on a timeout the waiting role
 // records an error bit and stops; the MMA issuer always commits the "done"
@@ -208,11 +212,13 @@ __device__ __forceinline__ void qg_tma_2d(void* dst, const CUtensorMap* map, uin
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// 32 consecutive accumulator columns (f32 bits) of this thread's TMEM lane.
-// 16 consecutive accumulator columns of the warp's 32 TMEM lanes.
-__device__ __forceinline__ void qg_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+// Two 16x256b fragments' worth: 32 accumulator columns of 16 TMEM lanes (the
+// address's lane field), four 8-column chunks; thread t gets, per chunk c,
+// r[4c .. 4c+1] = row t/4, columns 8c + 2(t%4) + {0, 1}, and r[4c+2 .. 4c+3]
+// the same columns of row t/4 + 8.
+__device__ __forceinline__ void qg_ld16x256(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 "
       "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n\t"
       "tcgen05.wait::ld.sync.aligned;"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
@@ -336,12 +342,18 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     }
   } else {
     // ---- epilogue: s32 dots -> reference-order f32 terms, partials, row sums ----
+    // The warp's 32 TMEM lanes (tile rows quad * 32 ..) and 32 columns (col0
+    // ..) are read as two 16x256b fragments of 16 lanes x 32 columns: thread
+    // t holds rows quad * 32 + 8 h + t / 4 (h = 0..3; h / 2 is the fragment)
+    // and, for c = 0..3, the column pair col0 + 8 c + 2 (t % 4) + {0, 1}.  A
+    // column pair's two scales come from one 8-byte load (4 addresses per
+    // warp), a row's from 4-byte loads (8 addresses per warp).
     const uint32_t e = warp - 2u, quad = warp & 3u, cg = e >> 2;
-    const uint32_t lrow = quad * 32u + lane;  // tile row of this thread
-    const uint32_t col0 = cg * QG_COLS;       // first tile column of this thread
-    // row sums c (updated once per super-block) in shared memory, columns
-    // 4 c4 .. 4 c4 + 3 at acc[32 c4]; super-block partials (updated every
-    // sub-block) in registers, reset to 0 after each super-block
+    const uint32_t rq = lane >> 2, cq = lane & 3u;
+    const uint32_t col0 = cg * QG_COLS;  // first tile column of this warp
+    // row sums c (updated once per super-block) in shared memory, this
+    // thread's 32 outputs as 8 float4 at acc[32 i]; super-block partials
+    // (updated every sub-block) in registers: part[8 h + 2 c + x]
     float4* acc = reinterpret_cast<float4*>(acc_s) + e * (QG_COLS / 4u) * 32u + lane;
     float part[QG_COLS];
 #pragma unroll
@@ -361,37 +373,41 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&tfull[a], (g / QG_ACCS) & 1u)) != 0;
         if (!ok) break;
         tc_fence_after();
-        const float as = as_s[(2u * j) * QG_BM + lrow], sum = as_s[(2u * j + 1u) * QG_BM + lrow];
-        const float2 as2 = make_float2(as, as), sum2 = make_float2(sum, sum);
-        // the accumulator's 32 columns in two halves of 16 (fewer live registers)
+        const float2* dsc = reinterpret_cast<const float2*>(bs_s + (2u * j) * QG_BN + col0) + cq;       // d*sc
+        const float2* nmn = reinterpret_cast<const float2*>(bs_s + (2u * j + 1u) * QG_BN + col0) + cq;  // -(dmin*m)
+        // the two fragments (16 lanes each) in turn: fewer live registers
 #pragma unroll
         for (uint32_t hh = 0; hh < 2; ++hh) {
           uint32_t r[16];
-          qg_ld16(tmem + ((quad * 32u) << 16) + a * QG_BN + col0 + 16u * hh, r);
+          qg_ld16x256(tmem + ((quad * 32u + 16u * hh) << 16) + a * QG_BN + col0, r);
           if (hh == 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[a]);  // accumulator a may be overwritten
           }
-          const float4* dsc = reinterpret_cast<const float4*>(bs_s + (2u * j) * QG_BN + col0 + 16u * hh);       // d*sc
-          const float4* nmn = reinterpret_cast<const float4*>(bs_s + (2u * j + 1u) * QG_BN + col0 + 16u * hh);  // -(dmin*m)
+          float2 as2[2], sum2[2];
 #pragma unroll
-          for (uint32_t c4 = 0; c4 < 4; ++c4) {
-            const float4 dd = dsc[c4], nn = nmn[c4];  // broadcast
-            const float2 d2[2] = {make_float2(dd.x, dd.y), make_float2(dd.z, dd.w)};
-            const float2 n2[2] = {make_float2(nn.x, nn.y), make_float2(nn.z, nn.w)};
+          for (uint32_t hl = 0; hl < 2; ++hl) {
+            const uint32_t lrow = quad * 32u + 16u * hh + 8u * hl + rq;
+            const float as = as_s[(2u * j) * QG_BM + lrow], sum = as_s[(2u * j + 1u) * QG_BM + lrow];
+            as2[hl] = make_float2(as, as);
+            sum2[hl] = make_float2(sum, sum);
+          }
 #pragma unroll
-            for (uint32_t i = 0; i < 2; ++i) {
-              const uint32_t cl = 4u * c4 + 2u * i, c = 16u * hh + cl;  // columns c, c + 1: the two lanes of a pair
-              const float2 dot = make_float2(__uint_as_float(r[cl]), __uint_as_float(r[cl + 1]));
+          for (uint32_t c = 0; c < 4; ++c) {
+            const float2 d2 = dsc[4u * c], n2 = nmn[4u * c];  // columns col0 + 8 c + 2 cq + {0, 1}
+#pragma unroll
+            for (uint32_t hl = 0; hl < 2; ++hl) {
+              const uint32_t pi = 8u * (2u * hh + hl) + 2u * c;  // part index of the pair
+              const float2 dot = make_float2(__uint_as_float(r[4u * c + 2u * hl]), __uint_as_float(r[4u * c + 2u * hl + 1u]));
               // t = ((d*sc)*as)*dot - ((dmin*m)*as)*sum   (:254-261), as t1 + (-t2): the four
               // products in pairs, t1 + t2 as two scalar adds (a packed add fed by a
               // packed multiply is contracted into a fused multiply-add by ptxas)
-              const float2 t1 = mul2_rn(mul2_rn(d2[i], as2), dot), t2 = mul2_rn(mul2_rn(n2[i], as2), sum2);
+              const float2 t1 = mul2_rn(mul2_rn(d2, as2[hl]), dot), t2 = mul2_rn(mul2_rn(n2, as2[hl]), sum2[hl]);
               const float2 t = make_float2(__fadd_rn(t1.x, t2.x), __fadd_rn(t1.y, t2.y));
-              const float2 pc = add2_rn(make_float2(part[c], part[c + 1]), t);  // partial += t
-              part[c] = pc.x;
-              part[c + 1] = pc.y;
+              const float2 pc = add2_rn(make_float2(part[pi], part[pi + 1]), t);  // partial += t
+              part[pi] = pc.x;
+              part[pi + 1] = pc.y;
             }
           }
         }
@@ -415,29 +431,37 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     if (!ok) {
       if (lane == 0) report(p.err, EOS_DEVERR_WAIT_FULL);
     } else {
-      const uint32_t row = m0 + lrow, gcol = n0 + col0;
-      if (row < p.m) {
-        float* crow = p.c + (size_t)row * p.ldc + gcol;
-        if (gcol + QG_COLS <= p.n && (p.ldc & 3u) == 0) {
+      // output pair (h, c): row m0 + quad * 32 + 8 h + t / 4, columns
+      // n0 + col0 + 8 c + 2 (t % 4) + {0, 1} = acc float4 2 h + c / 2, half c % 2;
+      // 8-byte stores where every destination allows them
+      bool pair_ok = (p.ldc & 1u) == 0 && (reinterpret_cast<uintptr_t>(p.c) & 7u) == 0;
+      for (uint32_t x = 0; x < p.n_extra; ++x) pair_ok = pair_ok && (reinterpret_cast<uintptr_t>(p.c_extra[x]) & 7u) == 0;
 #pragma unroll
-          for (uint32_t c4 = 0; c4 < QG_COLS / 4; ++c4) {
-            float4 v = acc[32 * c4];
+      for (uint32_t h = 0; h < 4; ++h) {
+        const uint32_t row = m0 + quad * 32u + 8u * h + rq;
+        if (row >= p.m) continue;
+#pragma unroll
+        for (uint32_t c = 0; c < 4; ++c) {
+          const float4 v4 = acc[32 * (2u * h + c / 2u)];
+          float2 v = (c & 1u) ? make_float2(v4.z, v4.w) : make_float2(v4.x, v4.y);
+          const uint32_t gcol = n0 + col0 + 8u * c + 2u * cq;
+          const size_t at = (size_t)row * p.ldc + gcol;
+          if (pair_ok && gcol + 2u <= p.n) {
             if (p.accumulate) {
-              const float4 o = *reinterpret_cast<const float4*>(crow + 4 * c4);
-              v = make_float4(__fadd_rn(o.x, v.x), __fadd_rn(o.y, v.y), __fadd_rn(o.z, v.z), __fadd_rn(o.w, v.w));
+              const float2 o = *reinterpret_cast<const float2*>(p.c + at);
+              v = make_float2(__fadd_rn(o.x, v.x), __fadd_rn(o.y, v.y));
             }
-            *reinterpret_cast<float4*>(crow + 4 * c4) = v;
-            for (uint32_t x = 0; x < p.n_extra; ++x)
-              *reinterpret_cast<float4*>(p.c_extra[x] + (size_t)row * p.ldc + gcol + 4 * c4) = v;
-          }
-        } else {
+            *reinterpret_cast<float2*>(p.c + at) = v;
+            for (uint32_t x = 0; x < p.n_extra; ++x) *reinterpret_cast<float2*>(p.c_extra[x] + at) = v;
+          } else {
 #pragma unroll
-          for (uint32_t c = 0; c < QG_COLS; ++c) {
-            const float4 v4 = acc[32 * (c / 4)];
-            const float v = (c & 3u) == 0 ? v4.x : ((c & 3u) == 1 ? v4.y : ((c & 3u) == 2 ? v4.z : v4.w));
-            if (gcol + c < p.n) {
-              crow[c] = p.accumulate ? __fadd_rn(crow[c], v) : v;
-              for (uint32_t x = 0; x < p.n_extra; ++x) p.c_extra[x][(size_t)row * p.ldc + gcol + c] = v;
+            for (uint32_t x2 = 0; x2 < 2; ++x2) {
+              if (gcol + x2 < p.n) {
+                const float vv = x2 ? v.y : v.x;
+                const float w = p.accumulate ? __fadd_rn(p.c[at + x2], vv) : vv;
+                p.c[at + x2] = w;
+                for (uint32_t x = 0; x < p.n_extra; ++x) p.c_extra[x][at + x2] = vv;
+              }
             }
           }
         }
