@@ -35,7 +35,9 @@ def _run(gpu, oracle, m, n, k, seed, a_scale=1.0, a=None):
 
 
 @pytest.mark.parametrize("m,n,k", [(128, 256, 256), (128, 512, 4096), (200, 300, 512), (384, 1000, 1024),
-                                   (512, 11008, 4096), (64, 256, 11008), (1, 130, 512), (257, 4, 768)])
+                                   (512, 11008, 4096), (64, 256, 11008), (1, 130, 512), (257, 4, 768),
+                                   # odd n: a column pair straddles the last column, rows of odd length
+                                   (200, 301, 512), (5, 7, 256)])
 def test_prefill_bit_exact_with_int8_reference(gpu, oracle, m, n, k):
     got, ref, *_ = _run(gpu, oracle, m, n, k, seed=m + n)
     np.testing.assert_array_equal(got.view(np.uint32), ref.reshape(m, n).view(np.uint32))
