@@ -177,3 +177,95 @@ def test_reference_engine_with_cuda_backend(gpu, oracle, tmp_path, name):
         err = np.max(np.abs(lg_gpu - lg_cpu), axis=1) / rms
         assert err.max() <= 2e-3, err
         assert len(gen_gpu) == N_GEN
+
+
+# The engine's microbenchmark, tools/eosllm-bench/main.c: bench_matmul_q
+# (:128-219) finds a backend by name in the engine's registry (find_backend,
+# :83-93), probes it and times ops.matmul_q over k_shapes (:40-50), and main()
+# lists the backends by name (:274-277), so timing the GPU needs one more
+# line there: bench_matmul_q("cuda", "q4_k", EOS_DT_Q4_K, 256).  This runs that
+# loop through the same registry for "cuda" and "x86_avx2", with records in
+# emit()'s format (:64-78), and checks the two backends' outputs bit for bit.
+BENCH_SHAPES = [(1, 1, 256), (1, 8, 512), (1, 64, 1024), (1, 128, 2048), (1, 512, 2048), (1, 256, 4096)]
+EOSI_MAX_BACKENDS = 16  # src/core/internal.h:21
+
+
+class _BackendVt(C.Structure):  # eos_backend_vt_t (include/eosllm/backend.h:67-82)
+    _fields_ = [("name", C.c_char_p), ("priority", C.c_int32), ("probe", C.c_void_p), ("ops", _Ops)]
+
+
+class _RegistryHead(C.Structure):  # leading fields of eosi_registry_t (src/core/internal.h:28-30)
+    _fields_ = [("backends", C.POINTER(_BackendVt) * EOSI_MAX_BACKENDS), ("n_backends", C.c_size_t)]
+
+
+def _n_iters(m, n, k):  # n_iters_for (main.c:53-61), capped lower to bound the test's time
+    return int(min(max(5e8 / (2.0 * m * n * k), 1), 2000))
+
+
+def _bench_child(shapes, weights, acts, q):
+    try:
+        import time
+        from oracle.oracle import REF_ENGINE
+        L = C.CDLL(REF_ENGINE, mode=C.RTLD_GLOBAL)
+        assert L.eos_init_defaults() == 0
+        glue = C.CDLL(GLUE, mode=C.RTLD_GLOBAL)
+        assert glue.eosi_backend_cuda_register() == 0
+        L.eosi_registry.restype = C.POINTER(_RegistryHead)
+        reg = L.eosi_registry().contents
+        vts = {}
+        for i in range(reg.n_backends):
+            vt = reg.backends[i]
+            if vt:
+                vts[vt.contents.name.decode()] = vt.contents
+        probe_t = C.CFUNCTYPE(C.c_int)
+        mm_t = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32)
+        out = {"names": sorted(vts), "records": [], "outputs": {}}
+        for name in ("cuda", "x86_avx2"):
+            vt = vts[name]
+            if vt.probe:
+                assert probe_t(vt.probe)() == 0, name
+            mm = mm_t(vt.ops.matmul_q)
+            outs = []
+            for (m, n, k), w, a in zip(shapes, weights, acts):
+                c = np.empty(m * n, np.float32)
+                assert mm(a.ctypes.data, w.ctypes.data, 33, c.ctypes.data, m, n, k) == 0, (name, m, n, k)
+                it = _n_iters(m, n, k)
+                t0 = time.perf_counter_ns()
+                for _ in range(it):
+                    mm(a.ctypes.data, w.ctypes.data, 33, c.ctypes.data, m, n, k)
+                t1 = time.perf_counter_ns()
+                ops = 2.0 * m * n * k
+                out["records"].append({"backend": name, "op": "matmul_q4_k", "m": m, "n": n, "k": k, "n_iters": it,
+                                       "total_ns": t1 - t0, "ns_per_iter": round((t1 - t0) / it, 1),
+                                       "giga_ops_per_s": round(ops * it / (t1 - t0), 2)})
+                outs.append(c)
+            out["outputs"][name] = outs
+        q.put(out)
+    except Exception as e:  # report, never hang the parent
+        q.put(repr(e))
+
+
+def test_engine_bench_matmul_q_through_the_registry(gpu, oracle, capsys):
+    from oracle.oracle import REF_ENGINE
+    if not (os.path.exists(REF_ENGINE) and os.path.exists(GLUE)):
+        pytest.skip("oracle/_ref not built (make -C oracle ref where the reference tree exists)")
+    import json
+
+    import torch.multiprocessing as mp
+    weights, acts = [], []
+    for i, (m, n, k) in enumerate(BENCH_SHAPES):
+        weights.append(oracle.q4_k_quantize(oracle.gauss(n * k, 60 + i, 0.1)))
+        acts.append(oracle.gauss(m * k, 70 + i, 1.0))
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_bench_child, args=(BENCH_SHAPES, weights, acts, q))
+    p.start()
+    res = q.get(timeout=900)
+    p.join(timeout=120)
+    assert not isinstance(res, str), res
+    assert "cuda" in res["names"] and "x86_avx2" in res["names"], res["names"]
+    for (m, n, k), g, r in zip(BENCH_SHAPES, res["outputs"]["cuda"], res["outputs"]["x86_avx2"]):
+        np.testing.assert_array_equal(g.view(np.uint32), r.view(np.uint32), err_msg=f"{m}x{n}x{k}")
+    with capsys.disabled():
+        for rec in res["records"]:
+            print(json.dumps(rec))
