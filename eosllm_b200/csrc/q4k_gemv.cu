@@ -81,21 +81,34 @@ __global__ void __launch_bounds__(256) act_pack_kernel(const float* __restrict__
 // per warp into whole 128-byte lines on the PCIe link.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) copy_out_kernel(const uint4* src, uint4* dst, uint32_t n16) {
-  pdl_wait();  // src is the previous grid's output
+  pdl_trigger();  // the done-flag kernel may become resident (it waits for this grid)
+  pdl_wait();     // src is the previous grid's output
   for (uint32_t i = blockIdx.x * 256u + threadIdx.x; i < n16; i += gridDim.x * 256u) dst[i] = src[i];
 }
 
 // One thread raises *flag (mapped host memory) once every kernel before it on
 // the stream has completed: the host waits for the word instead of for the
 // stream (no synchronisation call on the path of a host-pointer matmul).
+// Launched with programmatic dependent launch: resident while the copy runs,
+// it waits for the copy grid's completion (its stores performed), then
+// fences at system scope before the flag's release store.
 __global__ void done_flag_kernel(uint32_t* flag) {
+  pdl_wait();
   __threadfence_system();
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(1u) : "memory");
 }
 
 cudaError_t launch_done_flag(uint32_t* flag, cudaStream_t st) {
-  done_flag_kernel<<<1, 1, 0, st>>>(flag);
-  return cudaGetLastError();
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(1);
+  lc.blockDim = dim3(1);
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, done_flag_kernel, flag);
 }
 
 cudaError_t launch_copy_out(const void* src, void* dst, size_t bytes, cudaStream_t st) {
