@@ -199,8 +199,9 @@ __host__ __device__ constexpr uint32_t pf_attn_smem_bytes() {
   return 4u * (kPfQ * 32u * E + 2u * (kPfKC * (32u * E + 4u) + kPfKC * 32u * E) + 4u * 32u * E);
 }
 
-// Grid (hl, ceil(m / 16)), 128 threads.  CTA (h, b) owns query rows
-// [16 b, 16 b + 16) of local head h; warp w owns four of them.  Cache
+// Grid (hl, ceil(m / 16)), 128 threads.  CTA (h, y) owns query rows
+// [16 b, 16 b + 16) of local head h, b = ceil(m / 16) - 1 - y; warp w owns
+// four of them.  Cache
 // positions stream through shared memory 32 at a time (K and V rows of the
 // head's KV group, double-buffered: the next chunk's copies fly while this
 // one is used); lane j scores position c0 + j for the warp's four
@@ -215,7 +216,9 @@ __global__ void __launch_bounds__(128) pf_attn_kernel(const PfAttnParams p) {
   float* qs = sm;                          // [kPfQ][HD]
   float* kv0 = qs + kPfQ * HD;  // buffer b: K [kPfKC][KP] at kv0 + b (KP + HD) kPfKC, then V [kPfKC][HD]
   float* so = kv0 + 2u * kPfKC * (KP + HD);  // [4][HD]
-  const uint32_t hloc = blockIdx.x, i0 = blockIdx.y * kPfQ;
+  // query blocks in reverse launch order: the last ones of a head stream the
+  // most chunks (causal), so they start first and the short ones fill the tail
+  const uint32_t hloc = blockIdx.x, i0 = (gridDim.y - 1u - blockIdx.y) * kPfQ;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   const uint32_t gh = p.h0 + hloc;
   const uint32_t gkv = (gh * p.n_kv_head) / p.n_head;  // GQA map (text.c:367)
